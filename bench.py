@@ -1,0 +1,401 @@
+#!/usr/bin/env python
+"""Benchmark of the PaxBlock64 scan hot path (BASELINE metric: QPS at 1M x 768, 64 B/vec,
+shortlist 256; scan GB/s vs HBM peak).
+
+Workload (N=1): BASELINE config 2 — 1,000,000 unit-norm 768-d docs (x_d ~ (d+1)^-1/2 * z,
+z ~ Irwin-Hall(12)-6, L2-normalised; seeded), EDEN-prod 4-bit prefix + RaBitQ mid + folded tail,
+single-query batches (one query per step, noisy-copy queries, sigma 0.1), shortlist 256, full_64b,
+w_s4 0.20, cs_tolerance 1.0, temporal filter off. A step = plan build + fused scan/top-k of one
+query over the whole 64 MB corpus. L2 (126 MB, larger than the corpus) is flushed before every
+step by a 512 MiB device memset outside the per-step CUDA events.
+
+N > 1 (torchrun, one rank per GPU): each rank holds its own 1M-doc shard (weak scaling); a step is
+one query against every shard followed by an NCCL all-gather of the per-shard top-256 and a merge.
+value = N * steps / time (1M-doc shard queries per second, whole job).
+
+--impl reference: the reference's CPU scan restated by the oracle (scan_blocks with the Rayon
+sharding rules, all host threads) on the same workload, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mrl-index-rust-vector_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+METRIC = "QPS at 1M×768 64B/vec shortlist 256 (1/2/4/8 GPU); scan GB/s vs HBM peak"
+DOC_SEED, Q_SEED = 42, 7
+SIGMA = 0.1
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--docs", type=int, default=1_000_000)
+    ap.add_argument("--dims", type=int, default=768)
+    ap.add_argument("--k", type=int, default=256)
+    ap.add_argument("--mode", choices=["fast", "exact"], default="fast")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--e2e-steps", type=int, default=2000)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic(mode: str):
+    """dram bytes per scan launch recorded from an ncu capture (profiles/*.md), or None."""
+    path = os.path.join(ROOT, "profiles", f"scan_{mode}_1m.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        out, _ = self.p.communicate(timeout=10)
+        sm, mx, reasons = [], [], set()
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names[1:], f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def build_corpus_gpu(M, dev, n, dims, row0):
+    """Synthesise, fit (rank 0's EDEN mean is broadcast by the caller) and encode on the device."""
+    import torch
+
+    lib = M.load()
+    x = torch.empty((n, dims), dtype=torch.float32, device="cuda")
+    M._capi.check(dev.ptr, lib.mrl_synth_docs_device(dev.ptr, DOC_SEED, row0, n, dims, C.c_void_p(x.data_ptr())))
+    mean = np.zeros(64, np.float32)
+    M._capi.check(dev.ptr, lib.mrl_eden_fit_device(dev.ptr, C.c_void_p(x.data_ptr()), n, dims, 0, 64,
+                                                   mean.ctypes.data_as(C.c_void_p)))
+    return x, mean
+
+
+def encode_gpu(M, dev, x, n, dims, mean, block_id_base):
+    import torch
+
+    lib = M.load()
+    nb = (n + 63) // 64
+    pax = torch.empty(nb * 4096, dtype=torch.uint8, device="cuda")
+    fit = M.EdenFit(64, 4, 1, mean)
+    desc, keep = M.api._codec_desc(M.PrefixCodec.EDEN_PROD, M.MidCodec.RABITQ, fit, None)
+    segp = C.c_void_p()
+    M._capi.check(dev.ptr, lib.mrl_encode_device(dev.ptr, C.c_void_p(x.data_ptr()), n, dims, 8, C.byref(desc),
+                                                 C.c_void_p(pax.data_ptr()), block_id_base, C.byref(segp)))
+    return M.Segment(segp, dev), pax, desc, keep
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    import mrl_b200 as M
+
+    lib = M.load()
+    dev = M.Device(local)
+    torch_stream = torch.cuda.current_stream().cuda_stream
+    dev.set_stream(torch_stream)  # library kernels and torch events share one stream
+    n, dims, k = args.docs, args.dims, args.k
+    nb = (n + 63) // 64
+    warm = max(args.warmup, 3)
+
+    x, mean = build_corpus_gpu(M, dev, n, dims, row0=rank * n)
+    if world > 1:
+        mt = torch.from_numpy(mean).cuda()
+        dist.broadcast(mt, 0)
+        mean = mt.cpu().numpy()
+    seg, pax, desc, keep = encode_gpu(M, dev, x, n, dims, mean, block_id_base=rank * nb)
+    del x
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()  # release the 3 GB of f32 rows: only the 64 MB corpus stays resident
+
+    n_q = warm + args.steps
+    qd = torch.empty((n_q, dims), dtype=torch.float32, device="cuda")
+    M._capi.check(dev.ptr, lib.mrl_synth_queries_device(dev.ptr, DOC_SEED, n, Q_SEED, n_q, dims, C.c_float(SIGMA),
+                                                        C.c_void_p(qd.data_ptr()), None))
+    plans = C.c_void_p()
+    M._capi.check(dev.ptr, lib.mrl_plans_alloc(dev.ptr, 1, dims, C.byref(plans)))
+    mode = M.ScanMode.FAST if args.mode == "fast" else M.ScanMode.EXACT
+    cfg = M.ScanConfig(shortlist_cand=k, temporal_filter_enable=False, mode=mode).to_c()
+    out_ids = torch.empty((1, k), dtype=torch.int64, device="cuda")
+    out_sc = torch.empty((1, k), dtype=torch.float32, device="cuda")
+    out_cnt = torch.empty(1, dtype=torch.int32, device="cuda")
+    out_st = torch.zeros(args.steps + warm, dtype=torch.int32, device="cuda")
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    if world > 1:
+        g_ids = torch.empty((world, k), dtype=torch.int64, device="cuda")
+        g_sc = torch.empty((world, k), dtype=torch.float32, device="cuda")
+    qbytes = dims * 4
+
+    def one_step(i, ev):
+        flush.zero_()
+        ev[0].record()
+        M._capi.check(dev.ptr, lib.mrl_plan_build_device(dev.ptr, C.c_void_p(qd.data_ptr() + i * qbytes), 1, dims,
+                                                         C.byref(desc), plans))
+        ev[1].record()
+        M._capi.check(dev.ptr, lib.mrl_scan_device(dev.ptr, seg.ptr, plans, 0, 1, C.byref(cfg), None, None,
+                                                   C.c_void_p(out_ids.data_ptr()), C.c_void_p(out_sc.data_ptr()),
+                                                   C.c_void_p(out_cnt.data_ptr()),
+                                                   C.c_void_p(out_st.data_ptr() + 4 * i)))
+        ev[2].record()
+        if world > 1:
+            dist.all_gather_into_tensor(g_ids, out_ids)
+            dist.all_gather_into_tensor(g_sc, out_sc)
+            ids = g_ids.reshape(-1)
+            sc = g_sc.reshape(-1)
+            o1 = torch.sort(ids, stable=True).indices
+            o2 = torch.sort(sc[o1], descending=True, stable=True).indices
+            _top = ids[o1[o2[:k]]]
+        ev[3].record()
+
+    def mk():
+        return [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+
+    for i in range(warm):
+        one_step(i, mk())
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    evs = [mk() for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        one_step(warm + i, evs[i])
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    time.sleep(0.2)
+    clk = clocks.stop()
+    step_ms = np.array([e[0].elapsed_time(e[3]) for e in evs])
+    plan_ms = np.array([e[0].elapsed_time(e[1]) for e in evs])
+    scan_ms = np.array([e[1].elapsed_time(e[2]) for e in evs])
+    total_ms = float(step_ms.sum())
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    n_fallback = int((out_st[warm:] != 0).sum().item())
+
+    # e2e through the reference-facing C ABI with pinned host buffers (copies inside the timing)
+    e2e = None
+    if world == 1:
+        dev.set_stream(0)  # the context's own stream; mrl_scan synchronises it
+        qh = torch.empty((n_q, dims), dtype=torch.float32, pin_memory=True)
+        qh.copy_(qd.cpu())
+        ids_h = torch.empty(k, dtype=torch.int64, pin_memory=True)
+        sc_h = torch.empty(k, dtype=torch.float32, pin_memory=True)
+        cnt_h = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        e2e_steps = min(args.e2e_steps, n_q)
+        tot = 0.0
+        for i in range(e2e_steps + warm):
+            flush.zero_()
+            torch.cuda.synchronize()
+            s = time.perf_counter()
+            M._capi.check(dev.ptr, lib.mrl_plan_rebuild(dev.ptr, C.c_void_p(qh.data_ptr() + (i % n_q) * qbytes), 1,
+                                                        dims, C.byref(desc), plans))
+            M._capi.check(dev.ptr, lib.mrl_scan(dev.ptr, seg.ptr, plans, C.byref(cfg), None, None,
+                                                C.c_void_p(ids_h.data_ptr()), C.c_void_p(sc_h.data_ptr()),
+                                                C.c_void_p(cnt_h.data_ptr())))
+            if i >= warm:
+                tot += time.perf_counter() - s
+        e2e = {"value": e2e_steps / tot, "unit": "QPS", "h2d_bytes_per_step": qbytes + 192 * 4,
+               "d2h_bytes_per_step": k * 12 + 4, "steps": e2e_steps,
+               "path": "mrl_plan_rebuild + mrl_scan (host pinned buffers, synchronous)"}
+        dev.set_stream(torch_stream)
+
+    peak, peak_kind = measured_peaks()
+    alg_bytes = nb * 4096
+    scan_avg_s = float(scan_ms.mean()) / 1e3
+    achieved = alg_bytes / scan_avg_s / 1e9
+    line = {
+        "metric": METRIC,
+        "value": world * args.steps / (total_ms / 1e3),
+        "unit": "QPS" if world == 1 else "1M-doc shard queries/s",
+        "n_gpus": world, "steps": args.steps, "warmup": warm,
+        "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int32+f32" if args.mode == "fast" else "f32",
+        "data": "synthetic",
+        "config": {"workload": "config 2: single-query scan, 1M x 768 docs per GPU, EDEN-prod + RaBitQ + folded tail,"
+                               " shortlist 256, full_64b", "docs_per_gpu": n, "dims": dims, "batch": 1,
+                   "shortlist": k, "mode": args.mode, "parallelism": f"shard{world}",
+                   "l2": "flushed before every step (512 MiB memset, outside the per-step events)",
+                   "wall_s_bracketed": t1 - t0, "plan_ms_mean": float(plan_ms.mean()),
+                   "scan_ms_mean": float(scan_ms.mean()), "scan_ms_p50": float(np.median(scan_ms)),
+                   "scan_ms_p99": float(np.percentile(scan_ms, 99)), "reselection_steps": n_fallback},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "traffic": profiled_traffic(args.mode),
+                     "kernel": "scan_kernel", "alg_bytes_per_launch": alg_bytes},
+        "clocks": clk,
+        "gpu_launches": 2 * args.steps,
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args, pax, mean, qd, seg, M, dev, cfg)
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    seg.free()
+    lib.mrl_plans_free(dev.ptr, plans)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_baseline(args, pax, mean, qd, seg, M, dev, cfg):
+    """The oracle's threaded reference scan on a bounded sample of the same queries."""
+    import ora
+
+    blocks = pax.cpu().numpy()
+    qs = qd.cpu().numpy()
+    threads = os.cpu_count() or 1
+    ocfg = ora.scan_cfg(k=args.k)
+    n_done, t_tot, mism, maxrel = 0, 0.0, 0, 0.0
+    deadline = time.perf_counter() + args.cpu_seconds
+    while n_done < 3 or time.perf_counter() < deadline:
+        q = qs[n_done % qs.shape[0]]
+        p = ora.plan_build(q, eden_mean=mean)
+        s = time.perf_counter()
+        rid, rsc = ora.scan_blocks(blocks, p, ocfg, threads=threads)
+        t_tot += time.perf_counter() - s
+        if n_done < 5:  # parity spot check against the GPU result for the same query
+            gp = M.QueryPlan.from_query_eden(q, args.dims, M.EdenFit(64, 4, 1, mean), dev=dev)
+            hits = M.scan_blocks(seg, gp, M.ScanConfig(shortlist_cand=args.k, temporal_filter_enable=False,
+                                                       mode=M.ScanMode(cfg.mode)))
+            gmap = {h.id.as_u64(): h.score for h in hits}
+            rmap = dict(zip(map(int, rid), map(float, rsc)))
+            kth = float(rsc[-1])
+            for vid in set(gmap) ^ set(rmap):
+                s_ = rmap.get(vid, gmap.get(vid))
+                if abs(s_ - kth) > 1e-5 * abs(kth) + 1e-6:
+                    mism += 1
+            for vid in set(gmap) & set(rmap):
+                maxrel = max(maxrel, abs(gmap[vid] - rmap[vid]) / max(abs(rmap[vid]), 1e-6))
+        n_done += 1
+    return {"value": n_done / t_tot, "unit": "QPS", "cores": threads, "kind": "port",
+            "sample": f"{n_done} single queries, each a full scan of the same 1M x 768 corpus (oracle scan_blocks, "
+                      f"Rayon-rule sharding over {threads} threads)",
+            "parity_spot_check": {"queries": min(n_done, 5), "ids_outside_near_ties": mism,
+                                  "max_rel_score_diff": maxrel}}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import ora
+
+    threads = os.cpu_count() or 1
+    n, dims, k = args.docs, args.dims, args.k
+    warm = max(args.warmup, 3)
+    docs = ora.synth_docs(DOC_SEED, n, dims, threads=threads)
+    mean = ora.eden_fit_prefix(docs)
+    blocks = ora.encode_corpus(docs, eden_mean=mean, threads=threads)
+    del docs
+    qs, _ = ora.synth_queries(DOC_SEED, n, Q_SEED, warm + args.steps, dims, SIGMA)
+    cfg = ora.scan_cfg(k=k)
+    for i in range(warm):
+        ora.scan_blocks(blocks, ora.plan_build(qs[i], eden_mean=mean), cfg, threads=threads)
+    tot = 0.0
+    for i in range(args.steps):
+        s = time.perf_counter()
+        p = ora.plan_build(qs[warm + i], eden_mean=mean)
+        ora.scan_blocks(blocks, p, cfg, threads=threads)
+        tot += time.perf_counter() - s
+    val = args.steps / tot
+    line = {
+        "metric": METRIC, "value": val, "unit": "QPS", "n_gpus": world, "steps": args.steps, "warmup": warm,
+        "ms_per_step": tot * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "config 2: single-query scan, 1M x 768 docs, EDEN-prod + RaBitQ + folded tail, "
+                               "shortlist 256, full_64b", "docs": n, "dims": dims, "batch": 1, "shortlist": k},
+        "cpu_baseline": {"value": val, "unit": "QPS", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} single queries, each a full scan of the 1M x 768 corpus "
+                                   f"(oracle restatement of scan_blocks, Rayon-rule sharding over {threads} threads)"},
+        "e2e": {"value": val, "unit": "QPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,201 @@
+/*
+ * mrl_cuda.h — C ABI of the B200 (sm_100a) PaxBlock64 scan library (libmrl_b200.so).
+ *
+ * Drop-in boundary for the reference crate `mrl_index` v0.3.5 scan path. Each entry point names
+ * the reference interface it replaces (file:line relative to the reference project root). Plain
+ * pointers and sizes only; every function returns an int status (0 = OK, negative = error) and
+ * never aborts or throws across the boundary; `mrl_last_error` explains the last failure.
+ * Buffers are caller-owned unless a function says otherwise. A context drives one CUDA device
+ * and one stream; it is not thread-safe (callers serialise, as the reference's IndexEngine
+ * already does with its Mutex, src/engine.rs:564-581).
+ *
+ * Units: a block is one 4096-byte PaxBlock64 page (src/block.rs:130-144); a vector id is
+ * VectorId::as_u64 = block << 16 | slot (src/block.rs:213-215).
+ */
+#ifndef MRL_CUDA_H
+#define MRL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MRL_OK 0
+#define MRL_ERR_INVALID (-1) /* bad argument or contract violation (the reference panics) */
+#define MRL_ERR_CUDA (-2)    /* CUDA runtime failure or no usable sm_100 device */
+#define MRL_ERR_NOMEM (-3)   /* device allocation failed */
+
+#define MRL_PREFIX_MINMAX4 0u /* PrefixCodec::MinMax4, src/config.rs:12 */
+#define MRL_PREFIX_EDEN 1u    /* PrefixCodec::EdenProd, src/config.rs:15 */
+#define MRL_MID_RABITQ 0u     /* MidCodec::Rabitq, src/config.rs:24 */
+#define MRL_MID_EDEN_B1 1u    /* MidCodec::EdenB1, src/config.rs:27 */
+#define MRL_DEPTH_L0 0u       /* StrataDepth::L0Only, src/config.rs:38 */
+#define MRL_DEPTH_L1 1u       /* StrataDepth::L1Rabitq, src/config.rs:40 */
+#define MRL_DEPTH_FULL 2u     /* StrataDepth::Full64b, src/config.rs:46 */
+#define MRL_MODE_FAST 0u      /* fixed-point int32 stage sums; f32 scores within 1e-5 relative */
+#define MRL_MODE_EXACT 1u     /* f32 sequential sums, bit-identical to the reference arithmetic */
+
+typedef struct mrl_ctx mrl_ctx;
+typedef struct mrl_seg mrl_seg;
+typedef struct mrl_plans mrl_plans;
+
+/* Field-for-field C mirror of `QueryPlan` (src/scan.rs:19-71). */
+typedef struct mrl_query_plan {
+    uint32_t dims;
+    uint32_t prefix_codec;
+    uint32_t mid_codec;
+    uint32_t has_tail_fold;
+    float prefix[64];
+    float bit_weights[64][4];
+    float rabitq_q[128];
+    float rabitq_scale;
+    float rabitq_weights2[128];
+    float rabitq_base;
+    float rabitq_lut[32][16];
+    float tail_fold_q[64];
+    float tail_fold_weights2[64];
+    float tail_fold_base;
+    float q_tail_norm;
+    float q_mid_norm;
+    float q_after_prefix;
+    float q_after_s1;
+    float s4_abs_budget;
+    float prefix_l1;
+    float prefix_sum;
+    float eden_q_rot[64];
+    float eden_mean_ip;
+    float eden_inv_sqrt_d;
+    float eden_codebook[16];
+    float eden_mid_q_rot[128];
+    float eden_mid_mean_ip;
+    float eden_mid_inv_sqrt_d;
+    float eden_mid_codebook[2];
+} mrl_query_plan;
+
+/* Codec + fitted EDEN centres a plan is built against: `EdenFit` (src/eden.rs:104-113) as
+ * persisted in eden_prefix.json. Host pointers. */
+typedef struct mrl_codec_desc {
+    uint32_t prefix_codec;
+    uint32_t mid_codec;
+    const float* eden_mean; /* [64]; required when prefix_codec == MRL_PREFIX_EDEN */
+    uint64_t eden_seed;
+    const float* mid_mean;  /* [128]; required when mid_codec == MRL_MID_EDEN_B1 */
+    uint64_t mid_seed;
+} mrl_codec_desc;
+
+/* `ScanConfig` (src/config.rs:79-88) plus the device scoring mode. numa_sharding is a CPU
+ * scheduling knob and is ignored on the device. */
+typedef struct mrl_scan_cfg {
+    uint32_t shortlist_cand;
+    float cs_tolerance;
+    float stratum4_weight;
+    uint32_t strata_depth;
+    uint32_t temporal_filter_enable;
+    uint32_t numa_sharding;
+    uint32_t mode;
+} mrl_scan_cfg;
+
+/* ---- context ---------------------------------------------------------------------------- */
+/* Create a context on CUDA device `device` (needs compute capability 10.x). */
+int mrl_ctx_create(int device, mrl_ctx** out);
+void mrl_ctx_destroy(mrl_ctx* ctx);
+const char* mrl_last_error(const mrl_ctx* ctx);
+/* The CUDA stream the context launches on (cudaStream_t as void*). */
+void* mrl_ctx_stream(mrl_ctx* ctx);
+/* Use `stream` (cudaStream_t as void*; NULL = the context's own stream) for later launches. */
+int mrl_ctx_set_stream(mrl_ctx* ctx, void* stream);
+
+/* ---- segments: SegmentReader::open + as_slice (src/segment.rs:88-193) ------------------- */
+/* Upload `n_blocks` PaxBlock64 pages from host memory into HBM. Pages are transcoded on the
+ * device into the scan layout. `block_id_base` is added to the block index of every hit. */
+int mrl_segment_upload(mrl_ctx* ctx, const uint8_t* blocks, uint64_t n_blocks,
+                       uint32_t block_id_base, mrl_seg** out);
+/* SegmentReader::append_live (src/segment.rs:217-232): append one page. */
+int mrl_segment_append(mrl_ctx* ctx, mrl_seg* seg, const uint8_t* block4096);
+int mrl_segment_free(mrl_ctx* ctx, mrl_seg* seg);
+uint64_t mrl_segment_blocks(const mrl_seg* seg);
+/* Device pointer of the scan-layout pages (n_blocks * 4096 bytes) and block time ranges. */
+int mrl_segment_device_ptrs(const mrl_seg* seg, void** pages, void** block_ts);
+/* Copy the scan-layout pages and [min_ts, max_ts] pairs back to host memory (parity tests). */
+int mrl_segment_read_layout(mrl_ctx* ctx, const mrl_seg* seg, uint8_t* out_pages,
+                            uint32_t* out_ts);
+
+/* ---- plans: QueryPlan::from_query_codec (src/scan.rs:105-266) --------------------------- */
+/* Build `n_q` plans from host queries (row-major n_q x dims f32) on the device. */
+int mrl_plan_build(mrl_ctx* ctx, const float* queries, uint32_t n_q, uint32_t dims,
+                   const mrl_codec_desc* codec, mrl_plans** out);
+/* Allocate plan storage for `n_q` queries of `dims` without building. */
+int mrl_plans_alloc(mrl_ctx* ctx, uint32_t n_q, uint32_t dims, mrl_plans** out);
+/* Build plans from device-resident queries into preallocated storage, on the context stream. */
+int mrl_plan_build_device(mrl_ctx* ctx, const float* d_queries, uint32_t n_q, uint32_t dims,
+                          const mrl_codec_desc* codec, mrl_plans* plans);
+/* Rebuild plans [0, n_q) of existing storage from host queries, asynchronously on the context
+ * stream and without allocating (the per-query host path of QueryPipeline::build_plan,
+ * src/pipeline.rs:63-74). The host buffers may be reused once the call returns. */
+int mrl_plan_rebuild(mrl_ctx* ctx, const float* queries, uint32_t n_q, uint32_t dims,
+                     const mrl_codec_desc* codec, mrl_plans* plans);
+int mrl_plans_free(mrl_ctx* ctx, mrl_plans* plans);
+/* Read plan `i`'s reference fields back to the host (parity tests / debugging). */
+int mrl_plan_read(mrl_ctx* ctx, const mrl_plans* plans, uint32_t i, mrl_query_plan* out);
+
+/* ---- scan: scan_blocks / scan_blocks_stats (src/scan.rs:802-886) ------------------------ */
+/* Scan every plan against the segment. time_lo / time_hi are Option<u32> (NULL = None).
+ * Writes, per query q, up to k = cfg->shortlist_cand hits sorted by score descending into
+ * out_ids[q*k ..] and out_scores[q*k ..], and the hit count into out_counts[q]. Host
+ * buffers; synchronous. */
+int mrl_scan(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, const mrl_scan_cfg* cfg,
+             const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* out_ids,
+             float* out_scores, uint32_t* out_counts);
+/* Same scan for plans [q0, q0+n_q) writing device buffers, asynchronously on the context
+ * stream (no host synchronisation). out_status[q] (device, may be NULL) receives the selection
+ * status word: bit 0 = the exact re-selection path ran. */
+int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q0,
+                    uint32_t n_q, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+                    const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
+                    uint32_t* d_out_counts, uint32_t* d_out_status);
+/* Per-vector scores of plan `q` for every slot (n_blocks*64, host), and for MRL_MODE_FAST the
+ * three int32 stage sums per slot (prefix, mid band, folded tail; may be NULL). Inactive slots
+ * (tombstoned or temporally filtered) get score 0 and active 0. */
+int mrl_debug_vector_scores(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q,
+                            const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+                            const uint32_t* time_hi, float* out_scores, uint8_t* out_active,
+                            int32_t* out_partials);
+
+/* ---- encode: encode_block_with_fits (src/quantize.rs:36-96) ----------------------------- */
+/* Encode host rows (n x dims f32, rows 64*b .. 64*b+63 form block b) into PaxBlock64 pages.
+ * ts / src give each row's timestamp and source mask (NULL: ts = row index, src = DOC). */
+int mrl_encode_blocks(mrl_ctx* ctx, const float* rows, uint64_t n, uint32_t dims,
+                      const uint32_t* ts, const uint32_t* src, const mrl_codec_desc* codec,
+                      uint8_t* out_pages);
+/* Device-resident variant: rows, pages (NULL allowed) are device pointers; when `seg_out` is
+ * non-NULL a segment is also created directly in the scan layout. ts = row index. */
+int mrl_encode_device(mrl_ctx* ctx, const float* d_rows, uint64_t n, uint32_t dims, uint32_t src,
+                      const mrl_codec_desc* codec, uint8_t* d_pages, uint32_t block_id_base,
+                      mrl_seg** seg_out);
+/* EdenFit::fit_prefix / fit_band (src/eden.rs:116-161) over device rows; mean to host. */
+int mrl_eden_fit_device(mrl_ctx* ctx, const float* d_rows, uint64_t n, uint32_t dims,
+                        uint32_t start, uint32_t width, float* mean_out);
+
+/* ---- seeded synthetic inputs (benchmarks; same integer recipe as the test oracle) -------- */
+/* Docs: x_d = z_d / sqrt(d+1) with z ~ Irwin-Hall(12) - 6, L2-normalised. Device output. */
+int mrl_synth_docs_device(mrl_ctx* ctx, uint64_t seed, uint64_t row0, uint64_t n, uint32_t dims,
+                          float* d_out);
+/* Queries: a seeded doc plus sigma * z per dim, L2-normalised. Device output. */
+int mrl_synth_queries_device(mrl_ctx* ctx, uint64_t doc_seed, uint64_t n_docs, uint64_t q_seed,
+                             uint64_t n_q, uint32_t dims, float sigma, float* d_out,
+                             uint64_t* d_pick);
+
+/* ---- introspection --------------------------------------------------------------------- */
+/* Number of CTAs the scan kernel launches on this device and the per-CTA candidate list
+ * length used for shortlist k. */
+int mrl_scan_geometry(mrl_ctx* ctx, uint32_t k, uint32_t* ctas, uint32_t* list_len);
+/* Override the per-CTA candidate list length (0 = automatic). Smaller values exercise the
+ * exact re-selection path in tests. */
+int mrl_set_list_len(mrl_ctx* ctx, uint32_t list_len);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MRL_CUDA_H */

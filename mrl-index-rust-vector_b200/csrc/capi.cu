@@ -1,0 +1,578 @@
+// capi.cu — the C ABI of libmrl_b200 (include/mrl_cuda.h): contexts, device segments, plans,
+// scans and encodes. Host-side C++; every entry point catches its own failures and reports them
+// through a status code plus mrl_last_error, never by aborting.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "mrl_internal.cuh"
+
+struct mrl_ctx {
+    int device = 0;
+    int sms = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    unsigned long long* cta_keys = nullptr;  // sms * 32
+    unsigned int* ticket = nullptr;
+    uint32_t list_len_override = 0;
+    // grow-only scratch for host-facing calls: inputs (queries, rows, means) and outputs
+    void* tmp = nullptr;
+    size_t tmp_bytes = 0;
+    void* tmp_out = nullptr;
+    size_t tmp_out_bytes = 0;
+};
+
+struct mrl_seg {
+    uint4* pages = nullptr;
+    uint2* ts = nullptr;
+    uint64_t n_blocks = 0;
+    uint64_t cap_blocks = 0;
+    uint32_t block_id_base = 0;
+};
+
+struct mrl_plans {
+    mrl::DevPlan* d = nullptr;
+    uint32_t n_q = 0;
+    uint32_t dims = 0;
+};
+
+namespace {
+
+int fail(mrl_ctx* ctx, int code, const std::string& msg) {
+    if (ctx) ctx->err = msg;
+    return code;
+}
+
+int cuda_fail(mrl_ctx* ctx, cudaError_t e, const char* what) {
+    return fail(ctx, MRL_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define MRL_CUDA_TRY(ctx, expr)                                   \
+    do {                                                          \
+        cudaError_t _e = (expr);                                  \
+        if (_e != cudaSuccess) return cuda_fail((ctx), _e, #expr); \
+    } while (0)
+
+int set_device(mrl_ctx* ctx) {
+    const cudaError_t e = cudaSetDevice(ctx->device);
+    return e == cudaSuccess ? MRL_OK : cuda_fail(ctx, e, "cudaSetDevice");
+}
+
+int ensure_buf(mrl_ctx* ctx, void** buf, size_t* have, size_t bytes) {
+    if (*have >= bytes) return MRL_OK;
+    if (*buf) cudaFree(*buf);  // synchronises the device: no launch still reads the old buffer
+    *buf = nullptr;
+    *have = 0;
+    const cudaError_t e = cudaMalloc(buf, bytes);
+    if (e != cudaSuccess) return fail(ctx, MRL_ERR_NOMEM, std::string("cudaMalloc scratch: ") + cudaGetErrorString(e));
+    *have = bytes;
+    return MRL_OK;
+}
+int ensure_tmp(mrl_ctx* ctx, size_t bytes) { return ensure_buf(ctx, &ctx->tmp, &ctx->tmp_bytes, bytes); }
+int ensure_out(mrl_ctx* ctx, size_t bytes) { return ensure_buf(ctx, &ctx->tmp_out, &ctx->tmp_out_bytes, bytes); }
+
+uint32_t auto_list_len(uint32_t k, uint32_t ctas) {
+    // Expected top-k members per CTA is k/ctas; keep 2.5x that plus 8, as a power of two in
+    // [16, 32]. Larger concentrations are caught by the final selection's verification.
+    const double want = 2.5 * (double)k / (double)ctas + 8.0;
+    uint32_t l = 16;
+    while (l < want && l < 32) l <<= 1;
+    return l;
+}
+
+int check_cfg(mrl_ctx* ctx, const mrl_scan_cfg* cfg) {
+    if (!cfg) return fail(ctx, MRL_ERR_INVALID, "cfg is NULL");
+    if (cfg->shortlist_cand < 1 || cfg->shortlist_cand > 4096)
+        return fail(ctx, MRL_ERR_INVALID, "shortlist_cand must be in [1, 4096]");
+    if (cfg->strata_depth > MRL_DEPTH_FULL) return fail(ctx, MRL_ERR_INVALID, "strata_depth must be 0, 1 or 2");
+    if (cfg->mode > MRL_MODE_EXACT) return fail(ctx, MRL_ERR_INVALID, "mode must be MRL_MODE_FAST or MRL_MODE_EXACT");
+    if (!std::isfinite(cfg->stratum4_weight) || !std::isfinite(cfg->cs_tolerance))
+        return fail(ctx, MRL_ERR_INVALID, "stratum4_weight and cs_tolerance must be finite");
+    return MRL_OK;
+}
+
+mrl::ScanLaunch make_launch(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q,
+                            const mrl_scan_cfg* cfg, const uint32_t* lo, const uint32_t* hi) {
+    mrl::ScanLaunch p{};
+    p.pages = seg->pages;
+    p.block_ts = seg->ts;
+    p.n_blocks = (uint32_t)seg->n_blocks;
+    p.block_id_base = seg->block_id_base;
+    p.plan = plans->d + q;
+    p.k = cfg->shortlist_cand;
+    p.list_len = ctx->list_len_override ? ctx->list_len_override : auto_list_len(p.k, (uint32_t)ctx->sms);
+    p.w_s4 = cfg->stratum4_weight;
+    p.depth = cfg->strata_depth;
+    p.mode = cfg->mode;
+    p.use_time = cfg->temporal_filter_enable && (lo || hi) ? 1u : 0u;
+    p.has_lo = lo ? 1u : 0u;
+    p.lo = lo ? *lo : 0u;
+    p.has_hi = hi ? 1u : 0u;
+    p.hi = hi ? *hi : 0u;
+    p.cta_keys = ctx->cta_keys;
+    p.ticket = ctx->ticket;
+    return p;
+}
+
+int check_codec(mrl_ctx* ctx, const mrl_codec_desc* codec) {
+    if (!codec) return fail(ctx, MRL_ERR_INVALID, "codec is NULL");
+    if (codec->prefix_codec > MRL_PREFIX_EDEN || codec->mid_codec > MRL_MID_EDEN_B1)
+        return fail(ctx, MRL_ERR_INVALID, "unknown codec");
+    if (codec->prefix_codec == MRL_PREFIX_EDEN && !codec->eden_mean)
+        return fail(ctx, MRL_ERR_INVALID, "EdenProd requires EdenFit (eden_mean)");  // src/scan.rs:116
+    if (codec->mid_codec == MRL_MID_EDEN_B1 && !codec->mid_mean)
+        return fail(ctx, MRL_ERR_INVALID, "EdenB1 mid requires EdenFit (mid_mean)");   // src/scan.rs:121
+    return MRL_OK;
+}
+
+// Copies the codec's host means into device scratch at `dst` (64 + 128 floats).
+int upload_means(mrl_ctx* ctx, const mrl_codec_desc* codec, float* dst) {
+    float h[192];
+    for (int i = 0; i < 192; ++i) h[i] = 0.0f;
+    if (codec->eden_mean) std::memcpy(h, codec->eden_mean, 64 * sizeof(float));
+    if (codec->mid_mean) std::memcpy(h + 64, codec->mid_mean, 128 * sizeof(float));
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(dst, h, sizeof(h), cudaMemcpyHostToDevice, ctx->stream));
+    return MRL_OK;
+}
+
+int seg_reserve(mrl_ctx* ctx, mrl_seg* s, uint64_t blocks) {
+    if (blocks <= s->cap_blocks) return MRL_OK;
+    uint64_t cap = s->cap_blocks ? s->cap_blocks : 64;
+    while (cap < blocks) cap *= 2;
+    uint4* np = nullptr;
+    uint2* nt = nullptr;
+    if (cudaMalloc(&np, cap * (uint64_t)mrl::kBlockBytes) != cudaSuccess) return fail(ctx, MRL_ERR_NOMEM, "cudaMalloc pages");
+    if (cudaMalloc(&nt, cap * sizeof(uint2)) != cudaSuccess) {
+        cudaFree(np);
+        return fail(ctx, MRL_ERR_NOMEM, "cudaMalloc block_ts");
+    }
+    if (s->n_blocks) {
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(np, s->pages, s->n_blocks * (uint64_t)mrl::kBlockBytes, cudaMemcpyDeviceToDevice, ctx->stream));
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(nt, s->ts, s->n_blocks * sizeof(uint2), cudaMemcpyDeviceToDevice, ctx->stream));
+        MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    }
+    cudaFree(s->pages);
+    cudaFree(s->ts);
+    s->pages = np;
+    s->ts = nt;
+    s->cap_blocks = cap;
+    return MRL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mrl_ctx_create(int device, mrl_ctx** out) {
+    if (!out) return MRL_ERR_INVALID;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return MRL_ERR_CUDA;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return MRL_ERR_CUDA;
+    if (prop.major != 10) return MRL_ERR_CUDA;  // built for sm_100a only
+    mrl_ctx* ctx = new mrl_ctx();
+    ctx->device = device;
+    ctx->sms = prop.multiProcessorCount;
+    if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete ctx;
+        return MRL_ERR_CUDA;
+    }
+    ctx->stream = ctx->own_stream;
+    if (cudaMalloc(&ctx->cta_keys, sizeof(unsigned long long) * 32 * (size_t)ctx->sms) != cudaSuccess ||
+        cudaMalloc(&ctx->ticket, sizeof(unsigned int)) != cudaSuccess ||
+        cudaMemset(ctx->ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess) {
+        mrl_ctx_destroy(ctx);
+        return MRL_ERR_NOMEM;
+    }
+    *out = ctx;
+    return MRL_OK;
+}
+
+void mrl_ctx_destroy(mrl_ctx* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->cta_keys);
+    cudaFree(ctx->ticket);
+    cudaFree(ctx->tmp);
+    cudaFree(ctx->tmp_out);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+}
+
+const char* mrl_last_error(const mrl_ctx* ctx) { return ctx ? ctx->err.c_str() : "no context"; }
+
+void* mrl_ctx_stream(mrl_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+int mrl_ctx_set_stream(mrl_ctx* ctx, void* stream) {
+    if (!ctx) return MRL_ERR_INVALID;
+    ctx->stream = stream ? (cudaStream_t)stream : ctx->own_stream;
+    return MRL_OK;
+}
+
+int mrl_segment_upload(mrl_ctx* ctx, const uint8_t* blocks, uint64_t n_blocks, uint32_t block_id_base, mrl_seg** out) {
+    if (!ctx || !out) return MRL_ERR_INVALID;
+    *out = nullptr;
+    if (n_blocks && !blocks) return fail(ctx, MRL_ERR_INVALID, "blocks is NULL");
+    if (n_blocks >= (1ull << 26)) return fail(ctx, MRL_ERR_INVALID, "segment larger than 2^26 pages");
+    if ((uint64_t)block_id_base + n_blocks > (1ull << 32)) return fail(ctx, MRL_ERR_INVALID, "block ids overflow u32");
+    if (int rc = set_device(ctx)) return rc;
+    mrl_seg* s = new mrl_seg();
+    s->block_id_base = block_id_base;
+    if (int rc = seg_reserve(ctx, s, n_blocks ? n_blocks : 1)) { delete s; return rc; }
+    const uint64_t chunk = 16384;  // pages per staging copy (64 MiB)
+    if (n_blocks) {
+        if (int rc = ensure_tmp(ctx, std::min<uint64_t>(n_blocks, chunk) * mrl::kBlockBytes)) { mrl_segment_free(ctx, s); return rc; }
+        for (uint64_t b0 = 0; b0 < n_blocks; b0 += chunk) {
+            const uint64_t nb = std::min<uint64_t>(chunk, n_blocks - b0);
+            cudaError_t e = cudaMemcpyAsync(ctx->tmp, blocks + b0 * mrl::kBlockBytes, nb * mrl::kBlockBytes,
+                                            cudaMemcpyHostToDevice, ctx->stream);
+            if (e != cudaSuccess) { mrl_segment_free(ctx, s); return cuda_fail(ctx, e, "upload copy"); }
+            if (mrl::launch_transcode((const uint8_t*)ctx->tmp, nb, s->pages + b0 * 256, s->ts + b0, ctx->stream)) {
+                mrl_segment_free(ctx, s);
+                return cuda_fail(ctx, cudaGetLastError(), "transcode launch");
+            }
+        }
+    }
+    const cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) { mrl_segment_free(ctx, s); return cuda_fail(ctx, e, "segment upload"); }
+    s->n_blocks = n_blocks;
+    *out = s;
+    return MRL_OK;
+}
+
+int mrl_segment_append(mrl_ctx* ctx, mrl_seg* seg, const uint8_t* block4096) {
+    if (!ctx || !seg || !block4096) return MRL_ERR_INVALID;
+    if (seg->n_blocks + 1 >= (1ull << 26)) return fail(ctx, MRL_ERR_INVALID, "segment larger than 2^26 pages");
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = seg_reserve(ctx, seg, seg->n_blocks + 1)) return rc;
+    if (int rc = ensure_tmp(ctx, mrl::kBlockBytes)) return rc;
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->tmp, block4096, mrl::kBlockBytes, cudaMemcpyHostToDevice, ctx->stream));
+    if (mrl::launch_transcode((const uint8_t*)ctx->tmp, 1, seg->pages + seg->n_blocks * 256, seg->ts + seg->n_blocks, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "transcode launch");
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    seg->n_blocks += 1;
+    return MRL_OK;
+}
+
+int mrl_segment_free(mrl_ctx* ctx, mrl_seg* seg) {
+    if (!seg) return MRL_OK;
+    if (ctx) cudaSetDevice(ctx->device);
+    cudaFree(seg->pages);
+    cudaFree(seg->ts);
+    delete seg;
+    return MRL_OK;
+}
+
+uint64_t mrl_segment_blocks(const mrl_seg* seg) { return seg ? seg->n_blocks : 0; }
+
+int mrl_segment_device_ptrs(const mrl_seg* seg, void** pages, void** block_ts) {
+    if (!seg) return MRL_ERR_INVALID;
+    if (pages) *pages = seg->pages;
+    if (block_ts) *block_ts = seg->ts;
+    return MRL_OK;
+}
+
+int mrl_segment_read_layout(mrl_ctx* ctx, const mrl_seg* seg, uint8_t* out_pages, uint32_t* out_ts) {
+    if (!ctx || !seg) return MRL_ERR_INVALID;
+    if (int rc = set_device(ctx)) return rc;
+    if (out_pages && seg->n_blocks)
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_pages, seg->pages, seg->n_blocks * mrl::kBlockBytes, cudaMemcpyDeviceToHost, ctx->stream));
+    if (out_ts && seg->n_blocks)
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_ts, seg->ts, seg->n_blocks * sizeof(uint2), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return MRL_OK;
+}
+
+int mrl_plans_alloc(mrl_ctx* ctx, uint32_t n_q, uint32_t dims, mrl_plans** out) {
+    if (!ctx || !out) return MRL_ERR_INVALID;
+    *out = nullptr;
+    if (dims < 192) return fail(ctx, MRL_ERR_INVALID, "dims must be >= 192 (src/scan.rs:114)");
+    if (dims > 16384) return fail(ctx, MRL_ERR_INVALID, "dims must be <= 16384");
+    if (int rc = set_device(ctx)) return rc;
+    mrl_plans* p = new mrl_plans();
+    p->n_q = n_q;
+    p->dims = dims;
+    if (n_q && cudaMalloc(&p->d, sizeof(mrl::DevPlan) * (size_t)n_q) != cudaSuccess) {
+        delete p;
+        return fail(ctx, MRL_ERR_NOMEM, "cudaMalloc plans");
+    }
+    *out = p;
+    return MRL_OK;
+}
+
+int mrl_plan_build_device(mrl_ctx* ctx, const float* d_queries, uint32_t n_q, uint32_t dims,
+                          const mrl_codec_desc* codec, mrl_plans* plans) {
+    if (!ctx || !plans) return MRL_ERR_INVALID;
+    if (int rc = check_codec(ctx, codec)) return rc;
+    if (n_q > plans->n_q || dims != plans->dims) return fail(ctx, MRL_ERR_INVALID, "plan storage too small or dims mismatch");
+    if (n_q == 0) return MRL_OK;
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = ensure_tmp(ctx, 192 * sizeof(float))) return rc;
+    float* d_means = (float*)ctx->tmp;
+    if (int rc = upload_means(ctx, codec, d_means)) return rc;
+    if (mrl::launch_plan_build(d_queries, n_q, dims, codec->prefix_codec, codec->mid_codec, d_means, codec->eden_seed,
+                               codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr, codec->mid_seed,
+                               plans->d, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "plan launch");
+    return MRL_OK;
+}
+
+int mrl_plan_build(mrl_ctx* ctx, const float* queries, uint32_t n_q, uint32_t dims, const mrl_codec_desc* codec,
+                   mrl_plans** out) {
+    if (!ctx || !out) return MRL_ERR_INVALID;
+    *out = nullptr;
+    if (n_q && !queries) return fail(ctx, MRL_ERR_INVALID, "queries is NULL");
+    if (int rc = check_codec(ctx, codec)) return rc;
+    for (uint64_t i = 0; i < (uint64_t)n_q * dims; ++i)
+        if (!std::isfinite(queries[i])) return fail(ctx, MRL_ERR_INVALID, "query contains a non-finite value");
+    mrl_plans* p = nullptr;
+    if (int rc = mrl_plans_alloc(ctx, n_q, dims, &p)) return rc;
+    const size_t qbytes = (size_t)n_q * dims * sizeof(float);
+    if (int rc = ensure_tmp(ctx, 192 * sizeof(float) + qbytes)) { mrl_plans_free(ctx, p); return rc; }
+    float* d_means = (float*)ctx->tmp;
+    float* d_q = d_means + 192;
+    if (qbytes) {
+        cudaError_t e = cudaMemcpyAsync(d_q, queries, qbytes, cudaMemcpyHostToDevice, ctx->stream);
+        if (e != cudaSuccess) { mrl_plans_free(ctx, p); return cuda_fail(ctx, e, "query copy"); }
+    }
+    if (int rc = upload_means(ctx, codec, d_means)) { mrl_plans_free(ctx, p); return rc; }
+    if (n_q && mrl::launch_plan_build(d_q, n_q, dims, codec->prefix_codec, codec->mid_codec, d_means, codec->eden_seed,
+                                      codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr, codec->mid_seed, p->d,
+                                      ctx->stream)) {
+        mrl_plans_free(ctx, p);
+        return cuda_fail(ctx, cudaGetLastError(), "plan launch");
+    }
+    const cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) { mrl_plans_free(ctx, p); return cuda_fail(ctx, e, "plan build"); }
+    *out = p;
+    return MRL_OK;
+}
+
+int mrl_plan_rebuild(mrl_ctx* ctx, const float* queries, uint32_t n_q, uint32_t dims, const mrl_codec_desc* codec,
+                     mrl_plans* plans) {
+    if (!ctx || !plans) return MRL_ERR_INVALID;
+    if (n_q && !queries) return fail(ctx, MRL_ERR_INVALID, "queries is NULL");
+    if (int rc = check_codec(ctx, codec)) return rc;
+    if (n_q > plans->n_q || dims != plans->dims) return fail(ctx, MRL_ERR_INVALID, "plan storage too small or dims mismatch");
+    for (uint64_t i = 0; i < (uint64_t)n_q * dims; ++i)
+        if (!std::isfinite(queries[i])) return fail(ctx, MRL_ERR_INVALID, "query contains a non-finite value");
+    if (n_q == 0) return MRL_OK;
+    if (int rc = set_device(ctx)) return rc;
+    const size_t qbytes = (size_t)n_q * dims * sizeof(float);
+    if (int rc = ensure_tmp(ctx, 192 * sizeof(float) + qbytes)) return rc;
+    float* d_means = (float*)ctx->tmp;
+    float* d_q = d_means + 192;
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(d_q, queries, qbytes, cudaMemcpyHostToDevice, ctx->stream));
+    if (int rc = upload_means(ctx, codec, d_means)) return rc;
+    if (mrl::launch_plan_build(d_q, n_q, dims, codec->prefix_codec, codec->mid_codec, d_means, codec->eden_seed,
+                               codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr, codec->mid_seed, plans->d,
+                               ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "plan launch");
+    return MRL_OK;
+}
+
+int mrl_plans_free(mrl_ctx* ctx, mrl_plans* plans) {
+    if (!plans) return MRL_OK;
+    if (ctx) cudaSetDevice(ctx->device);
+    cudaFree(plans->d);
+    delete plans;
+    return MRL_OK;
+}
+
+int mrl_plan_read(mrl_ctx* ctx, const mrl_plans* plans, uint32_t i, mrl_query_plan* out) {
+    if (!ctx || !plans || !out) return MRL_ERR_INVALID;
+    if (i >= plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan index out of range");
+    if (int rc = set_device(ctx)) return rc;
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out, &plans->d[i].qp, sizeof(mrl_query_plan), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return MRL_OK;
+}
+
+int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q0, uint32_t n_q,
+                    const mrl_scan_cfg* cfg, const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* d_out_ids,
+                    float* d_out_scores, uint32_t* d_out_counts, uint32_t* d_out_status) {
+    if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if ((uint64_t)q0 + n_q > plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan range out of bounds");
+    if (n_q && (!d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "output is NULL");
+    if (int rc = set_device(ctx)) return rc;
+    const uint32_t k = cfg->shortlist_cand;
+    for (uint32_t i = 0; i < n_q; ++i) {
+        mrl::ScanLaunch p = make_launch(ctx, seg, plans, q0 + i, cfg, time_lo, time_hi);
+        p.out_ids = d_out_ids + (size_t)i * k;
+        p.out_scores = d_out_scores + (size_t)i * k;
+        p.out_count = d_out_counts + i;
+        p.out_status = d_out_status ? d_out_status + i : nullptr;
+        if (seg->n_blocks == 0) {
+            MRL_CUDA_TRY(ctx, cudaMemsetAsync(p.out_count, 0, sizeof(uint32_t), ctx->stream));
+            if (p.out_status) MRL_CUDA_TRY(ctx, cudaMemsetAsync(p.out_status, 0, sizeof(uint32_t), ctx->stream));
+            continue;
+        }
+        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+    }
+    return MRL_OK;
+}
+
+int mrl_scan(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+             const uint32_t* time_hi, uint64_t* out_ids, float* out_scores, uint32_t* out_counts) {
+    if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg)) return rc;
+    const uint32_t n_q = plans->n_q, k = cfg->shortlist_cand;
+    if (n_q == 0) return MRL_OK;
+    if (!out_ids || !out_scores || !out_counts) return fail(ctx, MRL_ERR_INVALID, "output is NULL");
+    if (int rc = set_device(ctx)) return rc;
+    const size_t nk = (size_t)n_q * k;
+    if (int rc = ensure_out(ctx, nk * (sizeof(uint64_t) + sizeof(float)) + 2 * sizeof(uint32_t) * n_q + 64)) return rc;
+    uint64_t* d_ids = (uint64_t*)ctx->tmp_out;
+    float* d_sc = (float*)(d_ids + nk);
+    uint32_t* d_cnt = (uint32_t*)(d_sc + nk);
+    if (int rc = mrl_scan_device(ctx, seg, plans, 0, n_q, cfg, time_lo, time_hi, d_ids, d_sc, d_cnt, nullptr)) return rc;
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_ids, d_ids, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_scores, d_sc, nk * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_counts, d_cnt, n_q * sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return MRL_OK;
+}
+
+int mrl_debug_vector_scores(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q, const mrl_scan_cfg* cfg,
+                            const uint32_t* time_lo, const uint32_t* time_hi, float* out_scores, uint8_t* out_active,
+                            int32_t* out_partials) {
+    if (!ctx || !seg || !plans || !out_scores || !out_active) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (q >= plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan index out of range");
+    if (int rc = set_device(ctx)) return rc;
+    const size_t n = (size_t)seg->n_blocks * 64;
+    if (n == 0) return MRL_OK;
+    if (int rc = ensure_out(ctx, n * (sizeof(float) + 1 + 3 * sizeof(int32_t)) + 64)) return rc;
+    float* d_sc = (float*)ctx->tmp_out;
+    int32_t* d_parts = (int32_t*)(d_sc + n);
+    uint8_t* d_act = (uint8_t*)(d_parts + 3 * n);
+    mrl::ScanLaunch p = make_launch(ctx, seg, plans, q, cfg, time_lo, time_hi);
+    if (mrl::launch_debug_scores(p, d_sc, d_act, d_parts, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "debug launch");
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_scores, d_sc, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_active, d_act, n, cudaMemcpyDeviceToHost, ctx->stream));
+    if (out_partials)
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_partials, d_parts, 3 * n * sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return MRL_OK;
+}
+
+int mrl_encode_device(mrl_ctx* ctx, const float* d_rows, uint64_t n, uint32_t dims, uint32_t src,
+                      const mrl_codec_desc* codec, uint8_t* d_pages, uint32_t block_id_base, mrl_seg** seg_out) {
+    if (!ctx) return MRL_ERR_INVALID;
+    if (seg_out) *seg_out = nullptr;
+    if (int rc = check_codec(ctx, codec)) return rc;
+    if (dims < 192) return fail(ctx, MRL_ERR_INVALID, "dims must be >= 192 (src/quantize.rs:47)");
+    if (codec->mid_codec == MRL_MID_EDEN_B1 && codec->prefix_codec != MRL_PREFIX_EDEN)
+        return fail(ctx, MRL_ERR_INVALID, "eden_mid requires eden prefix fit (src/quantize.rs:52-54)");
+    const uint64_t nb = (n + 63) / 64;
+    if (nb >= (1ull << 26)) return fail(ctx, MRL_ERR_INVALID, "segment larger than 2^26 pages");
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = ensure_tmp(ctx, 192 * sizeof(float))) return rc;
+    float* d_means = (float*)ctx->tmp;
+    if (int rc = upload_means(ctx, codec, d_means)) return rc;
+    mrl_seg* s = nullptr;
+    if (seg_out) {
+        s = new mrl_seg();
+        s->block_id_base = block_id_base;
+        if (int rc = seg_reserve(ctx, s, nb ? nb : 1)) { delete s; return rc; }
+    }
+    if (mrl::launch_encode(d_rows, n, dims, nullptr, nullptr, src, codec->prefix_codec, d_means, codec->eden_seed,
+                           codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr, codec->mid_seed, d_pages,
+                           s ? s->pages : nullptr, s ? s->ts : nullptr, ctx->stream)) {
+        mrl_segment_free(ctx, s);
+        return cuda_fail(ctx, cudaGetLastError(), "encode launch");
+    }
+    const cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) { mrl_segment_free(ctx, s); return cuda_fail(ctx, e, "encode"); }
+    if (s) { s->n_blocks = nb; *seg_out = s; }
+    return MRL_OK;
+}
+
+int mrl_encode_blocks(mrl_ctx* ctx, const float* rows, uint64_t n, uint32_t dims, const uint32_t* ts,
+                      const uint32_t* src, const mrl_codec_desc* codec, uint8_t* out_pages) {
+    if (!ctx || (n && (!rows || !out_pages))) return MRL_ERR_INVALID;
+    if (int rc = check_codec(ctx, codec)) return rc;
+    if (dims < 192) return fail(ctx, MRL_ERR_INVALID, "dims must be >= 192 (src/quantize.rs:47)");
+    if (codec->mid_codec == MRL_MID_EDEN_B1 && codec->prefix_codec != MRL_PREFIX_EDEN)
+        return fail(ctx, MRL_ERR_INVALID, "eden_mid requires eden prefix fit (src/quantize.rs:52-54)");
+    if (n == 0) return MRL_OK;
+    for (uint64_t i = 0; i < n * dims; ++i)
+        if (!std::isfinite(rows[i])) return fail(ctx, MRL_ERR_INVALID, "rows contain a non-finite value");
+    if (int rc = set_device(ctx)) return rc;
+    const uint64_t nb = (n + 63) / 64;
+    const size_t rbytes = n * dims * sizeof(float), pbytes = nb * mrl::kBlockBytes, abytes = n * sizeof(uint32_t);
+    if (int rc = ensure_tmp(ctx, 192 * sizeof(float) + rbytes + pbytes + 2 * abytes + 64)) return rc;
+    float* d_means = (float*)ctx->tmp;
+    float* d_rows = d_means + 192;
+    uint8_t* d_pax = (uint8_t*)(d_rows + n * dims);
+    uint32_t* d_ts = (uint32_t*)(d_pax + pbytes);
+    uint32_t* d_src = d_ts + n;
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(d_rows, rows, rbytes, cudaMemcpyHostToDevice, ctx->stream));
+    if (ts) MRL_CUDA_TRY(ctx, cudaMemcpyAsync(d_ts, ts, abytes, cudaMemcpyHostToDevice, ctx->stream));
+    if (src) MRL_CUDA_TRY(ctx, cudaMemcpyAsync(d_src, src, abytes, cudaMemcpyHostToDevice, ctx->stream));
+    if (int rc = upload_means(ctx, codec, d_means)) return rc;
+    if (mrl::launch_encode(d_rows, n, dims, ts ? d_ts : nullptr, src ? d_src : nullptr, 8u /* source::DOC */,
+                           codec->prefix_codec, d_means, codec->eden_seed,
+                           codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr, codec->mid_seed, d_pax, nullptr,
+                           nullptr, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "encode launch");
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_pages, d_pax, pbytes, cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return MRL_OK;
+}
+
+int mrl_eden_fit_device(mrl_ctx* ctx, const float* d_rows, uint64_t n, uint32_t dims, uint32_t start, uint32_t width,
+                        float* mean_out) {
+    if (!ctx || !d_rows || !mean_out) return MRL_ERR_INVALID;
+    if (n == 0) return fail(ctx, MRL_ERR_INVALID, "empty corpus for EdenFit (src/eden.rs:149)");
+    if (start + width > dims || width == 0 || (width & (width - 1)))
+        return fail(ctx, MRL_ERR_INVALID, "EDEN slice must be a power of two inside the row (src/eden.rs:138)");
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = ensure_tmp(ctx, width * sizeof(float))) return rc;
+    if (mrl::launch_eden_fit(d_rows, n, dims, start, width, (float*)ctx->tmp, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "eden fit launch");
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(mean_out, ctx->tmp, width * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return MRL_OK;
+}
+
+int mrl_synth_docs_device(mrl_ctx* ctx, uint64_t seed, uint64_t row0, uint64_t n, uint32_t dims, float* d_out) {
+    if (!ctx || (n && !d_out) || dims == 0) return MRL_ERR_INVALID;
+    if (int rc = set_device(ctx)) return rc;
+    if (mrl::launch_synth_docs(seed, row0, n, dims, d_out, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "synth launch");
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return MRL_OK;
+}
+
+int mrl_synth_queries_device(mrl_ctx* ctx, uint64_t doc_seed, uint64_t n_docs, uint64_t q_seed, uint64_t n_q,
+                             uint32_t dims, float sigma, float* d_out, uint64_t* d_pick) {
+    if (!ctx || (n_q && !d_out) || n_docs == 0 || dims == 0) return MRL_ERR_INVALID;
+    if (int rc = set_device(ctx)) return rc;
+    if (mrl::launch_synth_queries(doc_seed, n_docs, q_seed, n_q, dims, sigma, d_out, d_pick, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "synth launch");
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return MRL_OK;
+}
+
+int mrl_scan_geometry(mrl_ctx* ctx, uint32_t k, uint32_t* ctas, uint32_t* list_len) {
+    if (!ctx) return MRL_ERR_INVALID;
+    if (ctas) *ctas = (uint32_t)ctx->sms;
+    if (list_len) *list_len = ctx->list_len_override ? ctx->list_len_override : auto_list_len(k, (uint32_t)ctx->sms);
+    return MRL_OK;
+}
+
+int mrl_set_list_len(mrl_ctx* ctx, uint32_t list_len) {
+    if (!ctx) return MRL_ERR_INVALID;
+    if (list_len > 32) return fail(ctx, MRL_ERR_INVALID, "list_len must be <= 32");
+    ctx->list_len_override = list_len;
+    return MRL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,191 @@
+// mrl_internal.cuh — shared device structures and helpers of libmrl_b200 (sm_100a).
+//
+// HBM scan layout ("vector-major pages"): each 4096-byte PaxBlock64 page (src/block.rs:130-144)
+// is transcoded once at upload into four 1 KiB chunk planes; chunk c of slot v lives at byte
+// c*1024 + v*16 of the page, so a warp reading 32 consecutive slots of one chunk issues 32
+// contiguous 16-byte loads (512 B). Per slot (64 bytes, the same information as the page):
+//   chunk 0: 4-bit prefix levels of dims 0..31  (word j, nibble i = level of dim 8j+i)
+//   chunk 1: 4-bit prefix levels of dims 32..63
+//   chunk 2: the 128 stratum-1 bits (word j bit i = dim 32j+i)
+//   chunk 3: word 0/1 = the 64 stratum-4 bits; word 2 = f16 scale | f16 offset << 16;
+//            word 3 = f16 tail_norm | rho flags << 16 | tombstone << 24
+// Level bit order follows write_4bit_planes (src/quantize.rs:297-315): bit3 = stratum0,
+// bit2 = stratum2, bit1 = stratum3, bit0 = stratum5. Block header timestamps go to a separate
+// uint2 array [min_ts, max_ts] per page.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/mrl_cuda.h"
+
+namespace mrl {
+
+constexpr int kVPB = 64;
+constexpr int kBlockBytes = 4096;
+constexpr int kPrefix = 64;
+constexpr int kRabitq = 128;
+constexpr int kTailStart = 192;
+constexpr int kFold = 64;
+constexpr int kFoldBlocks = 9;
+constexpr int kS1Windows = 26;  // 5-dim windows over 128 mid-band bits (last one 3 dims)
+constexpr int kS4Windows = 13;  // 5-dim windows over 64 folded-tail bits (last one 4 dims)
+
+// PaxBlock64 field offsets (src/block.rs:31-144).
+constexpr int kOffMinTs = 0, kOffMaxTs = 4, kOffSrc = 8, kOffTomb = 16, kOffCrc = 24;
+constexpr int kOffMeta = 64, kOffS0 = 512, kOffS1 = 1024, kOffS2 = 2048, kOffS3 = 2560,
+              kOffS4 = 3072, kOffS5 = 3584;
+
+// Device-resident query plan: the reference QueryPlan plus the per-mode scoring tables.
+struct DevPlan {
+    mrl_query_plan qp;
+    // fast mode: exact int32 stage sums of 2^shift-scaled table entries
+    int32_t lut_prefix[kPrefix * 16];
+    int32_t lut_s1[kS1Windows * 32];
+    int32_t lut_s4[kS4Windows * 32];
+    int32_t lut_l0[kPrefix * 16];  // L0Only: stratum-0 bit of each level times bit_weights[d][3]
+    int32_t shift_prefix, shift_s1, shift_s4, shift_l0;
+    double unscale_prefix, unscale_s1, unscale_s4, unscale_l0;  // 2^-shift
+    // exact mode: f32 products and addends in reference order
+    float fp_prefix[kPrefix * 16];
+    float mid_w[kRabitq];   // Rabitq: rabitq_weights2; EdenB1: (c1 - c0) * q
+    float tail_w[kFold];    // tail_fold_weights2
+    float mid_base, tail_base, pad2, pad3;
+};
+static_assert(sizeof(mrl_query_plan) % 16 == 0, "plan alignment");
+static_assert(sizeof(DevPlan) % 16 == 0, "plan alignment");
+
+// ---------------------------------------------------------------------------------------------
+// Hashes shared with the reference: tail_rademacher (src/rotate.rs:53-67) and rademacher_diag
+// (src/eden.rs:75-88) use the same SplitMix-style sign mix.
+__host__ __device__ __forceinline__ float sign_hash(uint64_t a, uint64_t i) {
+    uint64_t x = (a * 0x9E3779B97F4A7C15ULL + i) * 0xBF58476D1CE4E5B9ULL;
+    x ^= x >> 30;
+    x *= 0x94D049BB133111EBULL;
+    x ^= x >> 27;
+    return (x & 1u) == 0 ? 1.0f : -1.0f;
+}
+
+// SplitMix64 output function (Steele, Lea & Flood 2014), for the seeded synthetic inputs.
+__host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ULL;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBULL;
+    return x ^ (x >> 31);
+}
+
+// Irwin-Hall(12) - 6 from twelve 16-bit midpoint-lattice uniforms: variance 1, exact in f32, and
+// free of transcendental functions so host and device produce identical values.
+__host__ __device__ __forceinline__ float ih_gauss(uint64_t seed, uint64_t idx) {
+    int64_t s = 0;
+    for (uint64_t j = 0; j < 3; ++j) {
+        const uint64_t h = splitmix64(seed * 0xD1B54A32D192ED03ULL + idx * 3 + j);
+        s += (int64_t)(h & 0xFFFF) + (int64_t)((h >> 16) & 0xFFFF) + (int64_t)((h >> 32) & 0xFFFF) +
+             (int64_t)(h >> 48);
+    }
+    const int32_t num = (int32_t)(2 * s + 12 - 786432);
+    return (float)num * (1.0f / 131072.0f);
+}
+
+// Lloyd-Max N(0,1) centroids (src/eden.rs:15-44).
+__host__ __device__ __forceinline__ float lloyd_b4(int i) {
+    constexpr float t[16] = {-2.73258958f, -2.06901724f, -1.61804640f, -1.25623121f,
+                             -0.94234046f, -0.65675912f, -0.38804830f, -0.12839503f,
+                             0.12839503f,  0.38804830f,  0.65675912f,  0.94234046f,
+                             1.25623121f,  1.61804640f,  2.06901724f,  2.73258958f};
+    return t[i];
+}
+constexpr float kLloydB1Hi = 0.79788456f;
+
+// Total order used by every selection stage: larger key = better hit. High word: the f32 score
+// mapped to an order-preserving unsigned (zero canonicalised to +0); low word: the complement of
+// the slot ordinal, so equal scores rank the lower (block, slot) first. Key 0 = no hit.
+__device__ __forceinline__ unsigned long long make_key(float score, uint32_t ordinal) {
+    uint32_t u = __float_as_uint(score);
+    if (score == 0.0f) u = 0u;
+    const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - ordinal);
+}
+__device__ __forceinline__ float key_score(unsigned long long k) {
+    const uint32_t o = (uint32_t)(k >> 32);
+    const uint32_t u = (o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o;
+    return __uint_as_float(u);
+}
+__device__ __forceinline__ uint32_t key_ordinal(unsigned long long k) {
+    return 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
+}
+
+// Per-slot rest statistics (VectorMeta::{mid_norm_f32, high_tail_norm_f32}, src/block.rs:60-90)
+// with the scan's clamps (src/scan.rs:495-496).
+struct SlotMeta {
+    float scale, offset, mid_n, high_n;
+    bool tomb;
+};
+__device__ __forceinline__ SlotMeta decode_slot_meta(uint32_t w2, uint32_t w3) {
+    SlotMeta m;
+    m.scale = __half2float(__ushort_as_half((unsigned short)(w2 & 0xFFFFu)));
+    m.offset = __half2float(__ushort_as_half((unsigned short)(w2 >> 16)));
+    const float tail = __half2float(__ushort_as_half((unsigned short)(w3 & 0xFFFFu)));
+    const uint32_t flags = (w3 >> 16) & 0xFFu;
+    m.tomb = ((w3 >> 24) & 1u) != 0;
+    const float rho = __fdiv_rn((float)flags, 255.0f);
+    const float t = fmaxf(tail, 0.0f);
+    const float r = fminf(fmaxf(rho, 0.0f), 1.0f);
+    const float mid = __fmul_rn(__fsqrt_rn(fmaxf(__fsub_rn(1.0f, __fmul_rn(r, r)), 0.0f)), t);
+    const float high = __fmul_rn(rho, t);
+    m.mid_n = fmaxf(mid, 1e-6f);
+    m.high_n = fmaxf(high, 0.0f);
+    return m;
+}
+
+}  // namespace mrl
+
+// Host-side launchers implemented in the .cu files, used by the C ABI layer.
+namespace mrl {
+struct Segment;
+int launch_plan_build(const float* d_queries, uint32_t n_q, uint32_t dims, uint32_t prefix_codec,
+                      uint32_t mid_codec, const float* d_eden_mean, uint64_t eden_seed,
+                      const float* d_mid_mean, uint64_t mid_seed, DevPlan* d_plans,
+                      cudaStream_t stream);
+int launch_transcode(const uint8_t* d_pax, uint64_t n_blocks, uint4* d_pages, uint2* d_ts,
+                     cudaStream_t stream);
+int launch_encode(const float* d_rows, uint64_t n, uint32_t dims, const uint32_t* d_ts,
+                  const uint32_t* d_src, uint32_t src_const, uint32_t prefix_codec,
+                  const float* d_eden_mean, uint64_t eden_seed, const float* d_mid_mean,
+                  uint64_t mid_seed, uint8_t* d_pax, uint4* d_pages, uint2* d_block_ts,
+                  cudaStream_t stream);
+int launch_eden_fit(const float* d_rows, uint64_t n, uint32_t dims, uint32_t start,
+                    uint32_t width, float* d_mean, cudaStream_t stream);
+int launch_synth_docs(uint64_t seed, uint64_t row0, uint64_t n, uint32_t dims, float* d_out,
+                      cudaStream_t stream);
+int launch_synth_queries(uint64_t doc_seed, uint64_t n_docs, uint64_t q_seed, uint64_t n_q,
+                         uint32_t dims, float sigma, float* d_out, uint64_t* d_pick,
+                         cudaStream_t stream);
+
+struct ScanLaunch {
+    const uint4* pages;
+    const uint2* block_ts;
+    uint32_t n_blocks;
+    uint32_t block_id_base;
+    const DevPlan* plan;
+    uint32_t k;
+    uint32_t list_len;
+    float w_s4;
+    uint32_t depth;
+    uint32_t mode;
+    uint32_t use_time;  // temporal filter active for this call
+    uint32_t has_lo, lo, has_hi, hi;
+    unsigned long long* cta_keys;  // scratch: ctas * 32
+    unsigned int* ticket;          // scratch: 1 (zero between launches)
+    uint64_t* out_ids;
+    float* out_scores;
+    uint32_t* out_count;
+    uint32_t* out_status;
+};
+int scan_ctas(int device_sms);
+size_t scan_smem_bytes(uint32_t ctas, uint32_t k);
+int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream);
+int launch_debug_scores(const ScanLaunch& p, float* d_scores, uint8_t* d_active,
+                        int32_t* d_partials, cudaStream_t stream);
+}  // namespace mrl

@@ -1,0 +1,636 @@
+// scan.cu — fused single-query PaxBlock64 scan + top-k for sm_100a.
+//
+// Replaces scan_blocks / scan_block / Shortlist (src/scan.rs:310-886). One launch scores every
+// live slot of a segment for one plan and leaves the top-k (by score, ties to the lower slot
+// ordinal) in the output buffers.
+//
+// Work split: a persistent grid of one 512-thread CTA per SM; warp w of CTA c scores pages
+// c + G*(w + 16*i) (G = grid size), two slots per lane, reading each slot's 64 bytes of the
+// vector-major page layout with four coalesced 16-byte loads per slot, prefetching the next page
+// while scoring the current one.
+//
+// Scoring (one thread per slot):
+//   * MRL_MODE_FAST — every stage inner product is an exact int32 sum of table entries held in
+//     shared memory: 64 per-dimension 16-entry prefix tables indexed by the slot's 4-bit level, and
+//     5-bit-window tables over the 128 mid-band and 64 folded-tail bits. Tables have <= 32 entries,
+//     so a warp-uniform table index never causes a shared-memory bank conflict. The integer sums
+//     are converted to f32 once and combined with the reference's f32 formulas.
+//   * MRL_MODE_EXACT — the reference's f32 loops in the reference order (sequential adds of
+//     rounded products), giving bit-identical scores.
+// Both compute the full score of every live slot (no stage pruning). Under the reference's
+// exactness condition (cs_tolerance >= 1 and w_s4*sqrt(2/pi)*sqrt(B) <= cs_tolerance, true for
+// the defaults) every stage bound of src/scan.rs:453-607 is >= the full score, so the reference's
+// final shortlist is exactly the top-k by full score; computing all scores reproduces it without
+// the order-dependent threshold.
+//
+// Selection: each warp keeps a sorted top-32 of its keys in registers (one key per lane) and
+// filters new keys against max(its own list_len-th key, a CTA-wide bound in shared memory);
+// survivors go through a per-warp shared-memory queue and are merged 32 at a time with warp
+// bitonic networks. Each CTA then publishes its exact top-`list_len` to global scratch, and the
+// last CTA to finish (atomic ticket) selects the global top-k by radix select + bitonic sort. The
+// union of per-CTA lists provably contains the global top-k unless some CTA's full list ends
+// above the selected threshold; such CTAs are rescanned by the last CTA and the selection is
+// redone over the enlarged set, so the result is exact for every input (status bit 0 reports it).
+#include "mrl_internal.cuh"
+
+namespace mrl {
+namespace {
+
+typedef unsigned long long u64;
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kWarps = 16;
+constexpr int kThreads = kWarps * 32;
+constexpr int kQueue = 64;
+constexpr int kTabInts = kPrefix * 16 + kS1Windows * 32 + kS4Windows * 32 + kPrefix * 16;  // 3296
+constexpr int kTabS1 = kPrefix * 16;
+constexpr int kTabS4 = kTabS1 + kS1Windows * 32;
+constexpr int kTabL0 = kTabS4 + kS4Windows * 32;
+// exact-mode layout inside the same table space (floats)
+constexpr int kTabMidW = kPrefix * 16;
+constexpr int kTabTailW = kTabMidW + kRabitq;
+constexpr int kTabBw3 = kTabTailW + kFold;
+
+struct Scalars {
+    float eden_mean_ip, prefix_sum, mid_mean_ip, w_s4, mid_base, tail_base;
+    double un_prefix, un_s1, un_s4, un_l0;
+    uint32_t eden, mid_b1, has_tail, depth;
+};
+
+__device__ __forceinline__ int lds_byte(const int* tab, uint32_t byte_off) {
+    return *reinterpret_cast<const int*>(reinterpret_cast<const char*>(tab) + byte_off);
+}
+
+__device__ __forceinline__ float unfix(int32_t v, double unscale) {
+    return __double2float_rn(__dmul_rn((double)v, unscale));
+}
+
+// Sum of 64 per-dimension table entries, tab[d*16 + level_d].
+__device__ __forceinline__ int32_t prefix_fixed(const uint4& c0, const uint4& c1, const int* tab) {
+    const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    int32_t acc0 = 0, acc1 = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t e = (w[j] << 2) & 0x3C3C3C3Cu;  // levels of dims 8j, 8j+2, 8j+4, 8j+6 (x4)
+        const uint32_t o = (w[j] >> 2) & 0x3C3C3C3Cu;  // levels of dims 8j+1, +3, +5, +7 (x4)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc0 += lds_byte(tab, (8 * j + 2 * k) * 64 + __byte_perm(e, 0, 0x4440 + k));
+            acc1 += lds_byte(tab, (8 * j + 2 * k + 1) * 64 + __byte_perm(o, 0, 0x4440 + k));
+        }
+    }
+    return acc0 + acc1;
+}
+
+// Sum over 5-bit windows of an `NBITS`-bit little-endian bit string held in `words`.
+template <int NBITS>
+__device__ __forceinline__ int32_t window_fixed(const uint32_t* words, const int* tab) {
+    constexpr int kWords = NBITS / 32;
+    constexpr int kWin = (NBITS + 4) / 5;
+    int32_t acc0 = 0, acc1 = 0;
+#pragma unroll
+    for (int g = 0; g < kWin; ++g) {
+        const int start = 5 * g, q = start >> 5, r = start & 31;
+        uint32_t idx4;
+        if (r < 2) {
+            idx4 = (words[q] << (2 - r)) & 0x7Cu;
+        } else if (r + 5 > 32 && q + 1 < kWords) {
+            idx4 = __funnelshift_r(words[q], words[q + 1], r - 2) & 0x7Cu;
+        } else {
+            idx4 = (words[q] >> (r - 2)) & 0x7Cu;
+        }
+        const int v = lds_byte(tab, g * 128 + idx4);
+        if (g & 1) acc1 += v; else acc0 += v;
+    }
+    return acc0 + acc1;
+}
+
+__device__ __forceinline__ uint32_t level_of(const uint4& c0, const uint4& c1, int d) {
+    const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    return (w[d >> 3] >> (4 * (d & 7))) & 15u;
+}
+
+struct Partials {
+    int32_t p, s1, s4;
+};
+
+// Full score of one slot; returns false for tombstoned slots.
+template <int MODE>
+__device__ __forceinline__ bool slot_score(const uint4& c0, const uint4& c1, const uint4& c2,
+                                           const uint4& c3, const int* tab, const Scalars& S,
+                                           float& score, Partials* parts) {
+    const SlotMeta m = decode_slot_meta(c3.z, c3.w);
+    if (m.tomb) return false;
+    if (MODE == MRL_MODE_FAST) {
+        const uint32_t s1w[4] = {c2.x, c2.y, c2.z, c2.w};
+        const uint32_t s4w[2] = {c3.x, c3.y};
+        if (S.depth == MRL_DEPTH_L0) {  // src/scan.rs:753-771
+            const int32_t P = prefix_fixed(c0, c1, tab + kTabL0);
+            const float cd = unfix(P, S.un_l0);
+            score = __fadd_rn(__fmul_rn(cd, m.scale), __fmul_rn(m.offset, S.prefix_sum));
+            if (parts) {
+                parts->p = P;
+                parts->s1 = window_fixed<128>(s1w, tab + kTabS1);
+                parts->s4 = window_fixed<64>(s4w, tab + kTabS4);
+            }
+            return true;
+        }
+        const int32_t P = prefix_fixed(c0, c1, tab);
+        const float cd = unfix(P, S.un_prefix);
+        float sc = S.eden ? __fadd_rn(S.eden_mean_ip, __fmul_rn(m.scale, cd))   // src/scan.rs:499-505
+                          : __fadd_rn(__fmul_rn(cd, m.scale), __fmul_rn(m.offset, S.prefix_sum));
+        int32_t s1 = 0, s4 = 0;
+        if (S.depth >= MRL_DEPTH_L1 || parts) s1 = window_fixed<128>(s1w, tab + kTabS1);
+        if ((S.depth == MRL_DEPTH_FULL && S.has_tail) || parts) s4 = window_fixed<64>(s4w, tab + kTabS4);
+        if (S.depth >= MRL_DEPTH_L1) {
+            const float v = unfix(s1, S.un_s1);
+            if (S.mid_b1) sc = __fadd_rn(sc, __fadd_rn(S.mid_mean_ip, __fmul_rn(m.offset, v)));  // :546-547
+            else sc = __fadd_rn(sc, __fmul_rn(v, m.mid_n));                                     // :566
+        }
+        if (S.depth == MRL_DEPTH_FULL && S.has_tail) {  // src/scan.rs:631
+            const float v = unfix(s4, S.un_s4);
+            sc = __fadd_rn(sc, __fmul_rn(__fmul_rn(v, fmaxf(m.high_n, 1e-6f)), S.w_s4));
+        }
+        if (parts) { parts->p = P; parts->s1 = s1; parts->s4 = s4; }
+        score = sc;
+        return true;
+    } else {
+        const float* ft = reinterpret_cast<const float*>(tab);
+        if (S.depth == MRL_DEPTH_L0) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int d = 0; d < kPrefix; ++d)
+                if (level_of(c0, c1, d) & 8u) acc = __fadd_rn(acc, ft[kTabBw3 + d]);
+            score = __fadd_rn(__fmul_rn(acc, m.scale), __fmul_rn(m.offset, S.prefix_sum));
+            return true;
+        }
+        float acc = 0.0f;  // src/scan.rs:456-487, per-slot sequential order over d
+        {
+            const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+            for (int d = 0; d < kPrefix; ++d) {
+                const uint32_t sh = 4 * (d & 7);
+                const uint32_t idx4 = sh >= 2 ? ((w[d >> 3] >> (sh - 2)) & 0x3Cu) : ((w[d >> 3] << 2) & 0x3Cu);
+                acc = __fadd_rn(acc, *reinterpret_cast<const float*>(reinterpret_cast<const char*>(ft) + d * 64 + idx4));
+            }
+        }
+        float sc = S.eden ? __fadd_rn(S.eden_mean_ip, __fmul_rn(m.scale, acc))
+                          : __fadd_rn(__fmul_rn(acc, m.scale), __fmul_rn(m.offset, S.prefix_sum));
+        if (S.depth >= MRL_DEPTH_L1) {  // src/scan.rs:520-569
+            const uint32_t s1w[4] = {c2.x, c2.y, c2.z, c2.w};
+            float s = S.mid_base;
+            const float4* mw = reinterpret_cast<const float4*>(ft + kTabMidW);
+#pragma unroll
+            for (int g = 0; g < kRabitq / 4; ++g) {
+                const float4 w4 = mw[g];
+                const uint32_t bits = s1w[g >> 3] >> (4 * (g & 7));
+                if (bits & 1u) s = __fadd_rn(s, w4.x);
+                if (bits & 2u) s = __fadd_rn(s, w4.y);
+                if (bits & 4u) s = __fadd_rn(s, w4.z);
+                if (bits & 8u) s = __fadd_rn(s, w4.w);
+            }
+            if (S.mid_b1) sc = __fadd_rn(sc, __fadd_rn(S.mid_mean_ip, __fmul_rn(m.offset, s)));
+            else sc = __fadd_rn(sc, __fmul_rn(s, m.mid_n));
+        }
+        if (S.depth == MRL_DEPTH_FULL && S.has_tail) {  // src/scan.rs:610-634
+            const uint32_t s4w[2] = {c3.x, c3.y};
+            float t = S.tail_base;
+            const float4* tw = reinterpret_cast<const float4*>(ft + kTabTailW);
+#pragma unroll
+            for (int g = 0; g < kFold / 4; ++g) {
+                const float4 w4 = tw[g];
+                const uint32_t bits = s4w[g >> 3] >> (4 * (g & 7));
+                if (bits & 1u) t = __fadd_rn(t, w4.x);
+                if (bits & 2u) t = __fadd_rn(t, w4.y);
+                if (bits & 4u) t = __fadd_rn(t, w4.z);
+                if (bits & 8u) t = __fadd_rn(t, w4.w);
+            }
+            sc = __fadd_rn(sc, __fmul_rn(__fmul_rn(t, fmaxf(m.high_n, 1e-6f)), S.w_s4));
+        }
+        score = sc;
+        return true;
+    }
+}
+
+struct Slot4 {
+    uint4 c0, c1, c2, c3;
+};
+
+__device__ __forceinline__ void load_slot(const uint4* __restrict__ pages, uint32_t b, int v, Slot4& s) {
+    const uint4* p = pages + (size_t)b * 256 + v;
+    s.c0 = __ldg(p);
+    s.c1 = __ldg(p + 64);
+    s.c2 = __ldg(p + 128);
+    s.c3 = __ldg(p + 192);
+}
+
+__device__ __forceinline__ bool block_live(const ScanLaunch& p, uint32_t b) {
+    if (!p.use_time) return true;
+    const uint2 t = __ldg(p.block_ts + b);  // [min_ts, max_ts], src/scan.rs:719-730
+    if (p.has_lo && t.y < p.lo) return false;
+    if (p.has_hi && t.x > p.hi) return false;
+    return true;
+}
+
+template <int MODE>
+__device__ __forceinline__ u64 slot_key(const Slot4& s, uint32_t ordinal, const int* tab, const Scalars& S) {
+    float sc;
+    if (!slot_score<MODE>(s.c0, s.c1, s.c2, s.c3, tab, S, sc, nullptr)) return 0ull;
+    return make_key(sc, ordinal);
+}
+
+// ---- warp sorting networks over 64-bit keys (lane i holds rank i, descending) ----
+__device__ __forceinline__ u64 umax64(u64 a, u64 b) { return a > b ? a : b; }
+__device__ __forceinline__ u64 umin64(u64 a, u64 b) { return a < b ? a : b; }
+
+__device__ __forceinline__ u64 warp_sort32(u64 x, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const u64 y = __shfl_xor_sync(kFull, x, j);
+            const bool keep_max = ((lane & j) == 0) == ((lane & k) == 0);
+            x = keep_max ? umax64(x, y) : umin64(x, y);
+        }
+    }
+    return x;
+}
+
+// Top 32 of two descending lists, descending.
+__device__ __forceinline__ u64 warp_merge32(u64 L, u64 S, int lane) {
+    u64 x = umax64(L, __shfl_sync(kFull, S, 31 - lane));
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1) {
+        const u64 y = __shfl_xor_sync(kFull, x, j);
+        x = ((lane & j) == 0) ? umax64(x, y) : umin64(x, y);
+    }
+    return x;
+}
+
+struct WarpSel {
+    u64 list;   // this lane's rank in the warp's top-32
+    u64 tau;    // list[list_len-1]
+    int qn;     // queued candidates
+};
+
+__device__ __forceinline__ void warp_flush(WarpSel& ws, u64* q, int lane, uint32_t list_len, u64* cta_tau) {
+    __syncwarp();
+    for (int base = 0; base < ws.qn; base += 32) {
+        u64 x = (base + lane < ws.qn) ? q[base + lane] : 0ull;
+        x = warp_sort32(x, lane);
+        ws.list = warp_merge32(ws.list, x, lane);
+    }
+    ws.qn = 0;
+    ws.tau = __shfl_sync(kFull, ws.list, list_len - 1);
+    if (lane == 0 && ws.tau) atomicMax(cta_tau, ws.tau);
+    __syncwarp();
+}
+
+__device__ __forceinline__ void warp_offer(WarpSel& ws, u64* q, int lane, uint32_t list_len, u64* cta_tau,
+                                           u64 k0, u64 k1) {
+    const u64 tc = *reinterpret_cast<volatile u64*>(cta_tau);
+    const u64 tau = umax64(ws.tau, tc);
+    const bool p0 = k0 > tau, p1 = k1 > tau;
+    const unsigned m0 = __ballot_sync(kFull, p0), m1 = __ballot_sync(kFull, p1);
+    const int nn = __popc(m0) + __popc(m1);
+    if (nn == 0) return;
+    if (ws.qn + nn > kQueue) warp_flush(ws, q, lane, list_len, cta_tau);
+    const unsigned lt = (1u << lane) - 1u;
+    if (p0) q[ws.qn + __popc(m0 & lt)] = k0;
+    if (p1) q[ws.qn + __popc(m0) + __popc(m1 & lt)] = k1;
+    ws.qn += nn;
+    if (ws.qn >= 32) warp_flush(ws, q, lane, list_len, cta_tau);
+}
+
+// ---- final selection helpers (last CTA) ----
+__device__ __forceinline__ void hist_add(unsigned* hist, bool valid, unsigned bin, int lane) {
+    const unsigned act = __ballot_sync(kFull, valid);
+    if (valid) {
+        const unsigned peers = __match_any_sync(act, bin);
+        if (lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (unsigned)__popc(peers));
+    }
+}
+
+struct SelState {
+    u64 prefix, mask;
+    unsigned rem;
+    unsigned done;
+    unsigned bin, before;
+};
+
+template <int MODE>
+struct Finisher {
+    const ScanLaunch& p;
+    const int* tab;
+    const Scalars& S;
+    u64* cand;        // G*32
+    const unsigned* flags;  // flagged CTA ids
+    unsigned nflag;
+    unsigned G;
+    unsigned list_len;
+
+    // Visit every candidate of the (virtual) set: U from shared memory plus, for flagged CTAs, a
+    // rescan of their pages keeping keys below their list minimum. fn(valid, key) is called
+    // warp-uniformly.
+    template <class Fn>
+    __device__ void visit(Fn fn) const {
+        const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+        const unsigned nu = G * 32;
+        for (unsigned base = 0; base < nu; base += kThreads) {
+            const unsigned i = base + tid;
+            const u64 x = i < nu ? cand[i] : 0ull;
+            fn(x != 0ull, x, lane);
+        }
+        for (unsigned f = 0; f < nflag; ++f) {
+            const unsigned c = flags[f];
+            const u64 minc = cand[c * 32 + list_len - 1];
+            for (uint32_t b = c + G * warp; b < p.n_blocks; b += G * kWarps) {
+                u64 k0 = 0, k1 = 0;
+                if (block_live(p, b)) {
+                    Slot4 s0, s1;
+                    load_slot(p.pages, b, lane, s0);
+                    load_slot(p.pages, b, lane + 32, s1);
+                    k0 = slot_key<MODE>(s0, b * 64 + lane, tab, S);
+                    k1 = slot_key<MODE>(s1, b * 64 + lane + 32, tab, S);
+                }
+                fn(k0 != 0ull && k0 < minc, k0, lane);
+                fn(k1 != 0ull && k1 < minc, k1, lane);
+            }
+        }
+    }
+};
+
+// Exact k-th largest key of the candidate set (radix select, 8 bits per pass from the top).
+// Returns a threshold T such that the keys >= T are exactly the top min(k, count) keys.
+template <int MODE>
+__device__ u64 select_threshold(const Finisher<MODE>& F, unsigned k, unsigned* hist, SelState* st) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid == 0) { st->prefix = 0; st->mask = 0; st->rem = k; st->done = 0; }
+    // total count
+    if (tid < 256) hist[tid] = 0;
+    __syncthreads();
+    F.visit([&](bool valid, u64, int ln) { hist_add(hist, valid, 0u, ln); });
+    __syncthreads();
+    const unsigned total = hist[0];
+    __syncthreads();
+    if (total <= k) return 1ull;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        if (tid < 256) hist[tid] = 0;
+        __syncthreads();
+        const u64 prefix = st->prefix, mask = st->mask;
+        F.visit([&](bool valid, u64 x, int ln) {
+            const bool in = valid && ((x & mask) == prefix);
+            hist_add(hist, in, (unsigned)((x >> shift) & 0xFFu), ln);
+        });
+        __syncthreads();
+        if (tid < 32) {
+            unsigned c[8];
+            unsigned lsum = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) { c[j] = hist[255 - 8 * lane - j]; lsum += c[j]; }
+            unsigned incl = lsum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned y = __shfl_up_sync(kFull, incl, o);
+                if (lane >= o) incl += y;
+            }
+            unsigned cum = incl - lsum;
+            const unsigned rem = st->rem;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (cum < rem && rem <= cum + c[j]) { st->bin = 255 - 8 * lane - j; st->before = cum; }
+                cum += c[j];
+            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const unsigned bin = st->bin;
+            st->prefix |= (u64)bin << shift;
+            st->mask |= 0xFFull << shift;
+            st->rem -= st->before;
+            if (hist[bin] == st->rem) st->done = 1;
+        }
+        __syncthreads();
+        if (st->done) break;
+    }
+    return st->prefix;
+}
+
+template <int MODE>
+__device__ void final_select(const ScanLaunch& p, const int* tab, const Scalars& S, u64* cand, u64* gath,
+                             unsigned* hist, unsigned* flags, SelState* st, unsigned* s_misc) {
+    const int tid = threadIdx.x;
+    const unsigned G = gridDim.x;
+    const unsigned nu = G * 32;
+    for (unsigned i = tid; i < nu; i += kThreads) cand[i] = __ldcg(p.cta_keys + i);
+    if (tid == 0) { s_misc[0] = 0; s_misc[1] = 0; }
+    __syncthreads();
+    Finisher<MODE> F{p, tab, S, cand, flags, 0u, G, p.list_len};
+    u64 tau = select_threshold<MODE>(F, p.k, hist, st);
+    // CTAs whose full list ends above the threshold may have dropped members of the top-k.
+    for (unsigned c = tid; c < G; c += kThreads) {
+        const u64 minc = cand[c * 32 + p.list_len - 1];
+        if (minc != 0ull && minc > tau) flags[atomicAdd(&s_misc[0], 1u)] = c;
+    }
+    __syncthreads();
+    const unsigned nflag = s_misc[0];
+    if (nflag) {
+        F.nflag = nflag;
+        tau = select_threshold<MODE>(F, p.k, hist, st);
+    }
+    // gather keys >= tau (exactly min(k, total) of them)
+    F.visit([&](bool valid, u64 x, int ln) {
+        const bool in = valid && x >= tau;
+        const unsigned m = __ballot_sync(kFull, in);
+        unsigned base = 0;
+        if (ln == 0 && m) base = atomicAdd(&s_misc[1], (unsigned)__popc(m));
+        base = __shfl_sync(kFull, base, 0);
+        if (in) gath[base + __popc(m & ((1u << ln) - 1u))] = x;
+    });
+    __syncthreads();
+    const unsigned ng = min(s_misc[1], p.k);
+    unsigned P2 = 1;
+    while (P2 < ng) P2 <<= 1;
+    for (unsigned i = ng + tid; i < P2; i += kThreads) gath[i] = 0ull;
+    __syncthreads();
+    for (unsigned kk = 2; kk <= P2; kk <<= 1) {
+        for (unsigned j = kk >> 1; j > 0; j >>= 1) {
+            for (unsigned i = tid; i < P2; i += kThreads) {
+                const unsigned ixj = i ^ j;
+                if (ixj > i) {
+                    const u64 a = gath[i], b = gath[ixj];
+                    const bool desc = (i & kk) == 0;
+                    if (desc ? (a < b) : (a > b)) { gath[i] = b; gath[ixj] = a; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (unsigned i = tid; i < ng; i += kThreads) {
+        const u64 key = gath[i];
+        const uint32_t ord = key_ordinal(key);
+        p.out_ids[i] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
+        p.out_scores[i] = key_score(key);
+    }
+    if (tid == 0) {
+        *p.out_count = ng;
+        if (p.out_status) *p.out_status = nflag ? 1u : 0u;
+        *p.ticket = 0u;  // ready for the next launch
+    }
+}
+
+__device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int mode, int* tab, Scalars& S,
+                                            const ScanLaunch& p) {
+    const int tid = threadIdx.x;
+    if (mode == MRL_MODE_FAST) {
+        for (int i = tid; i < kPrefix * 16; i += kThreads) tab[i] = P->lut_prefix[i];
+        for (int i = tid; i < kS1Windows * 32; i += kThreads) tab[kTabS1 + i] = P->lut_s1[i];
+        for (int i = tid; i < kS4Windows * 32; i += kThreads) tab[kTabS4 + i] = P->lut_s4[i];
+        for (int i = tid; i < kPrefix * 16; i += kThreads) tab[kTabL0 + i] = P->lut_l0[i];
+    } else {
+        float* ft = reinterpret_cast<float*>(tab);
+        for (int i = tid; i < kPrefix * 16; i += kThreads) ft[i] = P->fp_prefix[i];
+        for (int i = tid; i < kRabitq; i += kThreads) ft[kTabMidW + i] = P->mid_w[i];
+        for (int i = tid; i < kFold; i += kThreads) ft[kTabTailW + i] = P->tail_w[i];
+        for (int i = tid; i < kPrefix; i += kThreads) ft[kTabBw3 + i] = P->qp.bit_weights[i][3];
+    }
+    S.eden_mean_ip = P->qp.eden_mean_ip;
+    S.prefix_sum = P->qp.prefix_sum;
+    S.mid_mean_ip = P->qp.eden_mid_mean_ip;
+    S.w_s4 = p.w_s4;
+    S.mid_base = P->mid_base;
+    S.tail_base = P->tail_base;
+    S.un_prefix = P->unscale_prefix;
+    S.un_s1 = P->unscale_s1;
+    S.un_s4 = P->unscale_s4;
+    S.un_l0 = P->unscale_l0;
+    S.eden = P->qp.prefix_codec == MRL_PREFIX_EDEN;
+    S.mid_b1 = P->qp.mid_codec == MRL_MID_EDEN_B1;
+    S.has_tail = P->qp.has_tail_fold;
+    S.depth = p.depth;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
+    __shared__ __align__(16) int s_tab[kTabInts];
+    __shared__ u64 s_cta_tau;
+    __shared__ unsigned s_last;
+    __shared__ SelState s_sel;
+    __shared__ unsigned s_misc[4];
+    extern __shared__ __align__(16) unsigned char s_dyn[];
+    u64* s_queue = reinterpret_cast<u64*>(s_dyn);  // kWarps * kQueue
+    u64* s_lists = s_queue + kWarps * kQueue;       // kWarps * 32
+    u64* s_cand = s_lists + kWarps * 32;            // G * 32
+    const unsigned G = gridDim.x;
+    u64* s_gath = s_cand + G * 32;                  // pow2 >= k
+    unsigned P2 = 1;
+    while (P2 < p.k) P2 <<= 1;
+    unsigned* s_hist = reinterpret_cast<unsigned*>(s_gath + P2);  // 256
+    unsigned* s_flags = s_hist + 256;                            // G
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    Scalars S;
+    if (tid == 0) s_cta_tau = 0ull;
+    load_tables(p.plan, MODE, s_tab, S, p);
+    __syncthreads();
+
+    WarpSel ws{0ull, 0ull, 0};
+    u64* q = s_queue + warp * kQueue;
+    const uint32_t stride = G * kWarps;
+    uint32_t b = blockIdx.x + G * warp;
+    Slot4 a0, a1;
+    if (b < p.n_blocks) { load_slot(p.pages, b, lane, a0); load_slot(p.pages, b, lane + 32, a1); }
+    while (b < p.n_blocks) {
+        const uint32_t bn = b + stride;
+        Slot4 n0, n1;
+        if (bn < p.n_blocks) { load_slot(p.pages, bn, lane, n0); load_slot(p.pages, bn, lane + 32, n1); }
+        u64 k0 = 0ull, k1 = 0ull;
+        if (block_live(p, b)) {
+            k0 = slot_key<MODE>(a0, b * 64 + lane, s_tab, S);
+            k1 = slot_key<MODE>(a1, b * 64 + lane + 32, s_tab, S);
+        }
+        warp_offer(ws, q, lane, p.list_len, &s_cta_tau, k0, k1);
+        b = bn;
+        a0 = n0;
+        a1 = n1;
+    }
+    if (ws.qn) warp_flush(ws, q, lane, p.list_len, &s_cta_tau);
+
+    // CTA top-list_len from the warps' lists
+    s_lists[warp * 32 + lane] = ws.list;
+    __syncthreads();
+    if (warp == 0) {
+        u64 L = s_lists[lane];
+        for (int w = 1; w < kWarps; ++w) L = warp_merge32(L, s_lists[w * 32 + lane], lane);
+        p.cta_keys[blockIdx.x * 32 + lane] = (uint32_t)lane < p.list_len ? L : 0ull;
+        __threadfence();
+    }
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(p.ticket, 1u) == G - 1) ? 1u : 0u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    final_select<MODE>(p, s_tab, S, s_cand, s_gath, s_hist, s_flags, &s_sel, s_misc);
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads) debug_scores_kernel(const ScanLaunch p, float* out,
+                                                                uint8_t* active, int32_t* parts) {
+    __shared__ __align__(16) int s_tab[kTabInts];
+    Scalars S;
+    load_tables(p.plan, MODE, s_tab, S, p);
+    __syncthreads();
+    const uint32_t total = p.n_blocks * 64u;
+    for (uint32_t i = blockIdx.x * kThreads + threadIdx.x; i < total; i += gridDim.x * kThreads) {
+        const uint32_t b = i >> 6, v = i & 63u;
+        Slot4 s;
+        load_slot(p.pages, b, (int)v, s);
+        float sc = 0.0f;
+        Partials pr{0, 0, 0};
+        bool ok = block_live(p, b) &&
+                  slot_score<MODE>(s.c0, s.c1, s.c2, s.c3, s_tab, S, sc, MODE == MRL_MODE_FAST ? &pr : nullptr);
+        out[i] = ok ? sc : 0.0f;
+        active[i] = ok ? 1 : 0;
+        if (parts) {
+            parts[3 * (size_t)i] = ok ? pr.p : 0;
+            parts[3 * (size_t)i + 1] = ok ? pr.s1 : 0;
+            parts[3 * (size_t)i + 2] = ok ? pr.s4 : 0;
+        }
+    }
+}
+
+}  // namespace
+
+int scan_ctas(int device_sms) { return device_sms; }
+
+size_t scan_smem_bytes(uint32_t ctas, uint32_t k) {
+    size_t p2 = 1;
+    while (p2 < k) p2 <<= 1;
+    return sizeof(u64) * (kWarps * kQueue + kWarps * 32 + (size_t)ctas * 32 + p2) + sizeof(unsigned) * (256 + ctas);
+}
+
+int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream) {
+    const size_t smem = scan_smem_bytes(ctas, p.k);
+    if (p.mode == MRL_MODE_FAST) {
+        if (cudaFuncSetAttribute(scan_kernel<MRL_MODE_FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return -1;
+        scan_kernel<MRL_MODE_FAST><<<ctas, kThreads, smem, stream>>>(p);
+    } else {
+        if (cudaFuncSetAttribute(scan_kernel<MRL_MODE_EXACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return -1;
+        scan_kernel<MRL_MODE_EXACT><<<ctas, kThreads, smem, stream>>>(p);
+    }
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_debug_scores(const ScanLaunch& p, float* d_scores, uint8_t* d_active, int32_t* d_partials,
+                        cudaStream_t stream) {
+    const uint32_t total = p.n_blocks * 64u;
+    const uint32_t grid = total ? (total + kThreads - 1) / kThreads : 1;
+    if (p.mode == MRL_MODE_FAST)
+        debug_scores_kernel<MRL_MODE_FAST><<<grid, kThreads, 0, stream>>>(p, d_scores, d_active, d_partials);
+    else
+        debug_scores_kernel<MRL_MODE_EXACT><<<grid, kThreads, 0, stream>>>(p, d_scores, d_active, d_partials);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace mrl

@@ -1,0 +1,408 @@
+"""Parity of the CUDA product path (libmrl_b200 through its C ABI) with the CPU oracle.
+
+Bars: integer stage sums bit-exact; f32 scores within 1e-5 relative
+(MRL_MODE_FAST) or bit-identical (MRL_MODE_EXACT); top-k id lists identical except where scores
+tie (exactly, or within the tolerance for the fast mode).
+"""
+import ctypes as C
+import struct
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5
+ATOL = 1e-6
+
+
+def mb():
+    import mrl_b200
+
+    return mrl_b200
+
+
+@pytest.fixture(scope="module")
+def corpus768(ora):
+    n = 64 * 37 + 17  # ragged last block
+    docs = ora.synth_docs(42, n, 768)
+    mean = ora.eden_fit_prefix(docs)
+    eden = ora.encode_corpus(docs, eden_mean=mean)
+    minmax = ora.encode_corpus(docs, prefix_codec=ora.MINMAX4)
+    qs, picks = ora.synth_queries(42, n, 7, 4, 768)
+    return dict(n=n, docs=docs, mean=mean, eden=eden, minmax=minmax, qs=qs, picks=picks)
+
+
+def fit(mean, dim=64, bits=4):
+    return mb().EdenFit(dim, bits, 1, np.asarray(mean, np.float32))
+
+
+def ids_to_ord(ids):
+    return np.array([(int(i) >> 16) * 64 + (int(i) & 0xFFFF) for i in ids], np.int64)
+
+
+def assert_same_topk(got_ids, got_sc, ref_ids, ref_sc, tol):
+    """Equal id lists except where the reference's scores tie within `tol` of each other."""
+    assert len(got_ids) == len(ref_ids)
+    if tol == 0:
+        np.testing.assert_array_equal(np.sort(got_sc)[::-1].view(np.uint32), np.asarray(ref_sc).view(np.uint32))
+    else:
+        np.testing.assert_allclose(got_sc, ref_sc, rtol=RTOL, atol=ATOL)
+    if len(ref_sc) == 0:
+        return
+    kth = ref_sc[-1]
+    diff = set(map(int, got_ids)) ^ set(map(int, ref_ids))
+    ref_map = dict(zip(map(int, ref_ids), ref_sc))
+    got_map = dict(zip(map(int, got_ids), got_sc))
+    for vid in diff:
+        s = ref_map.get(vid, got_map.get(vid))
+        assert abs(float(s) - float(kth)) <= tol * abs(float(kth)) + (ATOL if tol else 0.0), (vid, s, kth)
+
+
+# ---- layout and plans ------------------------------------------------------------------------
+
+def test_transcode_matches_oracle(ora, dev, corpus768):
+    seg = mb().Segment.upload(corpus768["eden"], dev)
+    pages, ts = seg.read_layout()
+    nb = corpus768["eden"].size // 4096
+    assert seg.block_count() == nb
+    for b in range(nb):
+        exp, exp_ts = ora.device_layout(corpus768["eden"][b * 4096:(b + 1) * 4096])
+        assert np.array_equal(pages[b * 4096:(b + 1) * 4096], exp), b
+        assert np.array_equal(ts[2 * b:2 * b + 2], exp_ts)
+
+
+PLAN_FIELDS = ["prefix", "bit_weights", "rabitq_q", "rabitq_scale", "rabitq_weights2", "rabitq_base", "rabitq_lut",
+               "tail_fold_q", "tail_fold_weights2", "tail_fold_base", "q_tail_norm", "q_mid_norm", "q_after_prefix",
+               "q_after_s1", "s4_abs_budget", "prefix_l1", "prefix_sum", "eden_q_rot", "eden_mean_ip",
+               "eden_inv_sqrt_d", "eden_codebook", "eden_mid_q_rot", "eden_mid_mean_ip", "eden_mid_inv_sqrt_d",
+               "eden_mid_codebook", "dims", "prefix_codec", "mid_codec", "has_tail_fold"]
+
+
+@pytest.mark.parametrize("dims", [192, 200, 384, 768, 1000])
+@pytest.mark.parametrize("codec", ["minmax", "eden", "eden_b1"])
+def test_plan_fields_bit_identical(ora, dev, dims, codec):
+    rng = np.random.default_rng(dims)
+    q = rng.standard_normal(dims).astype(np.float32)
+    q /= np.linalg.norm(q)
+    mean = (rng.standard_normal(64) * 0.05).astype(np.float32)
+    mid_mean = (rng.standard_normal(128) * 0.05).astype(np.float32)
+    M = mb()
+    if codec == "minmax":
+        gp = M.QueryPlan.from_query(q, dims, dev=dev)
+        op = ora.plan_build(q, prefix_codec=ora.MINMAX4)
+    elif codec == "eden":
+        gp = M.QueryPlan.from_query_eden(q, dims, fit(mean), dev=dev)
+        op = ora.plan_build(q, prefix_codec=ora.EDEN_PROD, eden_mean=mean)
+    else:
+        gp = M.QueryPlan.from_query_eden_dual(q, dims, fit(mean), fit(mid_mean, 128, 1), dev=dev)
+        op = ora.plan_build(q, prefix_codec=ora.EDEN_PROD, mid_codec=ora.EDEN_B1, eden_mean=mean, mid_mean=mid_mean)
+    g = gp.fields(0)
+    for f in PLAN_FIELDS:
+        a = np.ctypeslib.as_array(getattr(g, f)) if not isinstance(getattr(g, f), (int, float)) else np.array(getattr(g, f))
+        b = np.ctypeslib.as_array(getattr(op, f)) if not isinstance(getattr(op, f), (int, float)) else np.array(getattr(op, f))
+        assert np.array_equal(np.asarray(a, np.float32).view(np.uint32), np.asarray(b, np.float32).view(np.uint32)), f
+
+
+def test_plan_rejects_contract_violations(dev):
+    M = mb()
+    with pytest.raises(ValueError):
+        M.QueryPlan.from_query(np.zeros(100, np.float32), 100, dev=dev)  # dims < 192
+    with pytest.raises(ValueError):
+        M.QueryPlan.from_queries(np.zeros((1, 768), np.float32), M.PrefixCodec.EDEN_PROD, dev=dev)  # no fit
+    q = np.zeros(768, np.float32)
+    q[5] = np.nan
+    with pytest.raises(M.MrlError):
+        M.QueryPlan.from_query(q, 768, dev=dev)
+
+
+# ---- per-slot scores ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("depth", [0, 1, 2])
+@pytest.mark.parametrize("codec", ["eden", "minmax"])
+def test_exact_mode_scores_bit_identical(ora, dev, corpus768, depth, codec):
+    M = mb()
+    blocks = corpus768[codec]
+    seg = M.Segment.upload(blocks, dev)
+    for q in corpus768["qs"][:2]:
+        if codec == "eden":
+            gp = M.QueryPlan.from_query_eden(q, 768, fit(corpus768["mean"]), dev=dev)
+            op = ora.plan_build(q, prefix_codec=ora.EDEN_PROD, eden_mean=corpus768["mean"])
+        else:
+            gp = M.QueryPlan.from_query(q, 768, dev=dev)
+            op = ora.plan_build(q, prefix_codec=ora.MINMAX4)
+        cfg = M.ScanConfig(shortlist_cand=64, strata_depth=M.StrataDepth(depth), mode=M.ScanMode.EXACT)
+        sc, act, _ = M.vector_scores(seg, gp, cfg)
+        rsc, ract = ora.full_scores(blocks, op, ora.scan_cfg(k=64, strata_depth=depth))
+        assert np.array_equal(act, ract)
+        assert np.array_equal(sc[act == 1].view(np.uint32), rsc[act == 1].view(np.uint32))
+
+
+@pytest.mark.parametrize("depth", [0, 1, 2])
+@pytest.mark.parametrize("codec", ["eden", "minmax"])
+def test_fast_mode_integer_sums_bit_exact(ora, dev, corpus768, depth, codec):
+    M = mb()
+    blocks = corpus768[codec]
+    seg = M.Segment.upload(blocks, dev)
+    for q in corpus768["qs"][:2]:
+        if codec == "eden":
+            gp = M.QueryPlan.from_query_eden(q, 768, fit(corpus768["mean"]), dev=dev)
+            op = ora.plan_build(q, prefix_codec=ora.EDEN_PROD, eden_mean=corpus768["mean"])
+        else:
+            gp = M.QueryPlan.from_query(q, 768, dev=dev)
+            op = ora.plan_build(q, prefix_codec=ora.MINMAX4)
+        cfg = M.ScanConfig(shortlist_cand=64, strata_depth=M.StrataDepth(depth), mode=M.ScanMode.FAST)
+        ocfg = ora.scan_cfg(k=64, strata_depth=depth)
+        sc, act, parts = M.vector_scores(seg, gp, cfg)
+        fp = ora.fixed_plan_build(op, ocfg)
+        oparts, osc, oact = ora.fixed_scores(blocks, op, fp, ocfg)
+        assert np.array_equal(act, oact)
+        a = act == 1
+        assert np.array_equal(parts[a], oparts[a])                                 # integer sums: bit-exact
+        assert np.array_equal(sc[a].view(np.uint32), osc[a].view(np.uint32))       # same f32 assembly
+        rsc, _ = ora.full_scores(blocks, op, ocfg)
+        np.testing.assert_allclose(sc[a], rsc[a], rtol=RTOL, atol=ATOL)            # vs reference f32
+
+
+def test_eden_b1_mid_codec(ora, dev):
+    """EdenB1 mid band (src/scan.rs:521-551, src/quantize.rs:265-295) end to end."""
+    M = mb()
+    docs = ora.synth_docs(8, 64 * 6, 768)
+    mean = ora.eden_fit_prefix(docs)
+    mid_mean = ora.eden_fit_band(docs, 64, 128)
+    blocks = ora.encode_corpus(docs, eden_mean=mean, mid_mean=mid_mean)
+    gb = M.encode_blocks(docs, 768, eden=fit(mean), eden_mid=fit(mid_mean, 128, 1), dev=dev)
+    assert np.array_equal(gb, blocks)
+    seg = M.Segment.upload(blocks, dev)
+    q, _ = ora.synth_queries(8, docs.shape[0], 1, 1, 768)
+    gp = M.QueryPlan.from_query_eden_dual(q[0], 768, fit(mean), fit(mid_mean, 128, 1), dev=dev)
+    op = ora.plan_build(q[0], prefix_codec=ora.EDEN_PROD, mid_codec=ora.EDEN_B1, eden_mean=mean, mid_mean=mid_mean)
+    ex, act, _ = M.vector_scores(seg, gp, M.ScanConfig(shortlist_cand=32, mode=M.ScanMode.EXACT))
+    rsc, ract = ora.full_scores(blocks, op, ora.scan_cfg(k=32))
+    assert np.array_equal(ex[act == 1].view(np.uint32), rsc[ract == 1].view(np.uint32))
+    fa, act2, _ = M.vector_scores(seg, gp, M.ScanConfig(shortlist_cand=32, mode=M.ScanMode.FAST))
+    np.testing.assert_allclose(fa[act2 == 1], rsc[ract == 1], rtol=RTOL, atol=ATOL)
+
+
+# ---- top-k --------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("k", [1, 16, 64, 256, 1000])
+@pytest.mark.parametrize("mode", ["exact", "fast"])
+def test_scan_topk_matches_reference_scan(ora, dev, corpus768, k, mode):
+    M = mb()
+    seg = M.Segment.upload(corpus768["eden"], dev)
+    qs = corpus768["qs"]
+    plans = M.QueryPlan.from_queries(qs, M.PrefixCodec.EDEN_PROD, eden=fit(corpus768["mean"]), dev=dev)
+    cfg = M.ScanConfig(shortlist_cand=k, mode=M.ScanMode.EXACT if mode == "exact" else M.ScanMode.FAST)
+    ids, scores, counts = M.scan_blocks_batch(seg, plans, cfg)
+    for qi, q in enumerate(qs):
+        op = ora.plan_build(q, eden_mean=corpus768["mean"])
+        ocfg = ora.scan_cfg(k=k)
+        rid, rsc = ora.scan_blocks(corpus768["eden"], op, ocfg, threads=4)   # the reference's scan
+        n = int(counts[qi])
+        gi, gs = ids[qi, :n], scores[qi, :n]
+        assert np.all(np.diff(gs) <= 0)                                       # sorted, descending
+        if mode == "exact":
+            assert_same_topk(gi, gs, rid, rsc, 0)
+        else:
+            fp = ora.fixed_plan_build(op, ocfg)
+            _, fsc, fact = ora.fixed_scores(corpus768["eden"], op, fp, ocfg)
+            ti, ts = ora.topk_by_key(fsc, fact, k)                            # exact top-k of the fixed scores
+            assert np.array_equal(gi, ti) and np.array_equal(gs.view(np.uint32), ts.view(np.uint32))
+            assert_same_topk(gi, gs, rid, rsc, RTOL)
+
+
+def test_forced_reselection_is_exact(ora, dev, corpus768):
+    """A per-CTA list of 1 entry forces the verification to fail and the last CTA to rescan:
+    the result must still be the exact top-k."""
+    M = mb()
+    seg = M.Segment.upload(corpus768["eden"], dev)
+    q = corpus768["qs"][0]
+    gp = M.QueryPlan.from_query_eden(q, 768, fit(corpus768["mean"]), dev=dev)
+    op = ora.plan_build(q, eden_mean=corpus768["mean"])
+    cfg = M.ScanConfig(shortlist_cand=256, mode=M.ScanMode.EXACT)
+    try:
+        for ll in (1, 2, 4):
+            dev.set_list_len(ll)
+            hits = M.scan_blocks(seg, gp, cfg)
+            fs, act = ora.full_scores(corpus768["eden"], op, ora.scan_cfg(k=256))
+            ti, ts = ora.topk_by_key(fs, act, 256)
+            assert [h.id.as_u64() for h in hits] == [int(i) for i in ti]
+            assert np.array_equal(np.array([h.score for h in hits], np.float32).view(np.uint32), ts.view(np.uint32))
+    finally:
+        dev.set_list_len(0)
+
+
+def test_ties_resolve_to_lower_slot(ora, dev):
+    """Identical vectors tie exactly; the result keeps the lowest (block, slot) ids, and the
+    heavy concentration of tied winners in the first pages exercises the exact re-selection."""
+    M = mb()
+    row = ora.synth_docs(3, 1, 768)
+    docs = np.repeat(row, 64 * 20, axis=0)
+    blocks = ora.encode_corpus(docs, prefix_codec=ora.MINMAX4)
+    seg = M.Segment.upload(blocks, dev)
+    gp = M.QueryPlan.from_query(row[0], 768, dev=dev)
+    for mode in (M.ScanMode.EXACT, M.ScanMode.FAST):
+        hits = M.scan_blocks(seg, gp, M.ScanConfig(shortlist_cand=100, mode=mode))
+        assert [h.id.block * 64 + h.id.slot for h in hits] == list(range(100))
+        assert len(set(h.score for h in hits)) == 1
+
+
+def test_edge_cases(ora, dev):
+    M = mb()
+    docs = ora.synth_docs(4, 64 * 3, 384)
+    blocks = ora.encode_corpus(docs, prefix_codec=ora.MINMAX4)
+    # tombstone everything in block 1 and flip one slot of block 2
+    b = blocks.copy().reshape(3, 4096)
+    b[1, 16:24] = 0xFF
+    t = struct.unpack_from("<Q", b[2], 16)[0] | (1 << 5)
+    struct.pack_into("<Q", b[2], 16, t)
+    blocks2 = b.reshape(-1)
+    seg = M.Segment.upload(blocks2, dev, block_id_base=1000)
+    gp = M.QueryPlan.from_query(docs[0], 384, dev=dev)
+    op = ora.plan_build(docs[0], prefix_codec=ora.MINMAX4)
+    for mode in (M.ScanMode.EXACT, M.ScanMode.FAST):
+        hits = M.scan_blocks(seg, gp, M.ScanConfig(shortlist_cand=4096, mode=mode))
+        assert len(hits) == 64 + 63                                   # K > live slots
+        assert all(h.id.block in (1000, 1002) for h in hits)
+        assert all(not (h.id.block == 1002 and h.id.slot == 5) for h in hits)
+        rid, rsc = ora.scan_blocks(blocks2, op, ora.scan_cfg(k=4096))
+        exp = sorted(((int(i) >> 16) + 1000) << 16 | (int(i) & 0xFFFF) for i in rid)
+        assert sorted(h.id.as_u64() for h in hits) == exp
+    # empty segment
+    empty = M.Segment.upload(np.zeros(0, np.uint8), dev)
+    assert M.scan_blocks(empty, gp, M.ScanConfig(shortlist_cand=10)) == []
+    # temporal filter (src/scan.rs:719-730): ts = row index, keep block 2 only
+    seg_t = M.Segment.upload(blocks, dev)
+    hits = M.scan_blocks(seg_t, gp, M.ScanConfig(shortlist_cand=500, temporal_filter_enable=True), time_lo=128)
+    assert len(hits) == 64 and all(h.id.block == 2 for h in hits)
+    hits = M.scan_blocks(seg_t, gp, M.ScanConfig(shortlist_cand=500, temporal_filter_enable=False), time_lo=128)
+    assert len(hits) == 192
+
+
+def test_append_live(ora, dev):
+    M = mb()
+    docs = ora.synth_docs(6, 64 * 5, 768)
+    mean = ora.eden_fit_prefix(docs)
+    blocks = ora.encode_corpus(docs, eden_mean=mean)
+    seg = M.Segment.upload(blocks[: 2 * 4096], dev)
+    for b in range(2, 5):
+        seg.append_live(blocks[b * 4096:(b + 1) * 4096])
+    assert seg.block_count() == 5
+    full = M.Segment.upload(blocks, dev)
+    gp = M.QueryPlan.from_query_eden(docs[7], 768, fit(mean), dev=dev)
+    cfg = M.ScanConfig(shortlist_cand=64)
+    assert M.scan_blocks(seg, gp, cfg) == M.scan_blocks(full, gp, cfg)
+    assert np.array_equal(seg.read_layout()[0], full.read_layout()[0])
+
+
+# ---- encode + synthetic inputs ------------------------------------------------------------------
+
+@pytest.mark.parametrize("dims", [384, 768])
+@pytest.mark.parametrize("codec", ["eden", "minmax"])
+def test_encode_blocks_byte_identical(ora, dev, dims, codec):
+    M = mb()
+    n = 64 * 5 + 9
+    docs = ora.synth_docs(13, n, dims)
+    mean = ora.eden_fit_prefix(docs)
+    ts = (np.arange(n) * 7 + 100).astype(np.uint32)
+    src = (1 << (np.arange(n) % 4)).astype(np.uint32)
+    if codec == "eden":
+        got = M.encode_blocks(docs, dims, eden=fit(mean), timestamps=ts, sources=src, dev=dev)
+    else:
+        got = M.encode_blocks(docs, dims, timestamps=ts, sources=src, dev=dev)
+    exp = np.concatenate([ora.encode_block(docs[b:b + 64], ts=ts[b:b + 64], src=src[b:b + 64],
+                                           prefix_codec=ora.EDEN_PROD if codec == "eden" else ora.MINMAX4,
+                                           eden_mean=mean) for b in range(0, n, 64)])
+    assert np.array_equal(got, exp)
+    for b in range(got.size // 4096):
+        assert ora.verify_crc(got[b * 4096:(b + 1) * 4096])
+
+
+def test_synth_fit_encode_device_match_oracle(ora, dev):
+    torch = pytest.importorskip("torch")
+    M = mb()
+    lib = M.load()
+    n, dims = 64 * 9 + 3, 768
+    x = torch.empty((n, dims), dtype=torch.float32, device="cuda")
+    assert lib.mrl_synth_docs_device(dev.ptr, 42, 0, n, dims, C.c_void_p(x.data_ptr())) == 0
+    docs = ora.synth_docs(42, n, dims)
+    assert np.array_equal(x.cpu().numpy(), docs)
+    qd = torch.empty((5, dims), dtype=torch.float32, device="cuda")
+    pk = torch.empty(5, dtype=torch.int64, device="cuda")
+    assert lib.mrl_synth_queries_device(dev.ptr, 42, n, 7, 5, dims, C.c_float(0.1), C.c_void_p(qd.data_ptr()),
+                                        C.c_void_p(pk.data_ptr())) == 0
+    oq, opk = ora.synth_queries(42, n, 7, 5, dims)
+    assert np.array_equal(qd.cpu().numpy(), oq) and np.array_equal(pk.cpu().numpy().astype(np.uint64), opk)
+    mean = np.zeros(64, np.float32)
+    assert lib.mrl_eden_fit_device(dev.ptr, C.c_void_p(x.data_ptr()), n, dims, 0, 64,
+                                   mean.ctypes.data_as(C.c_void_p)) == 0
+    assert np.array_equal(mean, ora.eden_fit_prefix(docs))
+    pax = torch.empty(((n + 63) // 64) * 4096, dtype=torch.uint8, device="cuda")
+    desc, keep = M.api._codec_desc(M.PrefixCodec.EDEN_PROD, M.MidCodec.RABITQ, fit(mean), None)
+    segp = C.c_void_p()
+    assert lib.mrl_encode_device(dev.ptr, C.c_void_p(x.data_ptr()), n, dims, 8, C.byref(desc),
+                                 C.c_void_p(pax.data_ptr()), 0, C.byref(segp)) == 0
+    blocks = ora.encode_corpus(docs, eden_mean=mean)
+    assert np.array_equal(pax.cpu().numpy(), blocks)
+    seg = M.Segment(segp, dev)
+    ref = M.Segment.upload(blocks, dev)
+    assert np.array_equal(seg.read_layout()[0], ref.read_layout()[0])
+    assert np.array_equal(seg.read_layout()[1], ref.read_layout()[1])
+
+
+# ---- full size (BASELINE config 2 shapes): size-independent properties ---------------------------
+
+def test_full_size_1m_properties(ora, dev):
+    """1,000,000 x 768 docs synthesised, fitted and encoded on the device; properties:
+    the device blocks of sampled pages equal the oracle's encode of the same rows; exact-mode
+    per-slot scores of sampled pages equal the oracle's bit for bit; both modes return the exact
+    top-256 of their own per-slot scores; fast and exact top-256 agree within the tolerance."""
+    torch = pytest.importorskip("torch")
+    M = mb()
+    lib = M.load()
+    n, dims, k = 1_000_000, 768, 256
+    x = torch.empty((n, dims), dtype=torch.float32, device="cuda")
+    assert lib.mrl_synth_docs_device(dev.ptr, 42, 0, n, dims, C.c_void_p(x.data_ptr())) == 0
+    mean = np.zeros(64, np.float32)
+    assert lib.mrl_eden_fit_device(dev.ptr, C.c_void_p(x.data_ptr()), n, dims, 0, 64,
+                                   mean.ctypes.data_as(C.c_void_p)) == 0
+    nb = (n + 63) // 64
+    pax = torch.empty(nb * 4096, dtype=torch.uint8, device="cuda")
+    desc, keep = M.api._codec_desc(M.PrefixCodec.EDEN_PROD, M.MidCodec.RABITQ, fit(mean), None)
+    segp = C.c_void_p()
+    assert lib.mrl_encode_device(dev.ptr, C.c_void_p(x.data_ptr()), n, dims, 8, C.byref(desc),
+                                 C.c_void_p(pax.data_ptr()), 0, C.byref(segp)) == 0
+    seg = M.Segment(segp, dev)
+    rng = np.random.default_rng(0)
+    sample = np.sort(rng.choice(nb, 24, replace=False))
+    host_blocks = pax.cpu().numpy()
+    for b in sample:
+        rows = ora.synth_docs(42, 64, dims, row0=int(b) * 64)
+        exp = ora.encode_block(rows, ts=np.arange(b * 64, b * 64 + 64), src=np.full(64, 8), eden_mean=mean)
+        assert np.array_equal(host_blocks[b * 4096:(b + 1) * 4096], exp)
+    del x
+    q, _ = ora.synth_queries(42, n, 7, 1, dims)
+    gp = M.QueryPlan.from_query_eden(q[0], dims, fit(mean), dev=dev)
+    op = ora.plan_build(q[0], eden_mean=mean)
+    res = {}
+    for mode in (M.ScanMode.EXACT, M.ScanMode.FAST):
+        cfg = M.ScanConfig(shortlist_cand=k, mode=mode)
+        sc, act, _ = M.vector_scores(seg, gp, cfg)
+        hits = M.scan_blocks(seg, gp, cfg)
+        gi = np.array([h.id.block * 64 + h.id.slot for h in hits])
+        gs = np.array([h.score for h in hits], np.float32)
+        order = np.lexsort((np.arange(sc.size), -sc.astype(np.float64)))
+        order = order[act[order] == 1][:k]
+        assert np.array_equal(gi, order) and np.array_equal(gs.view(np.uint32), sc[order].view(np.uint32))
+        res[mode] = (gi, gs, sc)
+        if mode == M.ScanMode.EXACT:
+            sub = np.concatenate([host_blocks[b * 4096:(b + 1) * 4096] for b in sample])
+            rs, ra = ora.full_scores(sub, op, ora.scan_cfg(k=k))
+            idx = np.concatenate([np.arange(b * 64, b * 64 + 64) for b in sample])
+            assert np.array_equal(sc[idx][ra == 1].view(np.uint32), rs[ra == 1].view(np.uint32))
+    ei, es, esc = res[M.ScanMode.EXACT]
+    fi, fs, fsc = res[M.ScanMode.FAST]
+    np.testing.assert_allclose(fsc, esc, rtol=RTOL, atol=ATOL)
+    vid = lambda o: (o // 64) << 16 | (o % 64)  # noqa: E731
+    assert_same_topk([vid(o) for o in fi], fs, [vid(o) for o in ei], es, RTOL)
