@@ -15,14 +15,23 @@ struct mrl_ctx {
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
     std::string err;
+    // scan scratch: per-CTA lists, control words, per-CTA flags, per-page owner (grow-only)
     unsigned long long* cta_keys = nullptr;  // sms * 32
-    unsigned int* ticket = nullptr;
+    unsigned int* ctl = nullptr;             // mrl::kCtlWords
+    uint8_t* cta_flags = nullptr;            // sms
+    uint8_t* owner = nullptr;
+    size_t owner_bytes = 0;
     uint32_t list_len_override = 0;
     // grow-only scratch for host-facing calls: inputs (queries, rows, means) and outputs
     void* tmp = nullptr;
     size_t tmp_bytes = 0;
     void* tmp_out = nullptr;
     size_t tmp_out_bytes = 0;
+    // device copy of the last codec centres uploaded (64 prefix + 128 mid floats) and its host
+    // twin, so repeated plan builds against one EdenFit issue no host->device copy
+    float* d_means = nullptr;
+    float h_means[192];
+    bool means_valid = false;
 };
 
 struct mrl_seg {
@@ -113,7 +122,9 @@ mrl::ScanLaunch make_launch(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
     p.has_hi = hi ? 1u : 0u;
     p.hi = hi ? *hi : 0u;
     p.cta_keys = ctx->cta_keys;
-    p.ticket = ctx->ticket;
+    p.ctl = ctx->ctl;
+    p.cta_flags = ctx->cta_flags;
+    p.owner = ctx->owner;
     return p;
 }
 
@@ -128,13 +139,20 @@ int check_codec(mrl_ctx* ctx, const mrl_codec_desc* codec) {
     return MRL_OK;
 }
 
-// Copies the codec's host means into device scratch at `dst` (64 + 128 floats).
-int upload_means(mrl_ctx* ctx, const mrl_codec_desc* codec, float* dst) {
+// Makes ctx->d_means hold the codec's centres (64 prefix + 128 mid floats); copies only when they
+// differ from the last upload. Returns the device pointer through `out`.
+int upload_means(mrl_ctx* ctx, const mrl_codec_desc* codec, float** out) {
     float h[192];
     for (int i = 0; i < 192; ++i) h[i] = 0.0f;
     if (codec->eden_mean) std::memcpy(h, codec->eden_mean, 64 * sizeof(float));
     if (codec->mid_mean) std::memcpy(h + 64, codec->mid_mean, 128 * sizeof(float));
-    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(dst, h, sizeof(h), cudaMemcpyHostToDevice, ctx->stream));
+    if (!ctx->means_valid || std::memcmp(h, ctx->h_means, sizeof(h)) != 0) {
+        std::memcpy(ctx->h_means, h, sizeof(h));
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->d_means, ctx->h_means, sizeof(h), cudaMemcpyHostToDevice, ctx->stream));
+        MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));  // h_means may change on the next call
+        ctx->means_valid = true;
+    }
+    *out = ctx->d_means;
     return MRL_OK;
 }
 
@@ -183,8 +201,11 @@ int mrl_ctx_create(int device, mrl_ctx** out) {
     }
     ctx->stream = ctx->own_stream;
     if (cudaMalloc(&ctx->cta_keys, sizeof(unsigned long long) * 32 * (size_t)ctx->sms) != cudaSuccess ||
-        cudaMalloc(&ctx->ticket, sizeof(unsigned int)) != cudaSuccess ||
-        cudaMemset(ctx->ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
+        cudaMalloc(&ctx->ctl, sizeof(unsigned int) * mrl::kCtlWords) != cudaSuccess ||
+        cudaMalloc(&ctx->cta_flags, (size_t)ctx->sms) != cudaSuccess ||
+        cudaMalloc(&ctx->d_means, 192 * sizeof(float)) != cudaSuccess ||
+        cudaMemset(ctx->ctl, 0, sizeof(unsigned int) * mrl::kCtlWords) != cudaSuccess ||
+        cudaMemset(ctx->cta_flags, 0, (size_t)ctx->sms) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) {
         mrl_ctx_destroy(ctx);
         return MRL_ERR_NOMEM;
@@ -198,9 +219,12 @@ void mrl_ctx_destroy(mrl_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->cta_keys);
-    cudaFree(ctx->ticket);
+    cudaFree(ctx->ctl);
+    cudaFree(ctx->cta_flags);
+    cudaFree(ctx->owner);
     cudaFree(ctx->tmp);
     cudaFree(ctx->tmp_out);
+    cudaFree(ctx->d_means);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
 }
@@ -313,9 +337,8 @@ int mrl_plan_build_device(mrl_ctx* ctx, const float* d_queries, uint32_t n_q, ui
     if (n_q > plans->n_q || dims != plans->dims) return fail(ctx, MRL_ERR_INVALID, "plan storage too small or dims mismatch");
     if (n_q == 0) return MRL_OK;
     if (int rc = set_device(ctx)) return rc;
-    if (int rc = ensure_tmp(ctx, 192 * sizeof(float))) return rc;
-    float* d_means = (float*)ctx->tmp;
-    if (int rc = upload_means(ctx, codec, d_means)) return rc;
+    float* d_means = nullptr;
+    if (int rc = upload_means(ctx, codec, &d_means)) return rc;
     if (mrl::launch_plan_build(d_queries, n_q, dims, codec->prefix_codec, codec->mid_codec, d_means, codec->eden_seed,
                                codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr, codec->mid_seed,
                                plans->d, ctx->stream))
@@ -334,14 +357,14 @@ int mrl_plan_build(mrl_ctx* ctx, const float* queries, uint32_t n_q, uint32_t di
     mrl_plans* p = nullptr;
     if (int rc = mrl_plans_alloc(ctx, n_q, dims, &p)) return rc;
     const size_t qbytes = (size_t)n_q * dims * sizeof(float);
-    if (int rc = ensure_tmp(ctx, 192 * sizeof(float) + qbytes)) { mrl_plans_free(ctx, p); return rc; }
-    float* d_means = (float*)ctx->tmp;
-    float* d_q = d_means + 192;
+    if (int rc = ensure_tmp(ctx, qbytes)) { mrl_plans_free(ctx, p); return rc; }
+    float* d_means = nullptr;
+    float* d_q = (float*)ctx->tmp;
     if (qbytes) {
         cudaError_t e = cudaMemcpyAsync(d_q, queries, qbytes, cudaMemcpyHostToDevice, ctx->stream);
         if (e != cudaSuccess) { mrl_plans_free(ctx, p); return cuda_fail(ctx, e, "query copy"); }
     }
-    if (int rc = upload_means(ctx, codec, d_means)) { mrl_plans_free(ctx, p); return rc; }
+    if (int rc = upload_means(ctx, codec, &d_means)) { mrl_plans_free(ctx, p); return rc; }
     if (n_q && mrl::launch_plan_build(d_q, n_q, dims, codec->prefix_codec, codec->mid_codec, d_means, codec->eden_seed,
                                       codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr, codec->mid_seed, p->d,
                                       ctx->stream)) {
@@ -365,11 +388,11 @@ int mrl_plan_rebuild(mrl_ctx* ctx, const float* queries, uint32_t n_q, uint32_t 
     if (n_q == 0) return MRL_OK;
     if (int rc = set_device(ctx)) return rc;
     const size_t qbytes = (size_t)n_q * dims * sizeof(float);
-    if (int rc = ensure_tmp(ctx, 192 * sizeof(float) + qbytes)) return rc;
-    float* d_means = (float*)ctx->tmp;
-    float* d_q = d_means + 192;
+    if (int rc = ensure_tmp(ctx, qbytes)) return rc;
+    float* d_means = nullptr;
+    float* d_q = (float*)ctx->tmp;
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(d_q, queries, qbytes, cudaMemcpyHostToDevice, ctx->stream));
-    if (int rc = upload_means(ctx, codec, d_means)) return rc;
+    if (int rc = upload_means(ctx, codec, &d_means)) return rc;
     if (mrl::launch_plan_build(d_q, n_q, dims, codec->prefix_codec, codec->mid_codec, d_means, codec->eden_seed,
                                codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr, codec->mid_seed, plans->d,
                                ctx->stream))
@@ -402,6 +425,7 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
     if ((uint64_t)q0 + n_q > plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan range out of bounds");
     if (n_q && (!d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "output is NULL");
     if (int rc = set_device(ctx)) return rc;
+    if (int rc = ensure_buf(ctx, (void**)&ctx->owner, &ctx->owner_bytes, seg->n_blocks ? seg->n_blocks : 1)) return rc;
     const uint32_t k = cfg->shortlist_cand;
     for (uint32_t i = 0; i < n_q; ++i) {
         mrl::ScanLaunch p = make_launch(ctx, seg, plans, q0 + i, cfg, time_lo, time_hi);
@@ -432,11 +456,16 @@ int mrl_scan(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, const mrl
     uint64_t* d_ids = (uint64_t*)ctx->tmp_out;
     float* d_sc = (float*)(d_ids + nk);
     uint32_t* d_cnt = (uint32_t*)(d_sc + nk);
-    if (int rc = mrl_scan_device(ctx, seg, plans, 0, n_q, cfg, time_lo, time_hi, d_ids, d_sc, d_cnt, nullptr)) return rc;
+    uint32_t* d_st = d_cnt + n_q;
+    if (int rc = mrl_scan_device(ctx, seg, plans, 0, n_q, cfg, time_lo, time_hi, d_ids, d_sc, d_cnt, d_st)) return rc;
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_ids, d_ids, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, ctx->stream));
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_scores, d_sc, nk * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_counts, d_cnt, n_q * sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream));
+    std::vector<uint32_t> st(n_q);
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(st.data(), d_st, n_q * sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream));
     MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    for (uint32_t q = 0; q < n_q; ++q)
+        if (st[q] & 2u) return fail(ctx, MRL_ERR_CUDA, "scan grid barrier timed out (CTAs not co-resident)");
     return MRL_OK;
 }
 
@@ -474,9 +503,8 @@ int mrl_encode_device(mrl_ctx* ctx, const float* d_rows, uint64_t n, uint32_t di
     const uint64_t nb = (n + 63) / 64;
     if (nb >= (1ull << 26)) return fail(ctx, MRL_ERR_INVALID, "segment larger than 2^26 pages");
     if (int rc = set_device(ctx)) return rc;
-    if (int rc = ensure_tmp(ctx, 192 * sizeof(float))) return rc;
-    float* d_means = (float*)ctx->tmp;
-    if (int rc = upload_means(ctx, codec, d_means)) return rc;
+    float* d_means = nullptr;
+    if (int rc = upload_means(ctx, codec, &d_means)) return rc;
     mrl_seg* s = nullptr;
     if (seg_out) {
         s = new mrl_seg();
@@ -508,16 +536,16 @@ int mrl_encode_blocks(mrl_ctx* ctx, const float* rows, uint64_t n, uint32_t dims
     if (int rc = set_device(ctx)) return rc;
     const uint64_t nb = (n + 63) / 64;
     const size_t rbytes = n * dims * sizeof(float), pbytes = nb * mrl::kBlockBytes, abytes = n * sizeof(uint32_t);
-    if (int rc = ensure_tmp(ctx, 192 * sizeof(float) + rbytes + pbytes + 2 * abytes + 64)) return rc;
-    float* d_means = (float*)ctx->tmp;
-    float* d_rows = d_means + 192;
+    if (int rc = ensure_tmp(ctx, rbytes + pbytes + 2 * abytes + 64)) return rc;
+    float* d_means = nullptr;
+    float* d_rows = (float*)ctx->tmp;
     uint8_t* d_pax = (uint8_t*)(d_rows + n * dims);
     uint32_t* d_ts = (uint32_t*)(d_pax + pbytes);
     uint32_t* d_src = d_ts + n;
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(d_rows, rows, rbytes, cudaMemcpyHostToDevice, ctx->stream));
     if (ts) MRL_CUDA_TRY(ctx, cudaMemcpyAsync(d_ts, ts, abytes, cudaMemcpyHostToDevice, ctx->stream));
     if (src) MRL_CUDA_TRY(ctx, cudaMemcpyAsync(d_src, src, abytes, cudaMemcpyHostToDevice, ctx->stream));
-    if (int rc = upload_means(ctx, codec, d_means)) return rc;
+    if (int rc = upload_means(ctx, codec, &d_means)) return rc;
     if (mrl::launch_encode(d_rows, n, dims, ts ? d_ts : nullptr, src ? d_src : nullptr, 8u /* source::DOC */,
                            codec->prefix_codec, d_means, codec->eden_seed,
                            codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr, codec->mid_seed, d_pax, nullptr,

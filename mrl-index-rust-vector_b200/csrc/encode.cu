@@ -91,7 +91,7 @@ __device__ void eden_slice(const float* mean, const float* diag, int d, int bits
     float cbuf[16];
     const int ncb = 1 << bits;
     if (bits == 4) {
-        for (int i = 0; i < 16; ++i) cbuf[i] = lloyd_b4(i);
+        for (int i = 0; i < 16; ++i) cbuf[i] = g_lloyd_b4[i];
     } else {
         cbuf[0] = -kLloydB1Hi;
         cbuf[1] = kLloydB1Hi;

@@ -88,14 +88,12 @@ __host__ __device__ __forceinline__ float ih_gauss(uint64_t seed, uint64_t idx) 
     return (float)num * (1.0f / 131072.0f);
 }
 
-// Lloyd-Max N(0,1) centroids (src/eden.rs:15-44).
-__host__ __device__ __forceinline__ float lloyd_b4(int i) {
-    constexpr float t[16] = {-2.73258958f, -2.06901724f, -1.61804640f, -1.25623121f,
-                             -0.94234046f, -0.65675912f, -0.38804830f, -0.12839503f,
-                             0.12839503f,  0.38804830f,  0.65675912f,  0.94234046f,
-                             1.25623121f,  1.61804640f,  2.06901724f,  2.73258958f};
-    return t[i];
-}
+// Lloyd-Max N(0,1) centroids (src/eden.rs:15-44), b = 4. Device code copies them into shared
+// memory once per CTA (a runtime-indexed local array would live on the stack).
+__device__ const float g_lloyd_b4[16] = {-2.73258958f, -2.06901724f, -1.61804640f, -1.25623121f,
+                                         -0.94234046f, -0.65675912f, -0.38804830f, -0.12839503f,
+                                         0.12839503f,  0.38804830f,  0.65675912f,  0.94234046f,
+                                         1.25623121f,  1.61804640f,  2.06901724f,  2.73258958f};
 constexpr float kLloydB1Hi = 0.79788456f;
 
 // Total order used by every selection stage: larger key = better hit. High word: the f32 score
@@ -176,8 +174,12 @@ struct ScanLaunch {
     uint32_t mode;
     uint32_t use_time;  // temporal filter active for this call
     uint32_t has_lo, lo, has_hi, hi;
-    unsigned long long* cta_keys;  // scratch: ctas * 32
-    unsigned int* ticket;          // scratch: 1 (zero between launches)
+    // scratch (owned by the context; zero-initialised once, left zeroed by every launch)
+    unsigned long long* cta_keys;  // ctas * 32: each CTA's exact top-list_len keys
+    unsigned int* ctl;             // [0] page counter, [1] barrier count, [2] barrier generation,
+                                   // [3] ticket, [4] any-CTA-flagged, [5] barrier timeout
+    uint8_t* cta_flags;            // ctas: CTA may have dropped a top-k key
+    uint8_t* owner;                // n_blocks: CTA that scored each page
     uint64_t* out_ids;
     float* out_scores;
     uint32_t* out_count;
@@ -186,6 +188,7 @@ struct ScanLaunch {
 int scan_ctas(int device_sms);
 size_t scan_smem_bytes(uint32_t ctas, uint32_t k);
 int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream);
+constexpr int kCtlWords = 8;
 int launch_debug_scores(const ScanLaunch& p, float* d_scores, uint8_t* d_active,
                         int32_t* d_partials, cudaStream_t stream);
 }  // namespace mrl

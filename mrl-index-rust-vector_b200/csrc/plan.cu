@@ -44,7 +44,9 @@ __device__ int stage_shift(double maxabs, int count) {
     frexp(maxabs * (double)count, &k);
     return 30 - k;
 }
-__device__ __forceinline__ int32_t fix(double v, int shift) { return __double2int_rn(ldexp(v, shift)); }
+// rint(v * 2^shift): `pow2` = 2^shift exactly, so the product is exact and the conversion rounds
+// to nearest-even once.
+__device__ __forceinline__ int32_t fix(double v, double pow2) { return __double2int_rn(__dmul_rn(v, pow2)); }
 
 // Block-wide max of non-negative doubles.
 __device__ double block_max(double v, double* red) {
@@ -56,6 +58,7 @@ __device__ double block_max(double v, double* red) {
     __syncthreads();
     return m;
 }
+
 
 __global__ void __launch_bounds__(kThreads)
 plan_kernel(const float* __restrict__ queries, uint32_t dims, uint32_t prefix_codec,
@@ -70,6 +73,7 @@ plan_kernel(const float* __restrict__ queries, uint32_t dims, uint32_t prefix_co
     __shared__ double s_val0[kRabitq];
     __shared__ double s_red[kThreads / 32];
     __shared__ float s_scal[16];
+    __shared__ float s_cb[16];
 
     const int tid = threadIdx.x;
     const float* q = queries + (size_t)blockIdx.x * dims;
@@ -77,6 +81,7 @@ plan_kernel(const float* __restrict__ queries, uint32_t dims, uint32_t prefix_co
     mrl_query_plan* qp = &P->qp;
 
     for (uint32_t i = tid; i < dims; i += kThreads) s_q[i] = q[i];
+    if (tid < 16) s_cb[tid] = g_lloyd_b4[tid];
     __syncthreads();
 
     // ---- prefix copy + bit weights (src/scan.rs:126-140)
@@ -209,13 +214,13 @@ plan_kernel(const float* __restrict__ queries, uint32_t dims, uint32_t prefix_co
         P->mid_base = mid_codec == MRL_MID_EDEN_B1 ? s_scal[9] : s_scal[6];
         P->tail_base = s_scal[7];
     }
-    if (tid < 16) qp->eden_codebook[tid] = prefix_codec == MRL_PREFIX_EDEN ? lloyd_b4(tid) : 0.0f;
+    if (tid < 16) qp->eden_codebook[tid] = prefix_codec == MRL_PREFIX_EDEN ? s_cb[tid] : 0.0f;
 
     // ---- exact-mode tables
     for (int e = tid; e < kPrefix * 16; e += kThreads) {
         const int d = e >> 4, l = e & 15;
         float v;
-        if (prefix_codec == MRL_PREFIX_EDEN) v = f_mul(lloyd_b4(l), f_mul(s_rot[d], inv_sqrt_64));
+        if (prefix_codec == MRL_PREFIX_EDEN) v = f_mul(s_cb[l], f_mul(s_rot[d], inv_sqrt_64));
         else v = f_mul((float)l, s_q[d]);
         P->fp_prefix[e] = v;
     }
@@ -235,25 +240,27 @@ plan_kernel(const float* __restrict__ queries, uint32_t dims, uint32_t prefix_co
     for (int e = tid; e < kPrefix * 16; e += kThreads) {
         const int d = e >> 4, l = e & 15;
         double v;
-        if (prefix_codec == MRL_PREFIX_EDEN) v = (double)lloyd_b4(l) * (double)f_mul(s_rot[d], inv_sqrt_64);
+        if (prefix_codec == MRL_PREFIX_EDEN) v = (double)s_cb[l] * (double)f_mul(s_rot[d], inv_sqrt_64);
         else v = (double)l * (double)s_q[d];
         mx = fmax(mx, fabs(v));
     }
     const int sh_p = stage_shift(block_max(mx, s_red), kPrefix);
+    const double pw_p = ldexp(1.0, sh_p);
     for (int e = tid; e < kPrefix * 16; e += kThreads) {
         const int d = e >> 4, l = e & 15;
         double v;
-        if (prefix_codec == MRL_PREFIX_EDEN) v = (double)lloyd_b4(l) * (double)f_mul(s_rot[d], inv_sqrt_64);
+        if (prefix_codec == MRL_PREFIX_EDEN) v = (double)s_cb[l] * (double)f_mul(s_rot[d], inv_sqrt_64);
         else v = (double)l * (double)s_q[d];
-        P->lut_prefix[e] = fix(v, sh_p);
+        P->lut_prefix[e] = fix(v, pw_p);
     }
     // L0Only: bit 3 of the level times bit_weights[d][3] (accum_plane, src/scan.rs:753-762)
     mx = 0.0;
     if (tid < kPrefix) mx = fabs((double)f_mul(s_q[tid], 8.0f));
     const int sh_0 = stage_shift(block_max(mx, s_red), kPrefix);
+    const double pw_0 = ldexp(1.0, sh_0);
     for (int e = tid; e < kPrefix * 16; e += kThreads) {
         const int d = e >> 4, l = e & 15;
-        P->lut_l0[e] = (l & 8) ? fix((double)f_mul(s_q[d], 8.0f), sh_0) : 0;
+        P->lut_l0[e] = (l & 8) ? fix((double)f_mul(s_q[d], 8.0f), pw_0) : 0;
     }
     // mid band: value of dim d for bit 1 / bit 0
     if (tid < kRabitq) {
@@ -271,12 +278,13 @@ plan_kernel(const float* __restrict__ queries, uint32_t dims, uint32_t prefix_co
     mx = 0.0;
     if (tid < kRabitq) mx = fmax(fabs(s_val1[tid]), fabs(s_val0[tid]));
     const int sh_1 = stage_shift(block_max(mx, s_red), kRabitq);
+    const double pw_1 = ldexp(1.0, sh_1);
     for (int e = tid; e < kS1Windows * 32; e += kThreads) {
         const int g = e >> 5, m = e & 31;
         const int w = min(5, kRabitq - 5 * g);
         int32_t s = 0;
         if (m < (1 << w))
-            for (int i = 0; i < w; ++i) s += fix(((m >> i) & 1) ? s_val1[5 * g + i] : s_val0[5 * g + i], sh_1);
+            for (int i = 0; i < w; ++i) s += fix(((m >> i) & 1) ? s_val1[5 * g + i] : s_val0[5 * g + i], pw_1);
         P->lut_s1[e] = s;
     }
     __syncthreads();
@@ -290,12 +298,13 @@ plan_kernel(const float* __restrict__ queries, uint32_t dims, uint32_t prefix_co
     mx = 0.0;
     if (tid < kFold) mx = fabs(s_val1[tid]);
     const int sh_4 = stage_shift(block_max(mx, s_red), kFold);
+    const double pw_4 = ldexp(1.0, sh_4);
     for (int e = tid; e < kS4Windows * 32; e += kThreads) {
         const int g = e >> 5, m = e & 31;
         const int w = min(5, kFold - 5 * g);
         int32_t s = 0;
         if (m < (1 << w))
-            for (int i = 0; i < w; ++i) s += fix(((m >> i) & 1) ? s_val1[5 * g + i] : s_val0[5 * g + i], sh_4);
+            for (int i = 0; i < w; ++i) s += fix(((m >> i) & 1) ? s_val1[5 * g + i] : s_val0[5 * g + i], pw_4);
         P->lut_s4[e] = s;
     }
     if (tid == 0) {

@@ -53,14 +53,20 @@ constexpr int kTabBw3 = kTabTailW + kFold;
 struct Scalars {
     float eden_mean_ip, prefix_sum, mid_mean_ip, w_s4, mid_base, tail_base;
     double un_prefix, un_s1, un_s4, un_l0;
-    uint32_t eden, mid_b1, has_tail, depth;
+    float unf_prefix, unf_s1, unf_s4, unf_l0;  // 2^-shift as f32 when every product stays normal
+    uint32_t eden, mid_b1, has_tail, depth, f32_unscale;
+    int32_t one;  // runtime 1: integer accumulations written as v * one + acc issue on the FMA pipe
 };
 
 __device__ __forceinline__ int lds_byte(const int* tab, uint32_t byte_off) {
     return *reinterpret_cast<const int*>(reinterpret_cast<const char*>(tab) + byte_off);
 }
 
-__device__ __forceinline__ float unfix(int32_t v, double unscale) {
+// v * 2^-shift rounded to f32. With |v| < 2^31 and -96 <= shift <= 126 every nonzero product
+// is a normal f32, so rounding v first and scaling by the exact power of two equals rounding the
+// exact product (the double-precision path, used otherwise).
+__device__ __forceinline__ float unfix(int32_t v, double unscale, float unscale_f, bool use_f) {
+    if (use_f) return __fmul_rn(__int2float_rn(v), unscale_f);
     return __double2float_rn(__dmul_rn((double)v, unscale));
 }
 
@@ -83,7 +89,7 @@ __device__ __forceinline__ int32_t prefix_fixed(const uint4& c0, const uint4& c1
 
 // Sum over 5-bit windows of an `NBITS`-bit little-endian bit string held in `words`.
 template <int NBITS>
-__device__ __forceinline__ int32_t window_fixed(const uint32_t* words, const int* tab) {
+__device__ __forceinline__ int32_t window_fixed(const uint32_t* words, const int* tab, int32_t one) {
     constexpr int kWords = NBITS / 32;
     constexpr int kWin = (NBITS + 4) / 5;
     int32_t acc0 = 0, acc1 = 0;
@@ -99,7 +105,7 @@ __device__ __forceinline__ int32_t window_fixed(const uint32_t* words, const int
             idx4 = (words[q] >> (r - 2)) & 0x7Cu;
         }
         const int v = lds_byte(tab, g * 128 + idx4);
-        if (g & 1) acc1 += v; else acc0 += v;
+        if (g & 1) acc1 = v * one + acc1; else acc0 = v * one + acc0;
     }
     return acc0 + acc1;
 }
@@ -113,41 +119,56 @@ struct Partials {
     int32_t p, s1, s4;
 };
 
+// VectorMeta decode (src/block.rs:60-90) with the scan's clamps (src/scan.rs:495-496); the
+// rho = flags/255 and sqrt(max(1 - rho^2, 0)) factors come from a 256-entry table computed with
+// the same correctly rounded f32 operations.
+__device__ __forceinline__ SlotMeta slot_meta_tab(uint32_t w2, uint32_t w3, const float2* rho_tab) {
+    SlotMeta m;
+    m.scale = __half2float(__ushort_as_half((unsigned short)(w2 & 0xFFFFu)));
+    m.offset = __half2float(__ushort_as_half((unsigned short)(w2 >> 16)));
+    const float t = fmaxf(__half2float(__ushort_as_half((unsigned short)(w3 & 0xFFFFu))), 0.0f);
+    const float2 rs = rho_tab[(w3 >> 16) & 0xFFu];
+    m.tomb = (w3 >> 24) != 0u;
+    m.mid_n = fmaxf(__fmul_rn(rs.y, t), 1e-6f);
+    m.high_n = fmaxf(__fmul_rn(rs.x, t), 0.0f);
+    return m;
+}
+
 // Full score of one slot; returns false for tombstoned slots.
 template <int MODE>
 __device__ __forceinline__ bool slot_score(const uint4& c0, const uint4& c1, const uint4& c2,
-                                           const uint4& c3, const int* tab, const Scalars& S,
-                                           float& score, Partials* parts) {
-    const SlotMeta m = decode_slot_meta(c3.z, c3.w);
+                                           const uint4& c3, const int* tab, const float2* rho_tab,
+                                           const Scalars& S, float& score, Partials* parts) {
+    const SlotMeta m = slot_meta_tab(c3.z, c3.w, rho_tab);
     if (m.tomb) return false;
     if (MODE == MRL_MODE_FAST) {
         const uint32_t s1w[4] = {c2.x, c2.y, c2.z, c2.w};
         const uint32_t s4w[2] = {c3.x, c3.y};
         if (S.depth == MRL_DEPTH_L0) {  // src/scan.rs:753-771
             const int32_t P = prefix_fixed(c0, c1, tab + kTabL0);
-            const float cd = unfix(P, S.un_l0);
+            const float cd = unfix(P, S.un_l0, S.unf_l0, S.f32_unscale);
             score = __fadd_rn(__fmul_rn(cd, m.scale), __fmul_rn(m.offset, S.prefix_sum));
             if (parts) {
                 parts->p = P;
-                parts->s1 = window_fixed<128>(s1w, tab + kTabS1);
-                parts->s4 = window_fixed<64>(s4w, tab + kTabS4);
+                parts->s1 = window_fixed<128>(s1w, tab + kTabS1, S.one);
+                parts->s4 = window_fixed<64>(s4w, tab + kTabS4, S.one);
             }
             return true;
         }
         const int32_t P = prefix_fixed(c0, c1, tab);
-        const float cd = unfix(P, S.un_prefix);
+        const float cd = unfix(P, S.un_prefix, S.unf_prefix, S.f32_unscale);
         float sc = S.eden ? __fadd_rn(S.eden_mean_ip, __fmul_rn(m.scale, cd))   // src/scan.rs:499-505
                           : __fadd_rn(__fmul_rn(cd, m.scale), __fmul_rn(m.offset, S.prefix_sum));
         int32_t s1 = 0, s4 = 0;
-        if (S.depth >= MRL_DEPTH_L1 || parts) s1 = window_fixed<128>(s1w, tab + kTabS1);
-        if ((S.depth == MRL_DEPTH_FULL && S.has_tail) || parts) s4 = window_fixed<64>(s4w, tab + kTabS4);
+        if (S.depth >= MRL_DEPTH_L1 || parts) s1 = window_fixed<128>(s1w, tab + kTabS1, S.one);
+        if ((S.depth == MRL_DEPTH_FULL && S.has_tail) || parts) s4 = window_fixed<64>(s4w, tab + kTabS4, S.one);
         if (S.depth >= MRL_DEPTH_L1) {
-            const float v = unfix(s1, S.un_s1);
+            const float v = unfix(s1, S.un_s1, S.unf_s1, S.f32_unscale);
             if (S.mid_b1) sc = __fadd_rn(sc, __fadd_rn(S.mid_mean_ip, __fmul_rn(m.offset, v)));  // :546-547
             else sc = __fadd_rn(sc, __fmul_rn(v, m.mid_n));                                     // :566
         }
         if (S.depth == MRL_DEPTH_FULL && S.has_tail) {  // src/scan.rs:631
-            const float v = unfix(s4, S.un_s4);
+            const float v = unfix(s4, S.un_s4, S.unf_s4, S.f32_unscale);
             sc = __fadd_rn(sc, __fmul_rn(__fmul_rn(v, fmaxf(m.high_n, 1e-6f)), S.w_s4));
         }
         if (parts) { parts->p = P; parts->s1 = s1; parts->s4 = s4; }
@@ -232,9 +253,10 @@ __device__ __forceinline__ bool block_live(const ScanLaunch& p, uint32_t b) {
 }
 
 template <int MODE>
-__device__ __forceinline__ u64 slot_key(const Slot4& s, uint32_t ordinal, const int* tab, const Scalars& S) {
+__device__ __forceinline__ u64 slot_key(const Slot4& s, uint32_t ordinal, const int* tab, const float2* rho_tab,
+                                        const Scalars& S) {
     float sc;
-    if (!slot_score<MODE>(s.c0, s.c1, s.c2, s.c3, tab, S, sc, nullptr)) return 0ull;
+    if (!slot_score<MODE>(s.c0, s.c1, s.c2, s.c3, tab, rho_tab, S, sc, nullptr)) return 0ull;
     return make_key(sc, ordinal);
 }
 
@@ -267,9 +289,9 @@ __device__ __forceinline__ u64 warp_merge32(u64 L, u64 S, int lane) {
 }
 
 struct WarpSel {
-    u64 list;   // this lane's rank in the warp's top-32
-    u64 tau;    // list[list_len-1]
-    int qn;     // queued candidates
+    u64 list;       // this lane's rank in the warp's top-32
+    uint32_t tau;   // high word of list[list_len-1] (0 until the list holds list_len keys)
+    int qn;         // queued candidates
 };
 
 __device__ __forceinline__ void warp_flush(WarpSel& ws, u64* q, int lane, uint32_t list_len, u64* cta_tau) {
@@ -280,19 +302,23 @@ __device__ __forceinline__ void warp_flush(WarpSel& ws, u64* q, int lane, uint32
         ws.list = warp_merge32(ws.list, x, lane);
     }
     ws.qn = 0;
-    ws.tau = __shfl_sync(kFull, ws.list, list_len - 1);
-    if (lane == 0 && ws.tau) atomicMax(cta_tau, ws.tau);
+    const u64 t = __shfl_sync(kFull, ws.list, list_len - 1);
+    ws.tau = (uint32_t)(t >> 32);
+    if (lane == 0 && t) atomicMax(cta_tau, t);
     __syncwarp();
 }
 
+// Offer two keys per lane. A key survives when its score word is >= the score word of the
+// current bound (the warp's list_len-th key or the CTA bound): a conservative test, exact ties are
+// settled by the 64-bit merges. Active keys always have a nonzero score word.
 __device__ __forceinline__ void warp_offer(WarpSel& ws, u64* q, int lane, uint32_t list_len, u64* cta_tau,
                                            u64 k0, u64 k1) {
-    const u64 tc = *reinterpret_cast<volatile u64*>(cta_tau);
-    const u64 tau = umax64(ws.tau, tc);
-    const bool p0 = k0 > tau, p1 = k1 > tau;
+    const uint32_t tc = (uint32_t)(*reinterpret_cast<volatile u64*>(cta_tau) >> 32);
+    const uint32_t tau = max(max(ws.tau, tc), 1u);
+    const bool p0 = (uint32_t)(k0 >> 32) >= tau, p1 = (uint32_t)(k1 >> 32) >= tau;
     const unsigned m0 = __ballot_sync(kFull, p0), m1 = __ballot_sync(kFull, p1);
+    if ((m0 | m1) == 0u) return;
     const int nn = __popc(m0) + __popc(m1);
-    if (nn == 0) return;
     if (ws.qn + nn > kQueue) warp_flush(ws, q, lane, list_len, cta_tau);
     const unsigned lt = (1u << lane) - 1u;
     if (p0) q[ws.qn + __popc(m0 & lt)] = k0;
@@ -302,6 +328,8 @@ __device__ __forceinline__ void warp_offer(WarpSel& ws, u64* q, int lane, uint32
 }
 
 // ---- final selection helpers (last CTA) ----
+constexpr int kBins = 2048;  // 11-bit radix digits
+
 __device__ __forceinline__ void hist_add(unsigned* hist, bool valid, unsigned bin, int lane) {
     const unsigned act = __ballot_sync(kFull, valid);
     if (valid) {
@@ -315,42 +343,45 @@ struct SelState {
     unsigned rem;
     unsigned done;
     unsigned bin, before;
+    unsigned warp_sum[kWarps];
 };
 
 template <int MODE>
 struct Finisher {
     const ScanLaunch& p;
     const int* tab;
+    const float2* rho_tab;
     const Scalars& S;
-    u64* cand;        // G*32
+    const u64* cand;        // G * 32, the first list_len of each CTA are live
     const unsigned* flags;  // flagged CTA ids
     unsigned nflag;
     unsigned G;
     unsigned list_len;
 
-    // Visit every candidate of the (virtual) set: U from shared memory plus, for flagged CTAs, a
-    // rescan of their pages keeping keys below their list minimum. fn(valid, key) is called
-    // warp-uniformly.
+    // Visit every candidate of the (virtual) set: the CTA lists in shared memory plus, for flagged
+    // CTAs, a rescan of the pages they scored keeping keys below their list minimum.
+    // fn(valid, key, lane) is called warp-uniformly.
     template <class Fn>
     __device__ void visit(Fn fn) const {
         const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-        const unsigned nu = G * 32;
+        const unsigned nu = G * list_len;
         for (unsigned base = 0; base < nu; base += kThreads) {
             const unsigned i = base + tid;
-            const u64 x = i < nu ? cand[i] : 0ull;
+            const u64 x = i < nu ? cand[(i / list_len) * 32 + (i % list_len)] : 0ull;
             fn(x != 0ull, x, lane);
         }
         for (unsigned f = 0; f < nflag; ++f) {
             const unsigned c = flags[f];
             const u64 minc = cand[c * 32 + list_len - 1];
-            for (uint32_t b = c + G * warp; b < p.n_blocks; b += G * kWarps) {
+            for (uint32_t b = warp; b < p.n_blocks; b += kWarps) {
+                if (__ldcg(p.owner + b) != (uint8_t)c) continue;  // warp-uniform
                 u64 k0 = 0, k1 = 0;
                 if (block_live(p, b)) {
                     Slot4 s0, s1;
                     load_slot(p.pages, b, lane, s0);
                     load_slot(p.pages, b, lane + 32, s1);
-                    k0 = slot_key<MODE>(s0, b * 64 + lane, tab, S);
-                    k1 = slot_key<MODE>(s1, b * 64 + lane + 32, tab, S);
+                    k0 = slot_key<MODE>(s0, b * 64 + lane, tab, rho_tab, S);
+                    k1 = slot_key<MODE>(s1, b * 64 + lane + 32, tab, rho_tab, S);
                 }
                 fn(k0 != 0ull && k0 < minc, k0, lane);
                 fn(k1 != 0ull && k1 < minc, k1, lane);
@@ -359,53 +390,62 @@ struct Finisher {
     }
 };
 
-// Exact k-th largest key of the candidate set (radix select, 8 bits per pass from the top).
-// Returns a threshold T such that the keys >= T are exactly the top min(k, count) keys.
+// Exact k-th largest key of the candidate set: radix select, 11-bit digits from the top with an
+// early exit once the current digit's bin holds exactly the keys still to be selected. Returns T
+// such that the keys >= T are exactly the top min(k, count) keys.
 template <int MODE>
 __device__ u64 select_threshold(const Finisher<MODE>& F, unsigned k, unsigned* hist, SelState* st) {
-    const int tid = threadIdx.x, lane = tid & 31;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) { st->prefix = 0; st->mask = 0; st->rem = k; st->done = 0; }
-    // total count
-    if (tid < 256) hist[tid] = 0;
+    if (tid == 0) hist[0] = 0;
     __syncthreads();
     F.visit([&](bool valid, u64, int ln) { hist_add(hist, valid, 0u, ln); });
     __syncthreads();
     const unsigned total = hist[0];
     __syncthreads();
     if (total <= k) return 1ull;
-    for (int shift = 56; shift >= 0; shift -= 8) {
-        if (tid < 256) hist[tid] = 0;
+    const int shifts[6] = {53, 42, 32, 21, 10, 0};
+    const int widths[6] = {11, 11, 10, 11, 11, 10};
+    for (int pass = 0; pass < 6; ++pass) {
+        const int shift = shifts[pass];
+        const unsigned nb = 1u << widths[pass];
+        for (unsigned i = tid; i < (unsigned)kBins; i += kThreads) hist[i] = 0;
         __syncthreads();
         const u64 prefix = st->prefix, mask = st->mask;
         F.visit([&](bool valid, u64 x, int ln) {
             const bool in = valid && ((x & mask) == prefix);
-            hist_add(hist, in, (unsigned)((x >> shift) & 0xFFu), ln);
+            hist_add(hist, in, (unsigned)((x >> shift) & (nb - 1)), ln);
         });
         __syncthreads();
-        if (tid < 32) {
-            unsigned c[8];
-            unsigned lsum = 0;
+        unsigned c[4], lsum = 0;  // descending scan: thread t owns bins nb-1-4t .. nb-4-4t
 #pragma unroll
-            for (int j = 0; j < 8; ++j) { c[j] = hist[255 - 8 * lane - j]; lsum += c[j]; }
-            unsigned incl = lsum;
+        for (int j = 0; j < 4; ++j) {
+            const int bin = (int)nb - 1 - 4 * tid - j;
+            c[j] = bin >= 0 ? hist[bin] : 0u;
+            lsum += c[j];
+        }
+        unsigned incl = lsum;
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const unsigned y = __shfl_up_sync(kFull, incl, o);
-                if (lane >= o) incl += y;
-            }
-            unsigned cum = incl - lsum;
-            const unsigned rem = st->rem;
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned y = __shfl_up_sync(kFull, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane == 31) st->warp_sum[warp] = incl;
+        __syncthreads();
+        unsigned wbase = 0;
+        for (int w = 0; w < warp; ++w) wbase += st->warp_sum[w];
+        unsigned cum = wbase + incl - lsum;
+        const unsigned rem = st->rem;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                if (cum < rem && rem <= cum + c[j]) { st->bin = 255 - 8 * lane - j; st->before = cum; }
-                cum += c[j];
-            }
+        for (int j = 0; j < 4; ++j) {
+            if (cum < rem && rem <= cum + c[j]) { st->bin = (unsigned)((int)nb - 1 - 4 * tid - j); st->before = cum; }
+            cum += c[j];
         }
         __syncthreads();
         if (tid == 0) {
             const unsigned bin = st->bin;
             st->prefix |= (u64)bin << shift;
-            st->mask |= 0xFFull << shift;
+            st->mask |= (u64)(nb - 1) << shift;
             st->rem -= st->before;
             if (hist[bin] == st->rem) st->done = 1;
         }
@@ -415,29 +455,21 @@ __device__ u64 select_threshold(const Finisher<MODE>& F, unsigned k, unsigned* h
     return st->prefix;
 }
 
+// Rare path, last CTA only: some CTA's exact list ended inside the top-k, so it may have dropped
+// members. Reselect over the union of lists plus those CTAs' rescanned keys and rewrite the output.
 template <int MODE>
-__device__ void final_select(const ScanLaunch& p, const int* tab, const Scalars& S, u64* cand, u64* gath,
-                             unsigned* hist, unsigned* flags, SelState* st, unsigned* s_misc) {
+__device__ void reselect(const ScanLaunch& p, const int* tab, const float2* rho_tab, const Scalars& S, u64* cand,
+                         u64* gath, unsigned* hist, unsigned* flags, SelState* st, unsigned* s_misc) {
     const int tid = threadIdx.x;
     const unsigned G = gridDim.x;
-    const unsigned nu = G * 32;
-    for (unsigned i = tid; i < nu; i += kThreads) cand[i] = __ldcg(p.cta_keys + i);
+    for (unsigned i = tid; i < G * 32; i += kThreads) cand[i] = __ldcg(p.cta_keys + i);
     if (tid == 0) { s_misc[0] = 0; s_misc[1] = 0; }
     __syncthreads();
-    Finisher<MODE> F{p, tab, S, cand, flags, 0u, G, p.list_len};
-    u64 tau = select_threshold<MODE>(F, p.k, hist, st);
-    // CTAs whose full list ends above the threshold may have dropped members of the top-k.
-    for (unsigned c = tid; c < G; c += kThreads) {
-        const u64 minc = cand[c * 32 + p.list_len - 1];
-        if (minc != 0ull && minc > tau) flags[atomicAdd(&s_misc[0], 1u)] = c;
-    }
+    for (unsigned c = tid; c < G; c += kThreads)
+        if (__ldcg(p.cta_flags + c)) flags[atomicAdd(&s_misc[0], 1u)] = c;
     __syncthreads();
-    const unsigned nflag = s_misc[0];
-    if (nflag) {
-        F.nflag = nflag;
-        tau = select_threshold<MODE>(F, p.k, hist, st);
-    }
-    // gather keys >= tau (exactly min(k, total) of them)
+    Finisher<MODE> F{p, tab, rho_tab, S, cand, flags, s_misc[0], G, p.list_len};
+    const u64 tau = select_threshold<MODE>(F, p.k, hist, st);
     F.visit([&](bool valid, u64 x, int ln) {
         const bool in = valid && x >= tau;
         const unsigned m = __ballot_sync(kFull, in);
@@ -471,15 +503,41 @@ __device__ void final_select(const ScanLaunch& p, const int* tab, const Scalars&
         p.out_ids[i] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
         p.out_scores[i] = key_score(key);
     }
-    if (tid == 0) {
-        *p.out_count = ng;
-        if (p.out_status) *p.out_status = nflag ? 1u : 0u;
-        *p.ticket = 0u;  // ready for the next launch
-    }
+    if (tid == 0) *p.out_count = ng;
 }
 
-__device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int mode, int* tab, Scalars& S,
-                                            const ScanLaunch& p) {
+// Grid-wide barrier (the launch is cooperative, so all CTAs are co-resident). Sense reversal
+// through a generation word; the wait is bounded and reports a timeout instead of hanging.
+__device__ bool grid_barrier(unsigned* ctl, unsigned G, volatile int* s_ok) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned* count = ctl + 1;
+        unsigned* gen = ctl + 2;
+        const unsigned my_gen = atomicAdd(gen, 0u);
+        __threadfence();
+        int ok = 1;
+        if (atomicAdd(count, 1u) == G - 1) {
+            atomicExch(count, 0u);
+            __threadfence();
+            atomicAdd(gen, 1u);
+        } else {
+            unsigned it = 0;
+            while (true) {
+                unsigned g;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(gen) : "memory");
+                if (g != my_gen) break;
+                if (++it > (1u << 22)) { ok = 0; atomicExch(ctl + 5, 1u); break; }  // ~0.3 s
+                __nanosleep(64);
+            }
+        }
+        *s_ok = ok;
+    }
+    __syncthreads();
+    return *s_ok != 0;
+}
+
+__device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int mode, int* tab, float2* rho_tab,
+                                            Scalars& S, const ScanLaunch& p) {
     const int tid = threadIdx.x;
     if (mode == MRL_MODE_FAST) {
         for (int i = tid; i < kPrefix * 16; i += kThreads) tab[i] = P->lut_prefix[i];
@@ -493,6 +551,12 @@ __device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int m
         for (int i = tid; i < kFold; i += kThreads) ft[kTabTailW + i] = P->tail_w[i];
         for (int i = tid; i < kPrefix; i += kThreads) ft[kTabBw3 + i] = P->qp.bit_weights[i][3];
     }
+    // rho_ratio = flags / 255 and sqrt(max(1 - r^2, 0)) (src/block.rs:74-84)
+    for (int i = tid; i < 256; i += kThreads) {
+        const float rho = __fdiv_rn((float)i, 255.0f);
+        const float r = fminf(fmaxf(rho, 0.0f), 1.0f);
+        rho_tab[i] = make_float2(rho, __fsqrt_rn(fmaxf(__fsub_rn(1.0f, __fmul_rn(r, r)), 0.0f)));
+    }
     S.eden_mean_ip = P->qp.eden_mean_ip;
     S.prefix_sum = P->qp.prefix_sum;
     S.mid_mean_ip = P->qp.eden_mid_mean_ip;
@@ -503,17 +567,40 @@ __device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int m
     S.un_s1 = P->unscale_s1;
     S.un_s4 = P->unscale_s4;
     S.un_l0 = P->unscale_l0;
+    const int sh[4] = {P->shift_prefix, P->shift_s1, P->shift_s4, P->shift_l0};
+    bool ok = true;
+    for (int i = 0; i < 4; ++i) ok = ok && sh[i] >= -96 && sh[i] <= 126;
+    S.f32_unscale = ok ? 1u : 0u;
+    S.unf_prefix = ok ? __double2float_rn(P->unscale_prefix) : 0.0f;
+    S.unf_s1 = ok ? __double2float_rn(P->unscale_s1) : 0.0f;
+    S.unf_s4 = ok ? __double2float_rn(P->unscale_s4) : 0.0f;
+    S.unf_l0 = ok ? __double2float_rn(P->unscale_l0) : 0.0f;
     S.eden = P->qp.prefix_codec == MRL_PREFIX_EDEN;
     S.mid_b1 = P->qp.mid_codec == MRL_MID_EDEN_B1;
     S.has_tail = P->qp.has_tail_fold;
     S.depth = p.depth;
+    S.one = (int32_t)(p.list_len != 0u);  // 1 for every launch; opaque to the compiler
+}
+
+// Pages are handed out dynamically (one atomic per warp and page, fetched one page ahead) so every
+// warp finishes at about the same time; owner[] records which CTA scored each page for the rare
+// rescan.
+__device__ __forceinline__ uint32_t grab_page(unsigned* counter, int lane) {
+    uint32_t b = 0;
+    if (lane == 0) b = atomicAdd(counter, 1u);
+    return __shfl_sync(kFull, b, 0);
 }
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     __shared__ __align__(16) int s_tab[kTabInts];
+    __shared__ float2 s_rho[256];
     __shared__ u64 s_cta_tau;
+    __shared__ unsigned s_seed_min, s_seed_cnt;
+    __shared__ unsigned s_rank[32];
+    __shared__ unsigned s_total;
     __shared__ unsigned s_last;
+    __shared__ int s_ok;
     __shared__ SelState s_sel;
     __shared__ unsigned s_misc[4];
     extern __shared__ __align__(16) unsigned char s_dyn[];
@@ -524,60 +611,151 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     u64* s_gath = s_cand + G * 32;                  // pow2 >= k
     unsigned P2 = 1;
     while (P2 < p.k) P2 <<= 1;
-    unsigned* s_hist = reinterpret_cast<unsigned*>(s_gath + P2);  // 256
-    unsigned* s_flags = s_hist + 256;                            // G
+    unsigned* s_hist = reinterpret_cast<unsigned*>(s_gath + P2);  // kBins
+    unsigned* s_flags = s_hist + kBins;                          // G
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    Scalars S;
-    if (tid == 0) s_cta_tau = 0ull;
-    load_tables(p.plan, MODE, s_tab, S, p);
-    __syncthreads();
+    const unsigned L = p.list_len;
+    unsigned* counter = p.ctl;
 
-    WarpSel ws{0ull, 0ull, 0};
-    u64* q = s_queue + warp * kQueue;
-    const uint32_t stride = G * kWarps;
-    uint32_t b = blockIdx.x + G * warp;
+    // first page in flight before the tables are read
+    uint32_t b = grab_page(counter, lane);
     Slot4 a0, a1;
     if (b < p.n_blocks) { load_slot(p.pages, b, lane, a0); load_slot(p.pages, b, lane + 32, a1); }
+    uint32_t bn = grab_page(counter, lane);
+
+    Scalars S;
+    if (tid == 0) { s_cta_tau = 0ull; s_seed_min = 0xFFFFFFFFu; s_seed_cnt = 0u; s_total = 0u; }
+    if (tid < 32) s_rank[tid] = 0u;
+    load_tables(p.plan, MODE, s_tab, s_rho, S, p);
+    __syncthreads();
+
+    WarpSel ws{0ull, 0u, 0};
+    u64* q = s_queue + warp * kQueue;
+    bool first = true;
     while (b < p.n_blocks) {
-        const uint32_t bn = b + stride;
         Slot4 n0, n1;
         if (bn < p.n_blocks) { load_slot(p.pages, bn, lane, n0); load_slot(p.pages, bn, lane + 32, n1); }
+        const uint32_t bnn = bn < p.n_blocks ? grab_page(counter, lane) : bn;
         u64 k0 = 0ull, k1 = 0ull;
         if (block_live(p, b)) {
-            k0 = slot_key<MODE>(a0, b * 64 + lane, s_tab, S);
-            k1 = slot_key<MODE>(a1, b * 64 + lane + 32, s_tab, S);
+            k0 = slot_key<MODE>(a0, b * 64 + lane, s_tab, s_rho, S);
+            k1 = slot_key<MODE>(a1, b * 64 + lane + 32, s_tab, s_rho, S);
         }
-        warp_offer(ws, q, lane, p.list_len, &s_cta_tau, k0, k1);
+        if (lane == 0) p.owner[b] = (uint8_t)blockIdx.x;
+        if (first) {
+            // Seed the CTA bound: each warp's best first-page key certifies one distinct key, so
+            // once all warps report, the smallest of their score words bounds the CTA's
+            // list_len-th key from below (list_len <= kWarps).
+            first = false;
+            const unsigned wmax = __reduce_max_sync(kFull, max((unsigned)(k0 >> 32), (unsigned)(k1 >> 32)));
+            if (lane == 0 && L <= (uint32_t)kWarps) {
+                atomicMin(&s_seed_min, wmax);
+                __threadfence_block();
+                if (atomicAdd(&s_seed_cnt, 1u) == (unsigned)kWarps - 1u) {
+                    const unsigned m = atomicMin(&s_seed_min, 0xFFFFFFFFu);
+                    if (m) atomicMax(&s_cta_tau, (u64)m << 32);
+                }
+            }
+        }
+        warp_offer(ws, q, lane, L, &s_cta_tau, k0, k1);
         b = bn;
+        bn = bnn;
         a0 = n0;
         a1 = n1;
     }
-    if (ws.qn) warp_flush(ws, q, lane, p.list_len, &s_cta_tau);
+    if (ws.qn) warp_flush(ws, q, lane, L, &s_cta_tau);
 
-    // CTA top-list_len from the warps' lists
+    // CTA top-list_len from the warps' lists: pairwise tree merge
     s_lists[warp * 32 + lane] = ws.list;
     __syncthreads();
+    for (int half = kWarps / 2; half >= 1; half >>= 1) {
+        if (warp < half) {
+            const u64 m = warp_merge32(s_lists[warp * 32 + lane], s_lists[(warp + half) * 32 + lane], lane);
+            __syncwarp();
+            s_lists[warp * 32 + lane] = m;
+        }
+        __syncthreads();
+    }
     if (warp == 0) {
-        u64 L = s_lists[lane];
-        for (int w = 1; w < kWarps; ++w) L = warp_merge32(L, s_lists[w * 32 + lane], lane);
-        p.cta_keys[blockIdx.x * 32 + lane] = (uint32_t)lane < p.list_len ? L : 0ull;
+        p.cta_keys[blockIdx.x * 32 + lane] = (uint32_t)lane < L ? s_lists[lane] : 0ull;
         __threadfence();
     }
+    if (!grid_barrier(p.ctl, G, &s_ok)) {
+        if (tid == 0 && p.out_status) *p.out_status = 2u;  // barrier timed out: no result
+        return;
+    }
+    if (blockIdx.x == 0 && tid == 0) atomicExch(counter, 0u);  // page counter ready for the next launch
+
+    // Global rank of each of this CTA's list keys: the number of larger keys in all CTA lists
+    // (lists are sorted, keys unique). Keys ranked below k are the top-k, written in place.
+    for (unsigned i = tid; i < G * L; i += kThreads) s_cand[i] = __ldcg(p.cta_keys + (i / L) * 32 + (i % L));
     __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(p.ticket, 1u) == G - 1) ? 1u : 0u;
+    const u64* mine = s_cand + blockIdx.x * L;
+    {
+        const unsigned ki = tid % L;           // key of mine handled by this thread
+        const unsigned cstep = kThreads / L;   // lists visited per pass
+        const u64 x = mine[ki];
+        unsigned cnt = 0, nz = 0;
+        for (unsigned c = tid / L; c < G; c += cstep) {
+            const u64* lst = s_cand + c * L;
+            unsigned lo = 0, hi = L;  // entries > x form a prefix of the descending list
+            while (lo < hi) {
+                const unsigned mid = (lo + hi) >> 1;
+                if (lst[mid] > x) lo = mid + 1; else hi = mid;
+            }
+            cnt += lo;
+            if (ki == 0) {  // one thread per list counts its live entries
+                unsigned l2 = 0, h2 = L;
+                while (l2 < h2) {
+                    const unsigned mid = (l2 + h2) >> 1;
+                    if (lst[mid] != 0ull) l2 = mid + 1; else h2 = mid;
+                }
+                nz += l2;
+            }
+        }
+        if (x != 0ull) atomicAdd(&s_rank[ki], cnt);
+        if (ki == 0 && nz) atomicAdd(&s_total, nz);
+    }
+    __syncthreads();
+    if (tid < L) {
+        const u64 x = mine[tid];
+        const unsigned r = s_rank[tid];
+        if (x != 0ull && r < p.k) {
+            const uint32_t ord = key_ordinal(x);
+            p.out_ids[r] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
+            p.out_scores[r] = key_score(x);
+        }
+        // A full list whose last key ranks inside the top-k may have dropped top-k keys.
+        if (tid == L - 1) {
+            const bool flagged = x != 0ull && r < p.k;
+            p.cta_flags[blockIdx.x] = flagged ? 1u : 0u;
+            if (flagged) atomicExch(p.ctl + 4, 1u);
+        }
+    }
+    if (blockIdx.x == 0 && tid == 0) *p.out_count = min(s_total, p.k);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(p.ctl + 3, 1u) == G - 1) ? 1u : 0u;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    final_select<MODE>(p, s_tab, S, s_cand, s_gath, s_hist, s_flags, &s_sel, s_misc);
+    const bool any = __ldcg(p.ctl + 4) != 0u;
+    if (any) reselect<MODE>(p, s_tab, s_rho, S, s_cand, s_gath, s_hist, s_flags, &s_sel, s_misc);
+    if (tid == 0) {
+        if (p.out_status) *p.out_status = any ? 1u : 0u;
+        p.ctl[3] = 0u;
+        p.ctl[4] = 0u;
+    }
 }
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) debug_scores_kernel(const ScanLaunch p, float* out,
                                                                 uint8_t* active, int32_t* parts) {
     __shared__ __align__(16) int s_tab[kTabInts];
+    __shared__ float2 s_rho[256];
     Scalars S;
-    load_tables(p.plan, MODE, s_tab, S, p);
+    load_tables(p.plan, MODE, s_tab, s_rho, S, p);
     __syncthreads();
     const uint32_t total = p.n_blocks * 64u;
     for (uint32_t i = blockIdx.x * kThreads + threadIdx.x; i < total; i += gridDim.x * kThreads) {
@@ -587,7 +765,7 @@ __global__ void __launch_bounds__(kThreads) debug_scores_kernel(const ScanLaunch
         float sc = 0.0f;
         Partials pr{0, 0, 0};
         bool ok = block_live(p, b) &&
-                  slot_score<MODE>(s.c0, s.c1, s.c2, s.c3, s_tab, S, sc, MODE == MRL_MODE_FAST ? &pr : nullptr);
+                  slot_score<MODE>(s.c0, s.c1, s.c2, s.c3, s_tab, s_rho, S, sc, MODE == MRL_MODE_FAST ? &pr : nullptr);
         out[i] = ok ? sc : 0.0f;
         active[i] = ok ? 1 : 0;
         if (parts) {
@@ -605,21 +783,19 @@ int scan_ctas(int device_sms) { return device_sms; }
 size_t scan_smem_bytes(uint32_t ctas, uint32_t k) {
     size_t p2 = 1;
     while (p2 < k) p2 <<= 1;
-    return sizeof(u64) * (kWarps * kQueue + kWarps * 32 + (size_t)ctas * 32 + p2) + sizeof(unsigned) * (256 + ctas);
+    return sizeof(u64) * (kWarps * kQueue + kWarps * 32 + (size_t)ctas * 32 + p2) + sizeof(unsigned) * (kBins + ctas);
 }
 
+// Cooperative launch: one CTA per SM, all co-resident (the grid barrier relies on it).
 int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream) {
     const size_t smem = scan_smem_bytes(ctas, p.k);
-    if (p.mode == MRL_MODE_FAST) {
-        if (cudaFuncSetAttribute(scan_kernel<MRL_MODE_FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return -1;
-        scan_kernel<MRL_MODE_FAST><<<ctas, kThreads, smem, stream>>>(p);
-    } else {
-        if (cudaFuncSetAttribute(scan_kernel<MRL_MODE_EXACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return -1;
-        scan_kernel<MRL_MODE_EXACT><<<ctas, kThreads, smem, stream>>>(p);
-    }
-    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    const void* fn = p.mode == MRL_MODE_FAST ? (const void*)scan_kernel<MRL_MODE_FAST>
+                                             : (const void*)scan_kernel<MRL_MODE_EXACT>;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -1;
+    ScanLaunch arg = p;
+    void* args[] = {&arg};
+    if (cudaLaunchCooperativeKernel(fn, dim3(ctas), dim3(kThreads), args, smem, stream) != cudaSuccess) return -1;
+    return 0;
 }
 
 int launch_debug_scores(const ScanLaunch& p, float* d_scores, uint8_t* d_active, int32_t* d_partials,
