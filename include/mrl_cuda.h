@@ -155,6 +155,23 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
                     uint32_t n_q, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                     const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
                     uint32_t* d_out_counts, uint32_t* d_out_status);
+/* No counterpart in the reference (its scan allocates its shortlist on the Rust heap per call).
+ * Same arguments, results and errors as mrl_scan_device, but the scan scratch comes from a static
+ * per-device region inside the library instead of the context, so a successful call allocates no
+ * device or host memory: for callers that must not allocate while answering a query. Limits, set
+ * by that region's fixed size (1,114,624 bytes): seg must hold at most MRL_STATIC_MAX_BLOCKS pages
+ * and the device at most MRL_STATIC_MAX_CTAS SMs, else MRL_ERR_INVALID with a message naming the
+ * limit. The first call on a device looks the region up (and may load the module), so make it
+ * before any stream capture begins. The region is shared by every context on a device: calls in
+ * flight at the same time on one device (other streams, contexts or threads) race on it, while
+ * calls ordered on one stream do not. Each call zeroes the region's control words on the context
+ * stream before its first launch. out_status bit 1 = grid barrier timed out (no result). */
+#define MRL_STATIC_MAX_BLOCKS 1048576u
+#define MRL_STATIC_MAX_CTAS 256u
+int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q0,
+                           uint32_t n_q, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+                           const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
+                           uint32_t* d_out_counts, uint32_t* d_out_status);
 /* Per-vector scores of plan `q` for every slot (n_blocks*64, host), and for MRL_MODE_FAST the
  * three int32 stage sums per slot (prefix, mid band, folded tail; may be NULL). Inactive slots
  * (tombstoned or temporally filtered) get score 0 and active 0. */

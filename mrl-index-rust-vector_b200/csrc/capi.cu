@@ -4,10 +4,27 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
 #include "mrl_internal.cuh"
+
+// Scan scratch for mrl_scan_device_static, placed in the module's own global memory so that entry
+// point allocates nothing. Layout (bytes): control words [0, 256), per-CTA flags [256, 512),
+// per-CTA key lists [512, 512 + 256*32*8), one owner byte per page after that. Sized for grids of
+// at most MRL_STATIC_MAX_CTAS CTAs and segments of at most MRL_STATIC_MAX_BLOCKS pages: 1,114,624
+// bytes per device in all.
+namespace {
+constexpr size_t kStaticCtlOff = 0;
+constexpr size_t kStaticFlagsOff = 256;
+constexpr size_t kStaticKeysOff = 512;
+constexpr size_t kStaticOwnerOff = kStaticKeysOff + (size_t)MRL_STATIC_MAX_CTAS * 32 * sizeof(unsigned long long);
+constexpr size_t kStaticBytes = kStaticOwnerOff + (size_t)MRL_STATIC_MAX_BLOCKS;
+static_assert(mrl::kCtlWords * sizeof(unsigned) <= kStaticFlagsOff - kStaticCtlOff, "control words overflow");
+static_assert(MRL_STATIC_MAX_CTAS <= 256, "owner bytes hold CTA indices < 256");
+}  // namespace
+static __device__ __align__(256) unsigned char g_static_scan_scratch[kStaticBytes];
 
 struct mrl_ctx {
     int device = 0;
@@ -68,6 +85,26 @@ int cuda_fail(mrl_ctx* ctx, cudaError_t e, const char* what) {
 int set_device(mrl_ctx* ctx) {
     const cudaError_t e = cudaSetDevice(ctx->device);
     return e == cudaSuccess ? MRL_OK : cuda_fail(ctx, e, "cudaSetDevice");
+}
+
+// Device address of g_static_scan_scratch on ctx's device (which must be current), looked up on
+// the first call per device and cached. The lookup may load this module onto the device, so the
+// first mrl_scan_device_static call on a device should come before any stream capture begins.
+constexpr int kStaticMaxDevices = 64;
+unsigned char* g_static_base[kStaticMaxDevices] = {};
+std::mutex g_static_mu;
+
+int static_scratch(mrl_ctx* ctx, unsigned char** out) {
+    if (ctx->device >= kStaticMaxDevices) return fail(ctx, MRL_ERR_INVALID, "device ordinal >= 64");
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_base[ctx->device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scan_scratch);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaGetSymbolAddress(g_static_scan_scratch)");
+        g_static_base[ctx->device] = static_cast<unsigned char*>(p);
+    }
+    *out = g_static_base[ctx->device];
+    return MRL_OK;
 }
 
 int ensure_buf(mrl_ctx* ctx, void** buf, size_t* have, size_t bytes) {
@@ -429,6 +466,57 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
     const uint32_t k = cfg->shortlist_cand;
     for (uint32_t i = 0; i < n_q; ++i) {
         mrl::ScanLaunch p = make_launch(ctx, seg, plans, q0 + i, cfg, time_lo, time_hi);
+        p.out_ids = d_out_ids + (size_t)i * k;
+        p.out_scores = d_out_scores + (size_t)i * k;
+        p.out_count = d_out_counts + i;
+        p.out_status = d_out_status ? d_out_status + i : nullptr;
+        if (seg->n_blocks == 0) {
+            MRL_CUDA_TRY(ctx, cudaMemsetAsync(p.out_count, 0, sizeof(uint32_t), ctx->stream));
+            if (p.out_status) MRL_CUDA_TRY(ctx, cudaMemsetAsync(p.out_status, 0, sizeof(uint32_t), ctx->stream));
+            continue;
+        }
+        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+    }
+    return MRL_OK;
+}
+
+// mrl_scan_device with the scan scratch taken from g_static_scan_scratch instead of the context's
+// buffers: on success it allocates no device or host memory. It is for callers that must not
+// allocate while answering a query, such as a serving process that reserved its device memory at
+// start-up, where a cudaMalloc could stall other streams or fail under memory pressure mid-request.
+// Of the scratch, only the control words must be zero when a launch starts; every completed scan
+// leaves them zero, and each call also zeroes them (one 32-byte memset on the context stream) so a
+// call after a barrier timeout starts clean. Lists, flags and owner bytes are written before they
+// are read. The scratch is one per device per process, so two calls in flight on the same device
+// at once (different streams, contexts or threads) race on it; calls ordered on one stream do not.
+int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q0, uint32_t n_q,
+                           const mrl_scan_cfg* cfg, const uint32_t* time_lo, const uint32_t* time_hi,
+                           uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_counts,
+                           uint32_t* d_out_status) {
+    if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if ((uint64_t)q0 + n_q > plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan range out of bounds");
+    if (n_q && (!d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "output is NULL");
+    if (seg->n_blocks > MRL_STATIC_MAX_BLOCKS)
+        return fail(ctx, MRL_ERR_INVALID,
+                    "segment has " + std::to_string(seg->n_blocks) +
+                        " pages; mrl_scan_device_static's static scratch holds at most " +
+                        std::to_string(MRL_STATIC_MAX_BLOCKS) + " (use mrl_scan_device)");
+    if ((uint32_t)ctx->sms > MRL_STATIC_MAX_CTAS)
+        return fail(ctx, MRL_ERR_INVALID,
+                    "device has " + std::to_string(ctx->sms) + " SMs; mrl_scan_device_static's static scratch holds at most " +
+                        std::to_string(MRL_STATIC_MAX_CTAS) + " CTA lists (use mrl_scan_device)");
+    if (int rc = set_device(ctx)) return rc;
+    unsigned char* base = nullptr;
+    if (int rc = static_scratch(ctx, &base)) return rc;
+    MRL_CUDA_TRY(ctx, cudaMemsetAsync(base + kStaticCtlOff, 0, sizeof(unsigned) * mrl::kCtlWords, ctx->stream));
+    const uint32_t k = cfg->shortlist_cand;
+    for (uint32_t i = 0; i < n_q; ++i) {
+        mrl::ScanLaunch p = make_launch(ctx, seg, plans, q0 + i, cfg, time_lo, time_hi);
+        p.cta_keys = reinterpret_cast<unsigned long long*>(base + kStaticKeysOff);
+        p.ctl = reinterpret_cast<unsigned int*>(base + kStaticCtlOff);
+        p.cta_flags = base + kStaticFlagsOff;
+        p.owner = base + kStaticOwnerOff;
         p.out_ids = d_out_ids + (size_t)i * k;
         p.out_scores = d_out_scores + (size_t)i * k;
         p.out_count = d_out_counts + i;
