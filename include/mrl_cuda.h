@@ -172,6 +172,18 @@ int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pl
                            uint32_t n_q, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                            const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
                            uint32_t* d_out_counts, uint32_t* d_out_status);
+/* Exchange step of the sharded scan. An exchange record holds one rank's top list: `stride` u64
+ * ids, then `stride` f32 scores, then the u32 count of valid entries, padded to
+ * MRL_MERGE_RECORD_BYTES(stride) bytes (a multiple of 16). mrl_scan_device fills one when its
+ * d_out_ids / d_out_scores / d_out_counts point at the record's three parts (k == stride). Each
+ * rank all-gathers the records (one collective), then mrl_merge_topk merges the n_lists records at
+ * d_lists (device, contiguous) into the global top-k, ordered by score descending then id
+ * ascending, on the context stream. Replaces the merge of per-shard shortlists in
+ * scan_blocks_stats (src/scan.rs:866-870) across GPUs. n_lists in [1, 1024], stride and k in
+ * [1, 4096]; d_lists 16-byte aligned. */
+#define MRL_MERGE_RECORD_BYTES(stride) ((((size_t)(stride)) * 12u + 4u + 15u) & ~(size_t)15u)
+int mrl_merge_topk(mrl_ctx* ctx, const void* d_lists, uint32_t n_lists, uint32_t stride, uint32_t k,
+                   uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_count);
 /* Per-vector scores of plan `q` for every slot (n_blocks*64, host), and for MRL_MODE_FAST the
  * three int32 stage sums per slot (prefix, mid band, folded tail; may be NULL). Inactive slots
  * (tombstoned or temporally filtered) get score 0 and active 0. */

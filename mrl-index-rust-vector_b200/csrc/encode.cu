@@ -119,10 +119,6 @@ __device__ void eden_slice(const float* mean, const float* diag, int d, int bits
     *alpha = f_mul(cn, ss);  // EdenCode::alpha, src/eden.rs:219-221
 }
 
-struct CrcTab {
-    uint32_t t[256];
-};
-
 __device__ uint32_t crc32_bytes(const uint8_t* p, int n, const uint32_t* tab) {
     uint32_t c = 0xFFFFFFFFu;
     for (int i = 0; i < n; ++i) c = tab[(c ^ p[i]) & 0xFFu] ^ (c >> 8);

@@ -188,6 +188,8 @@ struct ScanLaunch {
 int scan_ctas(int device_sms);
 size_t scan_smem_bytes(uint32_t ctas, uint32_t k);
 int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream);
+int launch_merge_topk(const void* d_lists, uint32_t n_lists, uint32_t stride, uint32_t k, uint64_t* d_out_ids,
+                      float* d_out_scores, uint32_t* d_out_count, cudaStream_t stream);
 constexpr int kCtlWords = 8;
 int launch_debug_scores(const ScanLaunch& p, float* d_scores, uint8_t* d_active,
                         int32_t* d_partials, cudaStream_t stream);

@@ -4,10 +4,10 @@
 // live slot of a segment for one plan and leaves the top-k (by score, ties to the lower slot
 // ordinal) in the output buffers.
 //
-// Work split: a persistent grid of one 512-thread CTA per SM; warp w of CTA c scores pages
-// c + G*(w + 16*i) (G = grid size), two slots per lane, reading each slot's 64 bytes of the
-// vector-major page layout with four coalesced 16-byte loads per slot, prefetching the next page
-// while scoring the current one.
+// Work split: a persistent cooperative grid of one 512-thread CTA per SM. Warps take pages from a
+// global counter (one atomic per warp and page, fetched one page ahead) and score two slots per
+// lane, reading each slot's 64 bytes of the vector-major page layout with four coalesced 16-byte
+// loads per slot, prefetching the next page while scoring the current one.
 //
 // Scoring (one thread per slot):
 //   * MRL_MODE_FAST — every stage inner product is an exact int32 sum of table entries held in
@@ -26,11 +26,13 @@
 // Selection: each warp keeps a sorted top-32 of its keys in registers (one key per lane) and
 // filters new keys against max(its own list_len-th key, a CTA-wide bound in shared memory);
 // survivors go through a per-warp shared-memory queue and are merged 32 at a time with warp
-// bitonic networks. Each CTA then publishes its exact top-`list_len` to global scratch, and the
-// last CTA to finish (atomic ticket) selects the global top-k by radix select + bitonic sort. The
-// union of per-CTA lists provably contains the global top-k unless some CTA's full list ends
-// above the selected threshold; such CTAs are rescanned by the last CTA and the selection is
-// redone over the enlarged set, so the result is exact for every input (status bit 0 reports it).
+// bitonic networks. Each CTA tree-merges its warps' lists and publishes its exact top-`list_len`
+// to global scratch; after a bounded grid barrier every CTA ranks its own list keys against all
+// CTA lists (binary search) and writes the keys ranked below k straight to the output. The union
+// of per-CTA lists contains the global top-k unless some CTA's full list ends inside it; such
+// CTAs raise a flag, and the last CTA (atomic ticket) rescans their pages (owner[]) and redoes
+// the selection by radix select + bitonic sort, so the result is exact for every input (status
+// bit 0 reports it).
 #include "mrl_internal.cuh"
 
 namespace mrl {

@@ -30,5 +30,13 @@ from .api import (  # noqa: F401
     scored_hits_to_row_ids,
     vector_scores,
 )
+from .shard import (  # noqa: F401
+    ShardExchange,
+    merge_topk_host,
+    pack_records,
+    record_bytes,
+    shard_range,
+    unpack_records,
+)
 
 load()

@@ -1,0 +1,108 @@
+"""Sharded scan across ranks (one process per GPU).
+
+Pages shard naturally: each rank holds a contiguous range of a corpus's pages (its segment's
+`block_id_base` is the range start, so ids are global) and scans only its own HBM. The single
+exchange step is the merge of the per-rank top-k lists. It replaces the merge of per-shard
+shortlists at the end of `scan_blocks_stats` (src/scan.rs:866-870) at GPU granularity:
+  * on the device: each rank's scan writes its top-k into an exchange record; `ShardExchange`
+    all-gathers the records with torch.distributed (one NCCL collective over NVLink) and merges
+    them with the library's `mrl_merge_topk` kernel, so every rank ends with the global top-k;
+  * on the host: `merge_topk_host` merges lists that are already in host memory (for example the
+    outputs of `mrl_scan`) with the same order.
+Order everywhere: score descending, then id (VectorId::as_u64) ascending.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Tuple
+
+import numpy as np
+
+from ._capi import check
+
+
+def shard_range(n_pages: int, world: int, rank: int) -> Tuple[int, int]:
+    """(first page, page count) of `rank`'s contiguous share of `n_pages` (sizes differ by <= 1)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    base, rem = divmod(int(n_pages), world)
+    start = rank * base + min(rank, rem)
+    return start, base + (1 if rank < rem else 0)
+
+
+def merge_topk_host(ids: np.ndarray, scores: np.ndarray, counts: np.ndarray, k: int):
+    """Merge per-shard top lists (rows of `ids` [n_lists, stride] u64 / `scores` f32, `counts[i]`
+    valid entries each) into the global top-k: returns (ids[n], scores[n]) with n <= k."""
+    ids = np.asarray(ids, np.uint64).reshape(len(counts), -1)
+    scores = np.asarray(scores, np.float32).reshape(len(counts), -1)
+    stride = ids.shape[1]
+    take = [min(int(c), stride) for c in counts]
+    all_ids = np.concatenate([ids[i, :n] for i, n in enumerate(take)]) if take else np.zeros(0, np.uint64)
+    all_sc = np.concatenate([scores[i, :n] for i, n in enumerate(take)]) if take else np.zeros(0, np.float32)
+    order = np.lexsort((all_ids, -all_sc.astype(np.float64)))[:k]
+    return all_ids[order], all_sc[order]
+
+
+def record_bytes(stride: int) -> int:
+    """Size of one exchange record (MRL_MERGE_RECORD_BYTES): stride u64 ids, stride f32 scores,
+    the u32 count, padded to a multiple of 16 bytes."""
+    return (int(stride) * 12 + 4 + 15) // 16 * 16
+
+
+def pack_records(ids: np.ndarray, scores: np.ndarray, counts: np.ndarray) -> np.ndarray:
+    """Host copy of n exchange records (rows of `ids` [n, stride] / `scores`, `counts[i]` valid)."""
+    ids = np.asarray(ids, np.uint64)
+    n, stride = ids.shape
+    rb = record_bytes(stride)
+    out = np.zeros((n, rb), np.uint8)
+    out[:, : 8 * stride] = ids.view(np.uint8).reshape(n, -1)
+    out[:, 8 * stride: 12 * stride] = np.asarray(scores, np.float32).view(np.uint8).reshape(n, -1)
+    out[:, 12 * stride: 12 * stride + 4] = np.asarray(counts, np.uint32).reshape(n, 1).view(np.uint8)
+    return out
+
+
+def unpack_records(records: np.ndarray, stride: int):
+    """Inverse of pack_records: (ids [n, stride] u64, scores [n, stride] f32, counts [n] u32)."""
+    rec = np.ascontiguousarray(records, np.uint8).reshape(-1, record_bytes(stride))
+    ids = rec[:, : 8 * stride].copy().view(np.uint64)
+    scores = rec[:, 8 * stride: 12 * stride].copy().view(np.float32)
+    counts = rec[:, 12 * stride: 12 * stride + 4].copy().view(np.uint32).reshape(-1)
+    return ids, scores, counts
+
+
+class ShardExchange:
+    """Device-side exchange of per-rank top-k lists. The scan writes its output straight into this
+    rank's exchange record (`ids`, `scores`, `count` views); one all-gather of records (NCCL over
+    NVLink) and the merge kernel then leave the global top-k in `top_ids`, `top_scores`,
+    `top_count` on every rank. Buffers are allocated once (torch device tensors)."""
+
+    def __init__(self, dev, k: int, group=None):
+        import torch
+        import torch.distributed as dist
+
+        self.dev, self.k, self.group = dev, int(k), group
+        self.world = dist.get_world_size(group)
+        cuda = torch.device("cuda", torch.cuda.current_device())
+        rb = record_bytes(self.k)
+        self.record = torch.zeros(rb, dtype=torch.uint8, device=cuda)
+        self.gathered = torch.zeros(self.world * rb, dtype=torch.uint8, device=cuda)
+        k8, k12 = 8 * self.k, 12 * self.k
+        self.ids = self.record[:k8].view(torch.int64)
+        self.scores = self.record[k8:k12].view(torch.float32)
+        self.count = self.record[k12:k12 + 4].view(torch.int32)
+        self.top_ids = torch.empty(self.k, dtype=torch.int64, device=cuda)
+        self.top_scores = torch.empty(self.k, dtype=torch.float32, device=cuda)
+        self.top_count = torch.empty(1, dtype=torch.int32, device=cuda)
+
+    def __call__(self):
+        """All-gather the records and merge. The collective runs on torch's current stream, which
+        must be the context's stream so it orders after the scan and before the merge."""
+        import torch.distributed as dist
+
+        dist.all_gather_into_tensor(self.gathered, self.record, group=self.group)
+        lib = self.dev.lib
+        check(self.dev.ptr, lib.mrl_merge_topk(self.dev.ptr, C.c_void_p(self.gathered.data_ptr()), self.world,
+                                               self.k, self.k, C.c_void_p(self.top_ids.data_ptr()),
+                                               C.c_void_p(self.top_scores.data_ptr()),
+                                               C.c_void_p(self.top_count.data_ptr())))
+        return self.top_ids, self.top_scores, self.top_count
