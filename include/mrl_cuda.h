@@ -159,7 +159,7 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
  * Same arguments, results and errors as mrl_scan_device, but the scan scratch comes from a static
  * per-device region inside the library instead of the context, so a successful call allocates no
  * device or host memory: for callers that must not allocate while answering a query. Limits, set
- * by that region's fixed size (1,114,624 bytes): seg must hold at most MRL_STATIC_MAX_BLOCKS pages
+ * by that region's fixed size (1,114,368 bytes): seg must hold at most MRL_STATIC_MAX_BLOCKS pages
  * and the device at most MRL_STATIC_MAX_CTAS SMs, else MRL_ERR_INVALID with a message naming the
  * limit. The first call on a device looks the region up (and may load the module), so make it
  * before any stream capture begins. The region is shared by every context on a device: calls in
@@ -220,8 +220,8 @@ int mrl_synth_queries_device(mrl_ctx* ctx, uint64_t doc_seed, uint64_t n_docs, u
 /* Number of CTAs the scan kernel launches on this device and the per-CTA candidate list
  * length used for shortlist k. */
 int mrl_scan_geometry(mrl_ctx* ctx, uint32_t k, uint32_t* ctas, uint32_t* list_len);
-/* Override the per-CTA candidate list length (0 = automatic). Smaller values exercise the
- * exact re-selection path in tests. */
+/* Override the per-CTA candidate list length: 0 = automatic, else a power of two <= 32. Smaller
+ * values exercise the exact re-selection path in tests. */
 int mrl_set_list_len(mrl_ctx* ctx, uint32_t list_len);
 
 #ifdef __cplusplus

@@ -11,17 +11,17 @@
 #include "mrl_internal.cuh"
 
 // Scan scratch for mrl_scan_device_static, placed in the module's own global memory so that entry
-// point allocates nothing. Layout (bytes): control words [0, 256), per-CTA flags [256, 512),
-// per-CTA key lists [512, 512 + 256*32*8), one owner byte per page after that. Sized for grids of
-// at most MRL_STATIC_MAX_CTAS CTAs and segments of at most MRL_STATIC_MAX_BLOCKS pages: 1,114,624
-// bytes per device in all.
+// point allocates nothing. Layout (bytes): control words [0, 256), per-CTA key lists
+// [256, 256 + 256*32*8), one owner byte per page after that. Sized for grids of at most
+// MRL_STATIC_MAX_CTAS CTAs and segments of at most MRL_STATIC_MAX_BLOCKS pages: 1,114,368 bytes
+// per device in all.
 namespace {
 constexpr size_t kStaticCtlOff = 0;
-constexpr size_t kStaticFlagsOff = 256;
-constexpr size_t kStaticKeysOff = 512;
+constexpr size_t kStaticKeysOff = 256;
 constexpr size_t kStaticOwnerOff = kStaticKeysOff + (size_t)MRL_STATIC_MAX_CTAS * 32 * sizeof(unsigned long long);
 constexpr size_t kStaticBytes = kStaticOwnerOff + (size_t)MRL_STATIC_MAX_BLOCKS;
-static_assert(mrl::kCtlWords * sizeof(unsigned) <= kStaticFlagsOff - kStaticCtlOff, "control words overflow");
+static_assert(kStaticBytes == 1114368, "static scratch size is documented in the header");
+static_assert(mrl::kCtlWords * sizeof(unsigned) <= kStaticKeysOff - kStaticCtlOff, "control words overflow");
 static_assert(MRL_STATIC_MAX_CTAS <= 256, "owner bytes hold CTA indices < 256");
 }  // namespace
 static __device__ __align__(256) unsigned char g_static_scan_scratch[kStaticBytes];
@@ -32,10 +32,9 @@ struct mrl_ctx {
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
     std::string err;
-    // scan scratch: per-CTA lists, control words, per-CTA flags, per-page owner (grow-only)
+    // scan scratch: per-CTA lists, control words, per-page owner (grow-only)
     unsigned long long* cta_keys = nullptr;  // sms * 32
     unsigned int* ctl = nullptr;             // mrl::kCtlWords
-    uint8_t* cta_flags = nullptr;            // sms
     uint8_t* owner = nullptr;
     size_t owner_bytes = 0;
     uint32_t list_len_override = 0;
@@ -160,7 +159,6 @@ mrl::ScanLaunch make_launch(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
     p.hi = hi ? *hi : 0u;
     p.cta_keys = ctx->cta_keys;
     p.ctl = ctx->ctl;
-    p.cta_flags = ctx->cta_flags;
     p.owner = ctx->owner;
     return p;
 }
@@ -239,10 +237,8 @@ int mrl_ctx_create(int device, mrl_ctx** out) {
     ctx->stream = ctx->own_stream;
     if (cudaMalloc(&ctx->cta_keys, sizeof(unsigned long long) * 32 * (size_t)ctx->sms) != cudaSuccess ||
         cudaMalloc(&ctx->ctl, sizeof(unsigned int) * mrl::kCtlWords) != cudaSuccess ||
-        cudaMalloc(&ctx->cta_flags, (size_t)ctx->sms) != cudaSuccess ||
         cudaMalloc(&ctx->d_means, 192 * sizeof(float)) != cudaSuccess ||
         cudaMemset(ctx->ctl, 0, sizeof(unsigned int) * mrl::kCtlWords) != cudaSuccess ||
-        cudaMemset(ctx->cta_flags, 0, (size_t)ctx->sms) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) {
         mrl_ctx_destroy(ctx);
         return MRL_ERR_NOMEM;
@@ -257,7 +253,6 @@ void mrl_ctx_destroy(mrl_ctx* ctx) {
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->cta_keys);
     cudaFree(ctx->ctl);
-    cudaFree(ctx->cta_flags);
     cudaFree(ctx->owner);
     cudaFree(ctx->tmp);
     cudaFree(ctx->tmp_out);
@@ -515,7 +510,6 @@ int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pl
         mrl::ScanLaunch p = make_launch(ctx, seg, plans, q0 + i, cfg, time_lo, time_hi);
         p.cta_keys = reinterpret_cast<unsigned long long*>(base + kStaticKeysOff);
         p.ctl = reinterpret_cast<unsigned int*>(base + kStaticCtlOff);
-        p.cta_flags = base + kStaticFlagsOff;
         p.owner = base + kStaticOwnerOff;
         p.out_ids = d_out_ids + (size_t)i * k;
         p.out_scores = d_out_scores + (size_t)i * k;
@@ -699,7 +693,8 @@ int mrl_scan_geometry(mrl_ctx* ctx, uint32_t k, uint32_t* ctas, uint32_t* list_l
 
 int mrl_set_list_len(mrl_ctx* ctx, uint32_t list_len) {
     if (!ctx) return MRL_ERR_INVALID;
-    if (list_len > 32) return fail(ctx, MRL_ERR_INVALID, "list_len must be <= 32");
+    if (list_len > 32 || (list_len & (list_len - 1)))
+        return fail(ctx, MRL_ERR_INVALID, "list_len must be 0 (auto) or a power of two <= 32");
     ctx->list_len_override = list_len;
     return MRL_OK;
 }

@@ -177,8 +177,7 @@ struct ScanLaunch {
     // scratch (owned by the context; zero-initialised once, left zeroed by every launch)
     unsigned long long* cta_keys;  // ctas * 32: each CTA's exact top-list_len keys
     unsigned int* ctl;             // [0] page counter, [1] barrier count, [2] barrier generation,
-                                   // [3] ticket, [4] any-CTA-flagged, [5] barrier timeout
-    uint8_t* cta_flags;            // ctas: CTA may have dropped a top-k key
+                                   // [5] barrier timeout; the others are reserved
     uint8_t* owner;                // n_blocks: CTA that scored each page
     uint64_t* out_ids;
     float* out_scores;

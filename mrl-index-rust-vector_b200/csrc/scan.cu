@@ -457,20 +457,19 @@ __device__ u64 select_threshold(const Finisher<MODE>& F, unsigned k, unsigned* h
     return st->prefix;
 }
 
-// Rare path, last CTA only: some CTA's exact list ended inside the top-k, so it may have dropped
-// members. Reselect over the union of lists plus those CTAs' rescanned keys and rewrite the output.
+// Rare path, one CTA: some CTA lists (`flags`, `nflag` of them) ended inside the top-k, so they may
+// have dropped members. Reselect over the union of lists plus those CTAs' rescanned keys and write
+// the whole output.
 template <int MODE>
 __device__ void reselect(const ScanLaunch& p, const int* tab, const float2* rho_tab, const Scalars& S, u64* cand,
-                         u64* gath, unsigned* hist, unsigned* flags, SelState* st, unsigned* s_misc) {
+                         u64* gath, unsigned* hist, const unsigned* flags, unsigned nflag, SelState* st,
+                         unsigned* s_misc) {
     const int tid = threadIdx.x;
     const unsigned G = gridDim.x;
     for (unsigned i = tid; i < G * 32; i += kThreads) cand[i] = __ldcg(p.cta_keys + i);
-    if (tid == 0) { s_misc[0] = 0; s_misc[1] = 0; }
+    if (tid == 0) s_misc[1] = 0;
     __syncthreads();
-    for (unsigned c = tid; c < G; c += kThreads)
-        if (__ldcg(p.cta_flags + c)) flags[atomicAdd(&s_misc[0], 1u)] = c;
-    __syncthreads();
-    Finisher<MODE> F{p, tab, rho_tab, S, cand, flags, s_misc[0], G, p.list_len};
+    Finisher<MODE> F{p, tab, rho_tab, S, cand, flags, nflag, G, p.list_len};
     const u64 tau = select_threshold<MODE>(F, p.k, hist, st);
     F.visit([&](bool valid, u64 x, int ln) {
         const bool in = valid && x >= tau;
@@ -529,7 +528,7 @@ __device__ bool grid_barrier(unsigned* ctl, unsigned G, volatile int* s_ok) {
                 asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(gen) : "memory");
                 if (g != my_gen) break;
                 if (++it > (1u << 22)) { ok = 0; atomicExch(ctl + 5, 1u); break; }  // ~0.3 s
-                __nanosleep(64);
+                if (it > 256) __nanosleep(64);
             }
         }
         *s_ok = ok;
@@ -545,7 +544,8 @@ __device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int m
         for (int i = tid; i < kPrefix * 16; i += kThreads) tab[i] = P->lut_prefix[i];
         for (int i = tid; i < kS1Windows * 32; i += kThreads) tab[kTabS1 + i] = P->lut_s1[i];
         for (int i = tid; i < kS4Windows * 32; i += kThreads) tab[kTabS4 + i] = P->lut_s4[i];
-        for (int i = tid; i < kPrefix * 16; i += kThreads) tab[kTabL0 + i] = P->lut_l0[i];
+        if (p.depth == MRL_DEPTH_L0)
+            for (int i = tid; i < kPrefix * 16; i += kThreads) tab[kTabL0 + i] = P->lut_l0[i];
     } else {
         float* ft = reinterpret_cast<float*>(tab);
         for (int i = tid; i < kPrefix * 16; i += kThreads) ft[i] = P->fp_prefix[i];
@@ -584,13 +584,33 @@ __device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int m
     S.one = (int32_t)(p.list_len != 0u);  // 1 for every launch; opaque to the compiler
 }
 
-// Pages are handed out dynamically (one atomic per warp and page, fetched one page ahead) so every
-// warp finishes at about the same time; owner[] records which CTA scored each page for the rare
-// rescan.
-__device__ __forceinline__ uint32_t grab_page(unsigned* counter, int lane) {
+// Page schedule: each warp's first two pages are static (pages gw and gw + W for global warp gw of
+// W), so the launch starts without contending on one atomic; later pages are handed out
+// dynamically from `base` on (one atomic per warp and page, fetched one page ahead) so every warp
+// finishes at about the same time. owner[] records which CTA scored each page for the rare rescan.
+__device__ __forceinline__ uint32_t grab_page(unsigned* counter, int lane, uint32_t base) {
     uint32_t b = 0;
     if (lane == 0) b = atomicAdd(counter, 1u);
-    return __shfl_sync(kFull, b, 0);
+    return __shfl_sync(kFull, b, 0) + base;
+}
+
+// Number of keys greater than x in lst[0..n), 1 <= n <= 32, sorted descending (keys unique, empty
+// slots 0 at the end): a branch-free binary lift of six fixed steps (clamped loads, selects), so
+// independent calls overlap.
+__device__ __forceinline__ unsigned count_greater(const u64* lst, unsigned n, u64 x) {
+    unsigned lo = 0;
+#pragma unroll
+    for (int s = 5; s >= 0; --s) {
+        const unsigned t = lo + (1u << s);
+        const u64 v = lst[min(t, n) - 1];
+        lo = (t <= n && v > x) ? t : lo;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ u64 shfl_xor_u64(u64 v, int o) {
+    const unsigned lo = __shfl_xor_sync(kFull, (unsigned)v, o), hi = __shfl_xor_sync(kFull, (unsigned)(v >> 32), o);
+    return ((u64)hi << 32) | lo;
 }
 
 template <int MODE>
@@ -599,18 +619,19 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     __shared__ float2 s_rho[256];
     __shared__ u64 s_cta_tau;
     __shared__ unsigned s_seed_min, s_seed_cnt;
-    __shared__ unsigned s_rank[32];
-    __shared__ unsigned s_total;
-    __shared__ unsigned s_last;
+    __shared__ unsigned s_part[kWarps * 32];
+    __shared__ u64 s_red64[kWarps];
+    __shared__ unsigned s_red32[kWarps];
+    __shared__ unsigned s_nflag;
     __shared__ int s_ok;
     __shared__ SelState s_sel;
     __shared__ unsigned s_misc[4];
     extern __shared__ __align__(16) unsigned char s_dyn[];
     u64* s_queue = reinterpret_cast<u64*>(s_dyn);  // kWarps * kQueue
     u64* s_lists = s_queue + kWarps * kQueue;       // kWarps * 32
-    u64* s_cand = s_lists + kWarps * 32;            // G * 32
+    u64* s_cand = s_lists + kWarps * 32;            // G * 33
     const unsigned G = gridDim.x;
-    u64* s_gath = s_cand + G * 32;                  // pow2 >= k
+    u64* s_gath = s_cand + G * 33;                  // pow2 >= k
     unsigned P2 = 1;
     while (P2 < p.k) P2 <<= 1;
     unsigned* s_hist = reinterpret_cast<unsigned*>(s_gath + P2);  // kBins
@@ -621,14 +642,13 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     unsigned* counter = p.ctl;
 
     // first page in flight before the tables are read
-    uint32_t b = grab_page(counter, lane);
+    const uint32_t W = G * kWarps, gw = (uint32_t)warp * G + blockIdx.x, dyn0 = 2 * W;
+    uint32_t b = gw, bn = gw + W;
     Slot4 a0, a1;
     if (b < p.n_blocks) { load_slot(p.pages, b, lane, a0); load_slot(p.pages, b, lane + 32, a1); }
-    uint32_t bn = grab_page(counter, lane);
 
     Scalars S;
-    if (tid == 0) { s_cta_tau = 0ull; s_seed_min = 0xFFFFFFFFu; s_seed_cnt = 0u; s_total = 0u; }
-    if (tid < 32) s_rank[tid] = 0u;
+    if (tid == 0) { s_cta_tau = 0ull; s_seed_min = 0xFFFFFFFFu; s_seed_cnt = 0u; s_nflag = 0u; }
     load_tables(p.plan, MODE, s_tab, s_rho, S, p);
     __syncthreads();
 
@@ -638,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     while (b < p.n_blocks) {
         Slot4 n0, n1;
         if (bn < p.n_blocks) { load_slot(p.pages, bn, lane, n0); load_slot(p.pages, bn, lane + 32, n1); }
-        const uint32_t bnn = bn < p.n_blocks ? grab_page(counter, lane) : bn;
+        const uint32_t bnn = bn < p.n_blocks ? grab_page(counter, lane, dyn0) : bn;
         u64 k0 = 0ull, k1 = 0ull;
         if (block_live(p, b)) {
             k0 = slot_key<MODE>(a0, b * 64 + lane, s_tab, s_rho, S);
@@ -689,66 +709,102 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     }
     if (blockIdx.x == 0 && tid == 0) atomicExch(counter, 0u);  // page counter ready for the next launch
 
-    // Global rank of each of this CTA's list keys: the number of larger keys in all CTA lists
-    // (lists are sorted, keys unique). Keys ranked below k are the top-k, written in place.
-    for (unsigned i = tid; i < G * L; i += kThreads) s_cand[i] = __ldcg(p.cta_keys + (i / L) * 32 + (i % L));
+    // Every CTA's list into shared memory, rows LP = L | 1 keys apart (an odd stride: threads that
+    // each read a different list hit different banks).
+    const unsigned LP = L | 1u;
+    for (unsigned c = warp; c < G; c += kWarps)
+        if ((unsigned)lane < L) s_cand[c * LP + lane] = __ldcg(p.cta_keys + c * 32 + lane);
     __syncthreads();
-    const u64* mine = s_cand + blockIdx.x * L;
+
+    // A CTA list may have dropped a top-k key only if it is full and its last key ranks below k.
+    // Ranks fall as keys grow, so ranking the largest last key of a full list (x_max) decides for
+    // all lists: rank(x_max) >= k clears every one. Each CTA computes this from the same lists, so
+    // all reach the same decision without further communication.
+    u64 last = 0ull;
+    unsigned live = 0;
+    if ((unsigned)tid < G) {
+        last = s_cand[tid * LP + L - 1];
+        live = count_greater(s_cand + tid * LP, L, 0ull);
+    }
     {
-        const unsigned ki = tid % L;           // key of mine handled by this thread
-        const unsigned cstep = kThreads / L;   // lists visited per pass
-        const u64 x = mine[ki];
-        unsigned cnt = 0, nz = 0;
-        for (unsigned c = tid / L; c < G; c += cstep) {
-            const u64* lst = s_cand + c * L;
-            unsigned lo = 0, hi = L;  // entries > x form a prefix of the descending list
-            while (lo < hi) {
-                const unsigned mid = (lo + hi) >> 1;
-                if (lst[mid] > x) lo = mid + 1; else hi = mid;
+        u64 m = last;
+        unsigned t = live;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const u64 y = shfl_xor_u64(m, o);
+            m = y > m ? y : m;
+            t += __shfl_xor_sync(kFull, t, o);
+        }
+        if (lane == 0) { s_red64[warp] = m; s_red32[warp] = t; }
+    }
+    __syncthreads();
+    u64 x_max = 0ull;
+    unsigned total = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+        x_max = s_red64[w] > x_max ? s_red64[w] : x_max;
+        total += s_red32[w];
+    }
+    // rank of x_max (threads c < G, list c) and of this CTA's own keys: lane l of warp w handles key
+    // l % L against the lists of group g = w * (32 / L) + l / L (lists g, g + NG, ...), partial
+    // counts reduced through shared memory
+    unsigned rx = ((unsigned)tid < G && x_max != 0ull) ? count_greater(s_cand + tid * LP, L, x_max) : 0u;
+    const u64* mine = s_cand + blockIdx.x * LP;
+    const unsigned per_warp = 32u / L, NG = kWarps * per_warp;
+    const unsigned ki = (unsigned)lane % L, gi = (unsigned)lane / L;
+    const u64 x = gi < per_warp ? mine[ki] : 0ull;
+    unsigned cnt = 0;
+    if (x != 0ull) {
+#pragma unroll 4
+        for (unsigned c = warp * per_warp + gi; c < G; c += NG) cnt += count_greater(s_cand + c * LP, L, x);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) rx += __shfl_xor_sync(kFull, rx, o);
+    // list_len is a power of two: fold the warp's key groups onto lanes 0 .. L-1
+    for (unsigned o = 16; o >= L; o >>= 1) cnt += __shfl_down_sync(kFull, cnt, o);
+    s_part[warp * 32 + lane] = cnt;
+    __syncthreads();  // every thread has read s_red32 above
+    if (lane == 0) s_red32[warp] = rx;
+    __syncthreads();
+    unsigned rank_xmax = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) rank_xmax += s_red32[w];
+    const bool clean = x_max == 0ull || rank_xmax >= p.k;
+
+    if (clean) {
+        // keys ranked below k are the top-k: each CTA writes its own in place
+        if ((unsigned)tid < L) {
+            const u64 key = mine[tid];
+            unsigned r = 0;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) r += s_part[w * 32 + tid];
+            if (key != 0ull && r < p.k) {
+                const uint32_t ord = key_ordinal(key);
+                p.out_ids[r] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
+                p.out_scores[r] = key_score(key);
             }
-            cnt += lo;
-            if (ki == 0) {  // one thread per list counts its live entries
-                unsigned l2 = 0, h2 = L;
-                while (l2 < h2) {
-                    const unsigned mid = (l2 + h2) >> 1;
-                    if (lst[mid] != 0ull) l2 = mid + 1; else h2 = mid;
-                }
-                nz += l2;
-            }
         }
-        if (x != 0ull) atomicAdd(&s_rank[ki], cnt);
-        if (ki == 0 && nz) atomicAdd(&s_total, nz);
+        if (blockIdx.x == 0 && tid == 0) {
+            *p.out_count = min(total, p.k);
+            if (p.out_status) *p.out_status = 0u;
+        }
+        return;
+    }
+    // Rare path: CTA 0 alone finds the flagged lists (full, last key ranked below k), reselects over
+    // the lists plus those CTAs' rescanned pages, and writes the whole output.
+    if (blockIdx.x != 0) return;
+    for (unsigned c = warp; c < G; c += kWarps) {
+        const u64 lc = s_cand[c * LP + L - 1];
+        if (lc == 0ull) continue;  // warp-uniform: list not full
+        unsigned r = 0;
+        for (unsigned j = lane; j < G; j += 32) r += count_greater(s_cand + j * LP, L, lc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(kFull, r, o);
+        if (lane == 0 && r < p.k) s_flags[atomicAdd(&s_nflag, 1u)] = c;
     }
     __syncthreads();
-    if (tid < L) {
-        const u64 x = mine[tid];
-        const unsigned r = s_rank[tid];
-        if (x != 0ull && r < p.k) {
-            const uint32_t ord = key_ordinal(x);
-            p.out_ids[r] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
-            p.out_scores[r] = key_score(x);
-        }
-        // A full list whose last key ranks inside the top-k may have dropped top-k keys.
-        if (tid == L - 1) {
-            const bool flagged = x != 0ull && r < p.k;
-            p.cta_flags[blockIdx.x] = flagged ? 1u : 0u;
-            if (flagged) atomicExch(p.ctl + 4, 1u);
-        }
-    }
-    if (blockIdx.x == 0 && tid == 0) *p.out_count = min(s_total, p.k);
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(p.ctl + 3, 1u) == G - 1) ? 1u : 0u;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const bool any = __ldcg(p.ctl + 4) != 0u;
-    if (any) reselect<MODE>(p, s_tab, s_rho, S, s_cand, s_gath, s_hist, s_flags, &s_sel, s_misc);
-    if (tid == 0) {
-        if (p.out_status) *p.out_status = any ? 1u : 0u;
-        p.ctl[3] = 0u;
-        p.ctl[4] = 0u;
-    }
+    reselect<MODE>(p, s_tab, s_rho, S, s_cand, s_gath, s_hist, s_flags, s_nflag, &s_sel, s_misc);
+    if (tid == 0 && p.out_status) *p.out_status = 1u;
 }
 
 template <int MODE>
@@ -785,7 +841,7 @@ int scan_ctas(int device_sms) { return device_sms; }
 size_t scan_smem_bytes(uint32_t ctas, uint32_t k) {
     size_t p2 = 1;
     while (p2 < k) p2 <<= 1;
-    return sizeof(u64) * (kWarps * kQueue + kWarps * 32 + (size_t)ctas * 32 + p2) + sizeof(unsigned) * (kBins + ctas);
+    return sizeof(u64) * (kWarps * kQueue + kWarps * 32 + (size_t)ctas * 33 + p2) + sizeof(unsigned) * (kBins + ctas);
 }
 
 // Cooperative launch: one CTA per SM, all co-resident (the grid barrier relies on it).
