@@ -199,23 +199,36 @@ def run_ours(args):
     qbytes = dims * 4
 
     def one_step(i, ev, do_flush=True):
+        """One query: plan build + scan + top-256 in one fused launch (mrl_query_scan_device), then
+        on N > 1 the exchange. Events: step start, [after the scan when N > 1], step end."""
         if do_flush:
             flush.add_(1.0)  # reads and writes 512 MiB: evicts the corpus from L2
         ev[0].record()
+        M._capi.check(dev.ptr, lib.mrl_query_scan_device(dev.ptr, seg.ptr, C.c_void_p(qd.data_ptr() + i * qbytes), 1,
+                                                         dims, C.byref(desc), plans, C.byref(cfg), None, None,
+                                                         C.c_void_p(out_ids.data_ptr()), C.c_void_p(out_sc.data_ptr()),
+                                                         C.c_void_p(out_cnt.data_ptr()),
+                                                         C.c_void_p(out_st.data_ptr() + 4 * i)))
+        if exch is not None:
+            ev[2].record()
+            exch()  # global top-k on every rank
+        ev[1].record()
+
+    def split_step(i, ev):
+        """The same query with the plan kernel and the scan kernel launched separately (for the
+        per-kernel breakdown; not part of the timed steps)."""
+        flush.add_(1.0)
+        ev[0].record()
         M._capi.check(dev.ptr, lib.mrl_plan_build_device(dev.ptr, C.c_void_p(qd.data_ptr() + i * qbytes), 1, dims,
                                                          C.byref(desc), plans))
-        ev[1].record()
+        ev[2].record()
         M._capi.check(dev.ptr, lib.mrl_scan_device(dev.ptr, seg.ptr, plans, 0, 1, C.byref(cfg), None, None,
                                                    C.c_void_p(out_ids.data_ptr()), C.c_void_p(out_sc.data_ptr()),
-                                                   C.c_void_p(out_cnt.data_ptr()),
-                                                   C.c_void_p(out_st.data_ptr() + 4 * i)))
-        ev[2].record()
-        if exch is not None:
-            exch()  # global top-k on every rank
-        ev[3].record()
+                                                   C.c_void_p(out_cnt.data_ptr()), None))
+        ev[1].record()
 
     def mk():
-        return [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        return [torch.cuda.Event(enable_timing=True) for _ in range(3)]
 
     for i in range(warm):
         one_step(i, mk())
@@ -236,15 +249,20 @@ def run_ours(args):
         dist.barrier()
     time.sleep(0.2)
     clk = clocks.stop()
-    # the same steps without the L2 flush (corpus resident in the 126 MB L2), for information
+    # for information: the same steps without the L2 flush (corpus resident in the 126 MB L2), and
+    # the plan and scan kernels launched separately
     evr = [mk() for _ in range(min(200, args.steps))]
     for i in range(len(evr)):
         one_step(warm + i, evr[i], do_flush=False)
+    evs2 = [mk() for _ in range(min(200, args.steps))]
+    for i in range(len(evs2)):
+        split_step(warm + i, evs2[i])
     torch.cuda.synchronize()
-    scan_l2_ms = np.array([e[1].elapsed_time(e[2]) for e in evr])
-    step_ms = np.array([e[0].elapsed_time(e[3]) for e in evs])
-    plan_ms = np.array([e[0].elapsed_time(e[1]) for e in evs])
-    scan_ms = np.array([e[1].elapsed_time(e[2]) for e in evs])
+    step_l2_ms = np.array([e[0].elapsed_time(e[2] if world > 1 else e[1]) for e in evr])
+    split_plan_ms = np.array([e[0].elapsed_time(e[2]) for e in evs2])
+    split_scan_ms = np.array([e[2].elapsed_time(e[1]) for e in evs2])
+    step_ms = np.array([e[0].elapsed_time(e[1]) for e in evs])
+    scan_ms = np.array([e[0].elapsed_time(e[2] if world > 1 else e[1]) for e in evs])  # the fused kernel
     total_ms = float(step_ms.sum())
     if world > 1:
         t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
@@ -267,16 +285,15 @@ def run_ours(args):
             flush.add_(1.0)
             torch.cuda.synchronize()
             s = time.perf_counter()
-            M._capi.check(dev.ptr, lib.mrl_plan_rebuild(dev.ptr, C.c_void_p(qh.data_ptr() + (i % n_q) * qbytes), 1,
-                                                        dims, C.byref(desc), plans))
-            M._capi.check(dev.ptr, lib.mrl_scan(dev.ptr, seg.ptr, plans, C.byref(cfg), None, None,
-                                                C.c_void_p(ids_h.data_ptr()), C.c_void_p(sc_h.data_ptr()),
-                                                C.c_void_p(cnt_h.data_ptr())))
+            M._capi.check(dev.ptr, lib.mrl_query_scan(dev.ptr, seg.ptr, C.c_void_p(qh.data_ptr() + (i % n_q) * qbytes),
+                                                      1, dims, C.byref(desc), plans, C.byref(cfg), None, None,
+                                                      C.c_void_p(ids_h.data_ptr()), C.c_void_p(sc_h.data_ptr()),
+                                                      C.c_void_p(cnt_h.data_ptr())))
             if i >= warm:
                 tot += time.perf_counter() - s
         e2e = {"value": e2e_steps / tot, "unit": "QPS", "h2d_bytes_per_step": qbytes,
                "d2h_bytes_per_step": k * 12 + 4, "steps": e2e_steps,
-               "path": "mrl_plan_rebuild + mrl_scan (host pinned buffers, synchronous)"}
+               "path": "mrl_query_scan: host query in, fused plan + scan launch, host top-256 out (pinned, synchronous)"}
         dev.set_stream(torch_stream)
     else:
         # every rank: host query -> plan -> local scan -> NCCL all-gather + merge kernel -> host result
@@ -285,6 +302,7 @@ def run_ours(args):
         ids_h = torch.empty(k, dtype=torch.int64, pin_memory=True)
         sc_h = torch.empty(k, dtype=torch.float32, pin_memory=True)
         cnt_h = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        q_dev = torch.empty(dims, dtype=torch.float32, device="cuda")
         stream = torch.cuda.current_stream()
         e2e_steps = min(args.e2e_steps, n_q)
         tot = 0.0
@@ -293,11 +311,12 @@ def run_ours(args):
             torch.cuda.synchronize()
             dist.barrier()
             s = time.perf_counter()
-            M._capi.check(dev.ptr, lib.mrl_plan_rebuild(dev.ptr, C.c_void_p(qh.data_ptr() + (i % n_q) * qbytes), 1,
-                                                        dims, C.byref(desc), plans))
-            M._capi.check(dev.ptr, lib.mrl_scan_device(dev.ptr, seg.ptr, plans, 0, 1, C.byref(cfg), None, None,
-                                                       C.c_void_p(out_ids.data_ptr()), C.c_void_p(out_sc.data_ptr()),
-                                                       C.c_void_p(out_cnt.data_ptr()), None))
+            q_dev.copy_(qh[i % n_q], non_blocking=True)
+            M._capi.check(dev.ptr, lib.mrl_query_scan_device(dev.ptr, seg.ptr, C.c_void_p(q_dev.data_ptr()), 1, dims,
+                                                             C.byref(desc), plans, C.byref(cfg), None, None,
+                                                             C.c_void_p(out_ids.data_ptr()),
+                                                             C.c_void_p(out_sc.data_ptr()),
+                                                             C.c_void_p(out_cnt.data_ptr()), None))
             g_ids, g_sc, g_cnt = exch()
             ids_h.copy_(g_ids, non_blocking=True)
             sc_h.copy_(g_sc, non_blocking=True)
@@ -309,8 +328,9 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e = {"value": world * e2e_steps / float(t.item()), "unit": "QPS", "h2d_bytes_per_step": qbytes,
                "d2h_bytes_per_step": k * 12 + 4, "steps": e2e_steps,
-               "path": "per rank: mrl_plan_rebuild + mrl_scan_device + NCCL all-gather + mrl_merge_topk + "
-                       "copy of the merged top-k to pinned host memory; max over ranks"}
+               "path": "per rank: query copy from pinned host memory + mrl_query_scan_device (fused plan + scan) + "
+                       "NCCL all-gather + mrl_merge_topk + copy of the merged top-k to pinned host memory; max "
+                       "over ranks"}
 
     peak, peak_kind = measured_peaks()
     alg_bytes = nb * 4096
@@ -332,15 +352,17 @@ def run_ours(args):
                                    " query over world x 1M docs, merged to a global top-256 by NCCL all-gather +"
                                    " mrl_merge_topk)",
                    "l2": "flushed before every step (read+write of a 512 MiB buffer, outside the per-step events)",
-                   "wall_s_bracketed": t1 - t0, "plan_ms_mean": float(plan_ms.mean()),
+                   "wall_s_bracketed": t1 - t0,
+                   "step_kernels": "one fused launch per query (plan build in every CTA + scan + top-256)",
                    "scan_ms_mean": float(scan_ms.mean()), "scan_ms_p50": float(np.median(scan_ms)),
                    "scan_ms_p99": float(np.percentile(scan_ms, 99)), "reselection_steps": n_fallback,
-                   "scan_ms_mean_l2_resident": float(scan_l2_ms.mean())},
+                   "scan_ms_mean_l2_resident": float(step_l2_ms.mean()),
+                   "separate_launches_ms": {"plan": float(split_plan_ms.mean()), "scan": float(split_scan_ms.mean())}},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "traffic": profiled_traffic(args.mode),
                      "kernel": "scan_kernel", "alg_bytes_per_launch": alg_bytes},
         "clocks": clk,
-        "gpu_launches": (2 if world == 1 else 3) * args.steps,
+        "gpu_launches": (1 if world == 1 else 2) * args.steps,
         "e2e": e2e,
     }
     if world == 1 and not args.no_cpu_baseline:

@@ -172,6 +172,21 @@ int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pl
                            uint32_t n_q, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                            const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
                            uint32_t* d_out_counts, uint32_t* d_out_status);
+/* ---- fused plan + scan: QueryPipeline::build_plan + scan_segments_into (src/pipeline.rs:63-133) -- */
+/* Build the plans of n_q device queries (row-major n_q x dims f32) into `plans` [0, n_q) and scan
+ * the segment with each, in one launch per query: every CTA builds the query's plan in shared
+ * memory while its first pages load, so no separate plan launch precedes the scan. Results and
+ * status as mrl_scan_device; asynchronous on the context stream. */
+int mrl_query_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const float* d_queries, uint32_t n_q,
+                          uint32_t dims, const mrl_codec_desc* codec, mrl_plans* plans,
+                          const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+                          const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
+                          uint32_t* d_out_counts, uint32_t* d_out_status);
+/* The same from host queries to host results (synchronous): copy in, fused launches, copy out. */
+int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint32_t n_q, uint32_t dims,
+                   const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg,
+                   const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* out_ids,
+                   float* out_scores, uint32_t* out_counts);
 /* Exchange step of the sharded scan. An exchange record holds one rank's top list: `stride` u64
  * ids, then `stride` f32 scores, then the u32 count of valid entries, padded to
  * MRL_MERGE_RECORD_BYTES(stride) bytes (a multiple of 16). mrl_scan_device fills one when its

@@ -525,6 +525,85 @@ int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pl
     return MRL_OK;
 }
 
+int mrl_query_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const float* d_queries, uint32_t n_q, uint32_t dims,
+                          const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg,
+                          const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
+                          uint32_t* d_out_counts, uint32_t* d_out_status) {
+    if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (int rc = check_codec(ctx, codec)) return rc;
+    if (n_q > plans->n_q || dims != plans->dims) return fail(ctx, MRL_ERR_INVALID, "plan storage too small or dims mismatch");
+    if (n_q && (!d_queries || !d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
+    if (n_q == 0) return MRL_OK;
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = ensure_buf(ctx, (void**)&ctx->owner, &ctx->owner_bytes, seg->n_blocks ? seg->n_blocks : 1)) return rc;
+    float* d_means = nullptr;
+    if (int rc = upload_means(ctx, codec, &d_means)) return rc;
+    const float* d_mid = codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr;
+    const uint32_t k = cfg->shortlist_cand;
+    for (uint32_t i = 0; i < n_q; ++i) {
+        mrl::ScanLaunch p = make_launch(ctx, seg, plans, i, cfg, time_lo, time_hi);
+        p.out_ids = d_out_ids + (size_t)i * k;
+        p.out_scores = d_out_scores + (size_t)i * k;
+        p.out_count = d_out_counts + i;
+        p.out_status = d_out_status ? d_out_status + i : nullptr;
+        if (seg->n_blocks == 0) {  // nothing to scan: build the plan alone
+            if (mrl::launch_plan_build(d_queries + (size_t)i * dims, 1, dims, codec->prefix_codec, codec->mid_codec,
+                                       d_means, codec->eden_seed, d_mid, codec->mid_seed, plans->d + i, ctx->stream))
+                return cuda_fail(ctx, cudaGetLastError(), "plan launch");
+            MRL_CUDA_TRY(ctx, cudaMemsetAsync(p.out_count, 0, sizeof(uint32_t), ctx->stream));
+            if (p.out_status) MRL_CUDA_TRY(ctx, cudaMemsetAsync(p.out_status, 0, sizeof(uint32_t), ctx->stream));
+            continue;
+        }
+        p.query = d_queries + (size_t)i * dims;
+        p.dims = dims;
+        p.prefix_codec = codec->prefix_codec;
+        p.mid_codec = codec->mid_codec;
+        p.eden_mean = d_means;
+        p.eden_seed = codec->eden_seed;
+        p.mid_mean = d_mid;
+        p.mid_seed = codec->mid_seed;
+        p.plan_out = plans->d + i;
+        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+    }
+    return MRL_OK;
+}
+
+int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint32_t n_q, uint32_t dims,
+                   const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+                   const uint32_t* time_hi, uint64_t* out_ids, float* out_scores, uint32_t* out_counts) {
+    if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (n_q == 0) return MRL_OK;
+    if (!queries || !out_ids || !out_scores || !out_counts) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
+    for (uint64_t i = 0; i < (uint64_t)n_q * dims; ++i)
+        if (!std::isfinite(queries[i])) return fail(ctx, MRL_ERR_INVALID, "query contains a non-finite value");
+    if (int rc = set_device(ctx)) return rc;
+    const size_t qbytes = (size_t)n_q * dims * sizeof(float);
+    const size_t nk = (size_t)n_q * cfg->shortlist_cand;
+    if (int rc = ensure_tmp(ctx, qbytes)) return rc;
+    if (int rc = ensure_out(ctx, nk * (sizeof(uint64_t) + sizeof(float)) + 2 * sizeof(uint32_t) * n_q + 64)) return rc;
+    float* d_q = (float*)ctx->tmp;
+    uint64_t* d_ids = (uint64_t*)ctx->tmp_out;
+    float* d_sc = (float*)(d_ids + nk);
+    uint32_t* d_cnt = (uint32_t*)(d_sc + nk);
+    uint32_t* d_st = d_cnt + n_q;
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(d_q, queries, qbytes, cudaMemcpyHostToDevice, ctx->stream));
+    if (int rc = mrl_query_scan_device(ctx, seg, d_q, n_q, dims, codec, plans, cfg, time_lo, time_hi, d_ids, d_sc, d_cnt,
+                                       d_st))
+        return rc;
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_ids, d_ids, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_scores, d_sc, nk * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    std::vector<uint32_t> cs(2 * (size_t)n_q);
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(cs.data(), d_cnt, 2 * sizeof(uint32_t) * n_q, cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    for (uint32_t q = 0; q < n_q; ++q) {
+        if (cs[n_q + q] & 2u) return fail(ctx, MRL_ERR_CUDA, "scan grid barrier timed out (CTAs not co-resident)");
+        out_counts[q] = cs[q];
+    }
+    return MRL_OK;
+}
+
 int mrl_merge_topk(mrl_ctx* ctx, const void* d_lists, uint32_t n_lists, uint32_t stride, uint32_t k,
                    uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_count) {
     if (!ctx) return MRL_ERR_INVALID;

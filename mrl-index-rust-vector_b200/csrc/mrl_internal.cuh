@@ -183,9 +183,17 @@ struct ScanLaunch {
     float* out_scores;
     uint32_t* out_count;
     uint32_t* out_status;
+    // fused plan build (query != nullptr): every CTA builds the plan of `query` in shared memory
+    // before scanning, and CTA 0 also stores it to plan_out
+    const float* query;
+    uint32_t dims, prefix_codec, mid_codec;
+    const float* eden_mean;
+    const float* mid_mean;
+    uint64_t eden_seed, mid_seed;
+    DevPlan* plan_out;
 };
 int scan_ctas(int device_sms);
-size_t scan_smem_bytes(uint32_t ctas, uint32_t k);
+size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims);
 int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream);
 int launch_merge_topk(const void* d_lists, uint32_t n_lists, uint32_t stride, uint32_t k, uint64_t* d_out_ids,
                       float* d_out_scores, uint32_t* d_out_count, cudaStream_t stream);

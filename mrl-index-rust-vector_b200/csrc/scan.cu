@@ -33,7 +33,9 @@
 // CTAs raise a flag, and the last CTA (atomic ticket) rescans their pages (owner[]) and redoes
 // the selection by radix select + bitonic sort, so the result is exact for every input (status
 // bit 0 reports it).
-#include "mrl_internal.cuh"
+#include <algorithm>
+
+#include "plan_build.cuh"
 
 namespace mrl {
 namespace {
@@ -72,8 +74,10 @@ __device__ __forceinline__ float unfix(int32_t v, double unscale, float unscale_
     return __double2float_rn(__dmul_rn((double)v, unscale));
 }
 
-// Sum of 64 per-dimension table entries, tab[d*16 + level_d].
-__device__ __forceinline__ int32_t prefix_fixed(const uint4& c0, const uint4& c1, const int* tab) {
+// Sum of 64 per-dimension table entries, tab[d*16 + level_d]. The accumulations are written as
+// v * one + acc (one == 1 at run time) so they issue on the FMA pipe, leaving the ALU pipe to the
+// byte extraction.
+__device__ __forceinline__ int32_t prefix_fixed(const uint4& c0, const uint4& c1, const int* tab, int32_t one) {
     const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
     int32_t acc0 = 0, acc1 = 0;
 #pragma unroll
@@ -82,8 +86,8 @@ __device__ __forceinline__ int32_t prefix_fixed(const uint4& c0, const uint4& c1
         const uint32_t o = (w[j] >> 2) & 0x3C3C3C3Cu;  // levels of dims 8j+1, +3, +5, +7 (x4)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            acc0 += lds_byte(tab, (8 * j + 2 * k) * 64 + __byte_perm(e, 0, 0x4440 + k));
-            acc1 += lds_byte(tab, (8 * j + 2 * k + 1) * 64 + __byte_perm(o, 0, 0x4440 + k));
+            acc0 = lds_byte(tab, (8 * j + 2 * k) * 64 + __byte_perm(e, 0, 0x4440 + k)) * one + acc0;
+            acc1 = lds_byte(tab, (8 * j + 2 * k + 1) * 64 + __byte_perm(o, 0, 0x4440 + k)) * one + acc1;
         }
     }
     return acc0 + acc1;
@@ -136,6 +140,24 @@ __device__ __forceinline__ SlotMeta slot_meta_tab(uint32_t w2, uint32_t w3, cons
     return m;
 }
 
+// Fast-mode score from the three integer stage sums (depth L1 or full; src/scan.rs:499-505,
+// 546-547, 566, 631).
+__device__ __forceinline__ float fast_score(const SlotMeta& m, int32_t P, int32_t s1, int32_t s4, const Scalars& S) {
+    const float cd = unfix(P, S.un_prefix, S.unf_prefix, S.f32_unscale);
+    float sc = S.eden ? __fadd_rn(S.eden_mean_ip, __fmul_rn(m.scale, cd))
+                      : __fadd_rn(__fmul_rn(cd, m.scale), __fmul_rn(m.offset, S.prefix_sum));
+    if (S.depth >= MRL_DEPTH_L1) {
+        const float v = unfix(s1, S.un_s1, S.unf_s1, S.f32_unscale);
+        if (S.mid_b1) sc = __fadd_rn(sc, __fadd_rn(S.mid_mean_ip, __fmul_rn(m.offset, v)));
+        else sc = __fadd_rn(sc, __fmul_rn(v, m.mid_n));
+    }
+    if (S.depth == MRL_DEPTH_FULL && S.has_tail) {
+        const float v = unfix(s4, S.un_s4, S.unf_s4, S.f32_unscale);
+        sc = __fadd_rn(sc, __fmul_rn(__fmul_rn(v, fmaxf(m.high_n, 1e-6f)), S.w_s4));
+    }
+    return sc;
+}
+
 // Full score of one slot; returns false for tombstoned slots.
 template <int MODE>
 __device__ __forceinline__ bool slot_score(const uint4& c0, const uint4& c1, const uint4& c2,
@@ -147,7 +169,7 @@ __device__ __forceinline__ bool slot_score(const uint4& c0, const uint4& c1, con
         const uint32_t s1w[4] = {c2.x, c2.y, c2.z, c2.w};
         const uint32_t s4w[2] = {c3.x, c3.y};
         if (S.depth == MRL_DEPTH_L0) {  // src/scan.rs:753-771
-            const int32_t P = prefix_fixed(c0, c1, tab + kTabL0);
+            const int32_t P = prefix_fixed(c0, c1, tab + kTabL0, S.one);
             const float cd = unfix(P, S.un_l0, S.unf_l0, S.f32_unscale);
             score = __fadd_rn(__fmul_rn(cd, m.scale), __fmul_rn(m.offset, S.prefix_sum));
             if (parts) {
@@ -157,24 +179,12 @@ __device__ __forceinline__ bool slot_score(const uint4& c0, const uint4& c1, con
             }
             return true;
         }
-        const int32_t P = prefix_fixed(c0, c1, tab);
-        const float cd = unfix(P, S.un_prefix, S.unf_prefix, S.f32_unscale);
-        float sc = S.eden ? __fadd_rn(S.eden_mean_ip, __fmul_rn(m.scale, cd))   // src/scan.rs:499-505
-                          : __fadd_rn(__fmul_rn(cd, m.scale), __fmul_rn(m.offset, S.prefix_sum));
+        const int32_t P = prefix_fixed(c0, c1, tab, S.one);
         int32_t s1 = 0, s4 = 0;
         if (S.depth >= MRL_DEPTH_L1 || parts) s1 = window_fixed<128>(s1w, tab + kTabS1, S.one);
         if ((S.depth == MRL_DEPTH_FULL && S.has_tail) || parts) s4 = window_fixed<64>(s4w, tab + kTabS4, S.one);
-        if (S.depth >= MRL_DEPTH_L1) {
-            const float v = unfix(s1, S.un_s1, S.unf_s1, S.f32_unscale);
-            if (S.mid_b1) sc = __fadd_rn(sc, __fadd_rn(S.mid_mean_ip, __fmul_rn(m.offset, v)));  // :546-547
-            else sc = __fadd_rn(sc, __fmul_rn(v, m.mid_n));                                     // :566
-        }
-        if (S.depth == MRL_DEPTH_FULL && S.has_tail) {  // src/scan.rs:631
-            const float v = unfix(s4, S.un_s4, S.unf_s4, S.f32_unscale);
-            sc = __fadd_rn(sc, __fmul_rn(__fmul_rn(v, fmaxf(m.high_n, 1e-6f)), S.w_s4));
-        }
         if (parts) { parts->p = P; parts->s1 = s1; parts->s4 = s4; }
-        score = sc;
+        score = fast_score(m, P, s1, s4, S);
         return true;
     } else {
         const float* ft = reinterpret_cast<const float*>(tab);
@@ -586,13 +596,10 @@ __device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int m
 
 // Page schedule: each warp's first two pages are static (pages gw and gw + W for global warp gw of
 // W), so the launch starts without contending on one atomic; later pages are handed out
-// dynamically from `base` on (one atomic per warp and page, fetched one page ahead) so every warp
-// finishes at about the same time. owner[] records which CTA scored each page for the rare rescan.
-__device__ __forceinline__ uint32_t grab_page(unsigned* counter, int lane, uint32_t base) {
-    uint32_t b = 0;
-    if (lane == 0) b = atomicAdd(counter, 1u);
-    return __shfl_sync(kFull, b, 0) + base;
-}
+// dynamically from 2W on (one atomic per warp and page, issued by lane 0 at the top of an
+// iteration and read by the warp only after the current page is scored, so its latency overlaps
+// the scoring), so every warp finishes at about the same time. owner[] records which CTA scored
+// each page for the rare rescan.
 
 // Number of keys greater than x in lst[0..n), 1 <= n <= 32, sorted descending (keys unique, empty
 // slots 0 at the end): a branch-free binary lift of six fixed steps (clamped loads, selects), so
@@ -613,7 +620,14 @@ __device__ __forceinline__ u64 shfl_xor_u64(u64 v, int o) {
     return ((u64)hi << 32) | lo;
 }
 
-template <int MODE>
+// Shared-memory layout of the fused plan build, aliasing the selection buffers (unused until the
+// scoring loop): the plan, the query copy, the build's scratch.
+__host__ __device__ constexpr size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+__host__ __device__ inline size_t fused_plan_bytes(uint32_t dims) {
+    return align16(sizeof(DevPlan)) + align16((size_t)dims * sizeof(float)) + align16(sizeof(planb::PlanShared));
+}
+
+template <int MODE, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     __shared__ __align__(16) int s_tab[kTabInts];
     __shared__ float2 s_rho[256];
@@ -649,7 +663,26 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
 
     Scalars S;
     if (tid == 0) { s_cta_tau = 0ull; s_seed_min = 0xFFFFFFFFu; s_seed_cnt = 0u; s_nflag = 0u; }
-    load_tables(p.plan, MODE, s_tab, s_rho, S, p);
+    const DevPlan* plan = p.plan;
+    if (FUSED) {
+        // QueryPipeline::build_plan fused into the scan (src/pipeline.rs:63-74): warps 0-3 of every
+        // CTA build the plan while the first pages are in flight; no CTA waits on another.
+        DevPlan* ps = reinterpret_cast<DevPlan*>(s_dyn);
+        float* s_qb = reinterpret_cast<float*>(s_dyn + align16(sizeof(DevPlan)));
+        planb::PlanShared* s_pb = reinterpret_cast<planb::PlanShared*>(
+            s_dyn + align16(sizeof(DevPlan)) + align16((size_t)p.dims * sizeof(float)));
+        if (tid < planb::kPlanThreads)
+            planb::build_plan(p.query, p.dims, p.prefix_codec, p.mid_codec, p.eden_mean, p.eden_seed, p.mid_mean,
+                              p.mid_seed, ps, s_qb, *s_pb);
+        __syncthreads();
+        if (blockIdx.x == 0 && p.plan_out) {  // keep the plan for mrl_plan_read and later scans
+            const uint4* src = reinterpret_cast<const uint4*>(ps);
+            uint4* dst = reinterpret_cast<uint4*>(p.plan_out);
+            for (unsigned i = tid; i < sizeof(DevPlan) / 16; i += kThreads) dst[i] = src[i];
+        }
+        plan = ps;
+    }
+    load_tables(plan, MODE, s_tab, s_rho, S, p);
     __syncthreads();
 
     WarpSel ws{0ull, 0u, 0};
@@ -658,7 +691,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     while (b < p.n_blocks) {
         Slot4 n0, n1;
         if (bn < p.n_blocks) { load_slot(p.pages, bn, lane, n0); load_slot(p.pages, bn, lane + 32, n1); }
-        const uint32_t bnn = bn < p.n_blocks ? grab_page(counter, lane, dyn0) : bn;
+        const bool more = bn < p.n_blocks;  // warp-uniform
+        uint32_t grabbed = 0;
+        if (more && lane == 0) grabbed = atomicAdd(counter, 1u);
         u64 k0 = 0ull, k1 = 0ull;
         if (block_live(p, b)) {
             k0 = slot_key<MODE>(a0, b * 64 + lane, s_tab, s_rho, S);
@@ -681,6 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
             }
         }
         warp_offer(ws, q, lane, L, &s_cta_tau, k0, k1);
+        const uint32_t bnn = more ? __shfl_sync(kFull, grabbed, 0) + dyn0 : bn;
         b = bn;
         bn = bnn;
         a0 = n0;
@@ -838,17 +874,22 @@ __global__ void __launch_bounds__(kThreads) debug_scores_kernel(const ScanLaunch
 
 int scan_ctas(int device_sms) { return device_sms; }
 
-size_t scan_smem_bytes(uint32_t ctas, uint32_t k) {
+size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims) {
     size_t p2 = 1;
     while (p2 < k) p2 <<= 1;
-    return sizeof(u64) * (kWarps * kQueue + kWarps * 32 + (size_t)ctas * 33 + p2) + sizeof(unsigned) * (kBins + ctas);
+    const size_t sel = sizeof(u64) * (kWarps * kQueue + kWarps * 32 + (size_t)ctas * 33 + p2) +
+                       sizeof(unsigned) * (kBins + ctas);
+    return fused_dims ? std::max(sel, fused_plan_bytes(fused_dims)) : sel;
 }
 
 // Cooperative launch: one CTA per SM, all co-resident (the grid barrier relies on it).
 int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream) {
-    const size_t smem = scan_smem_bytes(ctas, p.k);
-    const void* fn = p.mode == MRL_MODE_FAST ? (const void*)scan_kernel<MRL_MODE_FAST>
-                                             : (const void*)scan_kernel<MRL_MODE_EXACT>;
+    const bool fused = p.query != nullptr;
+    const size_t smem = scan_smem_bytes(ctas, p.k, fused ? p.dims : 0u);
+    const void* fn = p.mode == MRL_MODE_FAST ? (fused ? (const void*)scan_kernel<MRL_MODE_FAST, true>
+                                                      : (const void*)scan_kernel<MRL_MODE_FAST, false>)
+                                             : (fused ? (const void*)scan_kernel<MRL_MODE_EXACT, true>
+                                                      : (const void*)scan_kernel<MRL_MODE_EXACT, false>);
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -1;
     ScanLaunch arg = p;
     void* args[] = {&arg};

@@ -25,6 +25,7 @@ from .api import (  # noqa: F401
     default_device,
     encode_blocks,
     row_id_to_vector_id,
+    query_scan,
     scan_blocks,
     scan_blocks_batch,
     scored_hits_to_row_ids,

@@ -321,6 +321,25 @@ def _codec_desc(prefix_codec, mid_codec, eden: Optional[EdenFit], eden_mid: Opti
     return d, keep
 
 
+def _check_plan_args(queries, prefix_codec, mid_codec, eden, eden_mid) -> np.ndarray:
+    """The contract checks of QueryPlan::from_query_codec (src/scan.rs:113-124); returns the
+    queries as a contiguous [n_q, dims] f32 array."""
+    q = np.ascontiguousarray(np.atleast_2d(queries), np.float32)
+    if q.shape[1] < MRL_PREFIX_DIMS + RABITQ_DIMS:
+        raise ValueError("assertion failed: dims >= MRL_PREFIX_DIMS + RABITQ_DIMS")  # src/scan.rs:114
+    if prefix_codec == PrefixCodec.EDEN_PROD:
+        if eden is None:
+            raise ValueError("EdenProd requires EdenFit")
+        if eden.dim != MRL_PREFIX_DIMS or eden.bits != 4:
+            raise ValueError("EdenProd fit must have dim 64 and bits 4")
+    if mid_codec == MidCodec.EDEN_B1:
+        if eden_mid is None:
+            raise ValueError("EdenB1 mid requires EdenFit")
+        if eden_mid.dim != RABITQ_DIMS or eden_mid.bits != 1:
+            raise ValueError("EdenB1 mid fit must have dim 128 and bits 1")
+    return q
+
+
 class QueryPlan:
     """Device-resident plan(s) built by the plan kernel (QueryPlan::from_query_codec)."""
 
@@ -335,20 +354,8 @@ class QueryPlan:
                      eden: Optional[EdenFit] = None, eden_mid: Optional[EdenFit] = None,
                      dev: Optional[Device] = None) -> "QueryPlan":
         dev = dev or default_device()
-        q = np.ascontiguousarray(np.atleast_2d(queries), np.float32)
+        q = _check_plan_args(queries, prefix_codec, mid_codec, eden, eden_mid)
         n_q, dims = q.shape
-        if dims < MRL_PREFIX_DIMS + RABITQ_DIMS:
-            raise ValueError("assertion failed: dims >= MRL_PREFIX_DIMS + RABITQ_DIMS")  # src/scan.rs:114
-        if prefix_codec == PrefixCodec.EDEN_PROD:
-            if eden is None:
-                raise ValueError("EdenProd requires EdenFit")
-            if eden.dim != MRL_PREFIX_DIMS or eden.bits != 4:
-                raise ValueError("EdenProd fit must have dim 64 and bits 4")
-        if mid_codec == MidCodec.EDEN_B1:
-            if eden_mid is None:
-                raise ValueError("EdenB1 mid requires EdenFit")
-            if eden_mid.dim != RABITQ_DIMS or eden_mid.bits != 1:
-                raise ValueError("EdenB1 mid fit must have dim 128 and bits 1")
         desc, keep = _codec_desc(prefix_codec, mid_codec, eden, eden_mid)
         out = C.c_void_p()
         check(dev.ptr, dev.lib.mrl_plan_build(dev.ptr, q.ctypes.data_as(C.c_void_p), n_q, dims, C.byref(desc),
@@ -427,6 +434,32 @@ def scan_blocks_batch(segment: Segment, plan: QueryPlan, cfg, time_lo=None, time
     return ids, scores, counts
 
 
+def query_scan(segment: Segment, queries, cfg, prefix_codec=PrefixCodec.MIN_MAX4, mid_codec=MidCodec.RABITQ,
+               eden: Optional[EdenFit] = None, eden_mid: Optional[EdenFit] = None, time_lo=None, time_hi=None):
+    """Plan build + scan of every query in one fused launch per query (mrl_query_scan; the
+    reference's QueryPipeline::build_plan followed by scan_segments_into, src/pipeline.rs:63-133).
+    Returns (ids [n_q,k] u64, scores [n_q,k] f32, counts [n_q], plan) with the plans kept."""
+    dev = segment.dev
+    q = _check_plan_args(queries, prefix_codec, mid_codec, eden, eden_mid)
+    n_q, dims = q.shape
+    sc = _cfg_of(cfg)
+    c = sc.to_c()
+    k = int(sc.shortlist_cand)
+    plans = C.c_void_p()
+    check(dev.ptr, dev.lib.mrl_plans_alloc(dev.ptr, n_q, dims, C.byref(plans)))
+    plan = QueryPlan(plans, dev, n_q, dims)
+    desc, keep = _codec_desc(prefix_codec, mid_codec, eden, eden_mid)
+    ids = np.zeros((n_q, k), np.uint64)
+    scores = np.zeros((n_q, k), np.float32)
+    counts = np.zeros(n_q, np.uint32)
+    lo, hi = _time_ptrs(time_lo, time_hi)
+    check(dev.ptr, dev.lib.mrl_query_scan(dev.ptr, segment.ptr, q.ctypes.data_as(C.c_void_p), n_q, dims,
+                                          C.byref(desc), plans, C.byref(c), lo, hi, ids.ctypes.data_as(C.c_void_p),
+                                          scores.ctypes.data_as(C.c_void_p), counts.ctypes.data_as(C.c_void_p)))
+    del keep
+    return ids, scores, counts, plan
+
+
 def scan_blocks(segment: Segment, plan: QueryPlan, cfg, time_lo=None, time_hi=None) -> List[ScoredHit]:
     """`scan_blocks` (src/scan.rs:802-810): top `shortlist_cand` hits, score descending."""
     if plan.n_q != 1:
@@ -502,6 +535,25 @@ class QueryPipeline:
         if c.prefix_codec == PrefixCodec.EDEN_PROD and self.eden is not None:
             return QueryPlan.from_query_eden(query, c.embed_dims, self.eden, dev=self.dev)
         return QueryPlan.from_query(query, c.embed_dims, dev=self.dev)
+
+    def search(self, query, segment: Segment, time_lo=None, time_hi=None) -> List[ScoredHit]:
+        """build_plan + scan of one query in a single fused launch (mrl_query_scan)."""
+        c = self.cfg
+        if c.prefix_codec == PrefixCodec.EDEN_PROD and c.mid_codec == MidCodec.EDEN_B1 and self.eden and self.eden_mid:
+            codec = dict(prefix_codec=PrefixCodec.EDEN_PROD, mid_codec=MidCodec.EDEN_B1, eden=self.eden,
+                         eden_mid=self.eden_mid)
+        elif c.prefix_codec == PrefixCodec.EDEN_PROD and self.eden is not None:
+            codec = dict(prefix_codec=PrefixCodec.EDEN_PROD, mid_codec=MidCodec.RABITQ, eden=self.eden)
+        else:
+            codec = dict(prefix_codec=PrefixCodec.MIN_MAX4, mid_codec=MidCodec.RABITQ)
+        q = np.asarray(query, np.float32)
+        if q.size != c.embed_dims:
+            raise ValueError("assertion failed: query.len() == dims")
+        ids, scores, counts, plan = query_scan(segment, q.reshape(1, -1), c, time_lo=time_lo, time_hi=time_hi,
+                                               **codec)
+        plan.free()
+        n = int(counts[0])
+        return [ScoredHit(VectorId.from_u64(int(ids[0, i])), float(scores[0, i])) for i in range(n)]
 
     def scan_slab(self, query, segment: Segment, time_lo=None, time_hi=None):
         import time

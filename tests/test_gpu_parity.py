@@ -212,6 +212,69 @@ def test_scan_topk_matches_reference_scan(ora, dev, corpus768, k, mode):
             assert_same_topk(gi, gs, rid, rsc, RTOL)
 
 
+@pytest.mark.parametrize("k", [16, 256])
+@pytest.mark.parametrize("mode", ["exact", "fast"])
+@pytest.mark.parametrize("codec", ["minmax", "eden", "eden_b1"])
+def test_fused_query_scan_matches_plan_then_scan(ora, dev, corpus768, codec, mode, k):
+    """mrl_query_scan (plan built inside the scan launch) against mrl_plan_build + mrl_scan: the
+    stored plans are bit-identical to the plan kernel's and the results are identical."""
+    M = mb()
+    qs = corpus768["qs"]
+    mean = corpus768["mean"]
+    mid_mean = (np.random.default_rng(3).standard_normal(128) * 0.05).astype(np.float32)
+    if codec == "minmax":
+        seg = M.Segment.upload(corpus768["minmax"], dev)
+        kw = dict(prefix_codec=M.PrefixCodec.MIN_MAX4, mid_codec=M.MidCodec.RABITQ)
+    elif codec == "eden":
+        seg = M.Segment.upload(corpus768["eden"], dev)
+        kw = dict(prefix_codec=M.PrefixCodec.EDEN_PROD, mid_codec=M.MidCodec.RABITQ, eden=fit(mean))
+    else:
+        seg = M.Segment.upload(corpus768["eden"], dev)
+        kw = dict(prefix_codec=M.PrefixCodec.EDEN_PROD, mid_codec=M.MidCodec.EDEN_B1, eden=fit(mean),
+                  eden_mid=fit(mid_mean, 128, 1))
+    cfg = M.ScanConfig(shortlist_cand=k, mode=M.ScanMode.EXACT if mode == "exact" else M.ScanMode.FAST)
+    ref_plans = M.QueryPlan.from_queries(qs, dev=dev, **kw)
+    r_ids, r_sc, r_cnt = M.scan_blocks_batch(seg, ref_plans, cfg)
+    f_ids, f_sc, f_cnt, f_plans = M.query_scan(seg, qs, cfg, **kw)
+    assert np.array_equal(f_cnt, r_cnt)
+    for qi in range(len(qs)):
+        n = int(r_cnt[qi])
+        assert np.array_equal(f_ids[qi, :n], r_ids[qi, :n])
+        assert np.array_equal(f_sc[qi, :n].view(np.uint32), r_sc[qi, :n].view(np.uint32))
+        a, b = f_plans.fields(qi), ref_plans.fields(qi)
+        for f in PLAN_FIELDS:
+            x, y = getattr(a, f), getattr(b, f)
+            x = np.array(x) if isinstance(x, (int, float)) else np.ctypeslib.as_array(x)
+            y = np.array(y) if isinstance(y, (int, float)) else np.ctypeslib.as_array(y)
+            assert np.array_equal(np.asarray(x, np.float32).view(np.uint32), np.asarray(y, np.float32).view(np.uint32)), f
+    f_plans.free()
+    ref_plans.free()
+    seg.free()
+
+
+def test_fused_query_scan_edge_cases(ora, dev, corpus768):
+    """Empty segment (plans still built), temporal filter, QueryPipeline.search."""
+    M = mb()
+    q = corpus768["qs"][:2]
+    kw = dict(prefix_codec=M.PrefixCodec.EDEN_PROD, eden=fit(corpus768["mean"]))
+    empty = M.Segment.upload(np.zeros(0, np.uint8), dev)
+    ids, sc, cnt, plans = M.query_scan(empty, q, M.ScanConfig(shortlist_cand=16), **kw)
+    assert cnt.tolist() == [0, 0]
+    ref = M.QueryPlan.from_queries(q, dev=dev, **kw)
+    assert np.array_equal(np.ctypeslib.as_array(plans.fields(1).eden_q_rot),
+                          np.ctypeslib.as_array(ref.fields(1).eden_q_rot))
+    seg = M.Segment.upload(corpus768["eden"], dev)
+    cfg = M.ScanConfig(shortlist_cand=64, temporal_filter_enable=True)
+    ids, sc, cnt, _ = M.query_scan(seg, q, cfg, time_lo=64 * 30, **kw)
+    assert all(int(i) >> 16 >= 30 for i in ids[0, : cnt[0]])  # ts = row index: pages 0-29 end before 1920
+    r_ids, r_sc, r_cnt = M.scan_blocks_batch(seg, ref, cfg, time_lo=64 * 30)
+    assert np.array_equal(ids, r_ids) and np.array_equal(cnt, r_cnt)
+    pipe = M.QueryPipeline.with_eden(M.EngineConfig(embed_dims=768, shortlist_cand=64), fit(corpus768["mean"]), dev=dev)
+    hits = pipe.search(q[0], seg)
+    plan = pipe.build_plan(q[0])
+    assert hits == M.scan_blocks(seg, plan, pipe.cfg)
+
+
 def test_forced_reselection_is_exact(ora, dev, corpus768):
     """A per-CTA list of 1 entry forces the verification to fail and the last CTA to rescan:
     the result must still be the exact top-k."""
