@@ -1,9 +1,9 @@
 // plan_build.cuh — the query-side plan build (QueryPlan::from_query_codec, src/scan.rs:105-266) as
-// a device function for 128 threads (threads 0..127 of the calling CTA), shared by the standalone
-// plan kernel (plan.cu) and the scan kernel's fused plan prologue (scan.cu).
+// a device function run by a whole CTA (at least 128 threads), shared by the standalone plan kernel
+// (plan.cu) and the scan kernel's fused plan prologue (scan.cu).
 //
-// Four warps build independent parts of the plan (prefix, mid band, folded tail, long reductions)
-// with one 128-thread named barrier before the final scalars. FWHTs run on warp shuffles (each
+// Four warps build independent parts of the plan (prefix, mid band, folded tail, long reductions),
+// then every thread of the CTA fills the tables. FWHTs run on warp shuffles (each
 // butterfly output depends only on its two inputs, so the values equal the sequential loop's),
 // sequential reductions run on one lane in the reference's order, and every f32 operation is an
 // explicit round-to-nearest intrinsic (the library is compiled with -fmad=false) so the plan is
@@ -21,10 +21,6 @@ namespace mrl {
 namespace planb {
 
 constexpr int kPlanThreads = 128;
-
-// Barrier of the 128 plan threads only (named barrier 1), so a larger CTA can run the build in
-// its first four warps.
-__device__ __forceinline__ void plan_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 __device__ __forceinline__ float f_add(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ float f_sub(float a, float b) { return __fsub_rn(a, b); }
@@ -77,27 +73,22 @@ __device__ __forceinline__ double warp_max(double v) {
     return v;
 }
 
-// Fast-mode window table of one 1-bit stage (lut_s1 / lut_s4), built by one warp: entry (g, m) is
-// the exact integer sum over the window's dims i of fix(bit i of m ? val1 : val0). `fx` holds the
-// fixed values per dim interleaved (fx[2 i] for bit 0, fx[2 i + 1] for bit 1) in warp-private
-// shared memory, already synchronised; lane m computes entry m of every window.
-template <int WINDOWS, int DIMS>
-__device__ __forceinline__ void build_window_table(const int32_t* fx, int32_t* out, int lane) {
-    int b[5];
-#pragma unroll
-    for (int i = 0; i < 5; ++i) b[i] = (lane >> i) & 1;
-#pragma unroll 2
-    for (int g = 0; g < WINDOWS - 1; ++g) {  // full 5-dim windows
-        const int32_t* f = fx + 10 * g;
-        out[g * 32 + lane] = f[b[0]] + f[2 + b[1]] + f[4 + b[2]] + f[6 + b[3]] + f[8 + b[4]];
-    }
-    constexpr int g = WINDOWS - 1, w = DIMS - 5 * g;  // last window: w dims
-    const int32_t* f = fx + 10 * g;
+// Entry (g, m) of a fast-mode window table of one 1-bit stage (lut_s1 / lut_s4): the exact integer
+// sum over the window's dims i of fix(bit i of m ? val1 : val0). `fx` holds the fixed values per
+// dim interleaved (fx[2 i] for bit 0, fx[2 i + 1] for bit 1).
+template <int DIMS>
+__device__ __forceinline__ int32_t window_entry(const int32_t* fx, int g, int m) {
+    const int w = min(5, DIMS - 5 * g);
+    if (m >= (1 << w)) return 0;
     int32_t sum = 0;
-#pragma unroll
-    for (int i = 0; i < w; ++i) sum += f[2 * i + b[i]];
-    out[g * 32 + lane] = lane < (1 << w) ? sum : 0;
+    for (int i = 0; i < w; ++i) sum += fx[2 * (5 * g + i) + ((m >> i) & 1)];
+    return sum;
 }
+
+// What a plan build writes: kNeedAll = every field of DevPlan (the stored plan); a scan that only
+// needs its own mode's tables asks for kNeedFast (+ kNeedL0 at depth L0Only) or kNeedExact. The
+// scalars, shifts, bit weights, mid_w and tail_w are always written.
+constexpr uint32_t kNeedFast = 1u, kNeedExact = 2u, kNeedL0 = 4u, kNeedAll = 0xFu;
 
 // Shared scratch of one plan build (besides the dims-float query copy).
 struct PlanShared {
@@ -109,20 +100,39 @@ struct PlanShared {
     int32_t fx[2 * (kRabitq + kFold)];  // fixed 1-bit stage values, see build_window_table
     float scal[16];
     float cb[16];
+    float w[kPrefix];  // EDEN prefix weight per dim: rot[d] / sqrt(64)
+    double pw[2];      // 2^shift of the prefix and L0 tables
 };
 
-// Warp roles (the three plan branches are independent until the final scalars):
-//   warp 0: prefix — EDEN query rotation, prefix scalars, exact and fast prefix tables, L0 table;
-//   warp 1: mid band — RaBitQ and EdenB1 rotations, their scalars, mid_w and the S1 window table;
-//   warp 2: folded tail — fold, rotation, tail scalars, tail_w and the S4 window table;
-//   warp 3: q_tail_sq (the longest sequential sum) and rabitq_lut.
-// Threads 0..127 of the CTA build the plan of query `q` into P (global or shared memory), using
-// s_q (dims floats of shared memory) and sh. All 128 threads must call it.
-__device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t dims, uint32_t prefix_codec,
-                                           uint32_t mid_codec, const float* __restrict__ eden_mean,
-                                           uint64_t eden_seed, const float* __restrict__ mid_mean,
-                                           uint64_t mid_seed, DevPlan* P, float* s_q, PlanShared& sh) {
+// The build's inputs into shared memory: the query, the codec centres, the b=4 codebook. Every
+// thread of the CTA calls it; build_plan synchronises before reading them.
+__device__ __forceinline__ void plan_inputs(const float* __restrict__ q, uint32_t dims, const float* __restrict__ eden_mean,
+                                            const float* __restrict__ mid_mean, float* s_q, PlanShared& sh) {
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    for (uint32_t i = tid; i < dims; i += nthr) s_q[i] = q[i];
+    for (int i = tid; i < kPrefix + kRabitq; i += nthr) {  // either centre array may be NULL
+        const float* src = i < kPrefix ? eden_mean : mid_mean;
+        sh.mean[i] = src ? src[i < kPrefix ? i : i - kPrefix] : 0.0f;
+    }
+    if (tid < 16) sh.cb[tid] = g_lloyd_b4[tid];
+}
+
+// Phase A, threads 0..127 in four warp roles (the plan branches are independent until the final
+// scalars):
+//   warp 0: prefix — EDEN query rotation, prefix scalars, prefix weights and the prefix/L0 shifts;
+//   warp 1: mid band — RaBitQ and EdenB1 rotations, their scalars, mid_w, the S1 shift and fixed
+//           values;
+//   warp 2: folded tail — fold, rotation, tail scalars, tail_w, the S4 shift and fixed values;
+//   warp 3: q_tail_sq (the longest sequential sum) and, for a full plan, rabitq_lut.
+// Phase B, every thread of the CTA: the 1024-entry tables `need` asks for and the window tables.
+// Every thread of the CTA (at least 128) must call it, after plan_inputs; P may be global or shared
+// memory, s_q holds the dims floats plan_inputs loaded.
+__device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec, uint32_t mid_codec,
+                                           uint64_t eden_seed, uint64_t mid_seed, DevPlan* P, float* s_q,
+                                           PlanShared& sh, uint32_t need) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nthr = blockDim.x;
+    const bool full = need == kNeedAll;
     mrl_query_plan* qp = &P->qp;
     float* s_mean = sh.mean;
     float* s_rot = sh.rot;
@@ -136,13 +146,7 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
     const bool mid_b1 = mid_codec == MRL_MID_EDEN_B1;
     const bool has_tail = dims > (uint32_t)kTailStart;
 
-    for (uint32_t i = tid; i < dims; i += kPlanThreads) s_q[i] = q[i];
-    for (int i = tid; i < kPrefix + kRabitq; i += kPlanThreads) {  // either centre array may be NULL
-        const float* src = i < kPrefix ? eden_mean : mid_mean;
-        s_mean[i] = src ? src[i < kPrefix ? i : i - kPrefix] : 0.0f;
-    }
-    if (tid < 16) s_cb[tid] = g_lloyd_b4[tid];
-    plan_bar();
+    __syncthreads();  // plan_inputs done
 
     const float inv_sqrt_64 = __fdiv_rn(1.0f, __fsqrt_rn(64.0f));
     const float inv_sqrt_128 = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
@@ -157,7 +161,7 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
         for (int r = 0; r < 2; ++r) {
             const int d = lane + 32 * r;
             const float qd = s_q[d];
-            qp->prefix[d] = qd;
+            if (full) qp->prefix[d] = qd;
             qp->bit_weights[d][0] = f_mul(qd, 1.0f);
             qp->bit_weights[d][1] = f_mul(qd, 2.0f);
             qp->bit_weights[d][2] = f_mul(qd, 4.0f);
@@ -168,9 +172,9 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             s_rot[lane + 32 * r] = v[r];
-            qp->eden_q_rot[lane + 32 * r] = eden ? v[r] : 0.0f;
+            if (full) qp->eden_q_rot[lane + 32 * r] = eden ? v[r] : 0.0f;
         }
-        if (lane < 16) qp->eden_codebook[lane] = eden ? s_cb[lane] : 0.0f;
+        if (full && lane < 16) qp->eden_codebook[lane] = eden ? s_cb[lane] : 0.0f;
         __syncwarp();
         // prefix_l1, prefix_sum, eden_mean_ip: sequential in the reference's order (src/scan.rs:126-151)
         if (lane == 0) {
@@ -187,56 +191,30 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
             s_scal[1] = sum;
             s_scal[4] = ip;
         }
-        // exact-mode prefix table and fast-mode prefix table; four consecutive levels of one dim
-        // per step (entry e = 16 d + l)
-        double mx = 0.0;
-        for (int t = lane; t < kPrefix * 4; t += 32) {
-            const int d = t >> 2, l0 = (t & 3) * 4;
-            const float w = eden ? f_mul(s_rot[d], inv_sqrt_64) : 0.0f;
-            float4 o;
-            float* of = &o.x;
+        // Prefix weights and shifts. An entry is (double)cb[l] * w_d (EDEN) or (double)l * q_d
+        // (MinMax), both exact products, so the largest |entry| of dim d is max|cb| * |w_d| or
+        // 15 * |q_d|.
+        double cbmax = 0.0;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int l = l0 + j;
-                of[j] = eden ? f_mul(s_cb[l], w) : f_mul((float)l, s_q[d]);
-                const double dv = eden ? (double)s_cb[l] * (double)w : (double)l * (double)s_q[d];
-                mx = fmax(mx, fabs(dv));
-            }
-            reinterpret_cast<float4*>(P->fp_prefix)[t] = o;
+        for (int l = 0; l < 16; ++l) cbmax = fmax(cbmax, fabs((double)s_cb[l]));
+        double mx = 0.0, mx0 = 0.0;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int d = lane + 32 * r;
+            const float w = eden ? f_mul(s_rot[d], inv_sqrt_64) : 0.0f;
+            sh.w[d] = w;
+            mx = fmax(mx, eden ? cbmax * fabs((double)w) : 15.0 * fabs((double)s_q[d]));
+            mx0 = fmax(mx0, fabs((double)f_mul(s_q[d], 8.0f)));
         }
         const int sh_p = stage_shift(warp_max(mx), kPrefix);
-        const double pw_p = ldexp(1.0, sh_p);
-        for (int t = lane; t < kPrefix * 4; t += 32) {
-            const int d = t >> 2, l0 = (t & 3) * 4;
-            const float w = eden ? f_mul(s_rot[d], inv_sqrt_64) : 0.0f;
-            int4 o;
-            int* oi = &o.x;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int l = l0 + j;
-                oi[j] = fix(eden ? (double)s_cb[l] * (double)w : (double)l * (double)s_q[d], pw_p);
-            }
-            reinterpret_cast<int4*>(P->lut_prefix)[t] = o;
-        }
-        // L0Only: bit 3 of the level times bit_weights[d][3] (accum_plane, src/scan.rs:753-762)
-        mx = fmax(fabs((double)f_mul(s_q[lane], 8.0f)), fabs((double)f_mul(s_q[lane + 32], 8.0f)));
-        const int sh_0 = stage_shift(warp_max(mx), kPrefix);
-        const double pw_0 = ldexp(1.0, sh_0);
-        for (int t = lane; t < kPrefix * 4; t += 32) {
-            const int d = t >> 2, l0 = (t & 3) * 4;
-            const int32_t f = fix((double)f_mul(s_q[d], 8.0f), pw_0);
-            int4 o;
-            o.x = ((l0 + 0) & 8) ? f : 0;
-            o.y = ((l0 + 1) & 8) ? f : 0;
-            o.z = ((l0 + 2) & 8) ? f : 0;
-            o.w = ((l0 + 3) & 8) ? f : 0;
-            reinterpret_cast<int4*>(P->lut_l0)[t] = o;
-        }
+        const int sh_0 = stage_shift(warp_max(mx0), kPrefix);  // L0Only (accum_plane, src/scan.rs:753-762)
         if (lane == 0) {
             P->shift_prefix = sh_p;
             P->shift_l0 = sh_0;
             P->unscale_prefix = ldexp(1.0, -sh_p);
             P->unscale_l0 = ldexp(1.0, -sh_0);
+            sh.pw[0] = ldexp(1.0, sh_p);
+            sh.pw[1] = ldexp(1.0, sh_0);
         }
     } else if (warp == 1) {
         // ---- mid band: rotate_mid_band (src/rotate.rs:36-42) and the EdenB1 rotation (src/scan.rs:159-174)
@@ -255,10 +233,12 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
             const int i = lane + 32 * r;
             s_rq[i] = rq[r];
             s_mq[i] = mq[r];
-            qp->rabitq_q[i] = rq[r];
-            qp->eden_mid_q_rot[i] = mid_b1 ? mq[r] : 0.0f;
             const float pos = f_mul(rq[r], rabitq_scale);
-            qp->rabitq_weights2[i] = f_mul(2.0f, pos);
+            if (full) {
+                qp->rabitq_q[i] = rq[r];
+                qp->eden_mid_q_rot[i] = mid_b1 ? mq[r] : 0.0f;
+                qp->rabitq_weights2[i] = f_mul(2.0f, pos);
+            }
             double v1;
             if (mid_b1) {
                 const float qd = f_mul(mq[r], inv_sqrt_128);
@@ -297,7 +277,7 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
             s_scal[6] = base;
             s_scal[9] = b1;
         }
-        // fast-mode S1 window table
+        // fixed S1 values per dim for the window table
         const int sh_1 = stage_shift(warp_max(mx), kRabitq);
         const double pw_1 = ldexp(1.0, sh_1);
 #pragma unroll
@@ -309,8 +289,6 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
             s_fx[2 * i] = fix(-v1, pw_1);
             s_fx[2 * i + 1] = fix(v1, pw_1);
         }
-        __syncwarp();
-        build_window_table<kS1Windows, kRabitq>(s_fx, P->lut_s1, lane);
         if (lane == 0) {
             P->shift_s1 = sh_1;
             P->unscale_s1 = ldexp(1.0, -sh_1);
@@ -333,9 +311,11 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
         for (int r = 0; r < 2; ++r) {
             const int d = lane + 32 * r;
             s_tf[d] = u[r];
-            qp->tail_fold_q[d] = has_tail ? u[r] : 0.0f;
             const float pos = has_tail ? f_mul(u[r], tail_scale) : 0.0f;
-            qp->tail_fold_weights2[d] = has_tail ? f_mul(2.0f, pos) : 0.0f;
+            if (full) {
+                qp->tail_fold_q[d] = has_tail ? u[r] : 0.0f;
+                qp->tail_fold_weights2[d] = has_tail ? f_mul(2.0f, pos) : 0.0f;
+            }
             P->tail_w[d] = has_tail ? f_mul(2.0f, pos) : 0.0f;
             mx = fmax(mx, fabs((double)pos));
         }
@@ -354,6 +334,7 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
             s_scal[7] = tb;
             s_scal[8] = bud;
         }
+        // fixed S4 values per dim for the window table
         const int sh_4 = stage_shift(warp_max(mx), kFold);
         const double pw_4 = ldexp(1.0, sh_4);
 #pragma unroll
@@ -363,13 +344,11 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
             s_fx[2 * (kRabitq + d)] = fix(-pos, pw_4);
             s_fx[2 * (kRabitq + d) + 1] = fix(pos, pw_4);
         }
-        __syncwarp();
-        build_window_table<kS4Windows, kFold>(s_fx + 2 * kRabitq, P->lut_s4, lane);
         if (lane == 0) {
             P->shift_s4 = sh_4;
             P->unscale_s4 = ldexp(1.0, -sh_4);
         }
-    } else {
+    } else if (warp == 3) {
         // q_tail_sq (src/scan.rs:203-207): the longest sequential sum
         if (lane == 0) {
             float ts = 0.0f;
@@ -377,32 +356,81 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
             for (uint32_t d = kTailStart; d < dims; ++d) ts = f_add(ts, f_mul(s_q[d], s_q[d]));
             s_scal[2] = ts;
         }
-        // rabitq_lut (src/scan.rs:188-201): computed by the reference, unused by its stages; it
-        // needs the rotated mid band, so this warp rotates it again (cheaper than a barrier)
-        float rq[4];
+        if (full) {
+            // rabitq_lut (src/scan.rs:188-201): computed by the reference, unused by its stages; it
+            // needs the rotated mid band, so this warp rotates it again (cheaper than a barrier)
+            float rq[4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) rq[r] = s_q[kPrefix + lane + 32 * r];
-        fwht_warp<4>(rq, lane);
-        // lane holds rotated dims lane + 32 r; group g = dims 4g..4g+3 lives in lanes 4(g%8)..+3
+            for (int r = 0; r < 4; ++r) rq[r] = s_q[kPrefix + lane + 32 * r];
+            fwht_warp<4>(rq, lane);
+            // lane holds rotated dims lane + 32 r; group g = dims 4g..4g+3 lives in lanes 4(g%8)..+3
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int gl = (lane >> 2);  // group within this register's 32 dims
-            const float base_v = f_mul(rq[r], rabitq_scale);
-            float p[4];
+            for (int r = 0; r < 4; ++r) {
+                const int gl = (lane >> 2);  // group within this register's 32 dims
+                const float base_v = f_mul(rq[r], rabitq_scale);
+                float p[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) p[j] = __shfl_sync(0xffffffffu, base_v, (gl << 2) + j);
-            const int g = r * 8 + gl;
-            // this lane writes entries m = 4 (lane & 3) .. +3 of group g
+                for (int j = 0; j < 4; ++j) p[j] = __shfl_sync(0xffffffffu, base_v, (gl << 2) + j);
+                const int g = r * 8 + gl;
+                // this lane writes entries m = 4 (lane & 3) .. +3 of group g
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int m = (lane & 3) * 4 + j;
-                const float a0 = (m & 1) ? p[0] : -p[0], a1 = (m & 2) ? p[1] : -p[1];
-                const float a2 = (m & 4) ? p[2] : -p[2], a3 = (m & 8) ? p[3] : -p[3];
-                qp->rabitq_lut[g][m] = f_add(f_add(f_add(a0, a1), a2), a3);
+                for (int j = 0; j < 4; ++j) {
+                    const int m = (lane & 3) * 4 + j;
+                    const float a0 = (m & 1) ? p[0] : -p[0], a1 = (m & 2) ? p[1] : -p[1];
+                    const float a2 = (m & 4) ? p[2] : -p[2], a3 = (m & 8) ? p[3] : -p[3];
+                    qp->rabitq_lut[g][m] = f_add(f_add(f_add(a0, a1), a2), a3);
+                }
             }
         }
     }
-    plan_bar();
+    __syncthreads();
+
+    // ---- phase B: tables, four consecutive levels of one dim per item (entry e = 16 d + l)
+    if (need & kNeedFast) {
+        const double pw_p = sh.pw[0];
+        for (int t = tid; t < kPrefix * 4; t += nthr) {
+            const int d = t >> 2, l0 = (t & 3) * 4;
+            const float w = sh.w[d];
+            int4 o;
+            int* oi = &o.x;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int l = l0 + j;
+                oi[j] = fix(eden ? (double)s_cb[l] * (double)w : (double)l * (double)s_q[d], pw_p);
+            }
+            reinterpret_cast<int4*>(P->lut_prefix)[t] = o;
+        }
+        for (int t = tid; t < kS1Windows * 32; t += nthr) P->lut_s1[t] = window_entry<kRabitq>(s_fx, t >> 5, t & 31);
+        for (int t = tid; t < kS4Windows * 32; t += nthr)
+            P->lut_s4[t] = window_entry<kFold>(s_fx + 2 * kRabitq, t >> 5, t & 31);
+    }
+    if (need & kNeedL0) {  // bit 3 of the level times bit_weights[d][3] (accum_plane, src/scan.rs:753-762)
+        const double pw_0 = sh.pw[1];
+        for (int t = tid; t < kPrefix * 4; t += nthr) {
+            const int d = t >> 2, l0 = (t & 3) * 4;
+            const int32_t f = fix((double)f_mul(s_q[d], 8.0f), pw_0);
+            int4 o;
+            o.x = ((l0 + 0) & 8) ? f : 0;
+            o.y = ((l0 + 1) & 8) ? f : 0;
+            o.z = ((l0 + 2) & 8) ? f : 0;
+            o.w = ((l0 + 3) & 8) ? f : 0;
+            reinterpret_cast<int4*>(P->lut_l0)[t] = o;
+        }
+    }
+    if (need & kNeedExact) {  // f32 products of the reference's prefix loop (src/scan.rs:456-487)
+        for (int t = tid; t < kPrefix * 4; t += nthr) {
+            const int d = t >> 2, l0 = (t & 3) * 4;
+            const float w = sh.w[d];
+            float4 o;
+            float* of = &o.x;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int l = l0 + j;
+                of[j] = eden ? f_mul(s_cb[l], w) : f_mul((float)l, s_q[d]);
+            }
+            reinterpret_cast<float4*>(P->fp_prefix)[t] = o;
+        }
+    }
     if (tid == 0) {
         qp->dims = dims;
         qp->prefix_codec = prefix_codec;
@@ -430,7 +458,6 @@ __device__ __forceinline__ void build_plan(const float* __restrict__ q, uint32_t
         P->pad3 = 0.0f;
     }
 }
-
 
 }  // namespace planb
 }  // namespace mrl

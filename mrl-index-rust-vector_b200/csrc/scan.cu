@@ -655,6 +655,13 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     const unsigned L = p.list_len;
     unsigned* counter = p.ctl;
 
+    // fused plan build: its inputs first, so they are not queued behind the page loads
+    DevPlan* ps = reinterpret_cast<DevPlan*>(s_dyn);
+    float* s_qb = reinterpret_cast<float*>(s_dyn + align16(sizeof(DevPlan)));
+    planb::PlanShared* s_pb =
+        reinterpret_cast<planb::PlanShared*>(s_dyn + align16(sizeof(DevPlan)) + align16((size_t)p.dims * sizeof(float)));
+    if (FUSED) planb::plan_inputs(p.query, p.dims, p.eden_mean, p.mid_mean, s_qb, *s_pb);
+
     // first page in flight before the tables are read
     const uint32_t W = G * kWarps, gw = (uint32_t)warp * G + blockIdx.x, dyn0 = 2 * W;
     uint32_t b = gw, bn = gw + W;
@@ -665,15 +672,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     if (tid == 0) { s_cta_tau = 0ull; s_seed_min = 0xFFFFFFFFu; s_seed_cnt = 0u; s_nflag = 0u; }
     const DevPlan* plan = p.plan;
     if (FUSED) {
-        // QueryPipeline::build_plan fused into the scan (src/pipeline.rs:63-74): warps 0-3 of every
-        // CTA build the plan while the first pages are in flight; no CTA waits on another.
-        DevPlan* ps = reinterpret_cast<DevPlan*>(s_dyn);
-        float* s_qb = reinterpret_cast<float*>(s_dyn + align16(sizeof(DevPlan)));
-        planb::PlanShared* s_pb = reinterpret_cast<planb::PlanShared*>(
-            s_dyn + align16(sizeof(DevPlan)) + align16((size_t)p.dims * sizeof(float)));
-        if (tid < planb::kPlanThreads)
-            planb::build_plan(p.query, p.dims, p.prefix_codec, p.mid_codec, p.eden_mean, p.eden_seed, p.mid_mean,
-                              p.mid_seed, ps, s_qb, *s_pb);
+        // QueryPipeline::build_plan fused into the scan (src/pipeline.rs:63-74): every CTA builds the
+        // plan in shared memory while its first pages are in flight; no CTA waits on another.
+        // CTA 0 stores the complete plan; the others build only what this mode scans with
+        const uint32_t need = blockIdx.x == 0 && p.plan_out
+                                  ? planb::kNeedAll
+                                  : (MODE == MRL_MODE_FAST ? planb::kNeedFast | (p.depth == MRL_DEPTH_L0 ? planb::kNeedL0 : 0u)
+                                                           : planb::kNeedExact);
+        planb::build_plan(p.dims, p.prefix_codec, p.mid_codec, p.eden_seed, p.mid_seed, ps, s_qb, *s_pb, need);
         __syncthreads();
         if (blockIdx.x == 0 && p.plan_out) {  // keep the plan for mrl_plan_read and later scans
             const uint4* src = reinterpret_cast<const uint4*>(ps);
