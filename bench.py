@@ -392,7 +392,7 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     for sg in segs:
         sg.free()
     lib.mrl_plans_free(dev.ptr, plans)
@@ -473,10 +473,25 @@ def run_reference(args):
                                    f"(oracle restatement of scan_blocks, Rayon-rule sharding over {threads} threads)"},
         "e2e": {"value": val, "unit": "QPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_RESULT_OUT = None
+
+
+def emit(line):
+    """Write the result line to the original stdout (the only thing printed there)."""
+    out = _RESULT_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 
 
 def main():
+    global _RESULT_OUT
+    # Keep stdout for the one JSON line: anything else written to fd 1 (library banners such as
+    # NCCL's version line) goes to stderr.
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     args = parse()
     if args.impl == "reference":
         run_reference(args)
