@@ -56,6 +56,9 @@ def parse():
                     help="keep the scanned pages out of L2 by rotating over segments whose total exceeds L2 "
                          "(code stays cached, as in a serving loop) or by flushing L2 before every step")
     ap.add_argument("--segments", type=int, default=4, help="segments rotated over with --l2 rotate")
+    ap.add_argument("--exchange", choices=["nvlink", "nccl"], default="nvlink",
+                    help="N > 1: merge per-rank top-k records inside the scan launch over NVLink peer memory, "
+                         "or all-gather them with NCCL and merge with a second kernel")
     return ap.parse_args()
 
 
@@ -206,28 +209,40 @@ def run_ours(args):
     out_cnt = torch.empty(1, dtype=torch.int32, device="cuda")
     out_st = torch.zeros(args.steps + warm, dtype=torch.int32, device="cuda")
     flush = torch.zeros(128 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 512 MiB
-    exch = M.ShardExchange(dev, k) if world > 1 else None  # NCCL all-gather + mrl_merge_topk
-    if exch is not None:  # the scan writes straight into this rank's exchange record
+    exch = peer = None
+    if world > 1 and args.exchange == "nccl":
+        exch = M.ShardExchange(dev, k)  # NCCL all-gather + mrl_merge_topk
         out_ids, out_sc, out_cnt = exch.ids.view(1, k), exch.scores.view(1, k), exch.count
+    elif world > 1:
+        peer = M.PeerExchange(dev, k)  # records merged over NVLink inside the scan launch
     qbytes = dims * 4
 
     def one_step(i, ev, cold=True):
-        """One query: plan build + scan + top-256 in one fused launch (mrl_query_scan_device), then
-        on N > 1 the exchange. Events: step start, [after the scan when N > 1], step end. `cold`:
-        keep this step's pages out of L2 (segment rotation or flush); otherwise segment 0 again."""
+        """One query: plan build + scan + top-256 in one fused launch (mrl_query_scan_device, or
+        mrl_query_scan_exchange on N > 1), then with --exchange nccl the exchange. Events (when
+        `ev` is given): step start, [after the scan with --exchange nccl], step end. `cold`: keep
+        this step's pages out of L2 (segment rotation or flush); otherwise segment 0 again."""
         seg = segs[i % len(segs)] if cold else segs[0]
         if cold and args.l2 == "flush":
             flush.add_(1.0)  # reads and writes 512 MiB: evicts the corpus from L2
-        ev[0].record()
-        M._capi.check(dev.ptr, lib.mrl_query_scan_device(dev.ptr, seg.ptr, C.c_void_p(qd.data_ptr() + i * qbytes), 1,
-                                                         dims, C.byref(desc), plans, C.byref(cfg), None, None,
-                                                         C.c_void_p(out_ids.data_ptr()), C.c_void_p(out_sc.data_ptr()),
-                                                         C.c_void_p(out_cnt.data_ptr()),
-                                                         C.c_void_p(out_st.data_ptr() + 4 * i)))
+        if ev is not None:
+            ev[0].record()
+        if peer is not None:  # global top-k from the one launch
+            peer.scan(seg, qd.data_ptr() + i * qbytes, dims, desc, plans, cfg, out_ids.data_ptr(), out_sc.data_ptr(),
+                      out_cnt.data_ptr(), out_st.data_ptr() + 4 * i)
+        else:
+            M._capi.check(dev.ptr, lib.mrl_query_scan_device(dev.ptr, seg.ptr, C.c_void_p(qd.data_ptr() + i * qbytes),
+                                                             1, dims, C.byref(desc), plans, C.byref(cfg), None, None,
+                                                             C.c_void_p(out_ids.data_ptr()),
+                                                             C.c_void_p(out_sc.data_ptr()),
+                                                             C.c_void_p(out_cnt.data_ptr()),
+                                                             C.c_void_p(out_st.data_ptr() + 4 * i)))
         if exch is not None:
-            ev[2].record()
+            if ev is not None:
+                ev[2].record()
             exch()  # global top-k on every rank
-        ev[1].record()
+        if ev is not None:
+            ev[1].record()
 
     def split_step(i, ev):
         """The same query with the plan kernel and the scan kernel launched separately (for the
@@ -253,19 +268,52 @@ def run_ours(args):
     clocks = Clocks(local)
     clocks.start()
     time.sleep(0.3)
-    evs = [mk() for _ in range(args.steps)]
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        one_step(warm + i, evs[i])
-    torch.cuda.synchronize()
-    t1 = time.perf_counter()
+    if args.l2 == "rotate":
+        # nothing runs between steps, so one event pair brackets all K steps
+        ev_all = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        t0 = time.perf_counter()
+        ev_all[0].record()
+        for i in range(args.steps):
+            one_step(warm + i, None)
+        ev_all[1].record()
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        total_ms = ev_all[0].elapsed_time(ev_all[1])
+    else:
+        # per-step events exclude the flush between steps
+        evs = [mk() for _ in range(args.steps)]
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            one_step(warm + i, evs[i])
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        total_ms = float(sum(e[0].elapsed_time(e[1]) for e in evs))
     if world > 1:
         dist.barrier()
     time.sleep(0.2)
     clk = clocks.stop()
-    # for information: the same steps without the L2 flush (corpus resident in the 126 MB L2), and
-    # the plan and scan kernels launched separately
+    # for information (not timed): how fast the host enqueues steps compared with the device
+    n_enq = min(300, args.steps)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev_enq = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    h0 = time.perf_counter()
+    ev_enq[0].record()
+    for i in range(n_enq):
+        one_step(warm + i, None)
+    ev_enq[1].record()
+    h1 = time.perf_counter()
+    torch.cuda.synchronize()
+    host_enqueue_us = (h1 - h0) / n_enq * 1e6
+    device_us = ev_enq[0].elapsed_time(ev_enq[1]) / n_enq * 1e3
+    # per-step events over more cold steps (distribution, and the
+    # scan alone with --exchange nccl), the same steps on an L2-resident segment, and the plan and
+    # scan kernels launched separately
+    evd = [mk() for _ in range(min(500, args.steps))]
+    for i in range(len(evd)):
+        one_step(warm + i, evd[i])
     evr = [mk() for _ in range(min(200, args.steps))]
     for i in range(len(evr)):
         one_step(warm + i, evr[i], cold=False)
@@ -273,12 +321,10 @@ def run_ours(args):
     for i in range(len(evs2)):
         split_step(warm + i, evs2[i])
     torch.cuda.synchronize()
-    step_l2_ms = np.array([e[0].elapsed_time(e[2] if world > 1 else e[1]) for e in evr])
+    step_l2_ms = np.array([e[0].elapsed_time(e[2] if exch is not None else e[1]) for e in evr])
     split_plan_ms = np.array([e[0].elapsed_time(e[2]) for e in evs2])
     split_scan_ms = np.array([e[2].elapsed_time(e[1]) for e in evs2])
-    step_ms = np.array([e[0].elapsed_time(e[1]) for e in evs])
-    scan_ms = np.array([e[0].elapsed_time(e[2] if world > 1 else e[1]) for e in evs])  # the fused kernel
-    total_ms = float(step_ms.sum())
+    scan_ms = np.array([e[0].elapsed_time(e[2] if exch is not None else e[1]) for e in evd])  # the scan launch
     if world > 1:
         t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -330,13 +376,18 @@ def run_ours(args):
             dist.barrier()
             s = time.perf_counter()
             q_dev.copy_(qh[i % n_q], non_blocking=True)
-            M._capi.check(dev.ptr, lib.mrl_query_scan_device(dev.ptr, segs[i % len(segs)].ptr,
-                                                             C.c_void_p(q_dev.data_ptr()), 1, dims,
-                                                             C.byref(desc), plans, C.byref(cfg), None, None,
-                                                             C.c_void_p(out_ids.data_ptr()),
-                                                             C.c_void_p(out_sc.data_ptr()),
-                                                             C.c_void_p(out_cnt.data_ptr()), None))
-            g_ids, g_sc, g_cnt = exch()
+            if peer is not None:
+                peer.scan(segs[i % len(segs)], q_dev.data_ptr(), dims, desc, plans, cfg, out_ids.data_ptr(),
+                          out_sc.data_ptr(), out_cnt.data_ptr())
+                g_ids, g_sc, g_cnt = out_ids.view(-1), out_sc.view(-1), out_cnt.view(-1)
+            else:
+                M._capi.check(dev.ptr, lib.mrl_query_scan_device(dev.ptr, segs[i % len(segs)].ptr,
+                                                                 C.c_void_p(q_dev.data_ptr()), 1, dims,
+                                                                 C.byref(desc), plans, C.byref(cfg), None, None,
+                                                                 C.c_void_p(out_ids.data_ptr()),
+                                                                 C.c_void_p(out_sc.data_ptr()),
+                                                                 C.c_void_p(out_cnt.data_ptr()), None))
+                g_ids, g_sc, g_cnt = exch()
             ids_h.copy_(g_ids, non_blocking=True)
             sc_h.copy_(g_sc, non_blocking=True)
             cnt_h.copy_(g_cnt, non_blocking=True)
@@ -347,13 +398,16 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e = {"value": world * e2e_steps / float(t.item()), "unit": "QPS", "h2d_bytes_per_step": qbytes,
                "d2h_bytes_per_step": k * 12 + 4, "steps": e2e_steps,
-               "path": "per rank: query copy from pinned host memory + mrl_query_scan_device (fused plan + scan) + "
-                       "NCCL all-gather + mrl_merge_topk + copy of the merged top-k to pinned host memory; max "
-                       "over ranks"}
+               "path": ("per rank: query copy from pinned host memory + mrl_query_scan_exchange (fused plan + scan "
+                        "+ NVLink merge, one launch)" if peer is not None else
+                        "per rank: query copy from pinned host memory + mrl_query_scan_device (fused plan + scan) + "
+                        "NCCL all-gather + mrl_merge_topk") + " + copy of the merged top-k to pinned host memory; "
+                       "max over ranks"}
 
     peak, peak_kind = measured_peaks()
     alg_bytes = nb * 4096
-    scan_avg_s = float(scan_ms.mean()) / 1e3
+    # the dominant kernel's mean duration: the timed per-step time when the step is that one launch
+    scan_avg_s = (total_ms / args.steps if exch is None else float(scan_ms.mean())) / 1e3
     achieved = alg_bytes / scan_avg_s / 1e9
     line = {
         "metric": METRIC,
@@ -368,14 +422,19 @@ def run_ours(args):
                                " shortlist 256, full_64b", "docs_per_gpu": n, "dims": dims, "batch": 1,
                    "shortlist": k, "mode": args.mode, "parallelism": f"shard{world}",
                    "value_counts": "one query scanned over one rank's 1M-doc shard (weak scaling: each step is one"
-                                   " query over world x 1M docs, merged to a global top-256 by NCCL all-gather +"
-                                   " mrl_merge_topk)",
+                                   " query over world x 1M docs, merged to a global top-256)",
+                   "exchange": (None if world == 1 else "records merged inside the scan launch over NVLink peer "
+                                "memory (mrl_query_scan_exchange)" if peer is not None else
+                                "NCCL all-gather of records + mrl_merge_topk"),
                    "l2": (f"inputs larger than L2: steps rotate over {len(segs)} segments of the same shape "
                           f"({len(segs) * nb * 4096 / 1e6:.0f} MB of pages vs the 126 MB L2), so each step's pages "
                           "come from HBM while the kernel code stays cached" if args.l2 == "rotate" else
                           "flushed before every step (read+write of a 512 MiB buffer, outside the per-step events)"),
                    "wall_s_bracketed": t1 - t0,
                    "step_kernels": "one fused launch per query (plan build in every CTA + scan + top-256)",
+                   "host_enqueue_us_per_step": host_enqueue_us, "device_us_per_step_same_pass": device_us,
+                   "timing": ("one CUDA event pair around the K timed steps (nothing runs between steps)"
+                              if args.l2 == "rotate" else "per-step CUDA events, flush excluded"),
                    "scan_ms_mean": float(scan_ms.mean()), "scan_ms_p50": float(np.median(scan_ms)),
                    "scan_ms_p99": float(np.percentile(scan_ms, 99)), "reselection_steps": n_fallback,
                    "scan_ms_mean_l2_resident": float(step_l2_ms.mean()),
@@ -384,7 +443,7 @@ def run_ours(args):
                      "peak_kind": peak_kind, "traffic": profiled_traffic(args.mode),
                      "kernel": "scan_kernel", "alg_bytes_per_launch": alg_bytes},
         "clocks": clk,
-        "gpu_launches": (1 if world == 1 else 2) * args.steps,
+        "gpu_launches": (2 if exch is not None else 1) * args.steps,
         "e2e": e2e,
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -393,6 +452,8 @@ def run_ours(args):
         dist.barrier()
     if rank == 0:
         emit(line)
+    if peer is not None:
+        peer.close()  # barrier first: peers write into this rank's area
     for sg in segs:
         sg.free()
     lib.mrl_plans_free(dev.ptr, plans)

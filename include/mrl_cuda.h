@@ -187,6 +187,33 @@ int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint3
                    const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg,
                    const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* out_ids,
                    float* out_scores, uint32_t* out_counts);
+/* ---- NVLink exchange: the sharded scan's merge inside the scan launch --------------------- */
+/* One exchange per rank (one process per GPU of a node, up to 8). Each rank's scan leaves its
+ * top-k record (layout below) in its own exchange area and raises a flag there; the last CTA to
+ * finish waits (bounded, about 2 s) until every other rank's flag for the same query is up,
+ * reads their records over NVLink (peer loads) and merges them, so every rank ends with the
+ * global top-k from one launch, with no collective library call on the query path. Replaces the
+ * merge of per-shard shortlists in scan_blocks_stats (src/scan.rs:866-870) across GPUs. Set-up:
+ * mrl_exchange_create on every rank (it fills `ipc_handle`, 64 bytes, when world > 1),
+ * all-gather the handles (ordered by rank) by any means, then mrl_exchange_open. Every rank must
+ * then call mrl_query_scan_exchange for the same sequence of queries. Records are double-buffered
+ * by query parity, so no rank overwrites a record another rank may still read. world x
+ * MRL_MERGE_RECORD_BYTES(k) must not exceed 200 KiB (k <= 2048 at world 8). Destroy only after all
+ * ranks stopped scanning (a barrier). */
+typedef struct mrl_exchange mrl_exchange;
+int mrl_exchange_create(mrl_ctx* ctx, uint32_t world, uint32_t rank, uint32_t k, void* ipc_handle,
+                        mrl_exchange** out);
+int mrl_exchange_open(mrl_ctx* ctx, mrl_exchange* ex, const void* ipc_handles);
+int mrl_exchange_destroy(mrl_ctx* ctx, mrl_exchange* ex);
+/* Fused plan + scan of one device query (as mrl_query_scan_device with n_q = 1) whose outputs are
+ * the GLOBAL top-k over all ranks' segments. cfg->shortlist_cand must equal the exchange's k.
+ * out_status: bit 0 = re-selection ran, bit 1 = grid barrier timed out, bit 2 = a rank's record
+ * did not arrive in time (no result). */
+int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_query, uint32_t dims,
+                            const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg,
+                            const uint32_t* time_lo, const uint32_t* time_hi, mrl_exchange* ex,
+                            uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_count,
+                            uint32_t* d_out_status);
 /* Exchange step of the sharded scan. An exchange record holds one rank's top list: `stride` u64
  * ids, then `stride` f32 scores, then the u32 count of valid entries, padded to
  * MRL_MERGE_RECORD_BYTES(stride) bytes (a multiple of 16). mrl_scan_device fills one when its

@@ -64,6 +64,19 @@ struct mrl_plans {
     uint32_t dims = 0;
 };
 
+// NVLink exchange: this rank's area on this GPU (its record for both buffer parities, then one
+// flag word per parity) and the mapped areas of the other ranks of the node.
+struct mrl_exchange {
+    int device = 0;
+    uint32_t world = 0, rank = 0, k = 0;
+    size_t rb = 0;                               // bytes per record
+    unsigned char* local = nullptr;              // this rank's area (cudaMalloc)
+    unsigned char* area[mrl::kMaxRanks] = {};    // every rank's area (area[rank] == local)
+    uint32_t epoch = 0;
+    bool opened = false;
+    size_t bytes() const { return 2 * rb + 16; }
+};
+
 namespace {
 
 int fail(mrl_ctx* ctx, int code, const std::string& msg) {
@@ -601,6 +614,119 @@ int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint3
         if (cs[n_q + q] & 2u) return fail(ctx, MRL_ERR_CUDA, "scan grid barrier timed out (CTAs not co-resident)");
         out_counts[q] = cs[q];
     }
+    return MRL_OK;
+}
+
+int mrl_exchange_create(mrl_ctx* ctx, uint32_t world, uint32_t rank, uint32_t k, void* ipc_handle,
+                        mrl_exchange** out) {
+    if (!ctx || !out) return MRL_ERR_INVALID;
+    *out = nullptr;
+    if (world < 1 || world > (uint32_t)mrl::kMaxRanks) return fail(ctx, MRL_ERR_INVALID, "world must be in [1, 8]");
+    if (rank >= world) return fail(ctx, MRL_ERR_INVALID, "rank must be < world");
+    if (k < 1 || k > 4096) return fail(ctx, MRL_ERR_INVALID, "k must be in [1, 4096]");
+    if (world > 1 && !ipc_handle) return fail(ctx, MRL_ERR_INVALID, "ipc_handle is NULL");
+    if (int rc = set_device(ctx)) return rc;
+    mrl_exchange* ex = new mrl_exchange();
+    ex->device = ctx->device;
+    ex->world = world;
+    ex->rank = rank;
+    ex->k = k;
+    ex->rb = MRL_MERGE_RECORD_BYTES(k);
+    if (cudaMalloc(&ex->local, ex->bytes()) != cudaSuccess) {
+        delete ex;
+        return fail(ctx, MRL_ERR_NOMEM, "cudaMalloc exchange area");
+    }
+    const cudaError_t e = cudaMemset(ex->local, 0, ex->bytes());
+    if (e != cudaSuccess) { cudaFree(ex->local); delete ex; return cuda_fail(ctx, e, "exchange area memset"); }
+    ex->area[rank] = ex->local;
+    if (world > 1) {
+        cudaIpcMemHandle_t h;
+        const cudaError_t he = cudaIpcGetMemHandle(&h, ex->local);
+        if (he != cudaSuccess) { cudaFree(ex->local); delete ex; return cuda_fail(ctx, he, "cudaIpcGetMemHandle"); }
+        std::memcpy(ipc_handle, &h, sizeof(h));
+    } else {
+        ex->opened = true;
+    }
+    *out = ex;
+    return MRL_OK;
+}
+
+int mrl_exchange_open(mrl_ctx* ctx, mrl_exchange* ex, const void* ipc_handles) {
+    if (!ctx || !ex) return MRL_ERR_INVALID;
+    if (ex->opened) return MRL_OK;
+    if (!ipc_handles) return fail(ctx, MRL_ERR_INVALID, "ipc_handles is NULL");
+    if (int rc = set_device(ctx)) return rc;
+    for (uint32_t r = 0; r < ex->world; ++r) {
+        if (r == ex->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const unsigned char*>(ipc_handles) + (size_t)r * sizeof(h), sizeof(h));
+        void* ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (uint32_t q = 0; q < r; ++q)
+                if (q != ex->rank && ex->area[q]) { cudaIpcCloseMemHandle(ex->area[q]); ex->area[q] = nullptr; }
+            return cuda_fail(ctx, e, "cudaIpcOpenMemHandle (peer exchange area)");
+        }
+        ex->area[r] = static_cast<unsigned char*>(ptr);
+    }
+    ex->opened = true;
+    return MRL_OK;
+}
+
+int mrl_exchange_destroy(mrl_ctx* ctx, mrl_exchange* ex) {
+    if (!ex) return MRL_OK;
+    cudaSetDevice(ex->device);
+    cudaDeviceSynchronize();
+    for (uint32_t r = 0; r < ex->world; ++r)
+        if (r != ex->rank && ex->area[r]) cudaIpcCloseMemHandle(ex->area[r]);
+    cudaFree(ex->local);
+    delete ex;
+    (void)ctx;
+    return MRL_OK;
+}
+
+int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_query, uint32_t dims,
+                            const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg,
+                            const uint32_t* time_lo, const uint32_t* time_hi, mrl_exchange* ex, uint64_t* d_out_ids,
+                            float* d_out_scores, uint32_t* d_out_count, uint32_t* d_out_status) {
+    if (!ctx || !seg || !plans || !ex) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (int rc = check_codec(ctx, codec)) return rc;
+    if (!ex->opened) return fail(ctx, MRL_ERR_INVALID, "exchange not opened");
+    if (ex->device != ctx->device) return fail(ctx, MRL_ERR_INVALID, "exchange belongs to another device");
+    if (cfg->shortlist_cand != ex->k) return fail(ctx, MRL_ERR_INVALID, "shortlist_cand differs from the exchange's k");
+    if ((size_t)ex->world * ex->rb > 200 * 1024)
+        return fail(ctx, MRL_ERR_INVALID, "k x world too large to merge in shared memory; use mrl_merge_topk");
+    if (plans->n_q < 1 || dims != plans->dims) return fail(ctx, MRL_ERR_INVALID, "plan storage too small or dims mismatch");
+    if (!d_query || !d_out_ids || !d_out_scores || !d_out_count) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = ensure_buf(ctx, (void**)&ctx->owner, &ctx->owner_bytes, seg->n_blocks ? seg->n_blocks : 1)) return rc;
+    float* d_means = nullptr;
+    if (int rc = upload_means(ctx, codec, &d_means)) return rc;
+    mrl::ScanLaunch p = make_launch(ctx, seg, plans, 0, cfg, time_lo, time_hi);
+    p.out_ids = d_out_ids;
+    p.out_scores = d_out_scores;
+    p.out_count = d_out_count;
+    p.out_status = d_out_status;
+    p.query = d_query;
+    p.dims = dims;
+    p.prefix_codec = codec->prefix_codec;
+    p.mid_codec = codec->mid_codec;
+    p.eden_mean = d_means;
+    p.eden_seed = codec->eden_seed;
+    p.mid_mean = codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr;
+    p.mid_seed = codec->mid_seed;
+    p.plan_out = plans->d;
+    const uint32_t epoch = ++ex->epoch;
+    const size_t parity = epoch & 1u;
+    p.xch_world = ex->world;
+    p.xch_rank = ex->rank;
+    p.xch_epoch = epoch;
+    for (uint32_t w = 0; w < ex->world; ++w) {
+        p.xch_rec[w] = ex->area[w] + parity * ex->rb;
+        p.xch_flag[w] = reinterpret_cast<unsigned*>(ex->area[w] + 2 * ex->rb) + parity;
+    }
+    if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     return MRL_OK;
 }
 

@@ -161,6 +161,8 @@ int launch_synth_queries(uint64_t doc_seed, uint64_t n_docs, uint64_t q_seed, ui
                          uint32_t dims, float sigma, float* d_out, uint64_t* d_pick,
                          cudaStream_t stream);
 
+constexpr int kMaxRanks = 8;  // NVLink exchange: ranks of one node
+
 struct ScanLaunch {
     const uint4* pages;
     const uint2* block_ts;
@@ -177,7 +179,7 @@ struct ScanLaunch {
     // scratch (owned by the context; zero-initialised once, left zeroed by every launch)
     unsigned long long* cta_keys;  // ctas * 32: each CTA's exact top-list_len keys
     unsigned int* ctl;             // [0] page counter, [1] barrier count, [2] barrier generation,
-                                   // [5] barrier timeout; the others are reserved
+                                   // [5] barrier timeout, [6] CTAs done (exchange); others reserved
     uint8_t* owner;                // n_blocks: CTA that scored each page
     uint64_t* out_ids;
     float* out_scores;
@@ -191,9 +193,16 @@ struct ScanLaunch {
     const float* mid_mean;
     uint64_t eden_seed, mid_seed;
     DevPlan* plan_out;
+    // NVLink exchange (xch_world > 0): each rank's top-k record of this query stays in its own
+    // exchange area (buffer parity xch_epoch & 1); the last CTA completes this rank's record,
+    // raises its flag (release, system scope), waits (bounded) for every other rank's flag of
+    // this epoch, reads their records over NVLink and merges all into out_* (the global top-k)
+    uint32_t xch_world, xch_rank, xch_epoch;
+    const unsigned char* xch_rec[kMaxRanks];  // every rank's record of this parity
+    unsigned int* xch_flag[kMaxRanks];        // every rank's flag word of this parity
 };
 int scan_ctas(int device_sms);
-size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims);
+size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t xch_world);
 int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream);
 int launch_merge_topk(const void* d_lists, uint32_t n_lists, uint32_t stride, uint32_t k, uint64_t* d_out_ids,
                       float* d_out_scores, uint32_t* d_out_count, cudaStream_t stream);

@@ -34,7 +34,9 @@
 // the selection by radix select + bitonic sort, so the result is exact for every input (status
 // bit 0 reports it).
 #include <algorithm>
+#include <atomic>
 
+#include "exchange.cuh"
 #include "plan_build.cuh"
 
 namespace mrl {
@@ -615,6 +617,53 @@ __device__ __forceinline__ unsigned count_greater(const u64* lst, unsigned n, u6
     return lo;
 }
 
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Last step of the NVLink exchange, by the one CTA after this rank's record is complete in its own
+// area: raise this rank's flag (the release makes the record visible to the other GPUs), wait
+// (bounded, ~2 s) for every other rank's flag of this epoch, copy all records into shared memory
+// (`smem`, at least xch_world records; the others' over NVLink) and merge them into the
+// outputs. Status bit 2 reports a timeout.
+__device__ void xch_publish_and_merge(const ScanLaunch& p, unsigned char* smem, int* s_ok, unsigned status) {
+    const int tid = threadIdx.x;
+    const size_t rb = MRL_MERGE_RECORD_BYTES(p.k), words = rb / 16;
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        st_release_sys(p.xch_flag[p.xch_rank], p.xch_epoch);
+        int ok = 1;
+        for (unsigned r = 0; r < p.xch_world && ok; ++r) {
+            if (r == p.xch_rank) continue;
+            unsigned it = 0;
+            while (ld_acquire_sys(p.xch_flag[r]) != p.xch_epoch) {
+                if (++it > (1u << 22)) { ok = 0; break; }
+                if (it > 64) __nanosleep(256);
+            }
+        }
+        *s_ok = ok;
+    }
+    __syncthreads();
+    if (!*s_ok) {
+        if (tid == 0 && p.out_status) *p.out_status = status | 4u;  // a rank's record never arrived
+        return;
+    }
+    for (unsigned r = 0; r < p.xch_world; ++r) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.xch_rec[r]);
+        uint4* dst = reinterpret_cast<uint4*>(smem + r * rb);
+        for (size_t i = tid; i < words; i += kThreads) dst[i] = __ldcg(src + i);
+    }
+    __syncthreads();
+    xch::merge_records<false>(smem, p.xch_world, p.k, p.k, p.out_ids, p.out_scores, p.out_count);
+    if (tid == 0 && p.out_status) *p.out_status = status;
+}
+
 __device__ __forceinline__ u64 shfl_xor_u64(u64 v, int o) {
     const unsigned lo = __shfl_xor_sync(kFull, (unsigned)v, o), hi = __shfl_xor_sync(kFull, (unsigned)(v >> 32), o);
     return ((u64)hi << 32) | lo;
@@ -637,6 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     __shared__ u64 s_red64[kWarps];
     __shared__ unsigned s_red32[kWarps];
     __shared__ unsigned s_nflag;
+    __shared__ unsigned s_last;
     __shared__ int s_ok;
     __shared__ SelState s_sel;
     __shared__ unsigned s_misc[4];
@@ -813,6 +863,37 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     for (int w = 0; w < kWarps; ++w) rank_xmax += s_red32[w];
     const bool clean = x_max == 0ull || rank_xmax >= p.k;
 
+    if (clean && p.xch_world) {
+        // this rank's top-k into its record in every rank's area (peer stores over NVLink)
+        const size_t kk = p.k;
+        if ((unsigned)tid < L) {
+            const u64 key = mine[tid];
+            unsigned r = 0;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) r += s_part[w * 32 + tid];
+            if (key != 0ull && r < p.k) {  // into this rank's own record (local memory)
+                const uint32_t ord = key_ordinal(key);
+                unsigned char* rec = const_cast<unsigned char*>(p.xch_rec[p.xch_rank]);
+                reinterpret_cast<uint64_t*>(rec)[r] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
+                reinterpret_cast<float*>(rec + kk * 8)[r] = key_score(key);
+            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            s_last = atomicAdd(p.ctl + 6, 1u) == G - 1 ? 1u : 0u;
+        }
+        __syncthreads();
+        if (!s_last) return;
+        // the last CTA: every CTA's entries are in; add the count, then publish
+        __threadfence();
+        if (tid == 0) {
+            atomicExch(p.ctl + 6, 0u);  // ready for the next launch
+            *reinterpret_cast<uint32_t*>(const_cast<unsigned char*>(p.xch_rec[p.xch_rank]) + kk * 12) = min(total, p.k);
+        }
+        xch_publish_and_merge(p, s_dyn, &s_ok, 0u);
+        return;
+    }
     if (clean) {
         // keys ranked below k are the top-k: each CTA writes its own in place
         if ((unsigned)tid < L) {
@@ -845,6 +926,17 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
         if (lane == 0 && r < p.k) s_flags[atomicAdd(&s_nflag, 1u)] = c;
     }
     __syncthreads();
+    if (p.xch_world) {
+        // exchange: reselect into this rank's own record, copy it to the other ranks, signal, merge
+        ScanLaunch own = p;
+        unsigned char* mine_rec = const_cast<unsigned char*>(p.xch_rec[p.xch_rank]);
+        own.out_ids = reinterpret_cast<uint64_t*>(mine_rec);
+        own.out_scores = reinterpret_cast<float*>(mine_rec + (size_t)p.k * 8);
+        own.out_count = reinterpret_cast<uint32_t*>(mine_rec + (size_t)p.k * 12);
+        reselect<MODE>(own, s_tab, s_rho, S, s_cand, s_gath, s_hist, s_flags, s_nflag, &s_sel, s_misc);
+        xch_publish_and_merge(p, s_dyn, &s_ok, 1u);
+        return;
+    }
     reselect<MODE>(p, s_tab, s_rho, S, s_cand, s_gath, s_hist, s_flags, s_nflag, &s_sel, s_misc);
     if (tid == 0 && p.out_status) *p.out_status = 1u;
 }
@@ -880,23 +972,33 @@ __global__ void __launch_bounds__(kThreads) debug_scores_kernel(const ScanLaunch
 
 int scan_ctas(int device_sms) { return device_sms; }
 
-size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims) {
+size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t xch_world) {
     size_t p2 = 1;
     while (p2 < k) p2 <<= 1;
-    const size_t sel = sizeof(u64) * (kWarps * kQueue + kWarps * 32 + (size_t)ctas * 33 + p2) +
-                       sizeof(unsigned) * (kBins + ctas);
-    return fused_dims ? std::max(sel, fused_plan_bytes(fused_dims)) : sel;
+    size_t bytes = sizeof(u64) * (kWarps * kQueue + kWarps * 32 + (size_t)ctas * 33 + p2) +
+                   sizeof(unsigned) * (kBins + ctas);
+    if (fused_dims) bytes = std::max(bytes, fused_plan_bytes(fused_dims));
+    if (xch_world) bytes = std::max(bytes, (size_t)xch_world * MRL_MERGE_RECORD_BYTES(k));  // records to merge
+    return bytes;
 }
 
 // Cooperative launch: one CTA per SM, all co-resident (the grid barrier relies on it).
 int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream) {
     const bool fused = p.query != nullptr;
-    const size_t smem = scan_smem_bytes(ctas, p.k, fused ? p.dims : 0u);
+    const size_t smem = scan_smem_bytes(ctas, p.k, fused ? p.dims : 0u, p.xch_world);
     const void* fn = p.mode == MRL_MODE_FAST ? (fused ? (const void*)scan_kernel<MRL_MODE_FAST, true>
                                                       : (const void*)scan_kernel<MRL_MODE_FAST, false>)
                                              : (fused ? (const void*)scan_kernel<MRL_MODE_EXACT, true>
                                                       : (const void*)scan_kernel<MRL_MODE_EXACT, false>);
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -1;
+    // the attribute is per function and device: set it only when a launch needs more than before
+    static std::atomic<size_t> set_bytes[64][4];
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return -1;
+    std::atomic<size_t>& cur = set_bytes[device & 63][(p.mode == MRL_MODE_FAST ? 0 : 2) + (fused ? 1 : 0)];
+    if (smem > cur.load(std::memory_order_relaxed)) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -1;
+        cur.store(smem, std::memory_order_relaxed);
+    }
     ScanLaunch arg = p;
     void* args[] = {&arg};
     if (cudaLaunchCooperativeKernel(fn, dim3(ctas), dim3(kThreads), args, smem, stream) != cudaSuccess) return -1;

@@ -32,6 +32,7 @@ from .api import (  # noqa: F401
     vector_scores,
 )
 from .shard import (  # noqa: F401
+    PeerExchange,
     ShardExchange,
     merge_topk_host,
     pack_records,

@@ -92,6 +92,11 @@ SIGNATURES = {
                                    _vp, _vp, _vp, _vp]),
     "mrl_query_scan": (_i, [_vp, _vp, _vp, _u32, _u32, C.POINTER(CodecDesc), _vp, C.POINTER(ScanCfgC), _vp, _vp, _vp,
                             _vp, _vp]),
+    "mrl_exchange_create": (_i, [_vp, _u32, _u32, _u32, _vp, C.POINTER(_vp)]),
+    "mrl_exchange_open": (_i, [_vp, _vp, _vp]),
+    "mrl_exchange_destroy": (_i, [_vp, _vp]),
+    "mrl_query_scan_exchange": (_i, [_vp, _vp, _vp, _u32, C.POINTER(CodecDesc), _vp, C.POINTER(ScanCfgC), _vp, _vp,
+                                     _vp, _vp, _vp, _vp, _vp]),
     "mrl_merge_topk": (_i, [_vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp]),
     "mrl_scan_device_static": (_i, [_vp, _vp, _vp, _u32, _u32, C.POINTER(ScanCfgC), _vp, _vp, _vp, _vp, _vp, _vp]),
     "mrl_debug_vector_scores": (_i, [_vp, _vp, _vp, _u32, C.POINTER(ScanCfgC), _vp, _vp, _vp, _vp, _vp]),

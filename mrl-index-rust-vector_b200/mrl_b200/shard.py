@@ -8,7 +8,10 @@ shortlists at the end of `scan_blocks_stats` (src/scan.rs:866-870) at GPU granul
     all-gathers the records with torch.distributed (one NCCL collective over NVLink) and merges
     them with the library's `mrl_merge_topk` kernel, so every rank ends with the global top-k;
   * on the host: `merge_topk_host` merges lists that are already in host memory (for example the
-    outputs of `mrl_scan`) with the same order.
+    outputs of `mrl_scan`) with the same order;
+  * inside the scan launch: `PeerExchange` (mrl_exchange_*) has every rank's scan write its record
+    into all ranks' receive areas over NVLink and merge there, one launch per query and no
+    collective call on the query path.
 Order everywhere: score descending, then id (VectorId::as_u64) ascending.
 """
 from __future__ import annotations
@@ -106,3 +109,45 @@ class ShardExchange:
                                                C.c_void_p(self.top_scores.data_ptr()),
                                                C.c_void_p(self.top_count.data_ptr())))
         return self.top_ids, self.top_scores, self.top_count
+
+
+class PeerExchange:
+    """NVLink exchange (mrl_exchange_*): after set-up, `scan(...)` runs the fused plan + scan +
+    global merge of one query in a single launch on every rank. Set-up exchanges the receive
+    areas' IPC handles with torch.distributed (any backend); all ranks must then scan the same
+    sequence of queries. `close()` barriers before freeing, since peers write into this area."""
+
+    def __init__(self, dev, k: int, group=None):
+        import torch.distributed as dist
+
+        self.dev, self.k, self.group = dev, int(k), group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        lib = dev.lib
+        handle = (C.c_ubyte * 64)()
+        self.ptr = C.c_void_p()
+        check(dev.ptr, lib.mrl_exchange_create(dev.ptr, self.world, self.rank, self.k, C.cast(handle, C.c_void_p),
+                                               C.byref(self.ptr)))
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, bytes(handle), group=group)
+        allh = (C.c_ubyte * (64 * self.world)).from_buffer_copy(b"".join(gathered))
+        check(dev.ptr, lib.mrl_exchange_open(dev.ptr, self.ptr, C.cast(allh, C.c_void_p)))
+
+    def scan(self, segment, d_query: int, dims: int, desc, plans, cfg_c, d_ids: int, d_scores: int, d_count: int,
+             d_status: int = 0, time_lo=None, time_hi=None):
+        """Fused plan + scan of the device query at `d_query`; the device outputs receive the
+        global top-k over all ranks' segments (asynchronous on the context stream)."""
+        lo = None if time_lo is None else C.byref(C.c_uint32(int(time_lo)))
+        hi = None if time_hi is None else C.byref(C.c_uint32(int(time_hi)))
+        check(self.dev.ptr, self.dev.lib.mrl_query_scan_exchange(
+            self.dev.ptr, segment.ptr, C.c_void_p(d_query), dims, C.byref(desc), plans, C.byref(cfg_c), lo, hi,
+            self.ptr, C.c_void_p(d_ids), C.c_void_p(d_scores), C.c_void_p(d_count),
+            C.c_void_p(d_status) if d_status else None))
+
+    def close(self):
+        import torch.distributed as dist
+
+        if self.ptr:
+            dist.barrier(group=self.group)
+            self.dev.lib.mrl_exchange_destroy(self.dev.ptr, self.ptr)
+            self.ptr = C.c_void_p()

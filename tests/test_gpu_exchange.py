@@ -1,0 +1,150 @@
+"""The NVLink exchange (mrl_exchange_*, mrl_query_scan_exchange): the merge of per-rank top-k
+records inside the scan launch.
+
+On one GPU an exchange of world 1 must reproduce mrl_query_scan_device exactly, across
+consecutive queries (both buffer parities) and through the rare re-selection path. With two or
+more GPUs, two ranks (one process per GPU, handles exchanged over gloo) scan one half of a corpus
+each, and every rank must end with the global top-k of a single-GPU scan of the whole corpus.
+"""
+import ctypes as C
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def mb():
+    import mrl_b200
+
+    return mrl_b200
+
+
+def _corpus(ora, n=64 * 40 + 17, dims=768, seed=11):
+    docs = ora.synth_docs(seed, n, dims)
+    mean = ora.eden_fit_prefix(docs)
+    blocks = ora.encode_corpus(docs, eden_mean=mean)
+    qs, _ = ora.synth_queries(seed, n, 5, 4, dims)
+    return blocks, mean, qs
+
+
+def _device_outputs(k):
+    import torch
+
+    return (torch.full((k,), -1, dtype=torch.int64, device="cuda"), torch.zeros(k, dtype=torch.float32, device="cuda"),
+            torch.zeros(1, dtype=torch.int32, device="cuda"), torch.zeros(1, dtype=torch.int32, device="cuda"))
+
+
+@pytest.mark.parametrize("mode", ["FAST", "EXACT"])
+@pytest.mark.parametrize("list_len", [0, 1])
+def test_exchange_world1_matches_device_scan(ora, dev, mode, list_len):
+    import torch
+
+    M = mb()
+    lib = dev.lib
+    blocks, mean, qs = _corpus(ora)
+    seg = M.Segment.upload(blocks, dev)
+    k = 256
+    cfg = M.ScanConfig(shortlist_cand=k, mode=getattr(M.ScanMode, mode)).to_c()
+    desc, keep = M.api._codec_desc(M.PrefixCodec.EDEN_PROD, M.MidCodec.RABITQ, M.EdenFit(64, 4, 1, mean), None)
+    plans = C.c_void_p()
+    M._capi.check(dev.ptr, lib.mrl_plans_alloc(dev.ptr, 1, 768, C.byref(plans)))
+    ex = C.c_void_p()
+    M._capi.check(dev.ptr, lib.mrl_exchange_create(dev.ptr, 1, 0, k, None, C.byref(ex)))
+    dq = torch.from_numpy(np.ascontiguousarray(qs, np.float32)).cuda()
+    dev.set_list_len(list_len)
+    try:
+        for qi in range(len(qs)):  # consecutive queries alternate buffer parities
+            a = _device_outputs(k)
+            b = _device_outputs(k)
+            torch.cuda.synchronize()
+            qp = C.c_void_p(dq.data_ptr() + qi * 768 * 4)
+            M._capi.check(dev.ptr, lib.mrl_query_scan_device(dev.ptr, seg.ptr, qp, 1, 768, C.byref(desc), plans,
+                                                             C.byref(cfg), None, None, *[C.c_void_p(t.data_ptr()) for t in a]))
+            M._capi.check(dev.ptr, lib.mrl_query_scan_exchange(dev.ptr, seg.ptr, qp, 768, C.byref(desc), plans,
+                                                               C.byref(cfg), None, None, ex,
+                                                               *[C.c_void_p(t.data_ptr()) for t in b]))
+            torch.cuda.synchronize()
+            n = int(a[2].item())
+            assert int(b[2].item()) == n == k
+            assert int(b[3].item()) & 6 == 0  # no barrier or exchange timeout
+            assert torch.equal(a[0][:n], b[0][:n])
+            assert np.array_equal(a[1][:n].cpu().numpy().view(np.uint32), b[1][:n].cpu().numpy().view(np.uint32))
+            if list_len == 1:
+                assert int(b[3].item()) & 1 == 1  # the re-selection ran
+    finally:
+        dev.set_list_len(0)
+        lib.mrl_exchange_destroy(dev.ptr, ex)
+        lib.mrl_plans_free(dev.ptr, plans)
+        seg.free()
+    del keep
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank_main(rank, world, port, k, mode, list_len):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import mrl_b200 as M
+    import ora
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    dev = M.Device(rank)
+    try:
+        blocks, mean, qs = _corpus(ora)
+        pages = blocks.reshape(-1, 4096)
+        start, count = M.shard_range(pages.shape[0], world, rank)
+        seg = M.Segment.upload(pages[start:start + count].reshape(-1), dev, block_id_base=start)
+        whole = M.Segment.upload(blocks, dev)
+        cfg = M.ScanConfig(shortlist_cand=k, mode=getattr(M.ScanMode, mode)).to_c()
+        desc, keep = M.api._codec_desc(M.PrefixCodec.EDEN_PROD, M.MidCodec.RABITQ, M.EdenFit(64, 4, 1, mean), None)
+        plans = C.c_void_p()
+        M._capi.check(dev.ptr, dev.lib.mrl_plans_alloc(dev.ptr, 1, 768, C.byref(plans)))
+        px = M.PeerExchange(dev, k)
+        dq = torch.from_numpy(np.ascontiguousarray(qs, np.float32)).cuda()
+        dev.set_list_len(list_len)
+        for qi in range(len(qs)):
+            a = _device_outputs(k)
+            b = _device_outputs(k)
+            torch.cuda.synchronize()
+            qp = dq.data_ptr() + qi * 768 * 4
+            px.scan(seg, qp, 768, desc, plans, cfg, *[t.data_ptr() for t in b])
+            M._capi.check(dev.ptr, dev.lib.mrl_query_scan_device(dev.ptr, whole.ptr, C.c_void_p(qp), 1, 768,
+                                                                 C.byref(desc), plans, C.byref(cfg), None, None,
+                                                                 *[C.c_void_p(t.data_ptr()) for t in a]))
+            torch.cuda.synchronize()
+            n = int(a[2].item())
+            assert int(b[2].item()) == n, (rank, qi)
+            assert int(b[3].item()) & 6 == 0, (rank, qi, int(b[3].item()))
+            assert torch.equal(a[0][:n], b[0][:n]), (rank, qi)
+            assert np.array_equal(a[1][:n].cpu().numpy().view(np.uint32), b[1][:n].cpu().numpy().view(np.uint32))
+        dev.set_list_len(0)
+        px.close()
+        del keep
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode,list_len", [("FAST", 0), ("EXACT", 0), ("FAST", 1)])
+def test_exchange_two_ranks_global_topk(mode, list_len):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as tmp
+
+    tmp.spawn(_rank_main, args=(2, _free_port(), 256, mode, list_len), nprocs=2, join=True)
