@@ -190,7 +190,7 @@ int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint3
 /* ---- NVLink exchange: the sharded scan's merge inside the scan launch --------------------- */
 /* One exchange per rank (one process per GPU of a node, up to 8). Each rank's scan leaves its
  * top-k record (layout below) in its own exchange area and raises a flag there; the last CTA to
- * finish waits (bounded, about 2 s) until every other rank's flag for the same query is up,
+ * finish waits (bounded, about 2-3 s) until every other rank's flag for the same query is up,
  * reads their records over NVLink (peer loads) and merges them, so every rank ends with the
  * global top-k from one launch, with no collective library call on the query path. Replaces the
  * merge of per-shard shortlists in scan_blocks_stats (src/scan.rs:866-870) across GPUs. Set-up:

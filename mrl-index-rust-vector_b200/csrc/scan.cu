@@ -628,7 +628,7 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 
 // Last step of the NVLink exchange, by the one CTA after this rank's record is complete in its own
 // area: raise this rank's flag (the release makes the record visible to the other GPUs), wait
-// (bounded, ~2 s) for every other rank's flag of this epoch, copy all records into shared memory
+// (bounded, ~2-3 s) for every other rank's flag of this epoch, copy all records into shared memory
 // (`smem`, at least xch_world records; the others' over NVLink) and merge them into the
 // outputs. Status bit 2 reports a timeout.
 __device__ void xch_publish_and_merge(const ScanLaunch& p, unsigned char* smem, int* s_ok, unsigned status) {
@@ -643,7 +643,7 @@ __device__ void xch_publish_and_merge(const ScanLaunch& p, unsigned char* smem, 
             if (r == p.xch_rank) continue;
             unsigned it = 0;
             while (ld_acquire_sys(p.xch_flag[r]) != p.xch_epoch) {
-                if (++it > (1u << 22)) { ok = 0; break; }
+                if (++it > (1u << 21)) { ok = 0; break; }  // ~2-3 s of remote polls
                 if (it > 64) __nanosleep(256);
             }
         }

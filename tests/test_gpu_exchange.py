@@ -148,3 +148,62 @@ def test_exchange_two_ranks_global_topk(mode, list_len):
     import torch.multiprocessing as tmp
 
     tmp.spawn(_rank_main, args=(2, _free_port(), 256, mode, list_len), nprocs=2, join=True)
+
+
+def _rank_skip_main(rank, world, port, k):
+    """Rank 1 stays alive but skips one query: rank 0's wait for its flag must run out and report
+    status bit 2 without a result; both contexts stay usable and shut down cleanly."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    import mrl_b200 as M
+    import ora
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    dev = M.Device(rank)
+    try:
+        blocks, mean, qs = _corpus(ora)
+        pages = blocks.reshape(-1, 4096)
+        start, count = M.shard_range(pages.shape[0], world, rank)
+        seg = M.Segment.upload(pages[start:start + count].reshape(-1), dev, block_id_base=start)
+        cfg = M.ScanConfig(shortlist_cand=k).to_c()
+        desc, keep = M.api._codec_desc(M.PrefixCodec.EDEN_PROD, M.MidCodec.RABITQ, M.EdenFit(64, 4, 1, mean), None)
+        plans = C.c_void_p()
+        M._capi.check(dev.ptr, dev.lib.mrl_plans_alloc(dev.ptr, 1, 768, C.byref(plans)))
+        px = M.PeerExchange(dev, k)
+        dq = torch.from_numpy(np.ascontiguousarray(qs, np.float32)).cuda()
+        out = _device_outputs(k)
+        torch.cuda.synchronize()
+        px.scan(seg, dq.data_ptr(), 768, desc, plans, cfg, *[t.data_ptr() for t in out])  # both ranks
+        torch.cuda.synchronize()
+        assert int(out[3].item()) & 6 == 0
+        dist.barrier()
+        if rank == 0:  # rank 1 does not take part in this query
+            t0 = time.perf_counter()
+            px.scan(seg, dq.data_ptr() + 768 * 4, 768, desc, plans, cfg, *[t.data_ptr() for t in out])
+            torch.cuda.synchronize()
+            assert int(out[3].item()) & 4, int(out[3].item())  # the wait ran out
+            assert time.perf_counter() - t0 < 30
+            x = torch.ones(4, device="cuda") * 2  # the context still works
+            assert float(x.sum().item()) == 8.0
+        dist.barrier()
+        px.close()
+        del keep
+    finally:
+        dist.destroy_process_group()
+
+
+def test_exchange_missing_rank_times_out():
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as tmp
+
+    tmp.spawn(_rank_skip_main, args=(2, _free_port(), 256), nprocs=2, join=True)
