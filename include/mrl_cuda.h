@@ -112,6 +112,11 @@ int mrl_ctx_set_stream(mrl_ctx* ctx, void* stream);
  * device into the scan layout. `block_id_base` is added to the block index of every hit. */
 int mrl_segment_upload(mrl_ctx* ctx, const uint8_t* blocks, uint64_t n_blocks,
                        uint32_t block_id_base, mrl_seg** out);
+/* SegmentReader::open (src/segment.rs:88-162) into HBM: read a segment file (concatenated
+ * 4096-byte pages, e.g. segments/000001.pax) through pinned, double-buffered staging, so file
+ * reads overlap the copies and the transcode. A size that is not a multiple of 4096 fails with
+ * "corrupt segment size N (not multiple of 4096)" (SegmentError::CorruptSize). Synchronous. */
+int mrl_segment_load(mrl_ctx* ctx, const char* path, uint32_t block_id_base, mrl_seg** out);
 /* SegmentReader::append_live (src/segment.rs:217-232): append one page. */
 int mrl_segment_append(mrl_ctx* ctx, mrl_seg* seg, const uint8_t* block4096);
 int mrl_segment_free(mrl_ctx* ctx, mrl_seg* seg);
@@ -214,6 +219,45 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
                             const uint32_t* time_lo, const uint32_t* time_hi, mrl_exchange* ex,
                             uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_count,
                             uint32_t* d_out_status);
+/* ---- exact inner products: dot (src/embed.rs:115-152), bit-identical ------------------------ */
+/* RingBuffer::search_exact (src/ring.rs:109-119): exact dots of the query against n_pending
+ * unflushed vectors (device rows, n_pending x dims f32), top k written as one exchange record
+ * (layout below, stride k) with ids VectorId(u32::MAX, i).as_u64(), the engine's ring sentinel
+ * (src/engine.rs:584-594). mrl_merge_topk of the scan's record and this one gives the engine's
+ * merged shortlist. Asynchronous on the context stream. n_pending <= 4096. */
+int mrl_ring_search(mrl_ctx* ctx, const float* d_query, const float* d_pending, uint32_t n_pending,
+                    uint32_t dims, uint32_t k, void* d_record);
+/* QueryPipeline::rerank_exact_rows (src/pipeline.rs:157-169): exact dots of the query against
+ * the candidate rows (row ids into d_rows, n_rows x dims f32), all candidates returned sorted by
+ * score descending (equal scores keep candidate order). n_cand <= 4096. Synchronous (an out of
+ * range row id fails with MRL_ERR_INVALID). */
+int mrl_rerank_exact(mrl_ctx* ctx, const float* d_query, const float* d_rows, uint64_t n_rows,
+                     uint32_t dims, const uint64_t* d_cand, uint32_t n_cand, uint64_t* d_out_rows,
+                     float* d_out_scores);
+/* RingBuffer (src/ring.rs:49-119): its pending embeddings mirrored in HBM, rows in push order.
+ * The host keeps the rest of each PendingVector (passage id, timestamp, text). capacity is raised
+ * to 64 (RingBuffer::new) and may not exceed 4096; mrl_ring_push fails when the ring is full
+ * (RingBuffer::push flushes at 64, so an engine never fills it). mrl_ring_push copies one host row
+ * (dims f32) on the context stream; mrl_ring_drain drops the first n rows (flush_block's
+ * drain(..take)), keeping the order of the rest. */
+typedef struct mrl_ring mrl_ring;
+int mrl_ring_create(mrl_ctx* ctx, uint32_t dims, uint32_t capacity, mrl_ring** out);
+int mrl_ring_push(mrl_ctx* ctx, mrl_ring* ring, const float* row);
+int mrl_ring_drain(mrl_ctx* ctx, mrl_ring* ring, uint32_t n);
+uint32_t mrl_ring_len(const mrl_ring* ring);
+int mrl_ring_rows(const mrl_ring* ring, const float** d_rows);
+int mrl_ring_destroy(mrl_ctx* ctx, mrl_ring* ring);
+/* The scan half of IndexEngine::query_filtered (src/engine.rs:564-594) for one device query:
+ * fused plan + scan of `seg`, then the exact search of the ring's pending rows (NULL or empty:
+ * none), merged into one shortlist of at most cfg->shortlist_cand hits, ordered by score
+ * descending then id ascending (ring hits carry VectorId(u32::MAX, i), so a scanned hit keeps its
+ * place against an equal ring score, as Shortlist::push keeps the incumbent). Three launches
+ * when the ring holds rows, one otherwise; asynchronous on the context stream. */
+int mrl_engine_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* d_query, uint32_t dims,
+                    const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg,
+                    const uint32_t* time_lo, const uint32_t* time_hi, const mrl_ring* ring,
+                    uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_count,
+                    uint32_t* d_out_status);
 /* Exchange step of the sharded scan. An exchange record holds one rank's top list: `stride` u64
  * ids, then `stride` f32 scores, then the u32 count of valid entries, padded to
  * MRL_MERGE_RECORD_BYTES(stride) bytes (a multiple of 16). mrl_scan_device fills one when its

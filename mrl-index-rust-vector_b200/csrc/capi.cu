@@ -48,6 +48,19 @@ struct mrl_ctx {
     float* d_means = nullptr;
     float h_means[192];
     bool means_valid = false;
+    // grow-only scratch of the exact paths (scores, flag)
+    void* xbuf = nullptr;
+    size_t xbuf_bytes = 0;
+    // two merge records (scan, ring) of mrl_engine_scan
+    void* ebuf = nullptr;
+    size_t ebuf_bytes = 0;
+};
+
+// RingBuffer's pending embeddings (src/ring.rs:49-119) mirrored in HBM: `len` rows of `dims` f32
+// in push order.
+struct mrl_ring {
+    float* rows = nullptr;
+    uint32_t dims = 0, capacity = 0, len = 0;
 };
 
 struct mrl_seg {
@@ -270,6 +283,8 @@ void mrl_ctx_destroy(mrl_ctx* ctx) {
     cudaFree(ctx->tmp);
     cudaFree(ctx->tmp_out);
     cudaFree(ctx->d_means);
+    cudaFree(ctx->xbuf);
+    cudaFree(ctx->ebuf);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
 }
@@ -310,6 +325,64 @@ int mrl_segment_upload(mrl_ctx* ctx, const uint8_t* blocks, uint64_t n_blocks, u
     }
     const cudaError_t e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) { mrl_segment_free(ctx, s); return cuda_fail(ctx, e, "segment upload"); }
+    s->n_blocks = n_blocks;
+    *out = s;
+    return MRL_OK;
+}
+
+int mrl_segment_load(mrl_ctx* ctx, const char* path, uint32_t block_id_base, mrl_seg** out) {
+    if (!ctx || !path || !out) return MRL_ERR_INVALID;
+    *out = nullptr;
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return fail(ctx, MRL_ERR_INVALID, std::string("io: cannot open ") + path);
+    std::fseek(f, 0, SEEK_END);
+    const long long size = std::ftell(f);
+    std::fseek(f, 0, SEEK_SET);
+    if (size < 0) { std::fclose(f); return fail(ctx, MRL_ERR_INVALID, std::string("io: cannot size ") + path); }
+    if (size % mrl::kBlockBytes) {  // SegmentError::CorruptSize (src/segment.rs:17)
+        std::fclose(f);
+        return fail(ctx, MRL_ERR_INVALID, "corrupt segment size " + std::to_string(size) + " (not multiple of 4096)");
+    }
+    const uint64_t n_blocks = (uint64_t)size / mrl::kBlockBytes;
+    if (n_blocks >= (1ull << 26)) { std::fclose(f); return fail(ctx, MRL_ERR_INVALID, "segment larger than 2^26 pages"); }
+    if ((uint64_t)block_id_base + n_blocks > (1ull << 32)) { std::fclose(f); return fail(ctx, MRL_ERR_INVALID, "block ids overflow u32"); }
+    if (int rc = set_device(ctx)) { std::fclose(f); return rc; }
+    mrl_seg* s = new mrl_seg();
+    s->block_id_base = block_id_base;
+    if (int rc = seg_reserve(ctx, s, n_blocks ? n_blocks : 1)) { std::fclose(f); delete s; return rc; }
+    // Two pinned host buffers and two device staging buffers: the file read of chunk c+1 overlaps
+    // the copy and transcode of chunk c.
+    const uint64_t chunk = 16384;  // pages (64 MiB)
+    const size_t cb = (size_t)std::min<uint64_t>(n_blocks ? n_blocks : 1, chunk) * mrl::kBlockBytes;
+    uint8_t* host[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    int rc = ensure_tmp(ctx, 2 * cb);
+    for (int i = 0; i < 2 && rc == MRL_OK; ++i) {
+        if (cudaHostAlloc((void**)&host[i], cb, cudaHostAllocDefault) != cudaSuccess) rc = fail(ctx, MRL_ERR_NOMEM, "cudaHostAlloc staging");
+        else if (cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming) != cudaSuccess) rc = fail(ctx, MRL_ERR_CUDA, "event");
+    }
+    for (uint64_t b0 = 0, c = 0; rc == MRL_OK && b0 < n_blocks; b0 += chunk, ++c) {
+        const int i = (int)(c & 1);
+        const uint64_t nb = std::min<uint64_t>(chunk, n_blocks - b0);
+        if (c >= 2 && cudaEventSynchronize(done[i]) != cudaSuccess) { rc = fail(ctx, MRL_ERR_CUDA, "staging wait"); break; }
+        if (std::fread(host[i], mrl::kBlockBytes, nb, f) != nb) { rc = fail(ctx, MRL_ERR_INVALID, std::string("io: short read ") + path); break; }
+        uint8_t* dst = static_cast<uint8_t*>(ctx->tmp) + (size_t)i * cb;
+        cudaError_t e = cudaMemcpyAsync(dst, host[i], nb * mrl::kBlockBytes, cudaMemcpyHostToDevice, ctx->stream);
+        if (e != cudaSuccess) { rc = cuda_fail(ctx, e, "segment upload copy"); break; }
+        if (mrl::launch_transcode(dst, nb, s->pages + b0 * 256, s->ts + b0, ctx->stream)) {
+            rc = cuda_fail(ctx, cudaGetLastError(), "transcode launch");
+            break;
+        }
+        if (cudaEventRecord(done[i], ctx->stream) != cudaSuccess) { rc = fail(ctx, MRL_ERR_CUDA, "event record"); break; }
+    }
+    std::fclose(f);
+    const cudaError_t se = cudaStreamSynchronize(ctx->stream);
+    if (rc == MRL_OK && se != cudaSuccess) rc = cuda_fail(ctx, se, "segment load");
+    for (int i = 0; i < 2; ++i) {
+        if (host[i]) cudaFreeHost(host[i]);
+        if (done[i]) cudaEventDestroy(done[i]);
+    }
+    if (rc != MRL_OK) { mrl_segment_free(ctx, s); return rc; }
     s->n_blocks = n_blocks;
     *out = s;
     return MRL_OK;
@@ -728,6 +801,131 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
     }
     if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     return MRL_OK;
+}
+
+int mrl_ring_search(mrl_ctx* ctx, const float* d_query, const float* d_pending, uint32_t n_pending, uint32_t dims,
+                    uint32_t k, void* d_record) {
+    if (!ctx) return MRL_ERR_INVALID;
+    if (k < 1 || k > 4096) return fail(ctx, MRL_ERR_INVALID, "k must be in [1, 4096]");
+    if (n_pending > 4096) return fail(ctx, MRL_ERR_INVALID, "at most 4096 pending vectors");
+    if (dims < 1 || dims > 16384) return fail(ctx, MRL_ERR_INVALID, "dims must be in [1, 16384]");
+    if (!d_record || (n_pending && (!d_query || !d_pending))) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
+    if (reinterpret_cast<uintptr_t>(d_record) % 16) return fail(ctx, MRL_ERR_INVALID, "d_record must be 16-byte aligned");
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = ensure_buf(ctx, &ctx->xbuf, &ctx->xbuf_bytes, sizeof(float) * (n_pending + 4) + 16)) return rc;
+    float* d_scores = static_cast<float*>(ctx->xbuf);
+    uint32_t* d_bad = reinterpret_cast<uint32_t*>(d_scores + n_pending + 1);
+    unsigned char* rec = static_cast<unsigned char*>(d_record);
+    if (mrl::launch_exact_dots(d_query, d_pending, n_pending, dims, nullptr, n_pending, d_scores, d_bad, ctx->stream) ||
+        mrl::launch_exact_rank(d_scores, n_pending, nullptr, (uint64_t)0xFFFFFFFFu << 16, k,
+                               reinterpret_cast<uint64_t*>(rec), reinterpret_cast<float*>(rec + (size_t)k * 8),
+                               reinterpret_cast<uint32_t*>(rec + (size_t)k * 12), ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "ring search launch");
+    return MRL_OK;
+}
+
+int mrl_rerank_exact(mrl_ctx* ctx, const float* d_query, const float* d_rows, uint64_t n_rows, uint32_t dims,
+                     const uint64_t* d_cand, uint32_t n_cand, uint64_t* d_out_rows, float* d_out_scores) {
+    if (!ctx) return MRL_ERR_INVALID;
+    if (n_cand > 4096) return fail(ctx, MRL_ERR_INVALID, "at most 4096 candidates");
+    if (dims < 1 || dims > 16384) return fail(ctx, MRL_ERR_INVALID, "dims must be in [1, 16384]");
+    if (n_cand == 0) return MRL_OK;
+    if (!d_query || !d_rows || !d_cand || !d_out_rows || !d_out_scores) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = ensure_buf(ctx, &ctx->xbuf, &ctx->xbuf_bytes, sizeof(float) * (n_cand + 4) + 16)) return rc;
+    float* d_scores = static_cast<float*>(ctx->xbuf);
+    uint32_t* d_bad = reinterpret_cast<uint32_t*>(d_scores + n_cand + 1);
+    MRL_CUDA_TRY(ctx, cudaMemsetAsync(d_bad, 0, sizeof(uint32_t), ctx->stream));
+    if (mrl::launch_exact_dots(d_query, d_rows, n_rows, dims, d_cand, n_cand, d_scores, d_bad, ctx->stream) ||
+        mrl::launch_exact_rank(d_scores, n_cand, d_cand, 0, n_cand, d_out_rows, d_out_scores, nullptr, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "rerank launch");
+    uint32_t bad = 0;
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(&bad, d_bad, sizeof(bad), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    if (bad) return fail(ctx, MRL_ERR_INVALID, "candidate row id out of range");
+    return MRL_OK;
+}
+
+int mrl_ring_create(mrl_ctx* ctx, uint32_t dims, uint32_t capacity, mrl_ring** out) {
+    if (!ctx || !out) return MRL_ERR_INVALID;
+    *out = nullptr;
+    if (dims < 1 || dims > 16384) return fail(ctx, MRL_ERR_INVALID, "dims must be in [1, 16384]");
+    capacity = std::max<uint32_t>(capacity, 64);  // RingBuffer::new: capacity.max(VECTORS_PER_BLOCK)
+    if (capacity > 4096) return fail(ctx, MRL_ERR_INVALID, "ring capacity must be <= 4096");
+    if (int rc = set_device(ctx)) return rc;
+    mrl_ring* r = new mrl_ring();
+    r->dims = dims;
+    r->capacity = capacity;
+    const cudaError_t e = cudaMalloc(&r->rows, (size_t)capacity * dims * sizeof(float));
+    if (e != cudaSuccess) { delete r; return fail(ctx, MRL_ERR_NOMEM, "cudaMalloc ring rows"); }
+    *out = r;
+    return MRL_OK;
+}
+
+int mrl_ring_push(mrl_ctx* ctx, mrl_ring* ring, const float* row) {
+    if (!ctx || !ring || !row) return MRL_ERR_INVALID;
+    if (ring->len >= ring->capacity) return fail(ctx, MRL_ERR_INVALID, "ring is full (flush a block first)");
+    if (int rc = set_device(ctx)) return rc;
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(ring->rows + (size_t)ring->len * ring->dims, row, ring->dims * sizeof(float),
+                                      cudaMemcpyHostToDevice, ctx->stream));
+    ring->len += 1;
+    return MRL_OK;
+}
+
+int mrl_ring_drain(mrl_ctx* ctx, mrl_ring* ring, uint32_t n) {
+    if (!ctx || !ring) return MRL_ERR_INVALID;
+    n = std::min(n, ring->len);
+    const uint32_t rest = ring->len - n;
+    if (n && rest) {  // keep the order: rows [n, len) move to the front through the staging buffer
+        if (int rc = set_device(ctx)) return rc;
+        const size_t bytes = (size_t)rest * ring->dims * sizeof(float);
+        if (int rc = ensure_tmp(ctx, bytes)) return rc;
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->tmp, ring->rows + (size_t)n * ring->dims, bytes,
+                                          cudaMemcpyDeviceToDevice, ctx->stream));
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(ring->rows, ctx->tmp, bytes, cudaMemcpyDeviceToDevice, ctx->stream));
+    }
+    ring->len = rest;
+    return MRL_OK;
+}
+
+uint32_t mrl_ring_len(const mrl_ring* ring) { return ring ? ring->len : 0; }
+
+int mrl_ring_rows(const mrl_ring* ring, const float** d_rows) {
+    if (!ring || !d_rows) return MRL_ERR_INVALID;
+    *d_rows = ring->rows;
+    return MRL_OK;
+}
+
+int mrl_ring_destroy(mrl_ctx* ctx, mrl_ring* ring) {
+    if (!ring) return MRL_OK;
+    if (ctx) cudaSetDevice(ctx->device);
+    cudaFree(ring->rows);
+    delete ring;
+    return MRL_OK;
+}
+
+int mrl_engine_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* d_query, uint32_t dims,
+                    const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+                    const uint32_t* time_hi, const mrl_ring* ring, uint64_t* d_out_ids, float* d_out_scores,
+                    uint32_t* d_out_count, uint32_t* d_out_status) {
+    if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (ring && ring->dims != dims) return fail(ctx, MRL_ERR_INVALID, "ring dims differ from the query's");
+    if (!ring || ring->len == 0)  // nothing pending: the scan's list is the shortlist
+        return mrl_query_scan_device(ctx, seg, d_query, 1, dims, codec, plans, cfg, time_lo, time_hi, d_out_ids,
+                                     d_out_scores, d_out_count, d_out_status);
+    if (!d_out_ids || !d_out_scores || !d_out_count) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
+    const uint32_t k = cfg->shortlist_cand;
+    const size_t rb = MRL_MERGE_RECORD_BYTES(k);
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = ensure_buf(ctx, &ctx->ebuf, &ctx->ebuf_bytes, 2 * rb)) return rc;
+    unsigned char* rec = static_cast<unsigned char*>(ctx->ebuf);
+    if (int rc = mrl_query_scan_device(ctx, seg, d_query, 1, dims, codec, plans, cfg, time_lo, time_hi,
+                                       reinterpret_cast<uint64_t*>(rec), reinterpret_cast<float*>(rec + (size_t)k * 8),
+                                       reinterpret_cast<uint32_t*>(rec + (size_t)k * 12), d_out_status))
+        return rc;
+    if (int rc = mrl_ring_search(ctx, d_query, ring->rows, ring->len, dims, k, rec + rb)) return rc;
+    return mrl_merge_topk(ctx, rec, 2, k, k, d_out_ids, d_out_scores, d_out_count);
 }
 
 int mrl_merge_topk(mrl_ctx* ctx, const void* d_lists, uint32_t n_lists, uint32_t stride, uint32_t k,

@@ -31,6 +31,18 @@ from .api import (  # noqa: F401
     scored_hits_to_row_ids,
     vector_scores,
 )
+from .index import (  # noqa: F401
+    DeviceRing,
+    IndexDir,
+    PendingVector,
+    SegmentError,
+    SegmentWriter,
+    config_from_json,
+    config_to_json,
+    id_map_from_pages,
+    load_segment,
+    rerank_exact_rows,
+)
 from .shard import (  # noqa: F401
     PeerExchange,
     ShardExchange,

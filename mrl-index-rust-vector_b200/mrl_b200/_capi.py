@@ -97,7 +97,18 @@ SIGNATURES = {
     "mrl_exchange_destroy": (_i, [_vp, _vp]),
     "mrl_query_scan_exchange": (_i, [_vp, _vp, _vp, _u32, C.POINTER(CodecDesc), _vp, C.POINTER(ScanCfgC), _vp, _vp,
                                      _vp, _vp, _vp, _vp, _vp]),
+    "mrl_segment_load": (_i, [_vp, C.c_char_p, _u32, C.POINTER(_vp)]),
+    "mrl_ring_search": (_i, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
+    "mrl_rerank_exact": (_i, [_vp, _vp, _vp, _u64, _u32, _vp, _u32, _vp, _vp]),
     "mrl_merge_topk": (_i, [_vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp]),
+    "mrl_ring_create": (_i, [_vp, _u32, _u32, C.POINTER(_vp)]),
+    "mrl_ring_push": (_i, [_vp, _vp, _vp]),
+    "mrl_ring_drain": (_i, [_vp, _vp, _u32]),
+    "mrl_ring_len": (_u32, [_vp]),
+    "mrl_ring_rows": (_i, [_vp, C.POINTER(_vp)]),
+    "mrl_ring_destroy": (_i, [_vp, _vp]),
+    "mrl_engine_scan": (_i, [_vp, _vp, _vp, _u32, C.POINTER(CodecDesc), _vp, C.POINTER(ScanCfgC), _vp, _vp, _vp,
+                             _vp, _vp, _vp, _vp]),
     "mrl_scan_device_static": (_i, [_vp, _vp, _vp, _u32, _u32, C.POINTER(ScanCfgC), _vp, _vp, _vp, _vp, _vp, _vp]),
     "mrl_debug_vector_scores": (_i, [_vp, _vp, _vp, _u32, C.POINTER(ScanCfgC), _vp, _vp, _vp, _vp, _vp]),
     "mrl_encode_blocks": (_i, [_vp, _vp, _u64, _u32, _vp, _vp, C.POINTER(CodecDesc), _vp]),

@@ -1189,4 +1189,40 @@ int ora_topk_by_key(const float* scores, const uint8_t* active, uint64_t n, uint
     return (int)kk;
 }
 
+// ---- exact inner products on the query path -------------------------------------------------
+// dot / dot_768 (src/embed.rs:115-152).
+float ora_dot(const float* a, const float* b, uint64_t n) {
+    if (n == 768) {
+        float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        for (uint64_t i = 0; i < 768; i += 8)
+            for (int j = 0; j < 8; ++j) acc[j] = acc[j] + a[i + j] * b[i + j];
+        float r = acc[0];
+        for (int j = 1; j < 8; ++j) r = r + acc[j];
+        return r;
+    }
+    float s = -0.0f;
+    for (uint64_t i = 0; i < n; ++i) s = s + a[i] * b[i];
+    return s;
+}
+
+// RingBuffer::search_exact (src/ring.rs:109-119): scored.sort_by(desc) is stable.
+uint32_t ora_ring_search(const float* pending, uint64_t n, int dims, const float* q, uint32_t k, uint32_t* out_pos,
+                         float* out_scores) {
+    std::vector<std::pair<float, uint32_t>> sc(n);
+    for (uint64_t i = 0; i < n; ++i) sc[i] = {ora_dot(pending + i * (uint64_t)dims, q, (uint64_t)dims), (uint32_t)i};
+    std::stable_sort(sc.begin(), sc.end(), [](const auto& x, const auto& y) { return x.first > y.first; });
+    const uint32_t m = (uint32_t)std::min<uint64_t>(k, n);
+    for (uint32_t i = 0; i < m; ++i) { out_pos[i] = sc[i].second; out_scores[i] = sc[i].first; }
+    return m;
+}
+
+// QueryPipeline::rerank_exact_rows (src/pipeline.rs:157-169): dot(query, row), stable sort desc.
+void ora_rerank_rows(const float* rows, int dims, const float* q, const uint64_t* cand, uint64_t n_cand,
+                     uint64_t* out_rows, float* out_scores) {
+    std::vector<std::pair<float, uint64_t>> sc(n_cand);
+    for (uint64_t i = 0; i < n_cand; ++i) sc[i] = {ora_dot(q, rows + cand[i] * (uint64_t)dims, (uint64_t)dims), cand[i]};
+    std::stable_sort(sc.begin(), sc.end(), [](const auto& x, const auto& y) { return x.first > y.first; });
+    for (uint64_t i = 0; i < n_cand; ++i) { out_rows[i] = sc[i].second; out_scores[i] = sc[i].first; }
+}
+
 }  // extern "C"

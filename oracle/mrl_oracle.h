@@ -159,6 +159,20 @@ void ora_synth_queries(uint64_t doc_seed, uint64_t n_docs, uint64_t q_seed, uint
 int ora_topk_by_key(const float* scores, const uint8_t* active, uint64_t n, uint32_t k,
                     uint64_t* out_ids, float* out_scores);
 
+/* ---- exact inner products on the query path ---- */
+/* dot / dot_768 (src/embed.rs:115-152): at n == 768 eight accumulators over i = 0, 8, .. summed
+ * acc0 + .. + acc7 left to right; otherwise a sequential sum of products starting from -0.0
+ * (Iterator::sum for f32 in current Rust; only the sign of an all -0.0 sum depends on it). */
+float ora_dot(const float* a, const float* b, uint64_t n);
+/* RingBuffer::search_exact (src/ring.rs:109-119): dots of the query against n pending rows,
+ * stable sort by score descending, first k; returns the count, positions in out_pos. */
+uint32_t ora_ring_search(const float* pending, uint64_t n, int dims, const float* q, uint32_t k,
+                         uint32_t* out_pos, float* out_scores);
+/* QueryPipeline::rerank_exact_rows (src/pipeline.rs:157-169): dots against rows[cand[i]], stable
+ * sort by score descending. */
+void ora_rerank_rows(const float* rows, int dims, const float* q, const uint64_t* cand, uint64_t n_cand,
+                     uint64_t* out_rows, float* out_scores);
+
 #ifdef __cplusplus
 }
 #endif

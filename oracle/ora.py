@@ -132,6 +132,10 @@ def lib():
                                         C.c_float, f32p, u64p]
         L.ora_topk_by_key.argtypes = [f32p, u8p, C.c_uint64, C.c_uint32, u64p, f32p]
         L.ora_topk_by_key.restype = C.c_int
+        L.ora_dot.argtypes = [f32p, f32p, C.c_uint64]; L.ora_dot.restype = C.c_float
+        L.ora_ring_search.argtypes = [f32p, C.c_uint64, C.c_int, f32p, C.c_uint32, u32p, f32p]
+        L.ora_ring_search.restype = C.c_uint32
+        L.ora_rerank_rows.argtypes = [f32p, C.c_int, f32p, u64p, C.c_uint64, u64p, f32p]
     return _lib
 
 
@@ -327,3 +331,32 @@ def topk_by_key(scores, active, k):
     n = lib().ora_topk_by_key(np.ascontiguousarray(scores, np.float32),
                               np.ascontiguousarray(active, np.uint8), scores.size, k, ids, sc)
     return ids[:n], sc[:n]
+
+
+def dot(a, b) -> np.float32:
+    """dot / dot_768 of the reference (src/embed.rs:115-152)."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    return np.float32(lib().ora_dot(a, b, a.size))
+
+
+def ring_search(pending, q, k):
+    """RingBuffer::search_exact (src/ring.rs:109-119): (positions, scores) of the top k."""
+    pending = np.ascontiguousarray(np.atleast_2d(pending), np.float32)
+    q = np.ascontiguousarray(q, np.float32)
+    n = pending.shape[0] if pending.size else 0
+    pos = np.zeros(max(k, 1), np.uint32)
+    sc = np.zeros(max(k, 1), np.float32)
+    m = lib().ora_ring_search(pending, n, q.size, q, k, pos, sc)
+    return pos[:m], sc[:m]
+
+
+def rerank_rows(rows, q, cand):
+    """QueryPipeline::rerank_exact_rows (src/pipeline.rs:157-169): (row ids, scores) sorted."""
+    rows = np.ascontiguousarray(rows, np.float32)
+    q = np.ascontiguousarray(q, np.float32)
+    cand = np.ascontiguousarray(cand, np.uint64)
+    out_r = np.zeros(max(cand.size, 1), np.uint64)
+    out_s = np.zeros(max(cand.size, 1), np.float32)
+    lib().ora_rerank_rows(rows, q.size, q, cand, cand.size, out_r, out_s)
+    return out_r[:cand.size], out_s[:cand.size]
