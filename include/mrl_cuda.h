@@ -160,6 +160,18 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
                     uint32_t n_q, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                     const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
                     uint32_t* d_out_counts, uint32_t* d_out_status);
+/* scan_blocks for many plans in one pass over the pages (batched throughput): same arguments
+ * and outputs as mrl_scan_device, two launches for all n_q plans. In MRL_MODE_FAST at depth L1 or
+ * full, every result is bit-identical to mrl_scan_device's except for a query whose status has
+ * MRL_STATUS_UNCERTIFIED set: there, one SM's share of the segment held more than 32 of that
+ * query's top k, and the query must be rerun with mrl_scan_device (mrl_scan does this itself; it
+ * uses this path from 8 plans on). Other modes and depths run mrl_scan_device. Scratch: n_q x SMs
+ * x 256 bytes, grown on demand. */
+#define MRL_STATUS_UNCERTIFIED 8u
+int mrl_scan_batch_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q0,
+                          uint32_t n_q, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+                          const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
+                          uint32_t* d_out_counts, uint32_t* d_out_status);
 /* No counterpart in the reference (its scan allocates its shortlist on the Rust heap per call).
  * Same arguments, results and errors as mrl_scan_device, but the scan scratch comes from a static
  * per-device region inside the library instead of the context, so a successful call allocates no

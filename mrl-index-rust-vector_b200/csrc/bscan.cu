@@ -1,0 +1,428 @@
+// bscan.cu — batched fast-mode scan for sm_100a: a tile of query plans scored against every page
+// a CTA loads.
+//
+// The same scan as scan.cu's MRL_MODE_FAST (scan_blocks, src/scan.rs:802-886, for many plans),
+// restructured for throughput when many queries share one pass over the segment:
+//
+//   * Work split: one CTA per SM, each owning a contiguous range of pages (sizes differ by <= 1).
+//     A CTA walks its range once per tile of kTile queries; the pages come from L2 after the first
+//     tile (a 1M-vector segment is 64 MB, L2 is 126 MB).
+//   * Scoring: one thread per slot (two slots per lane and page). All three stages are sums of
+//     16-entry tables indexed by nibbles of the slot's 64 bytes: the 4-bit prefix levels (64
+//     dims), and the mid-band and folded-tail bits in 4-dim windows (32 + 16 windows, the plan's
+//     lut4_s1 / lut4_s4). The tables of two queries are interleaved (int2 per entry), so one
+//     64-bit shared load returns both queries' entries and a dim's table is exactly one 128-byte
+//     row of banks: no bank conflict for any index pattern. The stage sums are the same integers as
+//     the single-query kernel's (integer sums regrouped), and the f32 score formulas are the same
+//     functions, so every score is bit-identical to mrl_scan_device's fast mode.
+//   * Selection: per (warp, query) a sorted top-32 in registers, filtered against max(own 32nd
+//     key, the CTA's bound for that query), candidates queued in shared memory and merged 32 at a
+//     time (as in scan.cu). At the end of a tile the 16 warp lists of every query are tree-merged
+//     (all queries at once) into the CTA's exact top-32, written to global scratch.
+//   * bselect_kernel (one CTA per query): radix select of the k-th key over the G lists, then a
+//     bitonic sort of the top k. The union of CTA lists holds the exact top-k unless a CTA's full
+//     list ends inside it; such a query is reported (status bit 3) and the host entry reruns it
+//     through the single-query kernel, so host-facing results are exact for every input.
+#include "scan_common.cuh"
+
+namespace mrl {
+namespace {
+
+constexpr int kBWarps = 16;
+constexpr int kBThreads = kBWarps * 32;
+constexpr int kTile = 8;           // queries per tile (even)
+constexpr int kPairs = kTile / 2;
+constexpr int kBQueue = 64;        // queued candidates per (warp, query): one offer adds <= 64
+constexpr int kNibPrefix = kPrefix;          // 64 nibble tables
+constexpr int kNibS1 = kRabitq / 4;          // 32
+constexpr int kNibS4 = kFold / 4;            // 16
+constexpr int kNibTabs = kNibPrefix + kNibS1 + kNibS4;  // 112 tables of 16 entries per query
+constexpr int kSelThreads = 1024;
+constexpr int kSelBins = 2048;
+constexpr uint32_t kStatusUncertified = 8u;
+
+// Per (warp, query) selection state, all in shared memory: the sorted top-32 (wlist), the
+// warp's bound (high word of its 32nd key, 0 until full) and the queue fill.
+struct BWarpState {
+    uint32_t tau;
+    int qn;
+};
+
+struct BShared {
+    int2 tab[kPairs][kNibTabs * 16];   // 57,344 B: entry (t, l) of queries (2i, 2i+1)
+    Scalars S[kTile];
+    float2 rho[256];
+    u64 tau[kTile];                    // CTA bound per query (high word used)
+    BWarpState wst[kBWarps][kTile];
+    u64 queue[kBWarps][kTile][kBQueue];  // 64 KB
+    u64 wlist[kTile][kBWarps][32];       // 32 KB: each warp's top-32 per query, then the merge
+};
+
+__device__ __forceinline__ int2 lds64(const int2* tab, uint32_t byte_off) {
+    return *reinterpret_cast<const int2*>(reinterpret_cast<const char*>(tab) + byte_off);
+}
+
+// Sums, for two queries, of the nibble tables t0 .. t0 + 8*NW - 1 indexed by the nibbles of
+// `w` (nibble n of word j feeds table t0 + 8 j + n).
+template <int NW>
+__device__ __forceinline__ void nib_sum2(const uint32_t* w, const int2* tab, int32_t one, int32_t& a, int32_t& b) {
+    int32_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+#pragma unroll
+    for (int j = 0; j < NW; ++j) {
+        const uint32_t e = (w[j] << 3) & 0x78787878u;  // low nibbles x 8: tables 8j, 8j+2, 8j+4, 8j+6
+        const uint32_t o = (w[j] >> 1) & 0x78787878u;  // high nibbles x 8: tables 8j+1, +3, +5, +7
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int2 x = lds64(tab, (8 * j + 2 * k) * 128 + __byte_perm(e, 0, 0x4440 + k));
+            const int2 y = lds64(tab, (8 * j + 2 * k + 1) * 128 + __byte_perm(o, 0, 0x4440 + k));
+            a0 = x.x * one + a0;  // one == 1: the accumulations issue on the FMA pipe, the
+            b0 = x.y * one + b0;  // nibble extraction on the ALU pipe
+            a1 = y.x * one + a1;
+            b1 = y.y * one + b1;
+        }
+    }
+    a = a0 + a1;
+    b = b0 + b1;
+}
+
+__device__ __forceinline__ void bsel_flush(u64* wl, u64* q, int lane, u64* cta_tau, BWarpState* st) {
+    __syncwarp();
+    const int qn = st->qn;
+    u64 list = wl[lane];
+    for (int base = 0; base < qn; base += 32) {
+        u64 x = (base + lane < qn) ? q[base + lane] : 0ull;
+        x = warp_sort32(x, lane);
+        list = warp_merge32(list, x, lane);
+    }
+    const u64 t = __shfl_sync(kFull, list, 31);
+    wl[lane] = list;
+    __syncwarp();
+    if (lane == 0) {
+        st->qn = 0;
+        st->tau = (uint32_t)(t >> 32);
+        if (t) atomicMax(cta_tau, t);
+    }
+    __syncwarp();
+}
+
+__device__ __forceinline__ void bsel_offer(u64* wl, u64* q, int lane, u64* cta_tau, BWarpState* st, u64 k0,
+                                           u64 k1) {
+    const uint32_t tc = (uint32_t)(*reinterpret_cast<volatile u64*>(cta_tau) >> 32);
+    const uint32_t tau = max(max(st->tau, tc), 1u);
+    const bool p0 = (uint32_t)(k0 >> 32) >= tau, p1 = (uint32_t)(k1 >> 32) >= tau;
+    const unsigned m0 = __ballot_sync(kFull, p0), m1 = __ballot_sync(kFull, p1);
+    if ((m0 | m1) == 0u) return;
+    const int nn = __popc(m0) + __popc(m1);
+    if (st->qn + nn > kBQueue) bsel_flush(wl, q, lane, cta_tau, st);
+    const int qn = st->qn;
+    const unsigned lt = (1u << lane) - 1u;
+    if (p0) q[qn + __popc(m0 & lt)] = k0;
+    if (p1) q[qn + __popc(m0) + __popc(m1 & lt)] = k1;
+    __syncwarp();
+    if (lane == 0) st->qn = qn + nn;
+    __syncwarp();
+    if (qn + nn >= 32) bsel_flush(wl, q, lane, cta_tau, st);
+}
+
+// Integer stage sums of one slot for the query pair whose interleaved tables start at `tab`
+// (index h = query 2i + h).
+__device__ __forceinline__ void pair_sums(const Slot4& s, const int2* tab, uint32_t depth, int32_t one,
+                                          int32_t (&P)[2], int32_t (&S1)[2], int32_t (&S4)[2]) {
+    uint32_t pw[8] = {s.c0.x, s.c0.y, s.c0.z, s.c0.w, s.c1.x, s.c1.y, s.c1.z, s.c1.w};
+    uint32_t s1w[4] = {s.c2.x, s.c2.y, s.c2.z, s.c2.w};
+    uint32_t s4w[2] = {s.c3.x, s.c3.y};
+    // The words are the same for every query pair of a page; opaque copies keep the compiler from
+    // hoisting all 112 table offsets out of the pair loop (which would spill).
+#pragma unroll
+    for (int i = 0; i < 8; ++i) asm volatile("" : "+r"(pw[i]));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) asm volatile("" : "+r"(s1w[i]));
+    asm volatile("" : "+r"(s4w[0]), "+r"(s4w[1]));
+    S1[0] = S1[1] = S4[0] = S4[1] = 0;
+    nib_sum2<8>(pw, tab, one, P[0], P[1]);
+    if (depth >= MRL_DEPTH_L1) nib_sum2<4>(s1w, tab + kNibPrefix * 16, one, S1[0], S1[1]);
+    if (depth == MRL_DEPTH_FULL) nib_sum2<2>(s4w, tab + (kNibPrefix + kNibS1) * 16, one, S4[0], S4[1]);
+}
+
+struct BatchLaunch {
+    const uint4* pages;
+    const uint2* block_ts;
+    uint32_t n_blocks;
+    const DevPlan* plans;  // n_q plans
+    uint32_t n_q;
+    float w_s4;
+    uint32_t depth;
+    uint32_t use_time, has_lo, lo, has_hi, hi;
+    u64* lists;            // [n_q][G][32] keys: each CTA's exact top-32 per query
+};
+
+__device__ __forceinline__ bool page_live(const BatchLaunch& p, uint32_t b) {
+    if (!p.use_time) return true;
+    const uint2 t = __ldg(p.block_ts + b);  // [min_ts, max_ts], src/scan.rs:719-730
+    if (p.has_lo && t.y < p.lo) return false;
+    if (p.has_hi && t.x > p.hi) return false;
+    return true;
+}
+
+__global__ void __launch_bounds__(kBThreads, 1) bscan_kernel(const BatchLaunch p) {
+    extern __shared__ __align__(16) unsigned char b_dyn[];
+    BShared& sh = *reinterpret_cast<BShared*>(b_dyn);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t G = gridDim.x;
+    const uint32_t lo_b = (uint32_t)(((uint64_t)p.n_blocks * blockIdx.x) / G);
+    const uint32_t hi_b = (uint32_t)(((uint64_t)p.n_blocks * (blockIdx.x + 1)) / G);
+    fill_rho_tab(sh.rho, tid, kBThreads);
+    const int32_t one = (int32_t)(p.n_q != 0u);  // 1 at run time, opaque to the compiler
+
+    for (uint32_t q0 = 0; q0 < p.n_q; q0 += kTile) {
+        const uint32_t nq = min((uint32_t)kTile, p.n_q - q0);
+        __syncthreads();  // the previous tile's lists are written out
+        // tables of this tile: entry (t, l) of query 2i in .x, of query 2i+1 in .y (a missing
+        // query of an odd last tile reads as zeros and is never offered)
+#pragma unroll 4
+        for (int i = tid; i < kPairs * kNibTabs * 16; i += kBThreads) {
+            const int pr = i / (kNibTabs * 16), e = i % (kNibTabs * 16);
+            int2 v = make_int2(0, 0);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t qi = 2 * pr + h;
+                if (qi >= nq) continue;
+                const DevPlan* P = p.plans + q0 + qi;
+                int32_t x;
+                if (e < kNibPrefix * 16) x = P->lut_prefix[e];
+                else if (e < (kNibPrefix + kNibS1) * 16) x = P->lut4_s1[e - kNibPrefix * 16];
+                else x = P->lut4_s4[e - (kNibPrefix + kNibS1) * 16];
+                if (h) v.y = x; else v.x = x;
+            }
+            sh.tab[pr][e] = v;
+        }
+        if (tid < kTile) {
+            if ((uint32_t)tid < nq) fill_scalars(p.plans + q0 + tid, p.w_s4, p.depth, one, sh.S[tid]);
+            sh.tau[tid] = 0ull;
+        }
+        if (tid < kBWarps * kTile) sh.wst[tid / kTile][tid % kTile] = BWarpState{0u, 0};
+        for (int i = tid; i < kTile * kBWarps * 32; i += kBThreads) (&sh.wlist[0][0][0])[i] = 0ull;
+        __syncthreads();
+
+        for (uint32_t b = lo_b + warp; b < hi_b; b += kBWarps) {
+            if (!page_live(p, b)) continue;  // warp-uniform
+            Slot4 s0, s1;
+            load_slot(p.pages, b, lane, s0);
+            load_slot(p.pages, b, lane + 32, s1);
+            const SlotMeta m0 = slot_meta_tab(s0.c3.z, s0.c3.w, sh.rho);
+            const SlotMeta m1 = slot_meta_tab(s1.c3.z, s1.c3.w, sh.rho);
+            const uint32_t o0 = b * 64 + lane, o1 = o0 + 32;
+#pragma unroll 1
+            for (int pr = 0; pr < kPairs; ++pr) {
+                if ((uint32_t)(2 * pr) >= nq) break;  // warp-uniform
+                int32_t P0[2], A0[2], B0[2], P1[2], A1[2], B1[2];
+                pair_sums(s0, sh.tab[pr], p.depth, one, P0, A0, B0);
+                pair_sums(s1, sh.tab[pr], p.depth, one, P1, A1, B1);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int q = 2 * pr + h;
+                    if ((uint32_t)q < nq) {  // warp-uniform
+                        const Scalars& S = sh.S[q];
+                        const u64 k0 = m0.tomb ? 0ull : make_key(fast_score(m0, P0[h], A0[h], B0[h], S), o0);
+                        const u64 k1 = m1.tomb ? 0ull : make_key(fast_score(m1, P1[h], A1[h], B1[h], S), o1);
+                        bsel_offer(sh.wlist[q][warp], sh.queue[warp][q], lane, &sh.tau[q], &sh.wst[warp][q], k0, k1);
+                    }
+                }
+            }
+        }
+        for (int q = 0; q < kTile; ++q)
+            if (sh.wst[warp][q].qn) bsel_flush(sh.wlist[q][warp], sh.queue[warp][q], lane, &sh.tau[q], &sh.wst[warp][q]);
+        __syncthreads();
+        u64* lists = &sh.wlist[0][0][0];  // [kTile][kBWarps][32]
+        for (int half = kBWarps / 2; half >= 1; half >>= 1) {
+            for (int m = warp; m < kTile * half; m += kBWarps) {
+                const int q = m / half, i = m % half;
+                u64* a = lists + (q * kBWarps + i) * 32;
+                const u64 r = warp_merge32(a[lane], lists[(q * kBWarps + i + half) * 32 + lane], lane);
+                __syncwarp();
+                a[lane] = r;
+            }
+            __syncthreads();
+        }
+        for (int i = tid; i < (int)nq * 32; i += kBThreads) {
+            const int q = i >> 5;
+            p.lists[((size_t)(q0 + q) * G + blockIdx.x) * 32 + (i & 31)] = lists[(q * kBWarps) * 32 + (i & 31)];
+        }
+    }
+}
+
+// ---- per-query selection over the CTA lists ----
+
+struct SelectLaunch {
+    const u64* lists;  // [n_q][G][32]
+    uint32_t G, n_q, k, block_id_base;
+    uint64_t* out_ids;
+    float* out_scores;
+    uint32_t* out_counts;
+    uint32_t* out_status;
+};
+
+__global__ void __launch_bounds__(kSelThreads) bselect_kernel(const SelectLaunch p) {
+    extern __shared__ __align__(16) unsigned char s_dyn[];
+    const uint32_t q = blockIdx.x;
+    const uint32_t n = p.G * 32;
+    u64* keys = reinterpret_cast<u64*>(s_dyn);                  // n
+    unsigned* hist = reinterpret_cast<unsigned*>(keys + n);     // kSelBins
+    u64* top = reinterpret_cast<u64*>(hist + kSelBins);         // P2 (power of two >= k)
+    __shared__ u64 s_prefix, s_mask;
+    __shared__ unsigned s_rem, s_done, s_valid, s_cnt, s_flag, s_bin, s_above;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const u64* src = p.lists + (size_t)q * n;
+    for (uint32_t i = tid; i < n; i += kSelThreads) keys[i] = src[i];
+    if (tid == 0) { s_valid = 0; s_cnt = 0; s_flag = 0; s_prefix = 0; s_mask = 0; s_rem = p.k; s_done = 0; }
+    __syncthreads();
+    {
+        unsigned v = 0;
+        for (uint32_t i = tid; i < n; i += kSelThreads) v += keys[i] != 0ull;
+        v = __reduce_add_sync(kFull, v);
+        if (lane == 0 && v) atomicAdd(&s_valid, v);
+    }
+    __syncthreads();
+    const uint32_t k = p.k;
+    // threshold T: the keys >= T are exactly the top min(k, valid) keys (keys are unique)
+    u64 T = 1ull;
+    if (s_valid > k) {
+        // 11-bit digits from the top (bits 53-63, 42-52, 31-41, 20-30, 9-19), then bits 0-8
+        for (int d = 0; d < 6 && !s_done; ++d) {
+            const int shift = d < 5 ? 53 - 11 * d : 0;
+            const int bits = d < 5 ? 11 : 9;
+            const u64 dmask = (((u64)1 << bits) - 1) << shift;
+            for (int i = tid; i < kSelBins; i += kSelThreads) hist[i] = 0u;
+            __syncthreads();
+            const u64 pre = s_prefix, msk = s_mask;
+            for (uint32_t i = tid; i < n; i += kSelThreads) {
+                const u64 x = keys[i];
+                if (x != 0ull && (x & msk) == pre) atomicAdd(&hist[(x & dmask) >> shift], 1u);
+            }
+            __syncthreads();
+            if (warp == 0) {  // find the bin holding the s_rem-th key from the top
+                unsigned part = 0;
+                for (int j = 0; j < kSelBins / 32; ++j) part += hist[kSelBins - 1 - (lane * (kSelBins / 32) + j)];
+                unsigned incl = part;  // inclusive prefix over lanes (lane 0 = highest bins)
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const unsigned y = __shfl_up_sync(kFull, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                const unsigned rem = s_rem;
+                const unsigned excl = incl - part;
+                if (excl < rem && rem <= incl) {
+                    unsigned acc = excl;
+                    for (int j = 0; j < kSelBins / 32; ++j) {
+                        const int bin = kSelBins - 1 - (lane * (kSelBins / 32) + j);
+                        const unsigned h = hist[bin];
+                        if (acc + h >= rem) { s_bin = (unsigned)bin; s_above = acc; break; }
+                        acc += h;
+                    }
+                }
+            }
+            __syncthreads();
+            if (tid == 0) {
+                const unsigned bin = s_bin;
+                s_rem -= s_above;
+                s_prefix |= (u64)bin << shift;
+                s_mask |= dmask;
+                if (hist[bin] == s_rem) s_done = 1;
+            }
+            __syncthreads();
+        }
+        T = s_prefix;
+    }
+    // the top keys, then a bitonic sort (descending) of P2 slots
+    uint32_t P2 = 1;
+    while (P2 < k) P2 <<= 1;
+    for (uint32_t i = tid; i < P2; i += kSelThreads) top[i] = 0ull;
+    __syncthreads();
+    for (uint32_t i = tid; i < n; i += kSelThreads) {
+        const u64 x = keys[i];
+        if (x != 0ull && x >= T) {
+            const unsigned at = atomicAdd(&s_cnt, 1u);
+            if (at < P2) top[at] = x;
+        }
+        // a full CTA list whose last key is inside the top k may have dropped a top-k key
+        if ((i & 31u) == 31u && x != 0ull && x >= T) atomicOr(&s_flag, 1u);
+    }
+    __syncthreads();
+    for (uint32_t kk = 2; kk <= P2; kk <<= 1) {
+        for (uint32_t j = kk >> 1; j > 0; j >>= 1) {
+            for (uint32_t i = tid; i < P2; i += kSelThreads) {
+                const uint32_t ixj = i ^ j;
+                if (ixj > i) {
+                    const u64 a = top[i], b = top[ixj];
+                    const bool desc = (i & kk) == 0;
+                    if (desc ? (a < b) : (a > b)) { top[i] = b; top[ixj] = a; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    const uint32_t m = min(s_cnt, k);
+    for (uint32_t i = tid; i < m; i += kSelThreads) {
+        const u64 key = top[i];
+        const uint32_t ord = key_ordinal(key);
+        p.out_ids[(size_t)q * k + i] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
+        p.out_scores[(size_t)q * k + i] = key_score(key);
+    }
+    if (tid == 0) {
+        p.out_counts[q] = m;
+        if (p.out_status) p.out_status[q] = s_flag ? kStatusUncertified : 0u;
+    }
+}
+
+}  // namespace
+
+size_t batch_scratch_bytes(uint32_t ctas, uint32_t n_q) { return (size_t)n_q * ctas * 32 * sizeof(u64); }
+
+int launch_scan_batch(const uint4* pages, const uint2* block_ts, uint32_t n_blocks, uint32_t block_id_base,
+                      const DevPlan* plans, uint32_t n_q, uint32_t k, float w_s4, uint32_t depth, uint32_t use_time,
+                      uint32_t has_lo, uint32_t lo, uint32_t has_hi, uint32_t hi, uint32_t ctas, void* scratch,
+                      uint64_t* out_ids, float* out_scores, uint32_t* out_counts, uint32_t* out_status,
+                      cudaStream_t stream) {
+    if (n_q == 0) return 0;
+    if (k < 1 || k > 4096 || depth == MRL_DEPTH_L0 || ctas < 1) return -1;
+    static_assert(sizeof(BShared) <= 227 * 1024, "batched scan shared memory");
+    const size_t smem = sizeof(BShared);
+    if (cudaFuncSetAttribute(bscan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return -1;
+    BatchLaunch b{};
+    b.pages = pages;
+    b.block_ts = block_ts;
+    b.n_blocks = n_blocks;
+    b.plans = plans;
+    b.n_q = n_q;
+    b.w_s4 = w_s4;
+    b.depth = depth;
+    b.use_time = use_time;
+    b.has_lo = has_lo;
+    b.lo = lo;
+    b.has_hi = has_hi;
+    b.hi = hi;
+    b.lists = static_cast<u64*>(scratch);
+    bscan_kernel<<<ctas, kBThreads, smem, stream>>>(b);
+    if (cudaGetLastError() != cudaSuccess) return -1;
+    uint32_t P2 = 1;
+    while (P2 < k) P2 <<= 1;
+    const size_t ssmem = (size_t)ctas * 32 * sizeof(u64) + kSelBins * sizeof(unsigned) + (size_t)P2 * sizeof(u64);
+    if (ssmem > 227 * 1024) return -1;
+    if (cudaFuncSetAttribute(bselect_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem) != cudaSuccess)
+        return -1;
+    SelectLaunch s{};
+    s.lists = b.lists;
+    s.G = ctas;
+    s.n_q = n_q;
+    s.k = k;
+    s.block_id_base = block_id_base;
+    s.out_ids = out_ids;
+    s.out_scores = out_scores;
+    s.out_counts = out_counts;
+    s.out_status = out_status;
+    bselect_kernel<<<n_q, kSelThreads, ssmem, stream>>>(s);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace mrl

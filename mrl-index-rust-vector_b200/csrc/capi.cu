@@ -54,6 +54,9 @@ struct mrl_ctx {
     // two merge records (scan, ring) of mrl_engine_scan
     void* ebuf = nullptr;
     size_t ebuf_bytes = 0;
+    // per-(query, CTA) top lists of the batched scan
+    void* bbuf = nullptr;
+    size_t bbuf_bytes = 0;
 };
 
 // RingBuffer's pending embeddings (src/ring.rs:49-119) mirrored in HBM: `len` rows of `dims` f32
@@ -144,6 +147,9 @@ int ensure_buf(mrl_ctx* ctx, void** buf, size_t* have, size_t bytes) {
 }
 int ensure_tmp(mrl_ctx* ctx, size_t bytes) { return ensure_buf(ctx, &ctx->tmp, &ctx->tmp_bytes, bytes); }
 int ensure_out(mrl_ctx* ctx, size_t bytes) { return ensure_buf(ctx, &ctx->tmp_out, &ctx->tmp_out_bytes, bytes); }
+
+// mrl_scan switches to the batched scan from this many plans on (fast mode, depth L1 or full)
+constexpr uint32_t kBatchMinQueries = 8;
 
 uint32_t auto_list_len(uint32_t k, uint32_t ctas) {
     // Expected top-k members per CTA is k/ctas; keep 2.5x that plus 8, as a power of two in
@@ -285,6 +291,7 @@ void mrl_ctx_destroy(mrl_ctx* ctx) {
     cudaFree(ctx->d_means);
     cudaFree(ctx->xbuf);
     cudaFree(ctx->ebuf);
+    cudaFree(ctx->bbuf);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
 }
@@ -558,6 +565,29 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
         }
         if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     }
+    return MRL_OK;
+}
+
+int mrl_scan_batch_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q0, uint32_t n_q,
+                          const mrl_scan_cfg* cfg, const uint32_t* time_lo, const uint32_t* time_hi,
+                          uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_counts, uint32_t* d_out_status) {
+    if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if ((uint64_t)q0 + n_q > plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan range out of bounds");
+    if (n_q && (!d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "output is NULL");
+    if (n_q == 0) return MRL_OK;
+    if (cfg->mode != MRL_MODE_FAST || cfg->strata_depth == MRL_DEPTH_L0 || seg->n_blocks == 0)
+        return mrl_scan_device(ctx, seg, plans, q0, n_q, cfg, time_lo, time_hi, d_out_ids, d_out_scores, d_out_counts,
+                               d_out_status);
+    if (int rc = set_device(ctx)) return rc;
+    const uint32_t ctas = (uint32_t)ctx->sms;
+    if (int rc = ensure_buf(ctx, &ctx->bbuf, &ctx->bbuf_bytes, mrl::batch_scratch_bytes(ctas, n_q))) return rc;
+    const bool use_time = cfg->temporal_filter_enable && (time_lo || time_hi);
+    if (mrl::launch_scan_batch(seg->pages, seg->ts, (uint32_t)seg->n_blocks, seg->block_id_base, plans->d + q0, n_q,
+                               cfg->shortlist_cand, cfg->stratum4_weight, cfg->strata_depth, use_time ? 1u : 0u,
+                               time_lo ? 1u : 0u, time_lo ? *time_lo : 0u, time_hi ? 1u : 0u, time_hi ? *time_hi : 0u,
+                               ctas, ctx->bbuf, d_out_ids, d_out_scores, d_out_counts, d_out_status, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "batched scan launch");
     return MRL_OK;
 }
 
@@ -955,7 +985,22 @@ int mrl_scan(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, const mrl
     float* d_sc = (float*)(d_ids + nk);
     uint32_t* d_cnt = (uint32_t*)(d_sc + nk);
     uint32_t* d_st = d_cnt + n_q;
-    if (int rc = mrl_scan_device(ctx, seg, plans, 0, n_q, cfg, time_lo, time_hi, d_ids, d_sc, d_cnt, d_st)) return rc;
+    // many plans in fast mode: the batched scan, with the rare uncertified query rerun alone
+    const bool batch = n_q >= kBatchMinQueries && cfg->mode == MRL_MODE_FAST && cfg->strata_depth != MRL_DEPTH_L0;
+    if (batch) {
+        if (int rc = mrl_scan_batch_device(ctx, seg, plans, 0, n_q, cfg, time_lo, time_hi, d_ids, d_sc, d_cnt, d_st))
+            return rc;
+        std::vector<uint32_t> st(n_q);
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(st.data(), d_st, n_q * sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream));
+        MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+        for (uint32_t q = 0; q < n_q; ++q)
+            if (st[q] & MRL_STATUS_UNCERTIFIED)
+                if (int rc = mrl_scan_device(ctx, seg, plans, q, 1, cfg, time_lo, time_hi, d_ids + (size_t)q * k,
+                                             d_sc + (size_t)q * k, d_cnt + q, d_st + q))
+                    return rc;
+    } else if (int rc = mrl_scan_device(ctx, seg, plans, 0, n_q, cfg, time_lo, time_hi, d_ids, d_sc, d_cnt, d_st)) {
+        return rc;
+    }
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_ids, d_ids, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, ctx->stream));
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_scores, d_sc, nk * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_counts, d_cnt, n_q * sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream));

@@ -45,6 +45,9 @@ struct DevPlan {
     int32_t lut_s1[kS1Windows * 32];
     int32_t lut_s4[kS4Windows * 32];
     int32_t lut_l0[kPrefix * 16];  // L0Only: stratum-0 bit of each level times bit_weights[d][3]
+    // the same stage sums over 4-dim windows (16 entries each), for the batched scan
+    int32_t lut4_s1[(kRabitq / 4) * 16];
+    int32_t lut4_s4[(kFold / 4) * 16];
     int32_t shift_prefix, shift_s1, shift_s4, shift_l0;
     double unscale_prefix, unscale_s1, unscale_s4, unscale_l0;  // 2^-shift
     // exact mode: f32 products and addends in reference order
@@ -211,6 +214,14 @@ int launch_exact_rank(const float* d_scores, uint32_t n, const uint64_t* d_ids, 
 int launch_merge_topk(const void* d_lists, uint32_t n_lists, uint32_t stride, uint32_t k, uint64_t* d_out_ids,
                       float* d_out_scores, uint32_t* d_out_count, cudaStream_t stream);
 constexpr int kCtlWords = 8;
+// batched fast-mode scan (bscan.cu): per-(query, CTA) top-32 lists in `scratch`
+// (batch_scratch_bytes), then one selection CTA per query
+size_t batch_scratch_bytes(uint32_t ctas, uint32_t n_q);
+int launch_scan_batch(const uint4* pages, const uint2* block_ts, uint32_t n_blocks, uint32_t block_id_base,
+                      const DevPlan* plans, uint32_t n_q, uint32_t k, float w_s4, uint32_t depth, uint32_t use_time,
+                      uint32_t has_lo, uint32_t lo, uint32_t has_hi, uint32_t hi, uint32_t ctas, void* scratch,
+                      uint64_t* out_ids, float* out_scores, uint32_t* out_counts, uint32_t* out_status,
+                      cudaStream_t stream);
 int launch_debug_scores(const ScanLaunch& p, float* d_scores, uint8_t* d_active,
                         int32_t* d_partials, cudaStream_t stream);
 }  // namespace mrl

@@ -85,10 +85,18 @@ __device__ __forceinline__ int32_t window_entry(const int32_t* fx, int g, int m)
     return sum;
 }
 
+// Entry m of the 4-dim window table g of a 1-bit stage (lut4_s1 / lut4_s4): the same exact sum
+// over 4 dims instead of 5, so the batched scan's stage sums are the same integers.
+__device__ __forceinline__ int32_t window4_entry(const int32_t* fx, int g, int m) {
+    int32_t sum = 0;
+    for (int i = 0; i < 4; ++i) sum += fx[2 * (4 * g + i) + ((m >> i) & 1)];
+    return sum;
+}
+
 // What a plan build writes: kNeedAll = every field of DevPlan (the stored plan); a scan that only
 // needs its own mode's tables asks for kNeedFast (+ kNeedL0 at depth L0Only) or kNeedExact. The
 // scalars, shifts, bit weights, mid_w and tail_w are always written.
-constexpr uint32_t kNeedFast = 1u, kNeedExact = 2u, kNeedL0 = 4u, kNeedAll = 0xFu;
+constexpr uint32_t kNeedFast = 1u, kNeedExact = 2u, kNeedL0 = 4u, kNeedBatch = 8u, kNeedAll = 0xFu;
 
 // Shared scratch of one plan build (besides the dims-float query copy).
 struct PlanShared {
@@ -403,6 +411,11 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
         for (int t = tid; t < kS1Windows * 32; t += nthr) P->lut_s1[t] = window_entry<kRabitq>(s_fx, t >> 5, t & 31);
         for (int t = tid; t < kS4Windows * 32; t += nthr)
             P->lut_s4[t] = window_entry<kFold>(s_fx + 2 * kRabitq, t >> 5, t & 31);
+    }
+    if (need & kNeedBatch) {
+        for (int t = tid; t < (kRabitq / 4) * 16; t += nthr) P->lut4_s1[t] = window4_entry(s_fx, t >> 4, t & 15);
+        for (int t = tid; t < (kFold / 4) * 16; t += nthr)
+            P->lut4_s4[t] = window4_entry(s_fx + 2 * kRabitq, t >> 4, t & 15);
     }
     if (need & kNeedL0) {  // bit 3 of the level times bit_weights[d][3] (accum_plane, src/scan.rs:753-762)
         const double pw_0 = sh.pw[1];

@@ -88,6 +88,7 @@ SIGNATURES = {
     "mrl_plan_read": (_i, [_vp, _vp, _u32, C.POINTER(QueryPlanC)]),
     "mrl_scan": (_i, [_vp, _vp, _vp, C.POINTER(ScanCfgC), _vp, _vp, _vp, _vp, _vp]),
     "mrl_scan_device": (_i, [_vp, _vp, _vp, _u32, _u32, C.POINTER(ScanCfgC), _vp, _vp, _vp, _vp, _vp, _vp]),
+    "mrl_scan_batch_device": (_i, [_vp, _vp, _vp, _u32, _u32, C.POINTER(ScanCfgC), _vp, _vp, _vp, _vp, _vp, _vp]),
     "mrl_query_scan_device": (_i, [_vp, _vp, _vp, _u32, _u32, C.POINTER(CodecDesc), _vp, C.POINTER(ScanCfgC), _vp, _vp,
                                    _vp, _vp, _vp, _vp]),
     "mrl_query_scan": (_i, [_vp, _vp, _vp, _u32, _u32, C.POINTER(CodecDesc), _vp, C.POINTER(ScanCfgC), _vp, _vp, _vp,
