@@ -155,7 +155,8 @@ int mrl_scan(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, const mrl
              float* out_scores, uint32_t* out_counts);
 /* Same scan for plans [q0, q0+n_q) writing device buffers, asynchronously on the context
  * stream (no host synchronisation). out_status[q] (device, may be NULL) receives the selection
- * status word: bit 0 = the exact re-selection path ran. */
+ * status word: bit 0 = the exact re-selection path ran, bit 1 = a bounded wait ran out (no
+ * result). */
 int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q0,
                     uint32_t n_q, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                     const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
@@ -168,6 +169,12 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
  * uses this path from 8 plans on). Other modes and depths run mrl_scan_device. Scratch: n_q x SMs
  * x 256 bytes, grown on demand. */
 #define MRL_STATUS_UNCERTIFIED 8u
+/* Engines of the batched scan (mrl_set_batch_engine): the 5th-generation tensor cores (tcgen05
+ * kind::i8 GEMMs of the slots' one-hot levels and bits against the plans' 8-bit table digits, the
+ * default), or CUDA-core shared-memory table sums. Both give the same integers and scores. */
+#define MRL_BATCH_TENSOR 0u
+#define MRL_BATCH_CUDA_CORE 1u
+int mrl_set_batch_engine(mrl_ctx* ctx, uint32_t engine);
 int mrl_scan_batch_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q0,
                           uint32_t n_q, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                           const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,

@@ -24,6 +24,7 @@
 //     list ends inside it; such a query is reported (status bit 3) and the host entry reruns it
 //     through the single-query kernel, so host-facing results are exact for every input.
 #include "scan_common.cuh"
+#include "umma.cuh"
 
 namespace mrl {
 namespace {
@@ -255,6 +256,7 @@ __global__ void __launch_bounds__(kBThreads, 1) bscan_kernel(const BatchLaunch p
 
 struct SelectLaunch {
     const u64* lists;  // [n_q][G][32]
+    const uint32_t* err;  // scan error word (bit 1: a bounded wait ran out), ORed into every status
     uint32_t G, n_q, k, block_id_base;
     uint64_t* out_ids;
     float* out_scores;
@@ -370,25 +372,295 @@ __global__ void __launch_bounds__(kSelThreads) bselect_kernel(const SelectLaunch
     }
     if (tid == 0) {
         p.out_counts[q] = m;
-        if (p.out_status) p.out_status[q] = s_flag ? kStatusUncertified : 0u;
+        if (p.out_status) p.out_status[q] = (s_flag ? kStatusUncertified : 0u) | (p.err ? *p.err : 0u);
     }
+}
+
+// ---- tensor-core engine (tcgen05, kind::i8) ----
+//
+// The three stage sums of a slot for a query are dot products of 8-bit vectors:
+//   prefix  = sum over (d, l) of [level_d == l] * T[d][l]     (one-hot of the 64 levels, K = 1024)
+//   mid     = C1 + sum over d of bit_d * (fx1_d - fx0_d)        (the 128 mid-band bits, K = 128)
+//   tail    = C4 + sum over d of bit_d * (fx1_d - fx0_d)        (the 64 folded-tail bits, K = 64)
+// with the plan's int32 table entries split into four balanced base-256 digits in [-128, 127]
+// (T = t0 + 2^8 t1 + 2^16 t2 + 2^24 t3). One int8 GEMM per stage, A = the slots' 0/1 bytes
+// (128 slots x 1216 bytes, in tensor memory), B = the digits of 16 queries (64 rows x 1216 bytes,
+// shared memory), D = 64 int32 columns per stage in tensor memory; each digit column sums at most
+// 128 products of magnitude <= 128, and the stage sum is sum_j 2^(8j) D_j evaluated mod 2^32,
+// which is exact because the true sum fits in int32. So the stage sums are the same integers as
+// the table sums of the CUDA-core engine and of the single-query kernel.
+constexpr int kTQ = 16;                 // queries per tensor tile
+constexpr int kTN = 4 * kTQ;            // B rows: 4 digits per query
+constexpr int kKAll = kPrefix * 16 + kRabitq + kFold;   // 1216 bytes of A per slot
+constexpr int kACols = kKAll / 4;       // 304 tensor-memory columns hold a slot's A row
+constexpr int kColP = kACols, kColS1 = kColP + kTN, kColS4 = kColS1 + kTN;  // 304, 368, 432
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kBTileBytes = (uint32_t)kTN * kKAll;  // 77,824: 76 K-blocks of 8 row groups x 128 B
+constexpr uint32_t kKBlockBytes = (kTN / 8) * 128;        // 1,024: LBO (next 16 K bytes)
+constexpr uint32_t kWaitPolls = 1u << 20;
+
+// Byte offset of B element (row n, k) in the no-swizzle K-major core-matrix layout.
+__host__ __device__ __forceinline__ uint32_t b_offset(int n, int k) {
+    return (uint32_t)((k >> 4) * (kTN / 8) + (n >> 3)) * 128u + (uint32_t)(n & 7) * 16u + (uint32_t)(k & 15);
+}
+
+// B tiles and the constant terms of every query: digit j of entry k of query q at row 4 (q % 16) + j
+// of tile q / 16.
+__global__ void __launch_bounds__(256) tprep_kernel(const DevPlan* __restrict__ plans, uint32_t n_q,
+                                                    uint8_t* __restrict__ tiles, int32_t* __restrict__ consts) {
+    const uint32_t q = blockIdx.x;
+    const DevPlan* P = plans + q;
+    uint8_t* tile = tiles + (size_t)(q / kTQ) * kBTileBytes;
+    const int r0 = 4 * (int)(q % kTQ);
+    for (int k = threadIdx.x; k < kKAll; k += blockDim.x) {
+        int32_t T;
+        if (k < kPrefix * 16) {
+            T = P->lut_prefix[k];
+        } else if (k < kPrefix * 16 + kRabitq) {
+            const int d = k - kPrefix * 16, g = d >> 2;
+            T = P->lut4_s1[g * 16 + (1 << (d & 3))] - P->lut4_s1[g * 16];
+        } else {
+            const int d = k - kPrefix * 16 - kRabitq, g = d >> 2;
+            T = P->lut4_s4[g * 16 + (1 << (d & 3))] - P->lut4_s4[g * 16];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int32_t t = (int32_t)(int8_t)(T & 0xFF);  // balanced digit in [-128, 127]
+            tile[b_offset(r0 + j, k)] = (uint8_t)t;
+            T = (T - t) >> 8;
+        }
+    }
+    if (threadIdx.x == 0) {
+        int32_t c1 = 0, c4 = 0;
+        for (int g = 0; g < kRabitq / 4; ++g) c1 += P->lut4_s1[g * 16];
+        for (int g = 0; g < kFold / 4; ++g) c4 += P->lut4_s4[g * 16];
+        consts[2 * q] = c1;
+        consts[2 * q + 1] = c4;
+    }
+}
+
+struct TShared {
+    uint8_t B[kBTileBytes];              // offset 0 (1 KB aligned)
+    Scalars S[kTQ];
+    int32_t c1[kTQ], c4[kTQ];
+    float2 rho[256];
+    u64 tau[kTQ];
+    BWarpState wst[kBWarps][4];
+    u64 wlist[kBWarps][4][32];           // [warp][query of its group][32]
+    u64 queue[kBWarps][4][32];
+    uint64_t bar;
+    uint32_t taddr;
+};
+
+struct TensorLaunch {
+    BatchLaunch b;
+    const uint8_t* tiles;
+    const int32_t* consts;
+    uint32_t* err;
+};
+
+__device__ __forceinline__ void bsel_offer1(u64* wl, u64* q, int lane, u64* cta_tau, BWarpState* st, u64 k0) {
+    const uint32_t tc_ = (uint32_t)(*reinterpret_cast<volatile u64*>(cta_tau) >> 32);
+    const uint32_t tau = max(max(st->tau, tc_), 1u);
+    const bool p0 = (uint32_t)(k0 >> 32) >= tau;
+    const unsigned m0 = __ballot_sync(kFull, p0);
+    if (m0 == 0u) return;
+    const int nn = __popc(m0);
+    if (st->qn + nn > 32) bsel_flush(wl, q, lane, cta_tau, st);
+    const int qn = st->qn;
+    if (p0) q[qn + __popc(m0 & ((1u << lane) - 1u))] = k0;
+    __syncwarp();
+    if (lane == 0) st->qn = qn + nn;
+    __syncwarp();
+    if (qn + nn >= 32) bsel_flush(wl, q, lane, cta_tau, st);
+}
+
+// One-hot bytes of four 4-bit levels (nibbles 0..3 of `w` shifted by 4*n0) into 16 columns.
+__device__ __forceinline__ void onehot4(uint32_t w, uint32_t (&r)[16]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t l = (w >> (4 * i)) & 15u;
+        const uint32_t one = 1u << ((l & 3u) << 3);
+        const uint32_t hi = l >> 2;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) r[4 * i + c] = hi == (uint32_t)c ? one : 0u;
+    }
+}
+// 0/1 bytes of the 16 nibbles' bits of two words (64 bits) into 16 columns.
+__device__ __forceinline__ void bits16(uint32_t w0, uint32_t w1, uint32_t (&r)[16]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        r[i] = (((w0 >> (4 * i)) & 15u) * 0x00204081u) & 0x01010101u;
+        r[8 + i] = (((w1 >> (4 * i)) & 15u) * 0x00204081u) & 0x01010101u;
+    }
+}
+
+__device__ __forceinline__ int32_t digits4(const uint32_t* d) {
+    return (int32_t)(d[0] + (d[1] << 8) + (d[2] << 16) + (d[3] << 24));
+}
+
+__global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch t) {
+    extern __shared__ __align__(1024) unsigned char t_dyn[];
+    TShared& sh = *reinterpret_cast<TShared*>(t_dyn);
+    const BatchLaunch& p = t.b;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int qw = warp & 3, g4 = warp >> 2;  // lane quarter (slots) and column / query group
+    const uint32_t G = gridDim.x;
+    const uint32_t lo_b = (uint32_t)(((uint64_t)p.n_blocks * blockIdx.x) / G);
+    const uint32_t hi_b = (uint32_t)(((uint64_t)p.n_blocks * (blockIdx.x + 1)) / G);
+    if (warp == 0) {
+        tc::tmem_alloc(&sh.taddr, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    if (tid == 0) {
+        tc::mbar_init(&sh.bar, 1);
+        tc::fence_mbar_init();
+    }
+    fill_rho_tab(sh.rho, tid, kBThreads);
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tbase = sh.taddr;
+    const uint32_t my_lane = (uint32_t)(32 * qw) << 16;  // this warp's tensor-memory lane quarter
+    const uint32_t idesc = tc::idesc_i8(128, kTN);
+    const uint32_t b_smem = tc::smem_u32(sh.B);
+    uint32_t phase = 0;
+    bool failed = false;
+
+    for (uint32_t q0 = 0; q0 < p.n_q && !failed; q0 += kTQ) {
+        const uint32_t nq = min((uint32_t)kTQ, p.n_q - q0);
+        __syncthreads();
+        {  // this tile's B digits, scalars, constants; selection state reset
+            const uint4* src = reinterpret_cast<const uint4*>(t.tiles + (size_t)(q0 / kTQ) * kBTileBytes);
+            uint4* dst = reinterpret_cast<uint4*>(sh.B);
+            for (uint32_t i = tid; i < kBTileBytes / 16; i += kBThreads) dst[i] = __ldg(src + i);
+        }
+        if (tid < kTQ) {
+            if ((uint32_t)tid < nq) {
+                fill_scalars(p.plans + q0 + tid, p.w_s4, p.depth, 1, sh.S[tid]);
+                sh.c1[tid] = t.consts[2 * (q0 + tid)];
+                sh.c4[tid] = t.consts[2 * (q0 + tid) + 1];
+            }
+            sh.tau[tid] = 0ull;
+        }
+        if (tid < kBWarps * 4) sh.wst[tid >> 2][tid & 3] = BWarpState{0u, 0};
+        for (int i = tid; i < kBWarps * 4 * 32; i += kBThreads) (&sh.wlist[0][0][0])[i] = 0ull;
+        tc::fence_proxy_async_smem();  // generic-proxy writes of B -> tensor-core reads
+        tc::fence_before();
+        __syncthreads();
+        tc::fence_after();
+
+        for (uint32_t pg = lo_b; pg < hi_b; pg += 2) {
+            // ---- A: this thread's slot row (lane quarter qw), this warp's column share (g4)
+            const int r = 32 * qw + lane;
+            const uint32_t b = pg + (uint32_t)(r >> 6);
+            const int v = r & 63;
+            const bool live = b < hi_b && page_live(p, b);  // warp-uniform
+            Slot4 s;
+            if (live) {
+                load_slot(p.pages, b, v, s);
+            } else {
+                s.c0 = s.c1 = s.c2 = s.c3 = make_uint4(0u, 0u, 0u, 0u);
+            }
+            const SlotMeta m = slot_meta_tab(s.c3.z, s.c3.w, sh.rho);
+            {
+                // levels of dims 16 g4 .. 16 g4 + 15: words 2 g4 and 2 g4 + 1 of the prefix
+                const uint32_t wa = g4 < 2 ? (g4 == 0 ? s.c0.x : s.c0.z) : (g4 == 2 ? s.c1.x : s.c1.z);
+                const uint32_t wb = g4 < 2 ? (g4 == 0 ? s.c0.y : s.c0.w) : (g4 == 2 ? s.c1.y : s.c1.w);
+                uint32_t rr[16];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {  // dims 16 g4 + 4c .. + 3
+                    const uint32_t w = (c < 2 ? wa : wb) >> (16 * (c & 1));
+                    onehot4(w, rr);
+                    TC_ST16(tbase + my_lane + (uint32_t)(64 * g4 + 16 * c), rr);
+                }
+                if (g4 == 0) { bits16(s.c2.x, s.c2.y, rr); TC_ST16(tbase + my_lane + 256u, rr); }
+                if (g4 == 1) { bits16(s.c2.z, s.c2.w, rr); TC_ST16(tbase + my_lane + 272u, rr); }
+                if (g4 == 2) { bits16(s.c3.x, s.c3.y, rr); TC_ST16(tbase + my_lane + 288u, rr); }
+            }
+            tc::wait_st();
+            tc::fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                tc::fence_after();
+#pragma unroll 1
+                for (int k = 0; k < kPrefix * 16 / 32; ++k)
+                    tc::mma_i8_ts(tbase + kColP, tbase + 8u * k,
+                                  tc::sdesc_kmajor(b_smem + (uint32_t)(2 * k) * kKBlockBytes, kKBlockBytes, 128u),
+                                  idesc, k > 0);
+                for (int k = 0; k < kRabitq / 32; ++k)
+                    tc::mma_i8_ts(tbase + kColS1, tbase + 256u + 8u * k,
+                                  tc::sdesc_kmajor(b_smem + (uint32_t)(64 + 2 * k) * kKBlockBytes, kKBlockBytes, 128u),
+                                  idesc, k > 0);
+                for (int k = 0; k < kFold / 32; ++k)
+                    tc::mma_i8_ts(tbase + kColS4, tbase + 288u + 8u * k,
+                                  tc::sdesc_kmajor(b_smem + (uint32_t)(72 + 2 * k) * kKBlockBytes, kKBlockBytes, 128u),
+                                  idesc, k > 0);
+                tc::mma_commit(&sh.bar);
+            }
+            const bool ok = tc::mbar_wait(&sh.bar, phase, kWaitPolls);
+            phase ^= 1u;
+            if (__syncthreads_or(!ok)) {
+                failed = true;
+                break;
+            }
+            tc::fence_after();
+            // ---- epilogue: this thread's slot, queries 4 g4 .. 4 g4 + 3
+            uint32_t dp[16], d1[16], d4[16];
+            TC_LD16(dp, tbase + my_lane + (uint32_t)(kColP + 16 * g4));
+            TC_LD16(d1, tbase + my_lane + (uint32_t)(kColS1 + 16 * g4));
+            TC_LD16(d4, tbase + my_lane + (uint32_t)(kColS4 + 16 * g4));
+            tc::wait_ld();
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int q = 4 * g4 + j;
+                if ((uint32_t)q < nq) {  // warp-uniform
+                    const int32_t P = digits4(dp + 4 * j);
+                    const int32_t A1 = sh.c1[q] + digits4(d1 + 4 * j);
+                    const int32_t A4 = sh.c4[q] + digits4(d4 + 4 * j);
+                    const u64 key =
+                        (!live || m.tomb) ? 0ull : make_key(fast_score(m, P, A1, A4, sh.S[q]), b * 64 + v);
+                    bsel_offer1(sh.wlist[warp][j], sh.queue[warp][j], lane, &sh.tau[q], &sh.wst[warp][j], key);
+                }
+            }
+            tc::fence_before();
+            __syncthreads();  // tensor memory (A and D) free for the next slot tile
+        }
+        if (failed) break;
+        for (int j = 0; j < 4; ++j)
+            if (sh.wst[warp][j].qn) bsel_flush(sh.wlist[warp][j], sh.queue[warp][j], lane, &sh.tau[4 * g4 + j], &sh.wst[warp][j]);
+        __syncthreads();
+        if ((uint32_t)warp < nq) {  // warp w merges query w: the lists of the 4 lane quarters
+            const int g = warp >> 2, j = warp & 3;
+            const u64 a = warp_merge32(sh.wlist[4 * g + 0][j][lane], sh.wlist[4 * g + 1][j][lane], lane);
+            const u64 c = warp_merge32(sh.wlist[4 * g + 2][j][lane], sh.wlist[4 * g + 3][j][lane], lane);
+            p.lists[((size_t)(q0 + warp) * G + blockIdx.x) * 32 + lane] = warp_merge32(a, c, lane);
+        }
+    }
+    if (failed) {
+        if (tid == 0) atomicOr(t.err, 2u);
+        tc::mbar_wait(&sh.bar, phase ^ 1u, kWaitPolls);  // the MMAs in flight, bounded
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tbase, kTmemCols);
 }
 
 }  // namespace
 
-size_t batch_scratch_bytes(uint32_t ctas, uint32_t n_q) { return (size_t)n_q * ctas * 32 * sizeof(u64); }
+size_t batch_scratch_bytes(uint32_t ctas, uint32_t n_q) {
+    const size_t lists = (size_t)n_q * ctas * 32 * sizeof(u64);
+    const size_t tiles = (size_t)((n_q + kTQ - 1) / kTQ) * kBTileBytes;
+    return lists + tiles + (size_t)n_q * 2 * sizeof(int32_t) + 256;
+}
 
 int launch_scan_batch(const uint4* pages, const uint2* block_ts, uint32_t n_blocks, uint32_t block_id_base,
                       const DevPlan* plans, uint32_t n_q, uint32_t k, float w_s4, uint32_t depth, uint32_t use_time,
-                      uint32_t has_lo, uint32_t lo, uint32_t has_hi, uint32_t hi, uint32_t ctas, void* scratch,
-                      uint64_t* out_ids, float* out_scores, uint32_t* out_counts, uint32_t* out_status,
+                      uint32_t has_lo, uint32_t lo, uint32_t has_hi, uint32_t hi, uint32_t ctas, uint32_t engine,
+                      void* scratch, uint64_t* out_ids, float* out_scores, uint32_t* out_counts, uint32_t* out_status,
                       cudaStream_t stream) {
     if (n_q == 0) return 0;
     if (k < 1 || k > 4096 || depth == MRL_DEPTH_L0 || ctas < 1) return -1;
-    static_assert(sizeof(BShared) <= 227 * 1024, "batched scan shared memory");
-    const size_t smem = sizeof(BShared);
-    if (cudaFuncSetAttribute(bscan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-        return -1;
     BatchLaunch b{};
     b.pages = pages;
     b.block_ts = block_ts;
@@ -402,8 +674,34 @@ int launch_scan_batch(const uint4* pages, const uint2* block_ts, uint32_t n_bloc
     b.lo = lo;
     b.has_hi = has_hi;
     b.hi = hi;
-    b.lists = static_cast<u64*>(scratch);
-    bscan_kernel<<<ctas, kBThreads, smem, stream>>>(b);
+    // scratch: lists [n_q][ctas][32] keys | B digit tiles | per-query constants | error word
+    unsigned char* base = static_cast<unsigned char*>(scratch);
+    const size_t lists_bytes = (size_t)n_q * ctas * 32 * sizeof(u64);
+    const size_t tiles_bytes = (size_t)((n_q + kTQ - 1) / kTQ) * kBTileBytes;
+    b.lists = reinterpret_cast<u64*>(base);
+    uint8_t* tiles = base + ((lists_bytes + 255) & ~(size_t)255);
+    int32_t* consts = reinterpret_cast<int32_t*>(tiles + tiles_bytes);
+    uint32_t* err = reinterpret_cast<uint32_t*>(consts + 2 * (size_t)n_q);
+    if (engine == MRL_BATCH_TENSOR) {
+        static_assert(sizeof(TShared) <= 227 * 1024, "tensor batched scan shared memory");
+        // at least 120 KB, so that one CTA (and its 512 tensor-memory columns) occupies each SM
+        const size_t smem = sizeof(TShared) > 120 * 1024 ? sizeof(TShared) : 120 * 1024;
+        if (cudaFuncSetAttribute(tscan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return -1;
+        if (cudaMemsetAsync(tiles, 0, tiles_bytes, stream) != cudaSuccess) return -1;
+        if (cudaMemsetAsync(err, 0, sizeof(uint32_t), stream) != cudaSuccess) return -1;
+        tprep_kernel<<<n_q, 256, 0, stream>>>(plans, n_q, tiles, consts);
+        if (cudaGetLastError() != cudaSuccess) return -1;
+        TensorLaunch t{b, tiles, consts, err};
+        tscan_kernel<<<ctas, kBThreads, smem, stream>>>(t);
+    } else {
+        static_assert(sizeof(BShared) <= 227 * 1024, "batched scan shared memory");
+        const size_t smem = sizeof(BShared);
+        if (cudaFuncSetAttribute(bscan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return -1;
+        if (cudaMemsetAsync(err, 0, sizeof(uint32_t), stream) != cudaSuccess) return -1;
+        bscan_kernel<<<ctas, kBThreads, smem, stream>>>(b);
+    }
     if (cudaGetLastError() != cudaSuccess) return -1;
     uint32_t P2 = 1;
     while (P2 < k) P2 <<= 1;
@@ -413,6 +711,7 @@ int launch_scan_batch(const uint4* pages, const uint2* block_ts, uint32_t n_bloc
         return -1;
     SelectLaunch s{};
     s.lists = b.lists;
+    s.err = err;
     s.G = ctas;
     s.n_q = n_q;
     s.k = k;

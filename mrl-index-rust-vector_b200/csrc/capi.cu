@@ -54,9 +54,10 @@ struct mrl_ctx {
     // two merge records (scan, ring) of mrl_engine_scan
     void* ebuf = nullptr;
     size_t ebuf_bytes = 0;
-    // per-(query, CTA) top lists of the batched scan
+    // per-(query, CTA) top lists and tensor-core operand tiles of the batched scan
     void* bbuf = nullptr;
     size_t bbuf_bytes = 0;
+    uint32_t batch_engine = MRL_BATCH_TENSOR;
 };
 
 // RingBuffer's pending embeddings (src/ring.rs:49-119) mirrored in HBM: `len` rows of `dims` f32
@@ -586,7 +587,8 @@ int mrl_scan_batch_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pla
     if (mrl::launch_scan_batch(seg->pages, seg->ts, (uint32_t)seg->n_blocks, seg->block_id_base, plans->d + q0, n_q,
                                cfg->shortlist_cand, cfg->stratum4_weight, cfg->strata_depth, use_time ? 1u : 0u,
                                time_lo ? 1u : 0u, time_lo ? *time_lo : 0u, time_hi ? 1u : 0u, time_hi ? *time_hi : 0u,
-                               ctas, ctx->bbuf, d_out_ids, d_out_scores, d_out_counts, d_out_status, ctx->stream))
+                               ctas, ctx->batch_engine, ctx->bbuf, d_out_ids, d_out_scores, d_out_counts, d_out_status,
+                               ctx->stream))
         return cuda_fail(ctx, cudaGetLastError(), "batched scan launch");
     return MRL_OK;
 }
@@ -994,6 +996,8 @@ int mrl_scan(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, const mrl
         MRL_CUDA_TRY(ctx, cudaMemcpyAsync(st.data(), d_st, n_q * sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream));
         MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
         for (uint32_t q = 0; q < n_q; ++q)
+            if (st[q] & 2u) return fail(ctx, MRL_ERR_CUDA, "batched scan: a bounded tensor-core wait ran out");
+        for (uint32_t q = 0; q < n_q; ++q)
             if (st[q] & MRL_STATUS_UNCERTIFIED)
                 if (int rc = mrl_scan_device(ctx, seg, plans, q, 1, cfg, time_lo, time_hi, d_ids + (size_t)q * k,
                                              d_sc + (size_t)q * k, d_cnt + q, d_st + q))
@@ -1136,6 +1140,13 @@ int mrl_scan_geometry(mrl_ctx* ctx, uint32_t k, uint32_t* ctas, uint32_t* list_l
     if (!ctx) return MRL_ERR_INVALID;
     if (ctas) *ctas = (uint32_t)ctx->sms;
     if (list_len) *list_len = ctx->list_len_override ? ctx->list_len_override : auto_list_len(k, (uint32_t)ctx->sms);
+    return MRL_OK;
+}
+
+int mrl_set_batch_engine(mrl_ctx* ctx, uint32_t engine) {
+    if (!ctx) return MRL_ERR_INVALID;
+    if (engine > MRL_BATCH_CUDA_CORE) return fail(ctx, MRL_ERR_INVALID, "engine must be MRL_BATCH_TENSOR or MRL_BATCH_CUDA_CORE");
+    ctx->batch_engine = engine;
     return MRL_OK;
 }
 

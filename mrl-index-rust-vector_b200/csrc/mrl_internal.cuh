@@ -219,8 +219,8 @@ constexpr int kCtlWords = 8;
 size_t batch_scratch_bytes(uint32_t ctas, uint32_t n_q);
 int launch_scan_batch(const uint4* pages, const uint2* block_ts, uint32_t n_blocks, uint32_t block_id_base,
                       const DevPlan* plans, uint32_t n_q, uint32_t k, float w_s4, uint32_t depth, uint32_t use_time,
-                      uint32_t has_lo, uint32_t lo, uint32_t has_hi, uint32_t hi, uint32_t ctas, void* scratch,
-                      uint64_t* out_ids, float* out_scores, uint32_t* out_counts, uint32_t* out_status,
+                      uint32_t has_lo, uint32_t lo, uint32_t has_hi, uint32_t hi, uint32_t ctas, uint32_t engine,
+                      void* scratch, uint64_t* out_ids, float* out_scores, uint32_t* out_counts, uint32_t* out_status,
                       cudaStream_t stream);
 int launch_debug_scores(const ScanLaunch& p, float* d_scores, uint8_t* d_active,
                         int32_t* d_partials, cudaStream_t stream);

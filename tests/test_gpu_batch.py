@@ -1,7 +1,8 @@
-"""The batched fast-mode scan (mrl_scan_batch_device, and mrl_scan from 8 plans on) against the
-single-query scan (mrl_scan_device): identical ids and bit-identical scores for every query that
-is not reported uncertified, across codecs, depths, tile remainders, k, tombstones and the
-temporal filter; uncertified queries are rerun by mrl_scan, so its results always match."""
+"""The batched fast-mode scan (mrl_scan_batch_device, and mrl_scan from 8 plans on), with each of
+its engines (tcgen05 kind::i8 tensor cores, CUDA-core tables), against the single-query scan
+(mrl_scan_device): identical ids and bit-identical scores for every query that is not reported
+uncertified, across codecs, depths, tile remainders, k, tombstones and the temporal filter;
+uncertified queries are rerun by mrl_scan, so its results always match."""
 import ctypes as C
 
 import numpy as np
@@ -57,6 +58,14 @@ def _run(dev, fn, seg, plans, n_q, cfg_c, k, lo=None, hi=None):
             cnt.cpu().numpy().astype(np.int64), st.cpu().numpy().astype(np.int64))
 
 
+@pytest.fixture(params=["tensor", "cuda_core"])
+def engine(request, dev):
+    """Runs a test with each batched-scan engine (tcgen05 kind::i8, CUDA-core tables)."""
+    mb()._capi.check(dev.ptr, dev.lib.mrl_set_batch_engine(dev.ptr, 0 if request.param == "tensor" else 1))
+    yield request.param
+    dev.lib.mrl_set_batch_engine(dev.ptr, 0)
+
+
 def _compare(single, batch, allow_uncertified=True):
     si, ss, sn, _ = single
     bi, bs, bn, bst = batch
@@ -75,7 +84,7 @@ def _compare(single, batch, allow_uncertified=True):
 
 @pytest.mark.parametrize("codec", ["eden", "minmax", "eden_b1"])
 @pytest.mark.parametrize("depth", ["FULL_64B", "L1_RABITQ"])
-def test_batch_matches_single_query(ora, dev, codec, depth):
+def test_batch_matches_single_query(ora, dev, engine, codec, depth):
     M = mb()
     docs, blocks, mean, mid = _corpus(ora, 64 * 300 + 13, codec=codec)
     seg = M.Segment.upload(blocks, dev)
@@ -93,7 +102,7 @@ def test_batch_matches_single_query(ora, dev, codec, depth):
 
 @pytest.mark.parametrize("n_q", [1, 2, 8, 9])
 @pytest.mark.parametrize("k", [1, 16, 1000])
-def test_batch_sizes_and_k(ora, dev, n_q, k):
+def test_batch_sizes_and_k(ora, dev, engine, n_q, k):
     M = mb()
     docs, blocks, mean, _ = _corpus(ora, 64 * 400, seed=7)
     seg = M.Segment.upload(blocks, dev)
@@ -107,7 +116,7 @@ def test_batch_sizes_and_k(ora, dev, n_q, k):
     plans.free()
 
 
-def test_batch_uncertified_rerun_by_mrl_scan(ora, dev):
+def test_batch_uncertified_rerun_by_mrl_scan(ora, dev, engine):
     """k = 4096 over 200 pages: most SMs' shares hold more than 32 of the top k, so queries are
     reported uncertified; mrl_scan (host entry) reruns them and matches the single-query scan."""
     M = mb()
@@ -131,7 +140,7 @@ def test_batch_uncertified_rerun_by_mrl_scan(ora, dev):
     plans.free()
 
 
-def test_batch_tombstones_and_time_filter(ora, dev):
+def test_batch_tombstones_and_time_filter(ora, dev, engine):
     M = mb()
     rng = np.random.default_rng(5)
     docs = ora.synth_docs(12, 64 * 60, 768)
@@ -174,7 +183,7 @@ def test_batch_exact_mode_and_l0_fall_back(ora, dev):
     plans.free()
 
 
-def test_batch_against_oracle_fixed_scores(ora, dev):
+def test_batch_against_oracle_fixed_scores(ora, dev, engine):
     """The batched top-k equals the exact top-k of the oracle's fast-mode integer scores."""
     M = mb()
     docs, blocks, mean, _ = _corpus(ora, 64 * 120 + 5, seed=17)
@@ -199,7 +208,7 @@ def test_batch_against_oracle_fixed_scores(ora, dev):
     plans.free()
 
 
-def test_batch_many_pages_per_sm(dev):
+def test_batch_many_pages_per_sm(dev, engine):
     """A segment of 4,000 pages (about 27 per SM): every warp scores several pages per tile, so the
     candidate queues fill and flush repeatedly; results stay identical to the single-query scan."""
     import torch
