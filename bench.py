@@ -56,6 +56,10 @@ def parse():
                     help="keep the scanned pages out of L2 by rotating over segments whose total exceeds L2 "
                          "(code stays cached, as in a serving loop) or by flushing L2 before every step")
     ap.add_argument("--segments", type=int, default=4, help="segments rotated over with --l2 rotate")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="queries per step; > 1 runs BASELINE config 3 (batched scan, one GPU)")
+    ap.add_argument("--engine", choices=["tensor", "cuda_core"], default="tensor",
+                    help="batched-scan engine (--batch > 1)")
     ap.add_argument("--exchange", choices=["nvlink", "nccl"], default="nvlink",
                     help="N > 1: merge per-rank top-k records inside the scan launch over NVLink peer memory, "
                          "or all-gather them with NCCL and merge with a second kernel")
@@ -461,6 +465,159 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_batch(args):
+    """batches of --batch queries over the 1M x 768 corpus on one GPU. A step =
+    plan build of the batch (mrl_plan_build_device) + one batched scan (mrl_scan_batch_device: the
+    per-SM query-tile scan on the chosen engine, then one selection CTA per query)."""
+    import torch
+
+    torch.cuda.set_device(0)
+    torch.cuda.set_stream(torch.cuda.Stream())
+    import mrl_b200 as M
+
+    lib = M.load()
+    dev = M.Device(0)
+    torch_stream = torch.cuda.current_stream().cuda_stream
+    dev.set_stream(torch_stream)
+    M._capi.check(dev.ptr, lib.mrl_set_batch_engine(dev.ptr, 0 if args.engine == "tensor" else 1))
+    n, dims, k, B = args.docs, args.dims, args.k, args.batch
+    nb = (n + 63) // 64
+    warm = max(args.warmup, 3)
+    x, mean = build_corpus_gpu(M, dev, n, dims, row0=0)
+    seg, pax, desc, keep = encode_gpu(M, dev, x, n, dims, mean, block_id_base=0)
+    segs = [seg]
+    for r in range(1, max(args.segments, 1)):  # rotate: 4 x 64 MB of pages > L2
+        M._capi.check(dev.ptr, lib.mrl_synth_docs_device(dev.ptr, DOC_SEED, r * n, n, dims, C.c_void_p(x.data_ptr())))
+        sp = C.c_void_p()
+        M._capi.check(dev.ptr, lib.mrl_encode_device(dev.ptr, C.c_void_p(x.data_ptr()), n, dims, 8, C.byref(desc),
+                                                     None, 0, C.byref(sp)))
+        segs.append(M.Segment(sp, dev))
+    del x, pax
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    n_batches = warm + args.steps
+    qd = torch.empty((n_batches * B, dims), dtype=torch.float32, device="cuda")
+    M._capi.check(dev.ptr, lib.mrl_synth_queries_device(dev.ptr, DOC_SEED, n, Q_SEED, n_batches * B, dims,
+                                                        C.c_float(SIGMA), C.c_void_p(qd.data_ptr()), None))
+    plans = C.c_void_p()
+    M._capi.check(dev.ptr, lib.mrl_plans_alloc(dev.ptr, B, dims, C.byref(plans)))
+    cfg = M.ScanConfig(shortlist_cand=k, temporal_filter_enable=False).to_c()
+    ids = torch.empty(B * k, dtype=torch.int64, device="cuda")
+    sc = torch.empty(B * k, dtype=torch.float32, device="cuda")
+    cnt = torch.empty(B, dtype=torch.int32, device="cuda")
+    st = torch.zeros(B, dtype=torch.int32, device="cuda")
+    qbytes = B * dims * 4
+
+    def step(i, ev=None):
+        if ev is not None:
+            ev[0].record()
+        M._capi.check(dev.ptr, lib.mrl_plan_build_device(dev.ptr, C.c_void_p(qd.data_ptr() + i * qbytes), B, dims,
+                                                         C.byref(desc), plans))
+        if ev is not None:
+            ev[1].record()
+        M._capi.check(dev.ptr, lib.mrl_scan_batch_device(dev.ptr, segs[i % len(segs)].ptr, plans, 0, B, C.byref(cfg),
+                                                         None, None, C.c_void_p(ids.data_ptr()),
+                                                         C.c_void_p(sc.data_ptr()), C.c_void_p(cnt.data_ptr()),
+                                                         C.c_void_p(st.data_ptr())))
+        if ev is not None:
+            ev[2].record()
+
+    for i in range(warm):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = Clocks(0)
+    clocks.start()
+    time.sleep(0.3)
+    ev_all = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    t0 = time.perf_counter()
+    ev_all[0].record()
+    for i in range(args.steps):
+        step(warm + i)
+    ev_all[1].record()
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    total_ms = ev_all[0].elapsed_time(ev_all[1])
+    time.sleep(0.2)
+    clk = clocks.stop()
+    uncertified = int(((st & 8) != 0).sum().item())
+    # plan / scan split (information)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(min(5, args.steps))]
+    for i, e in enumerate(evs):
+        step(warm + i, e)
+    torch.cuda.synchronize()
+    plan_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in evs]))
+    scan_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in evs]))
+
+    # e2e through the host-facing C ABI: pinned host queries -> plans -> batched scan -> host results
+    dev.set_stream(0)
+    qh = torch.empty((B, dims), dtype=torch.float32, pin_memory=True)
+    ids_h = torch.empty(B * k, dtype=torch.int64, pin_memory=True)
+    sc_h = torch.empty(B * k, dtype=torch.float32, pin_memory=True)
+    cnt_h = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    e2e_steps = min(args.steps, 10)
+    tot = 0.0
+    for i in range(e2e_steps + 2):
+        qh.copy_(qd[(i % n_batches) * B:(i % n_batches + 1) * B].cpu())
+        torch.cuda.synchronize()
+        s0 = time.perf_counter()
+        M._capi.check(dev.ptr, lib.mrl_plan_rebuild(dev.ptr, C.c_void_p(qh.data_ptr()), B, dims, C.byref(desc), plans))
+        M._capi.check(dev.ptr, lib.mrl_scan(dev.ptr, segs[i % len(segs)].ptr, plans, C.byref(cfg), None, None,
+                                            C.c_void_p(ids_h.data_ptr()), C.c_void_p(sc_h.data_ptr()),
+                                            C.c_void_p(cnt_h.data_ptr())))
+        if i >= 2:
+            tot += time.perf_counter() - s0
+    e2e = {"value": B * e2e_steps / tot, "unit": "QPS", "h2d_bytes_per_step": qbytes,
+           "d2h_bytes_per_step": B * (k * 12 + 4), "steps": e2e_steps,
+           "path": "mrl_plan_rebuild (host queries) + mrl_scan (batched from 8 plans, host results, synchronous)"}
+    dev.set_stream(torch_stream)
+
+    pairs = B * n
+    step_s = total_ms / args.steps / 1e3
+    if args.engine == "tensor":
+        ops = pairs * (16 * 64 + 128 + 64) * 4 * 2  # executed int8 MMA ops: 1216 K bytes x 4 digits x 2
+        bf16, _ = measured_peaks_tensor()
+        roof = {"bound": "tensor", "achieved": ops / (scan_ms / 1e3) / 1e12, "peak": 2 * bf16, "unit": "TOP/s",
+                "frac": ops / (scan_ms / 1e3) / 1e12 / (2 * bf16),
+                "peak_kind": "2 x measured dense bf16 (tcgen05 kind::i8 dense rate is twice kind::f16 on B200)",
+                "kernel": "tscan_kernel", "traffic": None}
+    else:
+        cuda_core_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        alg = pairs * 512
+        roof = {"bound": "fp32/int pipes", "achieved": alg / (scan_ms / 1e3) / 1e12, "peak": cuda_core_peak,
+                "unit": "TOP/s", "frac": alg / (scan_ms / 1e3) / 1e12 / cuda_core_peak,
+                "peak_kind": "148 SMs x 128 lanes x 2 x 1965 MHz (nominal)", "kernel": "bscan_kernel",
+                "traffic": None}
+    line = {
+        "metric": METRIC, "value": B * args.steps / (total_ms / 1e3), "unit": "QPS", "n_gpus": 1,
+        "steps": args.steps, "warmup": warm, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 tensor + int32 + f32" if args.engine == "tensor" else
+        "int32+f32", "data": "synthetic",
+        "config": {"workload": f"config 3: batched scan, {B} queries per step over 1M x 768 docs, EDEN-prod + RaBitQ"
+                               " + folded tail, shortlist 256, full_64b", "docs": n, "dims": dims, "batch": B,
+                   "shortlist": k, "engine": args.engine, "parallelism": "single GPU",
+                   "l2": f"steps rotate over {len(segs)} segments ({len(segs) * nb * 4096 / 1e6:.0f} MB of pages)",
+                   "step_kernels": "plan_kernel, then tprep_kernel + tscan_kernel + bselect_kernel (tensor) or "
+                                   "bscan_kernel + bselect_kernel (cuda_core)",
+                   "plan_ms": plan_ms, "scan_ms": scan_ms, "uncertified_queries_last_step": uncertified,
+                   "algorithmic_ops_per_pair": 512, "wall_s_bracketed": t1 - t0},
+        "roofline": roof, "clocks": clk,
+        "gpu_launches": args.steps * (4 if args.engine == "tensor" else 3), "e2e": e2e,
+    }
+    emit(line)
+    for sg in segs:
+        sg.free()
+    lib.mrl_plans_free(dev.ptr, plans)
+
+
+def measured_peaks_tensor():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
 def cpu_baseline(args, pax, mean, qd, seg, M, dev, cfg):
     """The oracle's threaded reference scan on a bounded sample of the same queries."""
     import ora
@@ -556,6 +713,10 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.batch > 1:
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            raise SystemExit("--batch runs on one GPU (BASELINE config 3)")
+        run_batch(args)
     else:
         run_ours(args)
 
