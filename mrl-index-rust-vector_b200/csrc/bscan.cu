@@ -439,10 +439,38 @@ __global__ void __launch_bounds__(256) tprep_kernel(const DevPlan* __restrict__ 
     }
 }
 
+// The per-query constants of the f32 score path (fast_score with f32 unscaling), packed for
+// three 16-byte shared loads; flags: bit 0 EdenProd prefix, 1 EdenB1 mid, 2 depth >= L1, 3 depth
+// full with a tail fold, 4 f32 unscaling (else the query takes fast_score on its Scalars).
+struct __align__(16) QConst {
+    float eden_mean_ip, prefix_sum, mid_mean_ip, w_s4;
+    float unf_p, unf_s1, unf_s4;
+    uint32_t flags;
+    int32_t c1, c4, pad0, pad1;
+};
+
+// fast_score (scan_common.cuh) on a QConst: the same operations in the same order.
+__device__ __forceinline__ float qscore(const SlotMeta& m, int32_t P, int32_t s1, int32_t s4, const QConst& c) {
+    const float cd = __fmul_rn(__int2float_rn(P), c.unf_p);
+    float sc = (c.flags & 1u) ? __fadd_rn(c.eden_mean_ip, __fmul_rn(m.scale, cd))
+                              : __fadd_rn(__fmul_rn(cd, m.scale), __fmul_rn(m.offset, c.prefix_sum));
+    if (c.flags & 4u) {
+        const float v = __fmul_rn(__int2float_rn(s1), c.unf_s1);
+        if (c.flags & 2u) sc = __fadd_rn(sc, __fadd_rn(c.mid_mean_ip, __fmul_rn(m.offset, v)));
+        else sc = __fadd_rn(sc, __fmul_rn(v, m.mid_n));
+    }
+    if (c.flags & 8u) {
+        const float v = __fmul_rn(__int2float_rn(s4), c.unf_s4);
+        sc = __fadd_rn(sc, __fmul_rn(__fmul_rn(v, fmaxf(m.high_n, 1e-6f)), c.w_s4));
+    }
+    return sc;
+}
+
 struct TShared {
     uint8_t B[kBTileBytes];              // offset 0 (1 KB aligned)
     Scalars S[kTQ];
-    int32_t c1[kTQ], c4[kTQ];
+    QConst qc[kTQ];
+    uint4 onehot[16];                    // the 16 one-hot byte patterns of a 4-bit level
     float2 rho[256];
     u64 tau[kTQ];
     BWarpState wst[kBWarps][4];
@@ -475,15 +503,16 @@ __device__ __forceinline__ void bsel_offer1(u64* wl, u64* q, int lane, u64* cta_
     if (qn + nn >= 32) bsel_flush(wl, q, lane, cta_tau, st);
 }
 
-// One-hot bytes of four 4-bit levels (nibbles 0..3 of `w` shifted by 4*n0) into 16 columns.
-__device__ __forceinline__ void onehot4(uint32_t w, uint32_t (&r)[16]) {
+// One-hot bytes of the four 4-bit levels in nibbles 0..3 of `w`, 4 columns each, from the
+// 16-entry pattern table.
+__device__ __forceinline__ void onehot4(uint32_t w, const uint4* tab, uint32_t (&r)[16]) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const uint32_t l = (w >> (4 * i)) & 15u;
-        const uint32_t one = 1u << ((l & 3u) << 3);
-        const uint32_t hi = l >> 2;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) r[4 * i + c] = hi == (uint32_t)c ? one : 0u;
+        const uint4 x = tab[(w >> (4 * i)) & 15u];
+        r[4 * i] = x.x;
+        r[4 * i + 1] = x.y;
+        r[4 * i + 2] = x.z;
+        r[4 * i + 3] = x.w;
     }
 }
 // 0/1 bytes of the 16 nibbles' bits of two words (64 bits) into 16 columns.
@@ -517,6 +546,11 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
         tc::fence_mbar_init();
     }
     fill_rho_tab(sh.rho, tid, kBThreads);
+    if (tid < 16) {
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        w[tid >> 2] = 1u << (8 * (tid & 3));
+        sh.onehot[tid] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
@@ -538,8 +572,21 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
         if (tid < kTQ) {
             if ((uint32_t)tid < nq) {
                 fill_scalars(p.plans + q0 + tid, p.w_s4, p.depth, 1, sh.S[tid]);
-                sh.c1[tid] = t.consts[2 * (q0 + tid)];
-                sh.c4[tid] = t.consts[2 * (q0 + tid) + 1];
+                const Scalars& S = sh.S[tid];
+                QConst c;
+                c.eden_mean_ip = S.eden_mean_ip;
+                c.prefix_sum = S.prefix_sum;
+                c.mid_mean_ip = S.mid_mean_ip;
+                c.w_s4 = S.w_s4;
+                c.unf_p = S.unf_prefix;
+                c.unf_s1 = S.unf_s1;
+                c.unf_s4 = S.unf_s4;
+                c.flags = (S.eden ? 1u : 0u) | (S.mid_b1 ? 2u : 0u) | (S.depth >= MRL_DEPTH_L1 ? 4u : 0u) |
+                          (S.depth == MRL_DEPTH_FULL && S.has_tail ? 8u : 0u) | (S.f32_unscale ? 16u : 0u);
+                c.c1 = t.consts[2 * (q0 + tid)];
+                c.c4 = t.consts[2 * (q0 + tid) + 1];
+                c.pad0 = c.pad1 = 0;
+                sh.qc[tid] = c;
             }
             sh.tau[tid] = 0ull;
         }
@@ -550,17 +597,22 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
         __syncthreads();
         tc::fence_after();
 
+        // this thread's slot row of each tile: lane quarter qw; slot data one tile ahead
+        const int r = 32 * qw + lane;
+        const int v = r & 63;
+        Slot4 nxt;
+        nxt.c0 = nxt.c1 = nxt.c2 = nxt.c3 = make_uint4(0u, 0u, 0u, 0u);
+        if (lo_b + (uint32_t)(r >> 6) < hi_b && page_live(p, lo_b + (uint32_t)(r >> 6)))
+            load_slot(p.pages, lo_b + (uint32_t)(r >> 6), v, nxt);
         for (uint32_t pg = lo_b; pg < hi_b; pg += 2) {
-            // ---- A: this thread's slot row (lane quarter qw), this warp's column share (g4)
-            const int r = 32 * qw + lane;
+            // ---- A: this thread's slot row, this warp's column share (g4)
             const uint32_t b = pg + (uint32_t)(r >> 6);
-            const int v = r & 63;
             const bool live = b < hi_b && page_live(p, b);  // warp-uniform
-            Slot4 s;
-            if (live) {
-                load_slot(p.pages, b, v, s);
-            } else {
-                s.c0 = s.c1 = s.c2 = s.c3 = make_uint4(0u, 0u, 0u, 0u);
+            const Slot4 s = nxt;
+            {
+                const uint32_t bn = b + 2;
+                nxt.c0 = nxt.c1 = nxt.c2 = nxt.c3 = make_uint4(0u, 0u, 0u, 0u);
+                if (bn < hi_b && page_live(p, bn)) load_slot(p.pages, bn, v, nxt);
             }
             const SlotMeta m = slot_meta_tab(s.c3.z, s.c3.w, sh.rho);
             {
@@ -571,7 +623,7 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {  // dims 16 g4 + 4c .. + 3
                     const uint32_t w = (c < 2 ? wa : wb) >> (16 * (c & 1));
-                    onehot4(w, rr);
+                    onehot4(w, sh.onehot, rr);
                     TC_ST16(tbase + my_lane + (uint32_t)(64 * g4 + 16 * c), rr);
                 }
                 if (g4 == 0) { bits16(s.c2.x, s.c2.y, rr); TC_ST16(tbase + my_lane + 256u, rr); }
@@ -615,11 +667,12 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
             for (int j = 0; j < 4; ++j) {
                 const int q = 4 * g4 + j;
                 if ((uint32_t)q < nq) {  // warp-uniform
+                    const QConst c = sh.qc[q];
                     const int32_t P = digits4(dp + 4 * j);
-                    const int32_t A1 = sh.c1[q] + digits4(d1 + 4 * j);
-                    const int32_t A4 = sh.c4[q] + digits4(d4 + 4 * j);
-                    const u64 key =
-                        (!live || m.tomb) ? 0ull : make_key(fast_score(m, P, A1, A4, sh.S[q]), b * 64 + v);
+                    const int32_t A1 = c.c1 + digits4(d1 + 4 * j);
+                    const int32_t A4 = c.c4 + digits4(d4 + 4 * j);
+                    const float sc = (c.flags & 16u) ? qscore(m, P, A1, A4, c) : fast_score(m, P, A1, A4, sh.S[q]);
+                    const u64 key = (!live || m.tomb) ? 0ull : make_key(sc, b * 64 + v);
                     bsel_offer1(sh.wlist[warp][j], sh.queue[warp][j], lane, &sh.tau[q], &sh.wst[warp][j], key);
                 }
             }
