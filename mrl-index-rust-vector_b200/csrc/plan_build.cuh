@@ -117,12 +117,22 @@ struct PlanShared {
 __device__ __forceinline__ void plan_inputs(const float* __restrict__ q, uint32_t dims, const float* __restrict__ eden_mean,
                                             const float* __restrict__ mid_mean, float* s_q, PlanShared& sh) {
     const int tid = threadIdx.x, nthr = blockDim.x;
-    for (uint32_t i = tid; i < dims; i += nthr) s_q[i] = q[i];
-    for (int i = tid; i < kPrefix + kRabitq; i += nthr) {  // either centre array may be NULL
-        const float* src = i < kPrefix ? eden_mean : mid_mean;
-        sh.mean[i] = src ? src[i < kPrefix ? i : i - kPrefix] : 0.0f;
+    // the loads are issued before the stores that consume them, so their latencies overlap
+    float m = 0.0f, c = 0.0f;
+    if (tid < kPrefix + kRabitq) {  // either centre array may be NULL
+        const float* src = tid < kPrefix ? eden_mean : mid_mean;
+        m = src ? __ldg(src + (tid < kPrefix ? tid : tid - kPrefix)) : 0.0f;
     }
-    if (tid < 16) sh.cb[tid] = g_lloyd_b4[tid];
+    if (tid < 16) c = g_lloyd_b4[tid];
+    for (uint32_t i0 = tid; i0 < dims; i0 += 2u * nthr) {
+        const uint32_t i1 = i0 + nthr;
+        const float v0 = __ldg(q + i0);
+        const float v1 = i1 < dims ? __ldg(q + i1) : 0.0f;
+        s_q[i0] = v0;
+        if (i1 < dims) s_q[i1] = v1;
+    }
+    if (tid < kPrefix + kRabitq) sh.mean[tid] = m;
+    if (tid < 16) sh.cb[tid] = c;
 }
 
 // Phase A, threads 0..127 in four warp roles (the plan branches are independent until the final
@@ -357,11 +367,14 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
             P->unscale_s4 = ldexp(1.0, -sh_4);
         }
     } else if (warp == 3) {
-        // q_tail_sq (src/scan.rs:203-207): the longest sequential sum
+        // q_tail_sq (src/scan.rs:203-207): the longest sequential sum; only the stored plan's
+        // norms use it (no scan score does), so a scan's own table build skips it
         if (lane == 0) {
             float ts = 0.0f;
+            if (full) {
 #pragma unroll 8
-            for (uint32_t d = kTailStart; d < dims; ++d) ts = f_add(ts, f_mul(s_q[d], s_q[d]));
+                for (uint32_t d = kTailStart; d < dims; ++d) ts = f_add(ts, f_mul(s_q[d], s_q[d]));
+            }
             s_scal[2] = ts;
         }
         if (full) {

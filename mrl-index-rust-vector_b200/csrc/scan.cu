@@ -474,10 +474,23 @@ __device__ void xch_publish_and_merge(const ScanLaunch& p, unsigned char* smem, 
         if (tid == 0 && p.out_status) *p.out_status = status | 4u;  // a rank's record never arrived
         return;
     }
-    for (unsigned r = 0; r < p.xch_world; ++r) {
-        const uint4* src = reinterpret_cast<const uint4*>(p.xch_rec[r]);
-        uint4* dst = reinterpret_cast<uint4*>(smem + r * rb);
-        for (size_t i = tid; i < words; i += kThreads) dst[i] = __ldcg(src + i);
+    {
+        // every rank's record into shared memory; each thread has up to four (mostly remote) loads
+        // in flight before storing, instead of one NVLink round trip per rank in turn
+        const unsigned nw = (unsigned)words, total = p.xch_world * nw;
+        for (unsigned i0 = tid; i0 < total; i0 += 4u * kThreads) {
+            uint4 x[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const unsigned i = i0 + (unsigned)j * kThreads;
+                if (i < total) x[j] = __ldcg(reinterpret_cast<const uint4*>(p.xch_rec[i / nw]) + (i % nw));
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const unsigned i = i0 + (unsigned)j * kThreads;
+                if (i < total) reinterpret_cast<uint4*>(smem + (i / nw) * rb)[i % nw] = x[j];
+            }
+        }
     }
     __syncthreads();
     xch::merge_records<false>(smem, p.xch_world, p.k, p.k, p.out_ids, p.out_scores, p.out_count);
@@ -624,8 +637,23 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     // Every CTA's list into shared memory, rows LP = L | 1 keys apart (an odd stride: threads that
     // each read a different list hit different banks).
     const unsigned LP = L | 1u;
-    for (unsigned c = warp; c < G; c += kWarps)
-        if ((unsigned)lane < L) s_cand[c * LP + lane] = __ldcg(p.cta_keys + c * 32 + lane);
+    {
+        // four loads in flight per thread before their stores (the lists come from L2)
+        const unsigned nl = G * L, lsh = (unsigned)(__ffs((int)L) - 1);
+        for (unsigned i0 = tid; i0 < nl; i0 += 4u * kThreads) {
+            u64 x[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const unsigned i = i0 + (unsigned)j * kThreads;
+                x[j] = i < nl ? __ldcg(p.cta_keys + (i >> lsh) * 32 + (i & (L - 1))) : 0ull;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const unsigned i = i0 + (unsigned)j * kThreads;
+                if (i < nl) s_cand[(i >> lsh) * LP + (i & (L - 1))] = x[j];
+            }
+        }
+    }
     __syncthreads();
 
     // A CTA list may have dropped a top-k key only if it is full and its last key ranks below k.
