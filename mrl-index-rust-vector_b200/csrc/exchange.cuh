@@ -80,5 +80,73 @@ __device__ __forceinline__ void merge_records(const unsigned char* lists, uint32
     }
 }
 
+// Number of the first n entries of a sorted record part (ids, scores) that order before (sx, ix).
+__device__ __forceinline__ uint32_t count_before(const uint64_t* ids, const float* scores, uint32_t n, float sx,
+                                                 uint64_t ix) {
+    uint32_t lo = 0, hi = n;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (before(scores[mid], ids[mid], sx, ix)) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+// The same merge for records in shared memory (the scan kernel's NVLink exchange tail), as a tree
+// of pairwise merges: at each level every entry of a pair's two sorted records is placed by one
+// binary search in the partner record, the merged top-k becomes a record of the next level, and
+// the last level writes the outputs. Levels alternate between `recs` (n_lists records) and `tmp`
+// (room for ceil(n_lists / 2) records). Every thread of the CTA calls it.
+__device__ __forceinline__ void merge_records_tree(unsigned char* recs, unsigned char* tmp, uint32_t n_lists,
+                                                   uint32_t stride, uint32_t k, uint64_t* out_ids,
+                                                   float* out_scores, uint32_t* out_count) {
+    const size_t rb = MRL_MERGE_RECORD_BYTES(stride);
+    k = min(k, stride);
+    unsigned char* src = recs;
+    unsigned char* dst = tmp;
+    uint32_t n = n_lists;
+    for (;;) {
+        const bool last = n <= 2;
+        const uint32_t m = (n + 1) >> 1;
+        const uint32_t total = 2 * m * k;  // entry e: pair e / (2k), side (e / k) & 1, index e % k
+        for (uint32_t e = threadIdx.x; e < total; e += blockDim.x) {
+            const uint32_t pr = e / (2 * k), side = (e / k) & 1u, idx = e % k;
+            const uint32_t li = 2 * pr + side, qi = 2 * pr + (side ^ 1u);
+            if (li >= n) continue;
+            const Record L = record<false>(src, rb, stride, li);
+            if (idx >= L.count) continue;
+            const float sx = L.scores[idx];
+            const uint64_t ix = L.ids[idx];
+            uint32_t r = idx;
+            if (qi < n) {
+                const Record Q = record<false>(src, rb, stride, qi);
+                r += count_before(Q.ids, Q.scores, min(Q.count, k), sx, ix);
+            }
+            if (r < k) {
+                if (last) {
+                    out_ids[r] = ix;
+                    out_scores[r] = sx;
+                } else {
+                    unsigned char* d = dst + (size_t)pr * rb;
+                    reinterpret_cast<uint64_t*>(d)[r] = ix;
+                    reinterpret_cast<float*>(d + (size_t)stride * 8)[r] = sx;
+                }
+            }
+        }
+        if (threadIdx.x < m) {  // merged counts
+            const uint32_t a = record<false>(src, rb, stride, 2 * threadIdx.x).count;
+            const uint32_t b = 2 * threadIdx.x + 1 < n ? record<false>(src, rb, stride, 2 * threadIdx.x + 1).count : 0u;
+            const uint32_t c = min(min(a, k) + min(b, k), k);
+            if (last) *out_count = c;
+            else *reinterpret_cast<uint32_t*>(dst + (size_t)threadIdx.x * rb + (size_t)stride * 12) = c;
+        }
+        __syncthreads();
+        if (last) return;
+        unsigned char* t = src;
+        src = dst;
+        dst = t;
+        n = m;
+    }
+}
+
 }  // namespace xch
 }  // namespace mrl

@@ -201,6 +201,7 @@ struct ScanLaunch {
     // raises its flag (release, system scope), waits (bounded) for every other rank's flag of
     // this epoch, reads their records over NVLink and merges all into out_* (the global top-k)
     uint32_t xch_world, xch_rank, xch_epoch;
+    uint32_t xch_tree;  // set by launch_scan: merge as a pairwise tree (room for its buffers)
     const unsigned char* xch_rec[kMaxRanks];  // every rank's record of this parity
     unsigned int* xch_flag[kMaxRanks];        // every rank's flag word of this parity
 };

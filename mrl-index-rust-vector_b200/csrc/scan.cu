@@ -455,19 +455,23 @@ __device__ void xch_publish_and_merge(const ScanLaunch& p, unsigned char* smem, 
     const int tid = threadIdx.x;
     const size_t rb = MRL_MERGE_RECORD_BYTES(p.k), words = rb / 16;
     __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        st_release_sys(p.xch_flag[p.xch_rank], p.xch_epoch);
-        int ok = 1;
-        for (unsigned r = 0; r < p.xch_world && ok; ++r) {
-            if (r == p.xch_rank) continue;
-            unsigned it = 0;
-            while (ld_acquire_sys(p.xch_flag[r]) != p.xch_epoch) {
-                if (++it > (1u << 21)) { ok = 0; break; }  // ~2-3 s of remote polls
-                if (it > 64) __nanosleep(256);
-            }
+    if (tid < 32) {
+        // warp 0: lane 0 publishes this rank's flag; lane r polls rank r's flag, so the waits for
+        // all ranks overlap (one NVLink round trip when every record is already there)
+        if (tid == 0) {
+            __threadfence();
+            st_release_sys(p.xch_flag[p.xch_rank], p.xch_epoch);
         }
-        *s_ok = ok;
+        const bool mine = (unsigned)tid < p.xch_world && (unsigned)tid != p.xch_rank;
+        bool arrived = !mine;
+        unsigned it = 0;
+        while (!__all_sync(kFull, arrived)) {
+            if (!arrived) arrived = ld_acquire_sys(p.xch_flag[tid]) == p.xch_epoch;
+            if (++it > (1u << 21)) break;  // ~2-3 s of remote polls
+            if (it > 64) __nanosleep(256);
+        }
+        const bool ok = __all_sync(kFull, arrived);
+        if (tid == 0) *s_ok = ok ? 1 : 0;
     }
     __syncthreads();
     if (!*s_ok) {
@@ -493,7 +497,11 @@ __device__ void xch_publish_and_merge(const ScanLaunch& p, unsigned char* smem, 
         }
     }
     __syncthreads();
-    xch::merge_records<false>(smem, p.xch_world, p.k, p.k, p.out_ids, p.out_scores, p.out_count);
+    if (p.xch_tree)
+        xch::merge_records_tree(smem, smem + (size_t)p.xch_world * rb, p.xch_world, p.k, p.k, p.out_ids, p.out_scores,
+                                p.out_count);
+    else
+        xch::merge_records<false>(smem, p.xch_world, p.k, p.k, p.out_ids, p.out_scores, p.out_count);
     if (tid == 0 && p.out_status) *p.out_status = status;
 }
 
@@ -820,13 +828,24 @@ __global__ void __launch_bounds__(kThreads) debug_scores_kernel(const ScanLaunch
 
 int scan_ctas(int device_sms) { return device_sms; }
 
+// Shared memory of the exchange merge: the world's records, plus room for the merge tree's first
+// level (ceil(world / 2) records) when that stays within kXchTreeBytes; else the records alone and
+// the one-level merge.
+constexpr size_t kXchTreeBytes = 200 * 1024;
+bool xch_use_tree(uint32_t world, uint32_t k) {
+    return (size_t)(world + (world + 1) / 2) * MRL_MERGE_RECORD_BYTES(k) <= kXchTreeBytes;
+}
+size_t xch_merge_bytes(uint32_t world, uint32_t k) {
+    return (size_t)(xch_use_tree(world, k) ? world + (world + 1) / 2 : world) * MRL_MERGE_RECORD_BYTES(k);
+}
+
 size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t xch_world) {
     size_t p2 = 1;
     while (p2 < k) p2 <<= 1;
     size_t bytes = sizeof(u64) * (kWarps * kQueue + kWarps * 32 + (size_t)ctas * 33 + p2) +
                    sizeof(unsigned) * (kBins + ctas);
     if (fused_dims) bytes = std::max(bytes, fused_plan_bytes(fused_dims));
-    if (xch_world) bytes = std::max(bytes, (size_t)xch_world * MRL_MERGE_RECORD_BYTES(k));  // records to merge
+    if (xch_world) bytes = std::max(bytes, xch_merge_bytes(xch_world, k));  // records to merge
     return bytes;
 }
 
@@ -848,6 +867,7 @@ int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream) {
         cur.store(smem, std::memory_order_relaxed);
     }
     ScanLaunch arg = p;
+    arg.xch_tree = p.xch_world && xch_use_tree(p.xch_world, p.k) ? 1u : 0u;
     void* args[] = {&arg};
     if (cudaLaunchCooperativeKernel(fn, dim3(ctas), dim3(kThreads), args, smem, stream) != cudaSuccess) return -1;
     return 0;
