@@ -57,7 +57,8 @@ def parse():
                          "(code stays cached, as in a serving loop) or by flushing L2 before every step")
     ap.add_argument("--segments", type=int, default=4, help="segments rotated over with --l2 rotate")
     ap.add_argument("--batch", type=int, default=1,
-                    help="queries per step; > 1 runs BASELINE config 3 (batched scan, one GPU)")
+                    help="queries per step; > 1 runs BASELINE config 3 (one GPU) or config 4 (torchrun: --docs "
+                         "split across the ranks)")
     ap.add_argument("--engine", choices=["tensor", "cuda_core"], default="tensor",
                     help="batched-scan engine (--batch > 1)")
     ap.add_argument("--exchange", choices=["nvlink", "nccl"], default="nvlink",
@@ -466,38 +467,59 @@ def run_ours(args):
 
 
 def run_batch(args):
-    """batches of --batch queries over the 1M x 768 corpus on one GPU. A step =
-    plan build of the batch (mrl_plan_build_device) + one batched scan (mrl_scan_batch_device: the
-    per-SM query-tile scan on the chosen engine, then one selection CTA per query)."""
+    """BASELINE configs 3 and 4: batches of --batch queries. A step = plan build of the batch
+    (mrl_plan_build_device) + one batched scan (mrl_scan_batch_device: the per-SM query-tile scan on
+    the chosen engine, then one selection CTA per query). One GPU: config 3 over --docs docs. N GPUs
+    (torchrun): config 4, the --docs corpus split into contiguous page ranges, one per rank (strong
+    scaling); each rank's per-query top-k goes through BatchShardExchange (pack, one NCCL
+    all-gather of the batch's records, per-query merge kernel), so every rank ends each step with
+    the global top-k of every query."""
     import torch
+    import torch.distributed as dist
 
-    torch.cuda.set_device(0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
     torch.cuda.set_stream(torch.cuda.Stream())
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     import mrl_b200 as M
 
     lib = M.load()
-    dev = M.Device(0)
+    dev = M.Device(local)
     torch_stream = torch.cuda.current_stream().cuda_stream
     dev.set_stream(torch_stream)
     M._capi.check(dev.ptr, lib.mrl_set_batch_engine(dev.ptr, 0 if args.engine == "tensor" else 1))
-    n, dims, k, B = args.docs, args.dims, args.k, args.batch
+    n_total, dims, k, B = args.docs, args.dims, args.k, args.batch
+    pages_total = (n_total + 63) // 64
+    p0, npg = M.shard_range(pages_total, world, rank)
+    row0 = p0 * 64
+    n = max(min(n_total, (p0 + npg) * 64) - row0, 0)
     nb = (n + 63) // 64
     warm = max(args.warmup, 3)
-    x, mean = build_corpus_gpu(M, dev, n, dims, row0=0)
-    seg, pax, desc, keep = encode_gpu(M, dev, x, n, dims, mean, block_id_base=0)
+    x, mean = build_corpus_gpu(M, dev, n, dims, row0=row0)
+    if world > 1:  # one EDEN fit for the whole corpus: rank 0's
+        mt = torch.from_numpy(mean).cuda()
+        dist.broadcast(mt, 0)
+        mean = mt.cpu().numpy()
+    seg, pax, desc, keep = encode_gpu(M, dev, x, n, dims, mean, block_id_base=p0)
     segs = [seg]
-    for r in range(1, max(args.segments, 1)):  # rotate: 4 x 64 MB of pages > L2
-        M._capi.check(dev.ptr, lib.mrl_synth_docs_device(dev.ptr, DOC_SEED, r * n, n, dims, C.c_void_p(x.data_ptr())))
+    for r in range(1, max(args.segments, 1)):  # rotate over segments of the same shape: pages > L2
+        M._capi.check(dev.ptr, lib.mrl_synth_docs_device(dev.ptr, DOC_SEED, r * pages_total * 64 + row0, n, dims,
+                                                         C.c_void_p(x.data_ptr())))
         sp = C.c_void_p()
         M._capi.check(dev.ptr, lib.mrl_encode_device(dev.ptr, C.c_void_p(x.data_ptr()), n, dims, 8, C.byref(desc),
-                                                     None, 0, C.byref(sp)))
+                                                     None, p0, C.byref(sp)))
         segs.append(M.Segment(sp, dev))
     del x, pax
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     n_batches = warm + args.steps
     qd = torch.empty((n_batches * B, dims), dtype=torch.float32, device="cuda")
-    M._capi.check(dev.ptr, lib.mrl_synth_queries_device(dev.ptr, DOC_SEED, n, Q_SEED, n_batches * B, dims,
+    M._capi.check(dev.ptr, lib.mrl_synth_queries_device(dev.ptr, DOC_SEED, n_total, Q_SEED, n_batches * B, dims,
                                                         C.c_float(SIGMA), C.c_void_p(qd.data_ptr()), None))
     plans = C.c_void_p()
     M._capi.check(dev.ptr, lib.mrl_plans_alloc(dev.ptr, B, dims, C.byref(plans)))
@@ -506,6 +528,7 @@ def run_batch(args):
     sc = torch.empty(B * k, dtype=torch.float32, device="cuda")
     cnt = torch.empty(B, dtype=torch.int32, device="cuda")
     st = torch.zeros(B, dtype=torch.int32, device="cuda")
+    exch = M.BatchShardExchange(dev, B, k) if world > 1 else None
     qbytes = B * dims * 4
 
     def step(i, ev=None):
@@ -521,13 +544,23 @@ def run_batch(args):
                                                          C.c_void_p(st.data_ptr())))
         if ev is not None:
             ev[2].record()
+        if exch is not None:
+            exch(ids.data_ptr(), sc.data_ptr(), cnt.data_ptr())
+        if ev is not None:
+            ev[3].record()
+
+    def mk():
+        return [torch.cuda.Event(enable_timing=True) for _ in range(4)]
 
     for i in range(warm):
         step(i)
     torch.cuda.synchronize()
-    clocks = Clocks(0)
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(local)
     clocks.start()
     time.sleep(0.3)
+    torch.cuda.synchronize()
     ev_all = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     t0 = time.perf_counter()
     ev_all[0].record()
@@ -537,42 +570,68 @@ def run_batch(args):
     torch.cuda.synchronize()
     t1 = time.perf_counter()
     total_ms = ev_all[0].elapsed_time(ev_all[1])
+    if world > 1:
+        dist.barrier()
     time.sleep(0.2)
     clk = clocks.stop()
     uncertified = int(((st & 8) != 0).sum().item())
-    # plan / scan split (information)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(min(5, args.steps))]
+    evs = [mk() for _ in range(min(5, args.steps))]  # plan / scan / exchange split (information)
     for i, e in enumerate(evs):
         step(warm + i, e)
     torch.cuda.synchronize()
     plan_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in evs]))
     scan_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in evs]))
+    exch_ms = float(np.mean([e[2].elapsed_time(e[3]) for e in evs]))
+    if world > 1:
+        t = torch.tensor([total_ms, scan_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, scan_ms = float(t[0].item()), float(t[1].item())
 
-    # e2e through the host-facing C ABI: pinned host queries -> plans -> batched scan -> host results
-    dev.set_stream(0)
+    # e2e: pinned host queries -> plans -> batched scan (-> exchange) -> host results, max over ranks
     qh = torch.empty((B, dims), dtype=torch.float32, pin_memory=True)
     ids_h = torch.empty(B * k, dtype=torch.int64, pin_memory=True)
     sc_h = torch.empty(B * k, dtype=torch.float32, pin_memory=True)
     cnt_h = torch.empty(B, dtype=torch.int32, pin_memory=True)
     e2e_steps = min(args.steps, 10)
     tot = 0.0
+    if world == 1:
+        dev.set_stream(0)
     for i in range(e2e_steps + 2):
         qh.copy_(qd[(i % n_batches) * B:(i % n_batches + 1) * B].cpu())
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         s0 = time.perf_counter()
         M._capi.check(dev.ptr, lib.mrl_plan_rebuild(dev.ptr, C.c_void_p(qh.data_ptr()), B, dims, C.byref(desc), plans))
-        M._capi.check(dev.ptr, lib.mrl_scan(dev.ptr, segs[i % len(segs)].ptr, plans, C.byref(cfg), None, None,
-                                            C.c_void_p(ids_h.data_ptr()), C.c_void_p(sc_h.data_ptr()),
-                                            C.c_void_p(cnt_h.data_ptr())))
+        if world == 1:
+            M._capi.check(dev.ptr, lib.mrl_scan(dev.ptr, segs[i % len(segs)].ptr, plans, C.byref(cfg), None, None,
+                                                C.c_void_p(ids_h.data_ptr()), C.c_void_p(sc_h.data_ptr()),
+                                                C.c_void_p(cnt_h.data_ptr())))
+        else:
+            M._capi.check(dev.ptr, lib.mrl_scan_batch_device(dev.ptr, segs[i % len(segs)].ptr, plans, 0, B,
+                                                             C.byref(cfg), None, None, C.c_void_p(ids.data_ptr()),
+                                                             C.c_void_p(sc.data_ptr()), C.c_void_p(cnt.data_ptr()),
+                                                             C.c_void_p(st.data_ptr())))
+            g_ids, g_sc, g_cnt = exch(ids.data_ptr(), sc.data_ptr(), cnt.data_ptr())
+            ids_h.copy_(g_ids, non_blocking=True)
+            sc_h.copy_(g_sc, non_blocking=True)
+            cnt_h.copy_(g_cnt, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
         if i >= 2:
             tot += time.perf_counter() - s0
+    if world == 1:
+        dev.set_stream(torch_stream)
+    else:
+        t = torch.tensor([tot], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tot = float(t.item())
     e2e = {"value": B * e2e_steps / tot, "unit": "QPS", "h2d_bytes_per_step": qbytes,
            "d2h_bytes_per_step": B * (k * 12 + 4), "steps": e2e_steps,
-           "path": "mrl_plan_rebuild (host queries) + mrl_scan (batched from 8 plans, host results, synchronous)"}
-    dev.set_stream(torch_stream)
+           "path": ("mrl_plan_rebuild (host queries) + mrl_scan (batched from 8 plans, host results, synchronous)"
+                    if world == 1 else "per rank: mrl_plan_rebuild (host queries) + mrl_scan_batch_device + "
+                    "BatchShardExchange (pack, NCCL all-gather, per-query merge) + copy to pinned host; max over ranks")}
 
-    pairs = B * n
-    step_s = total_ms / args.steps / 1e3
+    pairs = B * n  # this rank's (query, doc) pairs per step
     if args.engine == "tensor":
         ops = pairs * (16 * 64 + 128 + 64) * 4 * 2  # executed int8 MMA ops: 1216 K bytes x 4 digits x 2
         bf16, _ = measured_peaks_tensor()
@@ -587,26 +646,36 @@ def run_batch(args):
                 "unit": "TOP/s", "frac": alg / (scan_ms / 1e3) / 1e12 / cuda_core_peak,
                 "peak_kind": "148 SMs x 128 lanes x 2 x 1965 MHz (nominal)", "kernel": "bscan_kernel",
                 "traffic": None}
+    workload = (f"config 3: batched scan, {B} queries per step over {n_total:,} x {dims} docs" if world == 1 else
+                f"config 4: sharded batched scan, {B} queries per step over {n_total:,} x {dims} docs split across "
+                f"{world} GPUs (NCCL all-gather of per-rank top-{k} + per-query merge)")
     line = {
-        "metric": METRIC, "value": B * args.steps / (total_ms / 1e3), "unit": "QPS", "n_gpus": 1,
+        "metric": METRIC, "value": B * args.steps / (total_ms / 1e3), "unit": "QPS", "n_gpus": world,
         "steps": args.steps, "warmup": warm, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8 tensor + int32 + f32" if args.engine == "tensor" else
-        "int32+f32", "data": "synthetic",
-        "config": {"workload": f"config 3: batched scan, {B} queries per step over 1M x 768 docs, EDEN-prod + RaBitQ"
-                               " + folded tail, shortlist 256, full_64b", "docs": n, "dims": dims, "batch": B,
-                   "shortlist": k, "engine": args.engine, "parallelism": "single GPU",
-                   "l2": f"steps rotate over {len(segs)} segments ({len(segs) * nb * 4096 / 1e6:.0f} MB of pages)",
-                   "step_kernels": "plan_kernel, then tprep_kernel + tscan_kernel + bselect_kernel (tensor) or "
-                                   "bscan_kernel + bselect_kernel (cuda_core)",
-                   "plan_ms": plan_ms, "scan_ms": scan_ms, "uncertified_queries_last_step": uncertified,
-                   "algorithmic_ops_per_pair": 512, "wall_s_bracketed": t1 - t0},
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "int8 tensor + int32 + f32" if args.engine == "tensor" else "int32+f32", "data": "synthetic",
+        "config": {"workload": workload + ", EDEN-prod + RaBitQ + folded tail, shortlist 256, full_64b",
+                   "docs_total": n_total, "docs_per_rank": n, "dims": dims, "batch": B, "shortlist": k,
+                   "engine": args.engine, "parallelism": f"shard{world}" if world > 1 else "single GPU",
+                   "l2": f"steps rotate over {len(segs)} segments ({len(segs) * nb * 4096 / 1e6:.0f} MB of pages per "
+                         "rank)", "step_kernels": "plan_kernel, then tprep_kernel + tscan_kernel + bselect_kernel "
+                                                  "(tensor) or bscan_kernel + bselect_kernel (cuda_core)"
+                                                  + ("; pack_records + NCCL all-gather + merge_topk_batch"
+                                                     if world > 1 else ""),
+                   "plan_ms": plan_ms, "scan_ms": scan_ms, "exchange_ms": exch_ms if world > 1 else None,
+                   "uncertified_queries_last_step": uncertified, "algorithmic_ops_per_pair": 512,
+                   "wall_s_bracketed": t1 - t0},
         "roofline": roof, "clocks": clk,
-        "gpu_launches": args.steps * (4 if args.engine == "tensor" else 3), "e2e": e2e,
+        "gpu_launches": args.steps * ((4 if args.engine == "tensor" else 3) + (2 if world > 1 else 0)), "e2e": e2e,
     }
-    emit(line)
+    if rank == 0:
+        emit(line)
     for sg in segs:
         sg.free()
     lib.mrl_plans_free(dev.ptr, plans)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def measured_peaks_tensor():
@@ -714,8 +783,6 @@ def main():
     if args.impl == "reference":
         run_reference(args)
     elif args.batch > 1:
-        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-            raise SystemExit("--batch runs on one GPU (BASELINE config 3)")
         run_batch(args)
     else:
         run_ours(args)

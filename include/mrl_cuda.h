@@ -289,6 +289,16 @@ int mrl_engine_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* d_query, uint
 #define MRL_MERGE_RECORD_BYTES(stride) ((((size_t)(stride)) * 12u + 4u + 15u) & ~(size_t)15u)
 int mrl_merge_topk(mrl_ctx* ctx, const void* d_lists, uint32_t n_lists, uint32_t stride, uint32_t k,
                    uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_count);
+/* The exchange step for a batch (each rank scans its pages for n_q queries with
+ * mrl_scan_batch_device). mrl_pack_records writes the batch's outputs (n_q rows of k ids / scores,
+ * n_q counts) as n_q records of stride k. After an all-gather of every rank's records (rank-major:
+ * record q of list r at (r * n_q + q) * MRL_MERGE_RECORD_BYTES(stride)), mrl_merge_topk_batch
+ * merges each query's n_lists records into its global top-k (rows of k in the outputs, counts),
+ * one CTA per query, in the same order as mrl_merge_topk. Device buffers, context stream. */
+int mrl_pack_records(mrl_ctx* ctx, const uint64_t* d_ids, const float* d_scores, const uint32_t* d_counts,
+                     uint32_t n_q, uint32_t k, void* d_records);
+int mrl_merge_topk_batch(mrl_ctx* ctx, const void* d_lists, uint32_t n_lists, uint32_t n_q, uint32_t stride,
+                         uint32_t k, uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_counts);
 /* Per-vector scores of plan `q` for every slot (n_blocks*64, host), and for MRL_MODE_FAST the
  * three int32 stage sums per slot (prefix, mid band, folded tail; may be NULL). Inactive slots
  * (tombstoned or temporally filtered) get score 0 and active 0. */

@@ -973,6 +973,31 @@ int mrl_merge_topk(mrl_ctx* ctx, const void* d_lists, uint32_t n_lists, uint32_t
     return MRL_OK;
 }
 
+int mrl_pack_records(mrl_ctx* ctx, const uint64_t* d_ids, const float* d_scores, const uint32_t* d_counts, uint32_t n_q,
+                     uint32_t k, void* d_records) {
+    if (!ctx) return MRL_ERR_INVALID;
+    if (k < 1 || k > 4096) return fail(ctx, MRL_ERR_INVALID, "k must be in [1, 4096]");
+    if (n_q && (!d_ids || !d_scores || !d_counts || !d_records)) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
+    if (reinterpret_cast<uintptr_t>(d_records) % 16) return fail(ctx, MRL_ERR_INVALID, "d_records must be 16-byte aligned");
+    if (int rc = set_device(ctx)) return rc;
+    if (mrl::launch_pack_records(d_ids, d_scores, d_counts, n_q, k, d_records, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "pack launch");
+    return MRL_OK;
+}
+
+int mrl_merge_topk_batch(mrl_ctx* ctx, const void* d_lists, uint32_t n_lists, uint32_t n_q, uint32_t stride, uint32_t k,
+                         uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_counts) {
+    if (!ctx) return MRL_ERR_INVALID;
+    if (n_lists < 1 || n_lists > 1024) return fail(ctx, MRL_ERR_INVALID, "n_lists must be in [1, 1024]");
+    if (stride < 1 || stride > 4096 || k < 1 || k > 4096) return fail(ctx, MRL_ERR_INVALID, "stride and k must be in [1, 4096]");
+    if (n_q && (!d_lists || !d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
+    if (reinterpret_cast<uintptr_t>(d_lists) % 16) return fail(ctx, MRL_ERR_INVALID, "d_lists must be 16-byte aligned");
+    if (int rc = set_device(ctx)) return rc;
+    if (mrl::launch_merge_topk_batch(d_lists, n_lists, n_q, stride, k, d_out_ids, d_out_scores, d_out_counts, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "batched merge launch");
+    return MRL_OK;
+}
+
 int mrl_scan(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
              const uint32_t* time_hi, uint64_t* out_ids, float* out_scores, uint32_t* out_counts) {
     if (!ctx || !seg || !plans) return MRL_ERR_INVALID;

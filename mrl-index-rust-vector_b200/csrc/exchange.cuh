@@ -45,11 +45,13 @@ __device__ __forceinline__ Record record(const unsigned char* lists, size_t reco
 // x of record i gets rank = (its position in record i) +
 // (the entries of every other record that order before it, by binary search: each record is
 // sorted by the same order) and is written to out[rank] when rank < k.
+// `list_bytes`: distance between consecutive records (MRL_MERGE_RECORD_BYTES(stride) when they are
+// contiguous).
 template <bool kGlobal>
-__device__ __forceinline__ void merge_records(const unsigned char* lists, uint32_t n_lists, uint32_t stride,
-                                              uint32_t k, uint64_t* out_ids, float* out_scores,
+__device__ __forceinline__ void merge_records(const unsigned char* lists, size_t list_bytes, uint32_t n_lists,
+                                              uint32_t stride, uint32_t k, uint64_t* out_ids, float* out_scores,
                                               uint32_t* out_count) {
-    const size_t rb = MRL_MERGE_RECORD_BYTES(stride);
+    const size_t rb = list_bytes;
     const uint32_t total = n_lists * stride;
     for (uint32_t e = threadIdx.x; e < total; e += blockDim.x) {
         const uint32_t i = e / stride, pos = e % stride;
@@ -78,6 +80,13 @@ __device__ __forceinline__ void merge_records(const unsigned char* lists, uint32
         for (uint32_t i = 0; i < n_lists; ++i) n += record<kGlobal>(lists, rb, stride, i).count;
         *out_count = min(n, k);
     }
+}
+
+template <bool kGlobal>
+__device__ __forceinline__ void merge_records(const unsigned char* lists, uint32_t n_lists, uint32_t stride,
+                                              uint32_t k, uint64_t* out_ids, float* out_scores,
+                                              uint32_t* out_count) {
+    merge_records<kGlobal>(lists, MRL_MERGE_RECORD_BYTES(stride), n_lists, stride, k, out_ids, out_scores, out_count);
 }
 
 // Number of the first n entries of a sorted record part (ids, scores) that order before (sx, ix).

@@ -214,6 +214,10 @@ int launch_exact_rank(const float* d_scores, uint32_t n, const uint64_t* d_ids, 
                       uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_count, cudaStream_t stream);
 int launch_merge_topk(const void* d_lists, uint32_t n_lists, uint32_t stride, uint32_t k, uint64_t* d_out_ids,
                       float* d_out_scores, uint32_t* d_out_count, cudaStream_t stream);
+int launch_pack_records(const uint64_t* d_ids, const float* d_scores, const uint32_t* d_counts, uint32_t n_q,
+                        uint32_t k, void* d_records, cudaStream_t stream);
+int launch_merge_topk_batch(const void* d_lists, uint32_t n_lists, uint32_t n_q, uint32_t stride, uint32_t k,
+                            uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_counts, cudaStream_t stream);
 constexpr int kCtlWords = 8;
 // batched fast-mode scan (bscan.cu): per-(query, CTA) top-32 lists in `scratch`
 // (batch_scratch_bytes), then one selection CTA per query

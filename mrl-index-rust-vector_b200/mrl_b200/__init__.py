@@ -44,6 +44,7 @@ from .index import (  # noqa: F401
     rerank_exact_rows,
 )
 from .shard import (  # noqa: F401
+    BatchShardExchange,
     PeerExchange,
     ShardExchange,
     merge_topk_host,

@@ -102,6 +102,8 @@ SIGNATURES = {
     "mrl_ring_search": (_i, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     "mrl_rerank_exact": (_i, [_vp, _vp, _vp, _u64, _u32, _vp, _u32, _vp, _vp]),
     "mrl_merge_topk": (_i, [_vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp]),
+    "mrl_pack_records": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _vp]),
+    "mrl_merge_topk_batch": (_i, [_vp, _vp, _u32, _u32, _u32, _u32, _vp, _vp, _vp]),
     "mrl_ring_create": (_i, [_vp, _u32, _u32, C.POINTER(_vp)]),
     "mrl_ring_push": (_i, [_vp, _vp, _vp]),
     "mrl_ring_drain": (_i, [_vp, _vp, _u32]),

@@ -111,6 +111,44 @@ class ShardExchange:
         return self.top_ids, self.top_scores, self.top_count
 
 
+class BatchShardExchange:
+    """The exchange step of the sharded batched scan: each rank's batched scan
+    results for n_q queries (`d_ids` / `d_scores` rows of k, `d_counts`) are packed into n_q
+    records, all-gathered (one NCCL collective over NVLink for the whole batch) and merged per
+    query on the device (mrl_merge_topk_batch), leaving every query's global top-k in `top_ids`,
+    `top_scores` (rows of k) and `top_counts` on every rank."""
+
+    def __init__(self, dev, n_q: int, k: int, group=None):
+        import torch
+        import torch.distributed as dist
+
+        self.dev, self.n_q, self.k, self.group = dev, int(n_q), int(k), group
+        self.world = dist.get_world_size(group)
+        cuda = torch.device("cuda", torch.cuda.current_device())
+        rb = record_bytes(self.k)
+        self.records = torch.zeros(self.n_q * rb, dtype=torch.uint8, device=cuda)
+        self.gathered = torch.zeros(self.world * self.n_q * rb, dtype=torch.uint8, device=cuda)
+        self.top_ids = torch.empty(self.n_q * self.k, dtype=torch.int64, device=cuda)
+        self.top_scores = torch.empty(self.n_q * self.k, dtype=torch.float32, device=cuda)
+        self.top_counts = torch.empty(self.n_q, dtype=torch.int32, device=cuda)
+
+    def __call__(self, d_ids: int, d_scores: int, d_counts: int):
+        """Pack, all-gather and merge. The collective runs on torch's current stream, which must be
+        the context's stream."""
+        import torch.distributed as dist
+
+        lib = self.dev.lib
+        check(self.dev.ptr, lib.mrl_pack_records(self.dev.ptr, C.c_void_p(d_ids), C.c_void_p(d_scores),
+                                                 C.c_void_p(d_counts), self.n_q, self.k,
+                                                 C.c_void_p(self.records.data_ptr())))
+        dist.all_gather_into_tensor(self.gathered, self.records, group=self.group)
+        check(self.dev.ptr, lib.mrl_merge_topk_batch(self.dev.ptr, C.c_void_p(self.gathered.data_ptr()), self.world,
+                                                     self.n_q, self.k, self.k, C.c_void_p(self.top_ids.data_ptr()),
+                                                     C.c_void_p(self.top_scores.data_ptr()),
+                                                     C.c_void_p(self.top_counts.data_ptr())))
+        return self.top_ids, self.top_scores, self.top_counts
+
+
 class PeerExchange:
     """NVLink exchange (mrl_exchange_*): after set-up, `scan(...)` runs the fused plan + scan +
     global merge of one query in a single launch on every rank. Set-up exchanges the receive

@@ -248,3 +248,51 @@ def test_batch_many_pages_per_sm(dev, engine):
     lib.mrl_plans_free(dev.ptr, plans)
     seg.free()
     del keep
+
+
+def test_batch_records_merge_equals_whole_corpus(ora, dev):
+    """Config 4's exchange step on one GPU: three page ranges scanned as separate segments (each
+    with its block_id_base), their batched results packed as records (mrl_pack_records), laid out
+    rank-major and merged per query (mrl_merge_topk_batch): identical to the batched scan of the
+    whole corpus."""
+    import torch
+
+    M = mb()
+    lib = dev.lib
+    docs, blocks, mean, _ = _corpus(ora, 64 * 150, seed=41)
+    n_q, k = 20, 64
+    qs, _ = ora.synth_queries(41, docs.shape[0], 8, n_q, 768)
+    plans = _plans(M, dev, qs, "eden", mean, None)
+    cfg = M.ScanConfig(shortlist_cand=k).to_c()
+    whole = M.Segment.upload(blocks, dev)
+    ref = _run(dev, lib.mrl_scan_batch_device, whole, plans, n_q, cfg, k)
+    rb = M.record_bytes(k)
+    gathered = torch.zeros(3 * n_q * rb, dtype=torch.uint8, device="cuda")
+    pages = blocks.reshape(-1, 4096)
+    for r in range(3):
+        p0, npg = M.shard_range(pages.shape[0], 3, r)
+        seg = M.Segment.upload(pages[p0:p0 + npg].reshape(-1), dev, block_id_base=p0)
+        ids = torch.zeros(n_q * k, dtype=torch.int64, device="cuda")
+        sc = torch.zeros(n_q * k, dtype=torch.float32, device="cuda")
+        cnt = torch.zeros(n_q, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        M._capi.check(dev.ptr, lib.mrl_scan_batch_device(dev.ptr, seg.ptr, plans.ptr, 0, n_q, C.byref(cfg), None, None,
+                                                         C.c_void_p(ids.data_ptr()), C.c_void_p(sc.data_ptr()),
+                                                         C.c_void_p(cnt.data_ptr()), None))
+        M._capi.check(dev.ptr, lib.mrl_pack_records(dev.ptr, C.c_void_p(ids.data_ptr()), C.c_void_p(sc.data_ptr()),
+                                                    C.c_void_p(cnt.data_ptr()), n_q, k,
+                                                    C.c_void_p(gathered.data_ptr() + r * n_q * rb)))
+        torch.cuda.synchronize()
+        seg.free()
+    out_i = torch.zeros(n_q * k, dtype=torch.int64, device="cuda")
+    out_s = torch.zeros(n_q * k, dtype=torch.float32, device="cuda")
+    out_c = torch.zeros(n_q, dtype=torch.int32, device="cuda")
+    M._capi.check(dev.ptr, lib.mrl_merge_topk_batch(dev.ptr, C.c_void_p(gathered.data_ptr()), 3, n_q, k, k,
+                                                    C.c_void_p(out_i.data_ptr()), C.c_void_p(out_s.data_ptr()),
+                                                    C.c_void_p(out_c.data_ptr())))
+    torch.cuda.synchronize()
+    got = (out_i.cpu().numpy().view(np.uint64).reshape(n_q, k), out_s.cpu().numpy().reshape(n_q, k),
+           out_c.cpu().numpy().astype(np.int64), np.zeros(n_q, np.int64))
+    assert _compare(ref, got, allow_uncertified=False) == n_q
+    whole.free()
+    plans.free()
