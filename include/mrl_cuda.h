@@ -119,6 +119,9 @@ int mrl_segment_upload(mrl_ctx* ctx, const uint8_t* blocks, uint64_t n_blocks,
 int mrl_segment_load(mrl_ctx* ctx, const char* path, uint32_t block_id_base, mrl_seg** out);
 /* SegmentReader::append_live (src/segment.rs:217-232): append one page. */
 int mrl_segment_append(mrl_ctx* ctx, mrl_seg* seg, const uint8_t* block4096);
+/* The same for n_blocks pages already in device memory (e.g. written by mrl_encode_device), on
+ * the context stream: live ingest without a host round trip. */
+int mrl_segment_append_device(mrl_ctx* ctx, mrl_seg* seg, const uint8_t* d_blocks, uint64_t n_blocks);
 int mrl_segment_free(mrl_ctx* ctx, mrl_seg* seg);
 uint64_t mrl_segment_blocks(const mrl_seg* seg);
 /* Device pointer of the scan-layout pages (n_blocks * 4096 bytes) and block time ranges. */
@@ -263,6 +266,15 @@ typedef struct mrl_ring mrl_ring;
 int mrl_ring_create(mrl_ctx* ctx, uint32_t dims, uint32_t capacity, mrl_ring** out);
 int mrl_ring_push(mrl_ctx* ctx, mrl_ring* ring, const float* row);
 int mrl_ring_drain(mrl_ctx* ctx, mrl_ring* ring, uint32_t n);
+/* mrl_ring_push for n rows already in device memory (n x dims f32), on the context stream. */
+int mrl_ring_push_device(mrl_ctx* ctx, mrl_ring* ring, const float* d_rows, uint32_t n);
+/* search_exact for a batch: n_q device queries (n_q x dims f32) against the ring's pending rows
+ * (NULL or empty: no hits), record q (stride k, the mrl_merge_topk layout) holding query q's top k
+ * with the ring sentinel ids; the same scores and order as mrl_ring_search. At most 1024 pending
+ * rows. With the batch's scan records (mrl_pack_records) laid out before them, mrl_merge_topk_batch
+ * with n_lists = 2 gives every query the engine's merged shortlist. */
+int mrl_ring_search_batch(mrl_ctx* ctx, const float* d_queries, uint32_t n_q, uint32_t dims,
+                          const mrl_ring* ring, uint32_t k, void* d_records);
 uint32_t mrl_ring_len(const mrl_ring* ring);
 int mrl_ring_rows(const mrl_ring* ring, const float** d_rows);
 int mrl_ring_destroy(mrl_ctx* ctx, mrl_ring* ring);

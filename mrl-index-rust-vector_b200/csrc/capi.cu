@@ -410,6 +410,18 @@ int mrl_segment_append(mrl_ctx* ctx, mrl_seg* seg, const uint8_t* block4096) {
     return MRL_OK;
 }
 
+int mrl_segment_append_device(mrl_ctx* ctx, mrl_seg* seg, const uint8_t* d_blocks, uint64_t n_blocks) {
+    if (!ctx || !seg || (n_blocks && !d_blocks)) return MRL_ERR_INVALID;
+    if (seg->n_blocks + n_blocks >= (1ull << 26)) return fail(ctx, MRL_ERR_INVALID, "segment larger than 2^26 pages");
+    if (n_blocks == 0) return MRL_OK;
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = seg_reserve(ctx, seg, seg->n_blocks + n_blocks)) return rc;
+    if (mrl::launch_transcode(d_blocks, n_blocks, seg->pages + seg->n_blocks * 256, seg->ts + seg->n_blocks, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "transcode launch");
+    seg->n_blocks += n_blocks;
+    return MRL_OK;
+}
+
 int mrl_segment_free(mrl_ctx* ctx, mrl_seg* seg) {
     if (!seg) return MRL_OK;
     if (ctx) cudaSetDevice(ctx->device);
@@ -901,6 +913,32 @@ int mrl_ring_push(mrl_ctx* ctx, mrl_ring* ring, const float* row) {
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(ring->rows + (size_t)ring->len * ring->dims, row, ring->dims * sizeof(float),
                                       cudaMemcpyHostToDevice, ctx->stream));
     ring->len += 1;
+    return MRL_OK;
+}
+
+int mrl_ring_push_device(mrl_ctx* ctx, mrl_ring* ring, const float* d_rows, uint32_t n) {
+    if (!ctx || !ring || (n && !d_rows)) return MRL_ERR_INVALID;
+    if ((uint64_t)ring->len + n > ring->capacity) return fail(ctx, MRL_ERR_INVALID, "ring is full (flush a block first)");
+    if (n == 0) return MRL_OK;
+    if (int rc = set_device(ctx)) return rc;
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(ring->rows + (size_t)ring->len * ring->dims, d_rows,
+                                      (size_t)n * ring->dims * sizeof(float), cudaMemcpyDeviceToDevice, ctx->stream));
+    ring->len += n;
+    return MRL_OK;
+}
+
+int mrl_ring_search_batch(mrl_ctx* ctx, const float* d_queries, uint32_t n_q, uint32_t dims, const mrl_ring* ring,
+                          uint32_t k, void* d_records) {
+    if (!ctx) return MRL_ERR_INVALID;
+    if (k < 1 || k > 4096) return fail(ctx, MRL_ERR_INVALID, "k must be in [1, 4096]");
+    if (ring && ring->dims != dims) return fail(ctx, MRL_ERR_INVALID, "ring dims differ from the queries'");
+    const uint32_t n = ring ? ring->len : 0;
+    if (n > 1024) return fail(ctx, MRL_ERR_INVALID, "at most 1024 pending rows for a batched ring search");
+    if (n_q && (!d_queries || !d_records)) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
+    if (reinterpret_cast<uintptr_t>(d_records) % 16) return fail(ctx, MRL_ERR_INVALID, "d_records must be 16-byte aligned");
+    if (int rc = set_device(ctx)) return rc;
+    if (mrl::launch_ring_search_batch(d_queries, n_q, dims, ring ? ring->rows : nullptr, n, k, d_records, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "batched ring search launch");
     return MRL_OK;
 }
 

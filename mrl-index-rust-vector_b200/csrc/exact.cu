@@ -89,7 +89,61 @@ rank_kernel(const float* __restrict__ scores, uint32_t n, const uint64_t* __rest
     if (threadIdx.x == 0 && out_count) *out_count = m;
 }
 
+// RingBuffer::search_exact for a batch: CTA q scores query q against the n pending rows (one warp
+// per row, the reference's dot), sorts (score desc, position asc) and writes its top k as record q
+// (stride k) with the ring sentinel ids VectorId(u32::MAX, position).
+constexpr int kRingThreads = 256;
+constexpr uint32_t kRingMaxRows = 1024;
+__global__ void __launch_bounds__(kRingThreads)
+ring_batch_kernel(const float* __restrict__ queries, uint32_t dims, const float* __restrict__ rows, uint32_t n,
+                  uint32_t k, unsigned char* __restrict__ records) {
+    __shared__ float s_sc[kRingMaxRows];
+    __shared__ unsigned long long s_key[kRingMaxRows];
+    const uint32_t q = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float* qv = queries + (size_t)q * dims;
+    for (uint32_t r = warp; r < n; r += kRingThreads / 32) {
+        const float sc = ref_dot(qv, rows + (size_t)r * dims, dims, lane);
+        if (lane == 0) s_sc[r] = sc;
+    }
+    __syncthreads();
+    uint32_t p2 = 1;
+    while (p2 < n) p2 <<= 1;
+    for (uint32_t i = threadIdx.x; i < p2; i += kRingThreads) s_key[i] = i < n ? make_key(s_sc[i], i) : 0ull;
+    __syncthreads();
+    for (uint32_t kk = 2; kk <= p2; kk <<= 1) {
+        for (uint32_t j = kk >> 1; j > 0; j >>= 1) {
+            for (uint32_t i = threadIdx.x; i < p2; i += kRingThreads) {
+                const uint32_t ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long a = s_key[i], b = s_key[ixj];
+                    const bool desc = (i & kk) == 0;
+                    if (desc ? (a < b) : (a > b)) { s_key[i] = b; s_key[ixj] = a; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    unsigned char* rec = records + (size_t)q * MRL_MERGE_RECORD_BYTES(k);
+    const uint32_t m = min(k, n);
+    for (uint32_t i = threadIdx.x; i < m; i += kRingThreads) {
+        const uint32_t pos = key_ordinal(s_key[i]);
+        reinterpret_cast<uint64_t*>(rec)[i] = ((uint64_t)0xFFFFFFFFu << 16) | pos;
+        reinterpret_cast<float*>(rec + (size_t)k * 8)[i] = s_sc[pos];  // the score itself (keeps -0.0)
+    }
+    if (threadIdx.x == 0) *reinterpret_cast<uint32_t*>(rec + (size_t)k * 12) = m;
+}
+
 }  // namespace
+
+int launch_ring_search_batch(const float* d_queries, uint32_t n_q, uint32_t dims, const float* d_rows, uint32_t n,
+                             uint32_t k, void* d_records, cudaStream_t stream) {
+    if (n_q == 0) return 0;
+    if (n > kRingMaxRows) return -1;
+    ring_batch_kernel<<<n_q, kRingThreads, 0, stream>>>(d_queries, dims, d_rows, n, k,
+                                                        static_cast<unsigned char*>(d_records));
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
 
 int launch_exact_dots(const float* d_query, const float* d_rows, uint64_t n_rows, uint32_t dims, const uint64_t* d_sel,
                       uint32_t n, float* d_scores, uint32_t* d_bad, cudaStream_t stream) {

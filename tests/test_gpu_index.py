@@ -234,3 +234,135 @@ def test_index_dir_lifecycle(ora, dev, tmp_path):
     ri, rs = _merged_reference(ora, pages2, qs[0], mean, np.zeros((0, 768), np.float32), 64)
     assert [h.id.as_u64() for h in hits] == [int(x) for x in ri]
     ix2.close()
+
+
+def _dev_rows(a):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+@pytest.mark.parametrize("n", [0, 1, 63, 200])
+def test_ring_search_batch_matches_single(ora, dev, n):
+    """mrl_ring_search_batch (one record per query, rows pushed from device memory) equals
+    mrl_ring_search of each query, bit for bit."""
+    import torch
+
+    M = mb()
+    lib = dev.lib
+    dims, n_q, k = 768, 5, 40
+    rows = _rows(n + 3, n, dims)
+    if n > 8:
+        rows[7] = rows[3]
+    qs = _rows(11, n_q, dims)
+    ring = M.DeviceRing(dims, 1024, dev)
+    d_rows = _dev_rows(rows) if n else torch.zeros(1, dims, device="cuda")
+    M._capi.check(dev.ptr, lib.mrl_ring_push_device(dev.ptr, ring.ptr, C.c_void_p(d_rows.data_ptr()), n))
+    dq = _dev_rows(qs)
+    rb = M.record_bytes(k)
+    recs = torch.zeros(n_q * rb, dtype=torch.uint8, device="cuda")
+    M._capi.check(dev.ptr, lib.mrl_ring_search_batch(dev.ptr, C.c_void_p(dq.data_ptr()), n_q, dims,
+                                                     ring.ptr if n else None, k, C.c_void_p(recs.data_ptr())))
+    one = torch.zeros(rb, dtype=torch.uint8, device="cuda")
+    rp = C.c_void_p()
+    M._capi.check(dev.ptr, lib.mrl_ring_rows(ring.ptr, C.byref(rp)))
+    for q in range(n_q):
+        M._capi.check(dev.ptr, lib.mrl_ring_search(dev.ptr, C.c_void_p(dq.data_ptr() + q * dims * 4), rp, n, dims, k,
+                                                   C.c_void_p(one.data_ptr())))
+        torch.cuda.synchronize()
+        a = one.cpu().numpy()
+        b = recs[q * rb:(q + 1) * rb].cpu().numpy()
+        m = int(a[12 * k:12 * k + 4].view(np.uint32)[0])
+        assert m == min(n, k) == int(b[12 * k:12 * k + 4].view(np.uint32)[0])
+        assert np.array_equal(a[:8 * m], b[:8 * m]) and np.array_equal(a[8 * k:8 * k + 4 * m], b[8 * k:8 * k + 4 * m])
+        pos, sc = ora.ring_search(rows, qs[q], k)
+        assert np.array_equal(a[:8 * m].view(np.uint64) & np.uint64(0xFFFF), pos.astype(np.uint64))
+    ring.close()
+
+
+def test_live_ingest_on_device(ora, dev):
+    """Device-side live ingest: rows pushed from device memory, 64 of them encoded on the device and
+    appended (mrl_segment_append_device), the ring drained; the segment equals an upload of the
+    oracle's pages, and a batch's merged shortlist (batched scan records + batched ring records,
+    mrl_merge_topk_batch) equals mrl_engine_scan of every query."""
+    import torch
+
+    M = mb()
+    lib = dev.lib
+    dims = 768
+    docs = ora.synth_docs(51, 64 * 40, dims)
+    mean = ora.eden_fit_prefix(docs)
+    base = ora.encode_corpus(docs, eden_mean=mean)
+    seg = M.Segment.upload(base, dev)
+    desc, keep = M.api._codec_desc(M.PrefixCodec.EDEN_PROD, M.MidCodec.RABITQ, M.EdenFit(64, 4, 1, mean), None)
+    live = ora.synth_docs(52, 64 + 17, dims)
+    ring = M.DeviceRing(dims, 1024, dev)
+    d_live = _dev_rows(live)
+    M._capi.check(dev.ptr, lib.mrl_ring_push_device(dev.ptr, ring.ptr, C.c_void_p(d_live.data_ptr()), 64 + 17))
+    rp = C.c_void_p()
+    M._capi.check(dev.ptr, lib.mrl_ring_rows(ring.ptr, C.byref(rp)))
+    pax = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    M._capi.check(dev.ptr, lib.mrl_encode_device(dev.ptr, rp, 64, dims, 8, C.byref(desc), C.c_void_p(pax.data_ptr()),
+                                                 0, None))
+    M._capi.check(dev.ptr, lib.mrl_segment_append_device(dev.ptr, seg.ptr, C.c_void_p(pax.data_ptr()), 1))
+    M._capi.check(dev.ptr, lib.mrl_ring_drain(dev.ptr, ring.ptr, 64))
+    torch.cuda.synchronize()
+    assert seg.block_count() == 41 and dev.lib.mrl_ring_len(ring.ptr) == 17
+    ref_pages = np.concatenate([base, ora.encode_block(live[:64], ts=np.arange(64), eden_mean=mean)])
+    full = M.Segment.upload(ref_pages, dev)
+    assert np.array_equal(seg.read_layout()[0], full.read_layout()[0])
+    full.free()
+    # a batch against segment + ring, merged per query, against the single-query engine scan
+    n_q, k = 9, 64
+    qs, _ = ora.synth_queries(51, docs.shape[0], 3, n_q, dims)
+    qs[0] = live[70]  # a pending row that must come first
+    dq = _dev_rows(qs)
+    plans = C.c_void_p()
+    M._capi.check(dev.ptr, lib.mrl_plans_alloc(dev.ptr, n_q, dims, C.byref(plans)))
+    M._capi.check(dev.ptr, lib.mrl_plan_build_device(dev.ptr, C.c_void_p(dq.data_ptr()), n_q, dims, C.byref(desc),
+                                                     plans))
+    cfg = M.ScanConfig(shortlist_cand=k).to_c()
+    ids = torch.zeros(n_q * k, dtype=torch.int64, device="cuda")
+    sc = torch.zeros(n_q * k, dtype=torch.float32, device="cuda")
+    cnt = torch.zeros(n_q, dtype=torch.int32, device="cuda")
+    st = torch.zeros(n_q, dtype=torch.int32, device="cuda")
+    M._capi.check(dev.ptr, lib.mrl_scan_batch_device(dev.ptr, seg.ptr, plans, 0, n_q, C.byref(cfg), None, None,
+                                                     C.c_void_p(ids.data_ptr()), C.c_void_p(sc.data_ptr()),
+                                                     C.c_void_p(cnt.data_ptr()), C.c_void_p(st.data_ptr())))
+    rb = M.record_bytes(k)
+    lists = torch.zeros(2 * n_q * rb, dtype=torch.uint8, device="cuda")
+    M._capi.check(dev.ptr, lib.mrl_pack_records(dev.ptr, C.c_void_p(ids.data_ptr()), C.c_void_p(sc.data_ptr()),
+                                                C.c_void_p(cnt.data_ptr()), n_q, k, C.c_void_p(lists.data_ptr())))
+    M._capi.check(dev.ptr, lib.mrl_ring_search_batch(dev.ptr, C.c_void_p(dq.data_ptr()), n_q, dims, ring.ptr, k,
+                                                     C.c_void_p(lists.data_ptr() + n_q * rb)))
+    out_i = torch.zeros(n_q * k, dtype=torch.int64, device="cuda")
+    out_s = torch.zeros(n_q * k, dtype=torch.float32, device="cuda")
+    out_c = torch.zeros(n_q, dtype=torch.int32, device="cuda")
+    M._capi.check(dev.ptr, lib.mrl_merge_topk_batch(dev.ptr, C.c_void_p(lists.data_ptr()), 2, n_q, k, k,
+                                                    C.c_void_p(out_i.data_ptr()), C.c_void_p(out_s.data_ptr()),
+                                                    C.c_void_p(out_c.data_ptr())))
+    torch.cuda.synchronize()
+    assert not np.any(st.cpu().numpy() & 8)
+    eplans = C.c_void_p()
+    M._capi.check(dev.ptr, lib.mrl_plans_alloc(dev.ptr, 1, dims, C.byref(eplans)))
+    gi = out_i.cpu().numpy().view(np.uint64).reshape(n_q, k)
+    gs = out_s.cpu().numpy().reshape(n_q, k)
+    for q in range(n_q):
+        e_i = torch.zeros(k, dtype=torch.int64, device="cuda")
+        e_s = torch.zeros(k, dtype=torch.float32, device="cuda")
+        e_c = torch.zeros(2, dtype=torch.int32, device="cuda")
+        M._capi.check(dev.ptr, lib.mrl_engine_scan(dev.ptr, seg.ptr, C.c_void_p(dq.data_ptr() + q * dims * 4), dims,
+                                                   C.byref(desc), eplans, C.byref(cfg), None, None, ring.ptr,
+                                                   C.c_void_p(e_i.data_ptr()), C.c_void_p(e_s.data_ptr()),
+                                                   C.c_void_p(e_c.data_ptr()), C.c_void_p(e_c.data_ptr() + 4)))
+        torch.cuda.synchronize()
+        n = int(e_c[0].item())
+        assert int(out_c[q].item()) == n == k
+        assert np.array_equal(gi[q], e_i.cpu().numpy().view(np.uint64))
+        assert np.array_equal(gs[q].view(np.uint32), e_s.cpu().numpy().view(np.uint32))
+    assert gi[0][0] == (0xFFFFFFFF << 16) | 6  # live[70] is pending row 6 after the drain
+    lib.mrl_plans_free(dev.ptr, plans)
+    lib.mrl_plans_free(dev.ptr, eplans)
+    ring.close()
+    seg.free()
+    del keep
