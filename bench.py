@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=1,
                     help="queries per step; > 1 runs BASELINE config 3 (one GPU) or config 4 (torchrun: --docs "
                          "split across the ranks)")
+    ap.add_argument("--live", type=int, default=0,
+                    help="with --batch: vectors ingested per step and rank through the device ring (config 5)")
     ap.add_argument("--engine", choices=["tensor", "cuda_core"], default="tensor",
                     help="batched-scan engine (--batch > 1)")
     ap.add_argument("--exchange", choices=["nvlink", "nccl"], default="nvlink",
@@ -505,9 +507,13 @@ def run_batch(args):
         mt = torch.from_numpy(mean).cuda()
         dist.broadcast(mt, 0)
         mean = mt.cpu().numpy()
-    seg, pax, desc, keep = encode_gpu(M, dev, x, n, dims, mean, block_id_base=p0)
+    live = max(int(args.live), 0)
+    # with live appends every rank's id range leaves room for the pages it will append
+    live_pages = (live * (max(args.warmup, 3) + args.steps + 20) + 63) // 64 if live else 0
+    id_base = rank * (((pages_total + world - 1) // world) + live_pages) if live else p0
+    seg, pax, desc, keep = encode_gpu(M, dev, x, n, dims, mean, block_id_base=id_base)
     segs = [seg]
-    for r in range(1, max(args.segments, 1)):  # rotate over segments of the same shape: pages > L2
+    for r in range(1, max(args.segments, 1) if not live else 1):  # rotate over segments: pages > L2
         M._capi.check(dev.ptr, lib.mrl_synth_docs_device(dev.ptr, DOC_SEED, r * pages_total * 64 + row0, n, dims,
                                                          C.c_void_p(x.data_ptr())))
         sp = C.c_void_p()
@@ -531,21 +537,78 @@ def run_batch(args):
     exch = M.BatchShardExchange(dev, B, k) if world > 1 else None
     qbytes = B * dims * 4
 
-    def step(i, ev=None):
-        if ev is not None:
-            ev[0].record()
-        M._capi.check(dev.ptr, lib.mrl_plan_build_device(dev.ptr, C.c_void_p(qd.data_ptr() + i * qbytes), B, dims,
-                                                         C.byref(desc), plans))
-        if ev is not None:
-            ev[1].record()
+    # live ingest: `live` new vectors per step and rank go through the device
+    # ring; every 64 pending are encoded on the device and appended to the segment, and each batch
+    # searches the pending rows exactly and merges them with the scan (two records per query)
+    ring = C.c_void_p()
+    live_state = {"pending": 0, "appended": 0}
+    if live:
+        if live > 4096 - 63:
+            raise SystemExit("--live must be <= 4033 vectors per step")
+        M._capi.check(dev.ptr, lib.mrl_ring_create(dev.ptr, dims, 4096, C.byref(ring)))
+        n_live = live * (n_batches + 20)
+        live_rows = torch.empty((n_live, dims), dtype=torch.float32, device="cuda")
+        M._capi.check(dev.ptr, lib.mrl_synth_docs_device(dev.ptr, DOC_SEED + 1, rank * n_live, n_live, dims,
+                                                         C.c_void_p(live_rows.data_ptr())))
+        live_pax = torch.empty(((live + 63) // 64 + 1) * 4096, dtype=torch.uint8, device="cuda")
+        rb = M.record_bytes(k)
+        lists = torch.zeros(2 * B * rb, dtype=torch.uint8, device="cuda")
+        m_ids = torch.empty(B * k, dtype=torch.int64, device="cuda")
+        m_sc = torch.empty(B * k, dtype=torch.float32, device="cuda")
+        m_cnt = torch.empty(B, dtype=torch.int32, device="cuda")
+    live_cursor = [0]
+
+    def ingest():
+        r0 = live_cursor[0] % (live_rows.shape[0] - live)
+        live_cursor[0] += live
+        M._capi.check(dev.ptr, lib.mrl_ring_push_device(dev.ptr, ring, C.c_void_p(live_rows.data_ptr() + r0 * dims * 4),
+                                                        live))
+        live_state["pending"] += live
+        f = live_state["pending"] // 64
+        if f:
+            rp = C.c_void_p()
+            M._capi.check(dev.ptr, lib.mrl_ring_rows(ring, C.byref(rp)))
+            M._capi.check(dev.ptr, lib.mrl_encode_device(dev.ptr, rp, 64 * f, dims, 8, C.byref(desc),
+                                                         C.c_void_p(live_pax.data_ptr()), 0, None))
+            M._capi.check(dev.ptr, lib.mrl_segment_append_device(dev.ptr, segs[0].ptr, C.c_void_p(live_pax.data_ptr()),
+                                                                 f))
+            M._capi.check(dev.ptr, lib.mrl_ring_drain(dev.ptr, ring, 64 * f))
+            live_state["pending"] -= 64 * f
+            live_state["appended"] += f
+
+    def scan_merge(i, ev=None):
+        """The batched scan of plans [0, B) (+ the ring, + the exchange): device results."""
         M._capi.check(dev.ptr, lib.mrl_scan_batch_device(dev.ptr, segs[i % len(segs)].ptr, plans, 0, B, C.byref(cfg),
                                                          None, None, C.c_void_p(ids.data_ptr()),
                                                          C.c_void_p(sc.data_ptr()), C.c_void_p(cnt.data_ptr()),
                                                          C.c_void_p(st.data_ptr())))
         if ev is not None:
             ev[2].record()
+        r_ids, r_sc, r_cnt = ids, sc, cnt
+        if live:
+            M._capi.check(dev.ptr, lib.mrl_pack_records(dev.ptr, C.c_void_p(ids.data_ptr()), C.c_void_p(sc.data_ptr()),
+                                                        C.c_void_p(cnt.data_ptr()), B, k,
+                                                        C.c_void_p(lists.data_ptr())))
+            M._capi.check(dev.ptr, lib.mrl_ring_search_batch(dev.ptr, C.c_void_p(qd.data_ptr() + (i % n_batches) * qbytes),
+                                                             B, dims, ring, k, C.c_void_p(lists.data_ptr() + B * rb)))
+            M._capi.check(dev.ptr, lib.mrl_merge_topk_batch(dev.ptr, C.c_void_p(lists.data_ptr()), 2, B, k, k,
+                                                            C.c_void_p(m_ids.data_ptr()), C.c_void_p(m_sc.data_ptr()),
+                                                            C.c_void_p(m_cnt.data_ptr())))
+            r_ids, r_sc, r_cnt = m_ids, m_sc, m_cnt
         if exch is not None:
-            exch(ids.data_ptr(), sc.data_ptr(), cnt.data_ptr())
+            r_ids, r_sc, r_cnt = exch(r_ids.data_ptr(), r_sc.data_ptr(), r_cnt.data_ptr())
+        return r_ids, r_sc, r_cnt
+
+    def step(i, ev=None):
+        if ev is not None:
+            ev[0].record()
+        if live:
+            ingest()
+        M._capi.check(dev.ptr, lib.mrl_plan_build_device(dev.ptr, C.c_void_p(qd.data_ptr() + i * qbytes), B, dims,
+                                                         C.byref(desc), plans))
+        if ev is not None:
+            ev[1].record()
+        scan_merge(i, ev)
         if ev is not None:
             ev[3].record()
 
@@ -594,7 +657,7 @@ def run_batch(args):
     cnt_h = torch.empty(B, dtype=torch.int32, pin_memory=True)
     e2e_steps = min(args.steps, 10)
     tot = 0.0
-    if world == 1:
+    if world == 1 and not live:
         dev.set_stream(0)
     for i in range(e2e_steps + 2):
         qh.copy_(qd[(i % n_batches) * B:(i % n_batches + 1) * B].cpu())
@@ -603,33 +666,36 @@ def run_batch(args):
             dist.barrier()
         s0 = time.perf_counter()
         M._capi.check(dev.ptr, lib.mrl_plan_rebuild(dev.ptr, C.c_void_p(qh.data_ptr()), B, dims, C.byref(desc), plans))
-        if world == 1:
+        if world == 1 and not live:
             M._capi.check(dev.ptr, lib.mrl_scan(dev.ptr, segs[i % len(segs)].ptr, plans, C.byref(cfg), None, None,
                                                 C.c_void_p(ids_h.data_ptr()), C.c_void_p(sc_h.data_ptr()),
                                                 C.c_void_p(cnt_h.data_ptr())))
         else:
-            M._capi.check(dev.ptr, lib.mrl_scan_batch_device(dev.ptr, segs[i % len(segs)].ptr, plans, 0, B,
-                                                             C.byref(cfg), None, None, C.c_void_p(ids.data_ptr()),
-                                                             C.c_void_p(sc.data_ptr()), C.c_void_p(cnt.data_ptr()),
-                                                             C.c_void_p(st.data_ptr())))
-            g_ids, g_sc, g_cnt = exch(ids.data_ptr(), sc.data_ptr(), cnt.data_ptr())
+            if live:
+                ingest()
+            g_ids, g_sc, g_cnt = scan_merge(i % n_batches)
             ids_h.copy_(g_ids, non_blocking=True)
             sc_h.copy_(g_sc, non_blocking=True)
             cnt_h.copy_(g_cnt, non_blocking=True)
             torch.cuda.current_stream().synchronize()
         if i >= 2:
             tot += time.perf_counter() - s0
-    if world == 1:
+    if world == 1 and not live:
         dev.set_stream(torch_stream)
-    else:
+    if world > 1:
         t = torch.tensor([tot], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         tot = float(t.item())
     e2e = {"value": B * e2e_steps / tot, "unit": "QPS", "h2d_bytes_per_step": qbytes,
            "d2h_bytes_per_step": B * (k * 12 + 4), "steps": e2e_steps,
            "path": ("mrl_plan_rebuild (host queries) + mrl_scan (batched from 8 plans, host results, synchronous)"
-                    if world == 1 else "per rank: mrl_plan_rebuild (host queries) + mrl_scan_batch_device + "
-                    "BatchShardExchange (pack, NCCL all-gather, per-query merge) + copy to pinned host; max over ranks")}
+                    if world == 1 and not live else
+                    "per rank: " + ("mrl_ring_push_device + (every 64 pending) mrl_encode_device + "
+                                    "mrl_segment_append_device + mrl_ring_drain, " if live else "")
+                    + "mrl_plan_rebuild (host queries) + mrl_scan_batch_device + "
+                    + ("mrl_pack_records + mrl_ring_search_batch + mrl_merge_topk_batch + " if live else "")
+                    + ("BatchShardExchange (pack, NCCL all-gather, per-query merge) + " if world > 1 else "")
+                    + "copy to pinned host" + ("; max over ranks" if world > 1 else ""))}
 
     pairs = B * n  # this rank's (query, doc) pairs per step
     if args.engine == "tensor":
@@ -646,7 +712,14 @@ def run_batch(args):
                 "unit": "TOP/s", "frac": alg / (scan_ms / 1e3) / 1e12 / cuda_core_peak,
                 "peak_kind": "148 SMs x 128 lanes x 2 x 1965 MHz (nominal)", "kernel": "bscan_kernel",
                 "traffic": None}
-    workload = (f"config 3: batched scan, {B} queries per step over {n_total:,} x {dims} docs" if world == 1 else
+    if live:
+        workload = (f"config 5 shape: batched scan, {B} queries per step over {n_total:,} x {dims} docs on {world} "
+                    f"GPU(s), {live} new vectors per step and rank ingested through the device ring (flushed every 64 "
+                    "into pages appended to the segment; pending rows searched exactly and merged per query)")
+    elif world == 1:
+        workload = f"config 3: batched scan, {B} queries per step over {n_total:,} x {dims} docs"
+    else:
+        workload = (
                 f"config 4: sharded batched scan, {B} queries per step over {n_total:,} x {dims} docs split across "
                 f"{world} GPUs (NCCL all-gather of per-rank top-{k} + per-query merge)")
     line = {
@@ -662,17 +735,23 @@ def run_batch(args):
                                                   "(tensor) or bscan_kernel + bselect_kernel (cuda_core)"
                                                   + ("; pack_records + NCCL all-gather + merge_topk_batch"
                                                      if world > 1 else ""),
-                   "plan_ms": plan_ms, "scan_ms": scan_ms, "exchange_ms": exch_ms if world > 1 else None,
+                   "plan_ms": plan_ms, "scan_ms": scan_ms,
+                   "exchange_ms": exch_ms if (world > 1 or live) else None,
+                   "live_vectors_per_step_per_rank": live, "live_pages_appended": live_state["appended"],
+                   "live_pending_rows": live_state["pending"],
                    "uncertified_queries_last_step": uncertified, "algorithmic_ops_per_pair": 512,
                    "wall_s_bracketed": t1 - t0},
         "roofline": roof, "clocks": clk,
-        "gpu_launches": args.steps * ((4 if args.engine == "tensor" else 3) + (2 if world > 1 else 0)), "e2e": e2e,
+        "gpu_launches": args.steps * ((4 if args.engine == "tensor" else 3) + (2 if world > 1 else 0)
+                                      + (3 + 2 * (live // 64 > 0) if live else 0)), "e2e": e2e,
     }
     if rank == 0:
         emit(line)
     for sg in segs:
         sg.free()
     lib.mrl_plans_free(dev.ptr, plans)
+    if live:
+        lib.mrl_ring_destroy(dev.ptr, ring)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
