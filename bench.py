@@ -590,7 +590,8 @@ def run_batch(args):
                                                         C.c_void_p(cnt.data_ptr()), B, k,
                                                         C.c_void_p(lists.data_ptr())))
             M._capi.check(dev.ptr, lib.mrl_ring_search_batch(dev.ptr, C.c_void_p(qd.data_ptr() + (i % n_batches) * qbytes),
-                                                             B, dims, ring, k, C.c_void_p(lists.data_ptr() + B * rb)))
+                                                             B, dims, ring, rank * 4096, k,
+                                                             C.c_void_p(lists.data_ptr() + B * rb)))
             M._capi.check(dev.ptr, lib.mrl_merge_topk_batch(dev.ptr, C.c_void_p(lists.data_ptr()), 2, B, k, k,
                                                             C.c_void_p(m_ids.data_ptr()), C.c_void_p(m_sc.data_ptr()),
                                                             C.c_void_p(m_cnt.data_ptr())))

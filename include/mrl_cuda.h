@@ -270,11 +270,14 @@ int mrl_ring_drain(mrl_ctx* ctx, mrl_ring* ring, uint32_t n);
 int mrl_ring_push_device(mrl_ctx* ctx, mrl_ring* ring, const float* d_rows, uint32_t n);
 /* search_exact for a batch: n_q device queries (n_q x dims f32) against the ring's pending rows
  * (NULL or empty: no hits), record q (stride k, the mrl_merge_topk layout) holding query q's top k
- * with the ring sentinel ids; the same scores and order as mrl_ring_search. At most 1024 pending
- * rows. With the batch's scan records (mrl_pack_records) laid out before them, mrl_merge_topk_batch
- * with n_lists = 2 gives every query the engine's merged shortlist. */
+ * with the ring sentinel ids VectorId(u32::MAX, slot_base + position); the same scores and order
+ * as mrl_ring_search. slot_base = 0 is the reference's sentinel; a sharded caller passes
+ * rank x 4096 so the ring hits of different ranks stay distinct after the records are merged
+ * across ranks (slot_base + pending rows must stay <= 65536). At most 1024 pending rows. With the
+ * batch's scan records (mrl_pack_records) laid out before them, mrl_merge_topk_batch with
+ * n_lists = 2 gives every query the engine's merged shortlist. */
 int mrl_ring_search_batch(mrl_ctx* ctx, const float* d_queries, uint32_t n_q, uint32_t dims,
-                          const mrl_ring* ring, uint32_t k, void* d_records);
+                          const mrl_ring* ring, uint32_t slot_base, uint32_t k, void* d_records);
 uint32_t mrl_ring_len(const mrl_ring* ring);
 int mrl_ring_rows(const mrl_ring* ring, const float** d_rows);
 int mrl_ring_destroy(mrl_ctx* ctx, mrl_ring* ring);

@@ -928,16 +928,18 @@ int mrl_ring_push_device(mrl_ctx* ctx, mrl_ring* ring, const float* d_rows, uint
 }
 
 int mrl_ring_search_batch(mrl_ctx* ctx, const float* d_queries, uint32_t n_q, uint32_t dims, const mrl_ring* ring,
-                          uint32_t k, void* d_records) {
+                          uint32_t slot_base, uint32_t k, void* d_records) {
     if (!ctx) return MRL_ERR_INVALID;
     if (k < 1 || k > 4096) return fail(ctx, MRL_ERR_INVALID, "k must be in [1, 4096]");
     if (ring && ring->dims != dims) return fail(ctx, MRL_ERR_INVALID, "ring dims differ from the queries'");
     const uint32_t n = ring ? ring->len : 0;
     if (n > 1024) return fail(ctx, MRL_ERR_INVALID, "at most 1024 pending rows for a batched ring search");
+    if ((uint64_t)slot_base + n > 65536u) return fail(ctx, MRL_ERR_INVALID, "slot_base + pending rows exceeds 65536");
     if (n_q && (!d_queries || !d_records)) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
     if (reinterpret_cast<uintptr_t>(d_records) % 16) return fail(ctx, MRL_ERR_INVALID, "d_records must be 16-byte aligned");
     if (int rc = set_device(ctx)) return rc;
-    if (mrl::launch_ring_search_batch(d_queries, n_q, dims, ring ? ring->rows : nullptr, n, k, d_records, ctx->stream))
+    if (mrl::launch_ring_search_batch(d_queries, n_q, dims, ring ? ring->rows : nullptr, n, slot_base, k, d_records,
+                                      ctx->stream))
         return cuda_fail(ctx, cudaGetLastError(), "batched ring search launch");
     return MRL_OK;
 }

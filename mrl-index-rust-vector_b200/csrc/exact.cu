@@ -96,7 +96,7 @@ constexpr int kRingThreads = 256;
 constexpr uint32_t kRingMaxRows = 1024;
 __global__ void __launch_bounds__(kRingThreads)
 ring_batch_kernel(const float* __restrict__ queries, uint32_t dims, const float* __restrict__ rows, uint32_t n,
-                  uint32_t k, unsigned char* __restrict__ records) {
+                  uint32_t slot_base, uint32_t k, unsigned char* __restrict__ records) {
     __shared__ float s_sc[kRingMaxRows];
     __shared__ unsigned long long s_key[kRingMaxRows];
     const uint32_t q = blockIdx.x;
@@ -128,7 +128,7 @@ ring_batch_kernel(const float* __restrict__ queries, uint32_t dims, const float*
     const uint32_t m = min(k, n);
     for (uint32_t i = threadIdx.x; i < m; i += kRingThreads) {
         const uint32_t pos = key_ordinal(s_key[i]);
-        reinterpret_cast<uint64_t*>(rec)[i] = ((uint64_t)0xFFFFFFFFu << 16) | pos;
+        reinterpret_cast<uint64_t*>(rec)[i] = ((uint64_t)0xFFFFFFFFu << 16) | (slot_base + pos);
         reinterpret_cast<float*>(rec + (size_t)k * 8)[i] = s_sc[pos];  // the score itself (keeps -0.0)
     }
     if (threadIdx.x == 0) *reinterpret_cast<uint32_t*>(rec + (size_t)k * 12) = m;
@@ -137,10 +137,10 @@ ring_batch_kernel(const float* __restrict__ queries, uint32_t dims, const float*
 }  // namespace
 
 int launch_ring_search_batch(const float* d_queries, uint32_t n_q, uint32_t dims, const float* d_rows, uint32_t n,
-                             uint32_t k, void* d_records, cudaStream_t stream) {
+                             uint32_t slot_base, uint32_t k, void* d_records, cudaStream_t stream) {
     if (n_q == 0) return 0;
     if (n > kRingMaxRows) return -1;
-    ring_batch_kernel<<<n_q, kRingThreads, 0, stream>>>(d_queries, dims, d_rows, n, k,
+    ring_batch_kernel<<<n_q, kRingThreads, 0, stream>>>(d_queries, dims, d_rows, n, slot_base, k,
                                                         static_cast<unsigned char*>(d_records));
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

@@ -211,7 +211,7 @@ int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream);
 int launch_exact_dots(const float* d_query, const float* d_rows, uint64_t n_rows, uint32_t dims, const uint64_t* d_sel,
                       uint32_t n, float* d_scores, uint32_t* d_bad, cudaStream_t stream);
 int launch_ring_search_batch(const float* d_queries, uint32_t n_q, uint32_t dims, const float* d_rows, uint32_t n,
-                             uint32_t k, void* d_records, cudaStream_t stream);
+                             uint32_t slot_base, uint32_t k, void* d_records, cudaStream_t stream);
 int launch_exact_rank(const float* d_scores, uint32_t n, const uint64_t* d_ids, uint64_t id_base, uint32_t keep,
                       uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_count, cudaStream_t stream);
 int launch_merge_topk(const void* d_lists, uint32_t n_lists, uint32_t stride, uint32_t k, uint64_t* d_out_ids,

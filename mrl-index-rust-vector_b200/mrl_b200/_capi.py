@@ -108,7 +108,7 @@ SIGNATURES = {
     "mrl_ring_push": (_i, [_vp, _vp, _vp]),
     "mrl_ring_drain": (_i, [_vp, _vp, _u32]),
     "mrl_ring_push_device": (_i, [_vp, _vp, _vp, _u32]),
-    "mrl_ring_search_batch": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _vp]),
+    "mrl_ring_search_batch": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _u32, _vp]),
     "mrl_segment_append_device": (_i, [_vp, _vp, _vp, _u64]),
     "mrl_ring_len": (_u32, [_vp]),
     "mrl_ring_rows": (_i, [_vp, C.POINTER(_vp)]),

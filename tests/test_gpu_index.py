@@ -245,7 +245,7 @@ def _dev_rows(a):
 @pytest.mark.parametrize("n", [0, 1, 63, 200])
 def test_ring_search_batch_matches_single(ora, dev, n):
     """mrl_ring_search_batch (one record per query, rows pushed from device memory) equals
-    mrl_ring_search of each query, bit for bit."""
+    mrl_ring_search of each query, bit for bit; a slot_base only moves the sentinel slots."""
     import torch
 
     M = mb()
@@ -262,7 +262,15 @@ def test_ring_search_batch_matches_single(ora, dev, n):
     rb = M.record_bytes(k)
     recs = torch.zeros(n_q * rb, dtype=torch.uint8, device="cuda")
     M._capi.check(dev.ptr, lib.mrl_ring_search_batch(dev.ptr, C.c_void_p(dq.data_ptr()), n_q, dims,
-                                                     ring.ptr if n else None, k, C.c_void_p(recs.data_ptr())))
+                                                     ring.ptr if n else None, 0, k, C.c_void_p(recs.data_ptr())))
+    based = torch.zeros_like(recs)  # rank 3's records in a sharded batch
+    M._capi.check(dev.ptr, lib.mrl_ring_search_batch(dev.ptr, C.c_void_p(dq.data_ptr()), n_q, dims,
+                                                     ring.ptr if n else None, 3 * 4096, k,
+                                                     C.c_void_p(based.data_ptr())))
+    if n:
+        with pytest.raises(M.MrlError, match="slot_base"):
+            M._capi.check(dev.ptr, lib.mrl_ring_search_batch(dev.ptr, C.c_void_p(dq.data_ptr()), n_q, dims, ring.ptr,
+                                                             65536 - n + 1, k, C.c_void_p(based.data_ptr())))
     one = torch.zeros(rb, dtype=torch.uint8, device="cuda")
     rp = C.c_void_p()
     M._capi.check(dev.ptr, lib.mrl_ring_rows(ring.ptr, C.byref(rp)))
@@ -277,6 +285,9 @@ def test_ring_search_batch_matches_single(ora, dev, n):
         assert np.array_equal(a[:8 * m], b[:8 * m]) and np.array_equal(a[8 * k:8 * k + 4 * m], b[8 * k:8 * k + 4 * m])
         pos, sc = ora.ring_search(rows, qs[q], k)
         assert np.array_equal(a[:8 * m].view(np.uint64) & np.uint64(0xFFFF), pos.astype(np.uint64))
+        c = based[q * rb:(q + 1) * rb].cpu().numpy()
+        assert np.array_equal(c[:8 * m].view(np.uint64), b[:8 * m].view(np.uint64) + np.uint64(3 * 4096))
+        assert np.array_equal(c[8 * k:], b[8 * k:])
     ring.close()
 
 
@@ -333,7 +344,7 @@ def test_live_ingest_on_device(ora, dev):
     lists = torch.zeros(2 * n_q * rb, dtype=torch.uint8, device="cuda")
     M._capi.check(dev.ptr, lib.mrl_pack_records(dev.ptr, C.c_void_p(ids.data_ptr()), C.c_void_p(sc.data_ptr()),
                                                 C.c_void_p(cnt.data_ptr()), n_q, k, C.c_void_p(lists.data_ptr())))
-    M._capi.check(dev.ptr, lib.mrl_ring_search_batch(dev.ptr, C.c_void_p(dq.data_ptr()), n_q, dims, ring.ptr, k,
+    M._capi.check(dev.ptr, lib.mrl_ring_search_batch(dev.ptr, C.c_void_p(dq.data_ptr()), n_q, dims, ring.ptr, 0, k,
                                                      C.c_void_p(lists.data_ptr() + n_q * rb)))
     out_i = torch.zeros(n_q * k, dtype=torch.int64, device="cuda")
     out_s = torch.zeros(n_q * k, dtype=torch.float32, device="cuda")

@@ -84,6 +84,81 @@ def test_two_rank_sharded_scan_matches_single_scan(ora, k):
     tmp.spawn(_rank_worker, args=(2, _free_port(), k), nprocs=2, join=True)
 
 
+def _batch_rank_worker(rank, world, port, k):
+    """Configs 4 and 5 on CPU: a batch of queries, each rank scanning its page range and searching
+    its own pending ring rows (sentinel slots rank x 4096 + position, as mrl_ring_search_batch
+    writes them with slot_base = rank x 4096), merging the two per query, packing one record per
+    query, one all-gather, and a per-query merge across ranks. Every rank must end with, for every
+    query, the top-k of the whole corpus plus every rank's ring, with every ring hit naming its
+    rank and row."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import ora
+    from mrl_b200.shard import merge_topk_host, pack_records, shard_range, unpack_records
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        blocks, mean, _ = _corpus(ora)
+        n_docs, dims = 64 * 40 + 17, 384
+        qs, _ = ora.synth_queries(5, n_docs, 21, 3, dims)
+        rings = [ora.synth_docs(60 + r, 10 + 13 * r, dims) for r in range(world)]
+        qs[1] = rings[1 % world][4]  # a pending row of another rank must lead query 1
+        cfg = ora.scan_cfg(k=k)
+        start, count = shard_range(blocks.shape[0], world, rank)
+        sentinel = np.uint64(0xFFFFFFFF) << np.uint64(16)
+        recs = []
+        for q in qs:
+            plan = ora.plan_build(q, eden_mean=mean)
+            ids, sc = ora.scan_blocks(blocks[start:start + count].reshape(-1), plan, cfg, threads=2)
+            gids = ((ids >> np.uint64(16)) + np.uint64(start)) << np.uint64(16) | (ids & np.uint64(0xFFFF))
+            pos, rsc = ora.ring_search(rings[rank], q, k)
+            rids = sentinel | (np.uint64(rank * 4096) + pos.astype(np.uint64))
+            pad_i = np.zeros((2, k), np.uint64)
+            pad_s = np.zeros((2, k), np.float32)
+            pad_i[0, :len(gids)], pad_s[0, :len(sc)] = gids, sc
+            pad_i[1, :len(rids)], pad_s[1, :len(rsc)] = rids, rsc
+            m_i, m_s = merge_topk_host(pad_i, pad_s, np.array([len(gids), len(rids)]), k)
+            pi = np.zeros((1, k), np.uint64)
+            ps = np.zeros((1, k), np.float32)
+            pi[0, :len(m_i)], ps[0, :len(m_s)] = m_i, m_s
+            recs.append(pack_records(pi, ps, np.array([len(m_i)]))[0])
+        rec = torch.from_numpy(np.stack(recs).reshape(-1))  # this rank's batch: one record per query
+        gathered = [torch.zeros_like(rec) for _ in range(world)]
+        dist.all_gather(gathered, rec)
+        g_ids, g_sc, g_cnt = unpack_records(torch.stack(gathered).numpy(), k)  # [world x n_q] records
+        n_q = len(qs)
+        for qi, q in enumerate(qs):
+            sel = [r * n_q + qi for r in range(world)]
+            m_ids, m_sc = merge_topk_host(g_ids[sel], g_sc[sel], g_cnt[sel], k)
+            # the whole corpus and every rank's ring, in one list
+            r_ids, r_sc = ora.scan_blocks(blocks.reshape(-1), ora.plan_build(q, eden_mean=mean), cfg, threads=2)
+            all_i, all_s = [r_ids.astype(np.uint64)], [r_sc]
+            for r in range(world):
+                pos, rsc = ora.ring_search(rings[r], q, k)
+                all_i.append(sentinel | (np.uint64(r * 4096) + pos.astype(np.uint64)))
+                all_s.append(rsc)
+            cat_i, cat_s = np.concatenate(all_i), np.concatenate(all_s)
+            order = np.lexsort((cat_i, -cat_s.astype(np.float64)))[:k]
+            assert np.array_equal(m_ids, cat_i[order]), (rank, qi)
+            assert np.array_equal(m_sc.view(np.uint32), cat_s[order].view(np.uint32)), (rank, qi)
+            if qi == 1:  # the planted pending row: rank 1's ring, row 4
+                assert m_ids[0] == sentinel | np.uint64((1 % world) * 4096 + 4)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("k", [16, 256])
+def test_two_rank_sharded_batch_with_rings(ora, k):
+    import torch.multiprocessing as tmp
+
+    tmp.spawn(_batch_rank_worker, args=(2, _free_port(), k), nprocs=2, join=True)
+
+
 def test_shard_range_covers_pages_once():
     from mrl_b200.shard import shard_range
 
