@@ -209,7 +209,10 @@ int mrl_query_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const float* d_queri
                           const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                           const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
                           uint32_t* d_out_counts, uint32_t* d_out_status);
-/* The same from host queries to host results (synchronous): copy in, fused launches, copy out. */
+/* The same from host queries to host results (synchronous). The query goes to the device from a
+ * pinned staging buffer of the context, and the scan stores its results straight into that
+ * buffer's device mapping, so the call makes one host-to-device copy and no device-to-host copy;
+ * the results are then copied to the caller's buffers on the host. */
 int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint32_t n_q, uint32_t dims,
                    const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg,
                    const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* out_ids,

@@ -58,6 +58,12 @@ struct mrl_ctx {
     void* bbuf = nullptr;
     size_t bbuf_bytes = 0;
     uint32_t batch_engine = MRL_BATCH_TENSOR;
+    // pinned host staging of mrl_query_scan, mapped into the device's address space: the query is
+    // copied to the device from here, and the scan kernel stores its results straight into it
+    // (no device-to-host copies on the query path)
+    void* h_io = nullptr;
+    void* h_io_dev = nullptr;
+    size_t h_io_bytes = 0;
 };
 
 // RingBuffer's pending embeddings (src/ring.rs:49-119) mirrored in HBM: `len` rows of `dims` f32
@@ -147,6 +153,29 @@ int ensure_buf(mrl_ctx* ctx, void** buf, size_t* have, size_t bytes) {
     return MRL_OK;
 }
 int ensure_tmp(mrl_ctx* ctx, size_t bytes) { return ensure_buf(ctx, &ctx->tmp, &ctx->tmp_bytes, bytes); }
+int ensure_host_io(mrl_ctx* ctx, size_t bytes) {
+    if (ctx->h_io_bytes >= bytes) return MRL_OK;
+    bytes = (bytes + 65535) & ~(size_t)65535;
+    if (ctx->h_io) {
+        cudaStreamSynchronize(ctx->stream);  // no launch still writes the old staging
+        cudaFreeHost(ctx->h_io);
+    }
+    ctx->h_io = ctx->h_io_dev = nullptr;
+    ctx->h_io_bytes = 0;
+    cudaError_t e = cudaHostAlloc(&ctx->h_io, bytes, cudaHostAllocMapped | cudaHostAllocPortable);
+    if (e != cudaSuccess) {
+        ctx->h_io = nullptr;
+        return fail(ctx, MRL_ERR_NOMEM, std::string("cudaHostAlloc staging: ") + cudaGetErrorString(e));
+    }
+    e = cudaHostGetDevicePointer(&ctx->h_io_dev, ctx->h_io, 0);
+    if (e != cudaSuccess) {
+        cudaFreeHost(ctx->h_io);
+        ctx->h_io = ctx->h_io_dev = nullptr;
+        return cuda_fail(ctx, e, "cudaHostGetDevicePointer");
+    }
+    ctx->h_io_bytes = bytes;
+    return MRL_OK;
+}
 int ensure_out(mrl_ctx* ctx, size_t bytes) { return ensure_buf(ctx, &ctx->tmp_out, &ctx->tmp_out_bytes, bytes); }
 
 // mrl_scan switches to the batched scan from this many plans on (fast mode, depth L1 or full)
@@ -293,6 +322,7 @@ void mrl_ctx_destroy(mrl_ctx* ctx) {
     cudaFree(ctx->xbuf);
     cudaFree(ctx->ebuf);
     cudaFree(ctx->bbuf);
+    if (ctx->h_io) cudaFreeHost(ctx->h_io);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
 }
@@ -706,31 +736,45 @@ int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint3
     if (int rc = check_cfg(ctx, cfg)) return rc;
     if (n_q == 0) return MRL_OK;
     if (!queries || !out_ids || !out_scores || !out_counts) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
-    for (uint64_t i = 0; i < (uint64_t)n_q * dims; ++i)
-        if (!std::isfinite(queries[i])) return fail(ctx, MRL_ERR_INVALID, "query contains a non-finite value");
     if (int rc = set_device(ctx)) return rc;
     const size_t qbytes = (size_t)n_q * dims * sizeof(float);
     const size_t nk = (size_t)n_q * cfg->shortlist_cand;
+    const size_t o_off = (qbytes + 255) & ~(size_t)255;
+    const size_t obytes = nk * (sizeof(uint64_t) + sizeof(float)) + 2 * sizeof(uint32_t) * n_q;
+    if (int rc = ensure_host_io(ctx, o_off + obytes)) return rc;
     if (int rc = ensure_tmp(ctx, qbytes)) return rc;
-    if (int rc = ensure_out(ctx, nk * (sizeof(uint64_t) + sizeof(float)) + 2 * sizeof(uint32_t) * n_q + 64)) return rc;
+    float* h_q = static_cast<float*>(ctx->h_io);
+    for (uint64_t i = 0; i < (uint64_t)n_q * dims; ++i) {
+        const float v = queries[i];
+        if (!std::isfinite(v)) return fail(ctx, MRL_ERR_INVALID, "query contains a non-finite value");
+        h_q[i] = v;
+    }
+    // results: in the mapped staging when there are pages to scan (the scan stores them there);
+    // an empty segment clears the counts with device memsets, so its results go to device scratch
+    const bool mapped = seg->n_blocks > 0;
+    if (!mapped)
+        if (int rc = ensure_out(ctx, obytes + 64)) return rc;
+    unsigned char* h_out = static_cast<unsigned char*>(ctx->h_io) + o_off;
+    unsigned char* d_out = mapped ? static_cast<unsigned char*>(ctx->h_io_dev) + o_off
+                                  : static_cast<unsigned char*>(ctx->tmp_out);
     float* d_q = (float*)ctx->tmp;
-    uint64_t* d_ids = (uint64_t*)ctx->tmp_out;
-    float* d_sc = (float*)(d_ids + nk);
-    uint32_t* d_cnt = (uint32_t*)(d_sc + nk);
+    uint64_t* d_ids = reinterpret_cast<uint64_t*>(d_out);
+    float* d_sc = reinterpret_cast<float*>(d_out + nk * sizeof(uint64_t));
+    uint32_t* d_cnt = reinterpret_cast<uint32_t*>(d_out + nk * (sizeof(uint64_t) + sizeof(float)));
     uint32_t* d_st = d_cnt + n_q;
-    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(d_q, queries, qbytes, cudaMemcpyHostToDevice, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(d_q, h_q, qbytes, cudaMemcpyHostToDevice, ctx->stream));
     if (int rc = mrl_query_scan_device(ctx, seg, d_q, n_q, dims, codec, plans, cfg, time_lo, time_hi, d_ids, d_sc, d_cnt,
                                        d_st))
         return rc;
-    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_ids, d_ids, nk * sizeof(uint64_t), cudaMemcpyDeviceToHost, ctx->stream));
-    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_scores, d_sc, nk * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-    std::vector<uint32_t> cs(2 * (size_t)n_q);
-    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(cs.data(), d_cnt, 2 * sizeof(uint32_t) * n_q, cudaMemcpyDeviceToHost, ctx->stream));
+    if (!mapped)
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(h_out, d_out, obytes, cudaMemcpyDeviceToHost, ctx->stream));
     MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
-    for (uint32_t q = 0; q < n_q; ++q) {
+    const uint32_t* cs = reinterpret_cast<const uint32_t*>(h_out + nk * (sizeof(uint64_t) + sizeof(float)));
+    for (uint32_t q = 0; q < n_q; ++q)
         if (cs[n_q + q] & 2u) return fail(ctx, MRL_ERR_CUDA, "scan grid barrier timed out (CTAs not co-resident)");
-        out_counts[q] = cs[q];
-    }
+    std::memcpy(out_ids, h_out, nk * sizeof(uint64_t));
+    std::memcpy(out_scores, h_out + nk * sizeof(uint64_t), nk * sizeof(float));
+    std::memcpy(out_counts, cs, n_q * sizeof(uint32_t));
     return MRL_OK;
 }
 
