@@ -384,9 +384,11 @@ def run_ours(args):
             s = time.perf_counter()
             q_dev.copy_(qh[i % n_q], non_blocking=True)
             if peer is not None:
-                peer.scan(segs[i % len(segs)], q_dev.data_ptr(), dims, desc, plans, cfg, out_ids.data_ptr(),
-                          out_sc.data_ptr(), out_cnt.data_ptr())
-                g_ids, g_sc, g_cnt = out_ids.view(-1), out_sc.view(-1), out_cnt.view(-1)
+                # the merged top-k is stored by the scan launch straight into pinned host memory
+                # (device-accessible under unified addressing): no device-to-host copies
+                peer.scan(segs[i % len(segs)], q_dev.data_ptr(), dims, desc, plans, cfg, ids_h.data_ptr(),
+                          sc_h.data_ptr(), cnt_h.data_ptr())
+                g_ids = None
             else:
                 M._capi.check(dev.ptr, lib.mrl_query_scan_device(dev.ptr, segs[i % len(segs)].ptr,
                                                                  C.c_void_p(q_dev.data_ptr()), 1, dims,
@@ -395,9 +397,10 @@ def run_ours(args):
                                                                  C.c_void_p(out_sc.data_ptr()),
                                                                  C.c_void_p(out_cnt.data_ptr()), None))
                 g_ids, g_sc, g_cnt = exch()
-            ids_h.copy_(g_ids, non_blocking=True)
-            sc_h.copy_(g_sc, non_blocking=True)
-            cnt_h.copy_(g_cnt, non_blocking=True)
+            if g_ids is not None:
+                ids_h.copy_(g_ids, non_blocking=True)
+                sc_h.copy_(g_sc, non_blocking=True)
+                cnt_h.copy_(g_cnt, non_blocking=True)
             stream.synchronize()
             if i >= warm:
                 tot += time.perf_counter() - s
@@ -406,10 +409,11 @@ def run_ours(args):
         e2e = {"value": world * e2e_steps / float(t.item()), "unit": "QPS", "h2d_bytes_per_step": qbytes,
                "d2h_bytes_per_step": k * 12 + 4, "steps": e2e_steps,
                "path": ("per rank: query copy from pinned host memory + mrl_query_scan_exchange (fused plan + scan "
-                        "+ NVLink merge, one launch)" if peer is not None else
+                        "+ NVLink merge, one launch, merged top-k stored into pinned host memory by the launch)"
+                        if peer is not None else
                         "per rank: query copy from pinned host memory + mrl_query_scan_device (fused plan + scan) + "
-                        "NCCL all-gather + mrl_merge_topk") + " + copy of the merged top-k to pinned host memory; "
-                       "max over ranks"}
+                        "NCCL all-gather + mrl_merge_topk + copy of the merged top-k to pinned host memory")
+                       + "; max over ranks"}
 
     peak, peak_kind = measured_peaks()
     alg_bytes = nb * 4096

@@ -66,12 +66,19 @@ def test_exchange_world1_matches_device_scan(ora, dev, mode, list_len):
             M._capi.check(dev.ptr, lib.mrl_query_scan_exchange(dev.ptr, seg.ptr, qp, 768, C.byref(desc), plans,
                                                                C.byref(cfg), None, None, ex,
                                                                *[C.c_void_p(t.data_ptr()) for t in b]))
+            # outputs in pinned host memory (device-accessible under unified addressing): the launch
+            # stores the merged top-k straight there
+            h = [t.cpu().pin_memory() for t in _device_outputs(k)]
+            M._capi.check(dev.ptr, lib.mrl_query_scan_exchange(dev.ptr, seg.ptr, qp, 768, C.byref(desc), plans,
+                                                               C.byref(cfg), None, None, ex,
+                                                               *[C.c_void_p(t.data_ptr()) for t in h]))
             torch.cuda.synchronize()
             n = int(a[2].item())
-            assert int(b[2].item()) == n == k
-            assert int(b[3].item()) & 6 == 0  # no barrier or exchange timeout
-            assert torch.equal(a[0][:n], b[0][:n])
+            assert int(b[2].item()) == n == k == int(h[2][0])
+            assert int(b[3].item()) & 6 == 0 and int(h[3][0]) & 6 == 0  # no barrier or exchange timeout
+            assert torch.equal(a[0][:n], b[0][:n]) and torch.equal(a[0][:n].cpu(), h[0][:n])
             assert np.array_equal(a[1][:n].cpu().numpy().view(np.uint32), b[1][:n].cpu().numpy().view(np.uint32))
+            assert np.array_equal(h[1][:n].numpy().view(np.uint32), b[1][:n].cpu().numpy().view(np.uint32))
             if list_len == 1:
                 assert int(b[3].item()) & 1 == 1  # the re-selection ran
     finally:
