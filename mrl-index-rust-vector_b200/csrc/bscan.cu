@@ -390,6 +390,7 @@ __global__ void __launch_bounds__(kSelThreads) bselect_kernel(const SelectLaunch
 // which is exact because the true sum fits in int32. So the stage sums are the same integers as
 // the table sums of the CUDA-core engine and of the single-query kernel.
 constexpr int kTQ = 16;                 // queries per tensor tile
+constexpr int kTG = 2;                  // query tiles per walk over the pages: one A build serves both
 constexpr int kTN = 4 * kTQ;            // B rows: 4 digits per query
 constexpr int kKAll = kPrefix * 16 + kRabitq + kFold;   // 1216 bytes of A per slot
 constexpr int kACols = kKAll / 4;       // 304 tensor-memory columns hold a slot's A row
@@ -467,15 +468,15 @@ __device__ __forceinline__ float qscore(const SlotMeta& m, int32_t P, int32_t s1
 }
 
 struct TShared {
-    uint8_t B[kBTileBytes];              // offset 0 (1 KB aligned)
-    Scalars S[kTQ];
-    QConst qc[kTQ];
+    uint8_t B[kTG][kBTileBytes];         // offset 0 (1 KB aligned); tile t at t x 77,824 (76 KB)
+    Scalars S[kTG * kTQ];
+    QConst qc[kTG * kTQ];
     uint4 onehot[16];                    // the 16 one-hot byte patterns of a 4-bit level
     float2 rho[256];
-    u64 tau[kTQ];
-    BWarpState wst[kBWarps][4];
-    u64 wlist[kBWarps][4][32];           // [warp][query of its group][32]
-    u64 queue[kBWarps][4][32];
+    u64 tau[kTG * kTQ];
+    BWarpState wst[kTG][kBWarps][4];
+    u64 wlist[kTG][kBWarps][4][32];      // [tile][warp][query of its group][32]
+    u64 queue[kTG][kBWarps][4][32];
     uint64_t bar;
     uint32_t taddr;
 };
@@ -528,6 +529,44 @@ __device__ __forceinline__ int32_t digits4(const uint32_t* d) {
     return (int32_t)(d[0] + (d[1] << 8) + (d[2] << 16) + (d[3] << 24));
 }
 
+// The 38 MMAs of one slot tile against one query tile's B digits (at b_smem), then the commit.
+__device__ __forceinline__ void tile_mmas(uint32_t tbase, uint32_t b_smem, uint32_t idesc, uint64_t* bar) {
+#pragma unroll 1
+    for (int k = 0; k < kPrefix * 16 / 32; ++k)
+        tc::mma_i8_ts(tbase + kColP, tbase + 8u * k,
+                      tc::sdesc_kmajor(b_smem + (uint32_t)(2 * k) * kKBlockBytes, kKBlockBytes, 128u), idesc, k > 0);
+    for (int k = 0; k < kRabitq / 32; ++k)
+        tc::mma_i8_ts(tbase + kColS1, tbase + 256u + 8u * k,
+                      tc::sdesc_kmajor(b_smem + (uint32_t)(64 + 2 * k) * kKBlockBytes, kKBlockBytes, 128u), idesc,
+                      k > 0);
+    for (int k = 0; k < kFold / 32; ++k)
+        tc::mma_i8_ts(tbase + kColS4, tbase + 288u + 8u * k,
+                      tc::sdesc_kmajor(b_smem + (uint32_t)(72 + 2 * k) * kKBlockBytes, kKBlockBytes, 128u), idesc,
+                      k > 0);
+    tc::mma_commit(bar);
+}
+
+// Scores of this thread's slot for queries 4 g4 .. 4 g4 + 3 of query tile tt (stage sums as
+// digit columns dp, d1, d4), offered to the tile's selection.
+__device__ __forceinline__ void tile_epilogue(TShared& sh, int tt, uint32_t nq, int g4, int warp, int lane,
+                                             const SlotMeta& m, bool live, uint32_t gid, const uint32_t (&dp)[16],
+                                             const uint32_t (&d1)[16], const uint32_t (&d4)[16]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int q = 4 * g4 + j;
+        if ((uint32_t)q < nq) {  // warp-uniform
+            const int qi = tt * kTQ + q;
+            const QConst c = sh.qc[qi];
+            const int32_t P = digits4(dp + 4 * j);
+            const int32_t A1 = c.c1 + digits4(d1 + 4 * j);
+            const int32_t A4 = c.c4 + digits4(d4 + 4 * j);
+            const float sc = (c.flags & 16u) ? qscore(m, P, A1, A4, c) : fast_score(m, P, A1, A4, sh.S[qi]);
+            const u64 key = (!live || m.tomb) ? 0ull : make_key(sc, gid);
+            bsel_offer1(sh.wlist[tt][warp][j], sh.queue[tt][warp][j], lane, &sh.tau[qi], &sh.wst[tt][warp][j], key);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch t) {
     extern __shared__ __align__(1024) unsigned char t_dyn[];
     TShared& sh = *reinterpret_cast<TShared*>(t_dyn);
@@ -557,20 +596,23 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
     const uint32_t tbase = sh.taddr;
     const uint32_t my_lane = (uint32_t)(32 * qw) << 16;  // this warp's tensor-memory lane quarter
     const uint32_t idesc = tc::idesc_i8(128, kTN);
-    const uint32_t b_smem = tc::smem_u32(sh.B);
+    const uint32_t b_smem = tc::smem_u32(&sh.B[0][0]);
     uint32_t phase = 0;
     bool failed = false;
 
-    for (uint32_t q0 = 0; q0 < p.n_q && !failed; q0 += kTQ) {
-        const uint32_t nq = min((uint32_t)kTQ, p.n_q - q0);
+    for (uint32_t q0 = 0; q0 < p.n_q && !failed; q0 += kTG * kTQ) {
+        const uint32_t nqg = min((uint32_t)(kTG * kTQ), p.n_q - q0);  // queries of this group
+        const int nt = (int)((nqg + kTQ - 1) / kTQ);                    // its query tiles (1 or 2)
+        const uint32_t nq0 = min((uint32_t)kTQ, nqg), nq1 = nqg - nq0;
         __syncthreads();
-        {  // this tile's B digits, scalars, constants; selection state reset
+        {  // the group's B digits, scalars, constants; selection state reset
             const uint4* src = reinterpret_cast<const uint4*>(t.tiles + (size_t)(q0 / kTQ) * kBTileBytes);
-            uint4* dst = reinterpret_cast<uint4*>(sh.B);
-            for (uint32_t i = tid; i < kBTileBytes / 16; i += kBThreads) dst[i] = __ldg(src + i);
+            uint4* dst = reinterpret_cast<uint4*>(&sh.B[0][0]);
+            const uint32_t n16 = (uint32_t)nt * (kBTileBytes / 16);
+            for (uint32_t i = tid; i < n16; i += kBThreads) dst[i] = __ldg(src + i);
         }
-        if (tid < kTQ) {
-            if ((uint32_t)tid < nq) {
+        if (tid < kTG * kTQ) {
+            if ((uint32_t)tid < nqg) {
                 fill_scalars(p.plans + q0 + tid, p.w_s4, p.depth, 1, sh.S[tid]);
                 const Scalars& S = sh.S[tid];
                 QConst c;
@@ -590,8 +632,8 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
             }
             sh.tau[tid] = 0ull;
         }
-        if (tid < kBWarps * 4) sh.wst[tid >> 2][tid & 3] = BWarpState{0u, 0};
-        for (int i = tid; i < kBWarps * 4 * 32; i += kBThreads) (&sh.wlist[0][0][0])[i] = 0ull;
+        if (tid < kTG * kBWarps * 4) (&sh.wst[0][0][0])[tid] = BWarpState{0u, 0};
+        for (int i = tid; i < kTG * kBWarps * 4 * 32; i += kBThreads) (&sh.wlist[0][0][0][0])[i] = 0ull;
         tc::fence_proxy_async_smem();  // generic-proxy writes of B -> tensor-core reads
         tc::fence_before();
         __syncthreads();
@@ -635,59 +677,62 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
             __syncthreads();
             if (tid == 0) {
                 tc::fence_after();
-#pragma unroll 1
-                for (int k = 0; k < kPrefix * 16 / 32; ++k)
-                    tc::mma_i8_ts(tbase + kColP, tbase + 8u * k,
-                                  tc::sdesc_kmajor(b_smem + (uint32_t)(2 * k) * kKBlockBytes, kKBlockBytes, 128u),
-                                  idesc, k > 0);
-                for (int k = 0; k < kRabitq / 32; ++k)
-                    tc::mma_i8_ts(tbase + kColS1, tbase + 256u + 8u * k,
-                                  tc::sdesc_kmajor(b_smem + (uint32_t)(64 + 2 * k) * kKBlockBytes, kKBlockBytes, 128u),
-                                  idesc, k > 0);
-                for (int k = 0; k < kFold / 32; ++k)
-                    tc::mma_i8_ts(tbase + kColS4, tbase + 288u + 8u * k,
-                                  tc::sdesc_kmajor(b_smem + (uint32_t)(72 + 2 * k) * kKBlockBytes, kKBlockBytes, 128u),
-                                  idesc, k > 0);
-                tc::mma_commit(&sh.bar);
+                tile_mmas(tbase, b_smem, idesc, &sh.bar);
             }
-            const bool ok = tc::mbar_wait(&sh.bar, phase, kWaitPolls);
+            bool ok = tc::mbar_wait(&sh.bar, phase, kWaitPolls);
             phase ^= 1u;
             if (__syncthreads_or(!ok)) {
                 failed = true;
                 break;
             }
             tc::fence_after();
-            // ---- epilogue: this thread's slot, queries 4 g4 .. 4 g4 + 3
+            // ---- epilogue: this thread's slot; tile 1's MMAs run while tile 0's scores are made
             uint32_t dp[16], d1[16], d4[16];
             TC_LD16(dp, tbase + my_lane + (uint32_t)(kColP + 16 * g4));
             TC_LD16(d1, tbase + my_lane + (uint32_t)(kColS1 + 16 * g4));
             TC_LD16(d4, tbase + my_lane + (uint32_t)(kColS4 + 16 * g4));
             tc::wait_ld();
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int q = 4 * g4 + j;
-                if ((uint32_t)q < nq) {  // warp-uniform
-                    const QConst c = sh.qc[q];
-                    const int32_t P = digits4(dp + 4 * j);
-                    const int32_t A1 = c.c1 + digits4(d1 + 4 * j);
-                    const int32_t A4 = c.c4 + digits4(d4 + 4 * j);
-                    const float sc = (c.flags & 16u) ? qscore(m, P, A1, A4, c) : fast_score(m, P, A1, A4, sh.S[q]);
-                    const u64 key = (!live || m.tomb) ? 0ull : make_key(sc, b * 64 + v);
-                    bsel_offer1(sh.wlist[warp][j], sh.queue[warp][j], lane, &sh.tau[q], &sh.wst[warp][j], key);
+            if (nt > 1) {
+                tc::fence_before();
+                __syncthreads();  // every thread has read D: tile 1's MMAs may overwrite it
+                if (tid == 0) {
+                    tc::fence_after();
+                    tile_mmas(tbase, b_smem + kBTileBytes, idesc, &sh.bar);
                 }
+            }
+            const uint32_t gid = b * 64 + v;
+            tile_epilogue(sh, 0, nq0, g4, warp, lane, m, live, gid, dp, d1, d4);
+            if (nt > 1) {
+                ok = tc::mbar_wait(&sh.bar, phase, kWaitPolls);
+                phase ^= 1u;
+                if (__syncthreads_or(!ok)) {
+                    failed = true;
+                    break;
+                }
+                tc::fence_after();
+                TC_LD16(dp, tbase + my_lane + (uint32_t)(kColP + 16 * g4));
+                TC_LD16(d1, tbase + my_lane + (uint32_t)(kColS1 + 16 * g4));
+                TC_LD16(d4, tbase + my_lane + (uint32_t)(kColS4 + 16 * g4));
+                tc::wait_ld();
+                tile_epilogue(sh, 1, nq1, g4, warp, lane, m, live, gid, dp, d1, d4);
             }
             tc::fence_before();
             __syncthreads();  // tensor memory (A and D) free for the next slot tile
         }
         if (failed) break;
-        for (int j = 0; j < 4; ++j)
-            if (sh.wst[warp][j].qn) bsel_flush(sh.wlist[warp][j], sh.queue[warp][j], lane, &sh.tau[4 * g4 + j], &sh.wst[warp][j]);
+        for (int tt = 0; tt < nt; ++tt)
+            for (int j = 0; j < 4; ++j)
+                if (sh.wst[tt][warp][j].qn)
+                    bsel_flush(sh.wlist[tt][warp][j], sh.queue[tt][warp][j], lane, &sh.tau[tt * kTQ + 4 * g4 + j],
+                               &sh.wst[tt][warp][j]);
         __syncthreads();
-        if ((uint32_t)warp < nq) {  // warp w merges query w: the lists of the 4 lane quarters
-            const int g = warp >> 2, j = warp & 3;
-            const u64 a = warp_merge32(sh.wlist[4 * g + 0][j][lane], sh.wlist[4 * g + 1][j][lane], lane);
-            const u64 c = warp_merge32(sh.wlist[4 * g + 2][j][lane], sh.wlist[4 * g + 3][j][lane], lane);
-            p.lists[((size_t)(q0 + warp) * G + blockIdx.x) * 32 + lane] = warp_merge32(a, c, lane);
+        for (int tt = 0; tt < nt; ++tt) {
+            if ((uint32_t)warp < (tt == 0 ? nq0 : nq1)) {  // warp w merges query w: the 4 lane quarters' lists
+                const int g = warp >> 2, j = warp & 3;
+                const u64 a = warp_merge32(sh.wlist[tt][4 * g + 0][j][lane], sh.wlist[tt][4 * g + 1][j][lane], lane);
+                const u64 c = warp_merge32(sh.wlist[tt][4 * g + 2][j][lane], sh.wlist[tt][4 * g + 3][j][lane], lane);
+                p.lists[((size_t)(q0 + tt * kTQ + warp) * G + blockIdx.x) * 32 + lane] = warp_merge32(a, c, lane);
+            }
         }
     }
     if (failed) {

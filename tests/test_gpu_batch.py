@@ -100,7 +100,7 @@ def test_batch_matches_single_query(ora, dev, engine, codec, depth):
     plans.free()
 
 
-@pytest.mark.parametrize("n_q", [1, 2, 8, 9])
+@pytest.mark.parametrize("n_q", [1, 2, 8, 9, 40])
 @pytest.mark.parametrize("k", [1, 16, 1000])
 def test_batch_sizes_and_k(ora, dev, engine, n_q, k):
     M = mb()
