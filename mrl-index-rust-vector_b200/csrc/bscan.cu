@@ -471,7 +471,6 @@ struct TShared {
     uint8_t B[kTG][kBTileBytes];         // offset 0 (1 KB aligned); tile t at t x 77,824 (76 KB)
     Scalars S[kTG * kTQ];
     QConst qc[kTG * kTQ];
-    uint4 onehot[16];                    // the 16 one-hot byte patterns of a 4-bit level
     float2 rho[256];
     u64 tau[kTG * kTQ];
     BWarpState wst[kTG][kBWarps][4];
@@ -504,16 +503,19 @@ __device__ __forceinline__ void bsel_offer1(u64* wl, u64* q, int lane, u64* cta_
     if (qn + nn >= 32) bsel_flush(wl, q, lane, cta_tau, st);
 }
 
-// One-hot bytes of the four 4-bit levels in nibbles 0..3 of `w`, 4 columns each, from the
-// 16-entry pattern table.
-__device__ __forceinline__ void onehot4(uint32_t w, const uint4* tab, uint32_t (&r)[16]) {
+// One-hot bytes of the four 4-bit levels in nibbles 0..3 of `w`, 4 columns each: level l sets
+// byte l & 3 of column l >> 2 (ALU only; a shared-memory pattern table costs bank conflicts
+// under the data-dependent indices).
+__device__ __forceinline__ void onehot4(uint32_t w, uint32_t (&r)[16]) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const uint4 x = tab[(w >> (4 * i)) & 15u];
-        r[4 * i] = x.x;
-        r[4 * i + 1] = x.y;
-        r[4 * i + 2] = x.z;
-        r[4 * i + 3] = x.w;
+        const uint32_t l = (w >> (4 * i)) & 15u;
+        const uint32_t bit = 1u << ((l & 3u) << 3);
+        const uint32_t c = l >> 2;
+        r[4 * i] = c == 0u ? bit : 0u;
+        r[4 * i + 1] = c == 1u ? bit : 0u;
+        r[4 * i + 2] = c == 2u ? bit : 0u;
+        r[4 * i + 3] = c == 3u ? bit : 0u;
     }
 }
 // 0/1 bytes of the 16 nibbles' bits of two words (64 bits) into 16 columns.
@@ -530,19 +532,20 @@ __device__ __forceinline__ int32_t digits4(const uint32_t* d) {
 }
 
 // The 38 MMAs of one slot tile against one query tile's B digits (at b_smem), then the commit.
+// Fully unrolled: consecutive K steps are 2 KB apart in B, i.e. +128 in the descriptor's
+// start-address field (address >> 4; B ends below 256 KB, so the field never carries).
 __device__ __forceinline__ void tile_mmas(uint32_t tbase, uint32_t b_smem, uint32_t idesc, uint64_t* bar) {
-#pragma unroll 1
+    const uint64_t d0 = tc::sdesc_kmajor(b_smem, kKBlockBytes, 128u);
+    constexpr uint64_t kStep = (2u * kKBlockBytes) >> 4;
+#pragma unroll
     for (int k = 0; k < kPrefix * 16 / 32; ++k)
-        tc::mma_i8_ts(tbase + kColP, tbase + 8u * k,
-                      tc::sdesc_kmajor(b_smem + (uint32_t)(2 * k) * kKBlockBytes, kKBlockBytes, 128u), idesc, k > 0);
+        tc::mma_i8_ts(tbase + kColP, tbase + 8u * k, d0 + kStep * k, idesc, k > 0);
+#pragma unroll
     for (int k = 0; k < kRabitq / 32; ++k)
-        tc::mma_i8_ts(tbase + kColS1, tbase + 256u + 8u * k,
-                      tc::sdesc_kmajor(b_smem + (uint32_t)(64 + 2 * k) * kKBlockBytes, kKBlockBytes, 128u), idesc,
-                      k > 0);
+        tc::mma_i8_ts(tbase + kColS1, tbase + 256u + 8u * k, d0 + kStep * (32 + k), idesc, k > 0);
+#pragma unroll
     for (int k = 0; k < kFold / 32; ++k)
-        tc::mma_i8_ts(tbase + kColS4, tbase + 288u + 8u * k,
-                      tc::sdesc_kmajor(b_smem + (uint32_t)(72 + 2 * k) * kKBlockBytes, kKBlockBytes, 128u), idesc,
-                      k > 0);
+        tc::mma_i8_ts(tbase + kColS4, tbase + 288u + 8u * k, d0 + kStep * (36 + k), idesc, k > 0);
     tc::mma_commit(bar);
 }
 
@@ -585,11 +588,6 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
         tc::fence_mbar_init();
     }
     fill_rho_tab(sh.rho, tid, kBThreads);
-    if (tid < 16) {
-        uint32_t w[4] = {0u, 0u, 0u, 0u};
-        w[tid >> 2] = 1u << (8 * (tid & 3));
-        sh.onehot[tid] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
@@ -665,7 +663,7 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {  // dims 16 g4 + 4c .. + 3
                     const uint32_t w = (c < 2 ? wa : wb) >> (16 * (c & 1));
-                    onehot4(w, sh.onehot, rr);
+                    onehot4(w, rr);
                     TC_ST16(tbase + my_lane + (uint32_t)(64 * g4 + 16 * c), rr);
                 }
                 if (g4 == 0) { bits16(s.c2.x, s.c2.y, rr); TC_ST16(tbase + my_lane + 256u, rr); }
@@ -679,7 +677,9 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
                 tc::fence_after();
                 tile_mmas(tbase, b_smem, idesc, &sh.bar);
             }
-            bool ok = tc::mbar_wait(&sh.bar, phase, kWaitPolls);
+            // one thread polls the mbarrier; the others sleep in the CTA barrier (no issue slots
+            // or shared-memory polls taken from the MMA issue)
+            bool ok = tid != 0 || tc::mbar_wait(&sh.bar, phase, kWaitPolls);
             phase ^= 1u;
             if (__syncthreads_or(!ok)) {
                 failed = true;
@@ -703,7 +703,7 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
             const uint32_t gid = b * 64 + v;
             tile_epilogue(sh, 0, nq0, g4, warp, lane, m, live, gid, dp, d1, d4);
             if (nt > 1) {
-                ok = tc::mbar_wait(&sh.bar, phase, kWaitPolls);
+                ok = tid != 0 || tc::mbar_wait(&sh.bar, phase, kWaitPolls);
                 phase ^= 1u;
                 if (__syncthreads_or(!ok)) {
                     failed = true;
