@@ -469,3 +469,31 @@ def test_full_size_1m_properties(ora, dev):
     np.testing.assert_allclose(fsc, esc, rtol=RTOL, atol=ATOL)
     vid = lambda o: (o // 64) << 16 | (o % 64)  # noqa: E731
     assert_same_topk([vid(o) for o in fi], fs, [vid(o) for o in ei], es, RTOL)
+
+
+def test_query_scan_host_staging_regrows(ora, dev, corpus768):
+    """mrl_query_scan's pinned, device-mapped staging (query in, results stored by the scan) across
+    calls whose sizes grow and shrink: one query, then the whole set, then a shortlist of 4,096,
+    then one query again; each call equals the plan + scan path, and a non-finite query is refused
+    before anything is staged."""
+    M = mb()
+    qs = corpus768["qs"]
+    kw = dict(prefix_codec=M.PrefixCodec.EDEN_PROD, eden=fit(corpus768["mean"]))
+    seg = M.Segment.upload(corpus768["eden"], dev)
+    ref = M.QueryPlan.from_queries(qs, dev=dev, **kw)
+    for n, k in ((1, 16), (len(qs), 256), (1, 4096), (1, 16)):
+        cfg = M.ScanConfig(shortlist_cand=k)
+        ids, sc, cnt, plans = M.query_scan(seg, qs[:n], cfg, **kw)
+        r_ids, r_sc, r_cnt = M.scan_blocks_batch(seg, ref, cfg)
+        assert np.array_equal(cnt, r_cnt[:n])
+        for qi in range(n):
+            m = int(cnt[qi])
+            assert np.array_equal(ids[qi, :m], r_ids[qi, :m])
+            assert np.array_equal(sc[qi, :m].view(np.uint32), r_sc[qi, :m].view(np.uint32))
+        plans.free()
+    bad = qs[:1].copy()
+    bad[0, 5] = np.nan
+    with pytest.raises(M.MrlError, match="non-finite"):
+        M.query_scan(seg, bad, M.ScanConfig(shortlist_cand=16), **kw)
+    ref.free()
+    seg.free()
