@@ -78,12 +78,12 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
-def profiled_traffic(mode: str):
+def profiled_traffic(mode: str, key: str = "traffic_bytes_per_launch"):
     """dram bytes per scan launch recorded from an ncu capture (profiles/*.md), or None."""
     path = os.path.join(ROOT, "profiles", f"scan_{mode}_1m.md")
     try:
         for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
+            if line.startswith(key + ":"):
                 return int(float(line.split(":", 1)[1].strip()))
     except OSError:
         pass
@@ -707,20 +707,23 @@ def run_batch(args):
                     + "copy to pinned host" + ("; max over ranks" if world > 1 else ""))}
 
     pairs = B * n  # this rank's (query, doc) pairs per step
+    # DRAM bytes per scan launch from the committed ncu capture of this exact shape, else None
+    profiled = world == 1 and not live and n_total == 1_000_000 and dims == 768 and B == 1024 and k == 256
     if args.engine == "tensor":
         ops = pairs * (16 * 64 + 128 + 64) * 4 * 2  # executed int8 MMA ops: 1216 K bytes x 4 digits x 2
         bf16, _ = measured_peaks_tensor()
         roof = {"bound": "tensor", "achieved": ops / (scan_ms / 1e3) / 1e12, "peak": 2 * bf16, "unit": "TOP/s",
                 "frac": ops / (scan_ms / 1e3) / 1e12 / (2 * bf16),
                 "peak_kind": "2 x measured dense bf16 (tcgen05 kind::i8 dense rate is twice kind::f16 on B200)",
-                "kernel": "tscan_kernel", "traffic": None}
+                "kernel": "tscan_kernel",
+                "traffic": profiled_traffic("batch", "traffic_bytes_per_launch_tensor") if profiled else None}
     else:
         cuda_core_peak = 148 * 128 * 2 * 1.965e9 / 1e12
         alg = pairs * 512
         roof = {"bound": "fp32/int pipes", "achieved": alg / (scan_ms / 1e3) / 1e12, "peak": cuda_core_peak,
                 "unit": "TOP/s", "frac": alg / (scan_ms / 1e3) / 1e12 / cuda_core_peak,
                 "peak_kind": "148 SMs x 128 lanes x 2 x 1965 MHz (nominal)", "kernel": "bscan_kernel",
-                "traffic": None}
+                "traffic": profiled_traffic("batch", "traffic_bytes_per_launch_cuda_core") if profiled else None}
     if live:
         workload = (f"config 5 shape: batched scan, {B} queries per step over {n_total:,} x {dims} docs on {world} "
                     f"GPU(s), {live} new vectors per step and rank ingested through the device ring (flushed every 64 "
