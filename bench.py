@@ -6,13 +6,19 @@ Workload (N=1): BASELINE config 2 — 1,000,000 unit-norm 768-d docs (x_d ~ (d+1
 z ~ Irwin-Hall(12)-6, L2-normalised; seeded), EDEN-prod 4-bit prefix + RaBitQ mid + folded tail,
 single-query batches (one query per step, noisy-copy queries, sigma 0.1), shortlist 256, full_64b,
 w_s4 0.20, cs_tolerance 1.0, temporal filter off. A step = plan build + fused scan/top-k of one
-query over the whole 64 MB corpus. L2 (126 MB, larger than the corpus) is flushed before every
-step by a read-modify-write pass over a 512 MiB buffer, outside the per-step CUDA events (a plain
-memset does not evict: its stores do not displace the corpus lines).
+query over the whole 64 MB corpus (one launch). Pages are kept out of L2 by default by rotating the
+steps over 4 segments of the same shape (256 MB of pages against the 126 MB L2), so every step's
+pages come from HBM while the kernel code stays cached, as in a serving loop (`--l2 rotate`);
+`--l2 flush` instead flushes L2 before every step with a read-modify-write pass over a 512 MiB
+buffer outside the per-step CUDA events.
 
 N > 1 (torchrun, one rank per GPU): each rank holds its own 1M-doc shard (weak scaling); a step is
-one query against every shard followed by an NCCL all-gather of the per-shard top-256 and a merge.
-value = N * steps / time (1M-doc shard queries per second, whole job).
+one query against every shard, the per-rank top-256 records merged inside the scan launch over
+NVLink peer memory by default (`--exchange nvlink`; `--exchange nccl`: an NCCL all-gather of the
+records and a merge kernel). value = N * steps / time (1M-doc shard queries per second, whole job).
+
+--batch B: BASELINE configs 3-5 (batched scans; see run_batch). --workload config1: BASELINE
+config 1 (384-d, 2,048 pages, 1,000 queries, shortlist 256 then exact top-10; see run_config1).
 
 --impl reference: the reference's CPU scan restated by the oracle (scan_blocks with the Rayon
 sharding rules, all host threads) on the same workload, rank 0 only.

@@ -34,7 +34,7 @@ extern "C" {
 #define MRL_DEPTH_L0 0u       /* StrataDepth::L0Only, src/config.rs:38 */
 #define MRL_DEPTH_L1 1u       /* StrataDepth::L1Rabitq, src/config.rs:40 */
 #define MRL_DEPTH_FULL 2u     /* StrataDepth::Full64b, src/config.rs:46 */
-#define MRL_MODE_FAST 0u      /* fixed-point int32 stage sums; f32 scores within 1e-5 relative */
+#define MRL_MODE_FAST 0u      /* fixed-point int32 stage sums choose candidates; results rescored exactly */
 #define MRL_MODE_EXACT 1u     /* f32 sequential sums, bit-identical to the reference arithmetic */
 
 typedef struct mrl_ctx mrl_ctx;
@@ -86,7 +86,13 @@ typedef struct mrl_codec_desc {
 } mrl_codec_desc;
 
 /* `ScanConfig` (src/config.rs:79-88) plus the device scoring mode. numa_sharding is a CPU
- * scheduling knob and is ignored on the device. */
+ * scheduling knob and is ignored on the device. Every scan returns the top shortlist_cand hits by
+ * full score. That is the reference's own result whenever its pruning bounds (src/scan.rs:508-514,
+ * 572-584, 587-607) are never below a full score: cs_tolerance >= 0 at L0Only, >= sqrt(2/pi) from
+ * L1Rabitq on, and with the folded tail (Full64b, dims > 192) also cs_tolerance >= 1 and
+ * |stratum4_weight| * sqrt(2/pi) * sqrt(B) <= cs_tolerance, B = min((dims - 192) / 64, 9). The
+ * defaults (1.0, 0.20) qualify. Outside that region the reference's result depends on the order it
+ * scans blocks in, and scans fail with MRL_ERR_INVALID naming the violated condition. */
 typedef struct mrl_scan_cfg {
     uint32_t shortlist_cand;
     float cs_tolerance;
@@ -189,7 +195,10 @@ int mrl_scan_batch_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pla
  * by that region's fixed size (1,114,368 bytes): seg must hold at most MRL_STATIC_MAX_BLOCKS pages
  * and the device at most MRL_STATIC_MAX_CTAS SMs, else MRL_ERR_INVALID with a message naming the
  * limit. The first call on a device looks the region up (and may load the module), so make it
- * before any stream capture begins. The region is shared by every context on a device: calls in
+ * before any stream capture begins. The looked-up address is kept for the life of the process and
+ * is valid only while the device's primary context lives: after cudaDeviceReset (or anything else
+ * that destroys the primary context) do not call this function again in the same process. The
+ * region is shared by every context on a device: calls in
  * flight at the same time on one device (other streams, contexts or threads) race on it, while
  * calls ordered on one stream do not. Each call zeroes the region's control words on the context
  * stream before its first launch. out_status bit 1 = grid barrier timed out (no result). */
@@ -324,6 +333,17 @@ int mrl_debug_vector_scores(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
                             const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                             const uint32_t* time_hi, float* out_scores, uint8_t* out_active,
                             int32_t* out_partials);
+
+/* The bound E the fast mode's final ranking uses for plan q over seg: every slot's fast-mode score
+ * (the fixed-point stage sums) is within E of its exact-mode score (the reference's f32 loops).
+ * Derived from the plan's per-stage magnitudes and the segment's maxima of |scale|, |offset|, mid_n
+ * and max(high_n, 1e-6), which every call that adds pages keeps current. Synchronous. */
+int mrl_debug_score_bound(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q,
+                          const mrl_scan_cfg* cfg, float* out_bound);
+/* The context's 8 scan control words (page counter, grid barrier count and generation, timeout
+ * flag, exchange count, exit count). Every scan launch leaves all of them but the barrier
+ * generation (word 2) at zero, whichever path it took. Synchronous. */
+int mrl_debug_control_words(mrl_ctx* ctx, uint32_t* out);
 
 /* ---- encode: encode_block_with_fits (src/quantize.rs:36-96) ----------------------------- */
 /* Encode host rows (n x dims f32, rows 64*b .. 64*b+63 form block b) into PaxBlock64 pages.

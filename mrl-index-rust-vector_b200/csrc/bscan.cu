@@ -258,11 +258,21 @@ struct SelectLaunch {
     const u64* lists;  // [n_q][G][32]
     const uint32_t* err;  // scan error word (bit 1: a bounded wait ran out), ORed into every status
     uint32_t G, n_q, k, block_id_base;
+    // exact finishing: the pages (candidates are rescored in the reference's f32 order), the plans,
+    // the segment's meta maxima (fast/exact score bound), and the scan's w_s4 and depth
+    const uint4* pages;
+    const DevPlan* plans;
+    const float* metamax;
+    float w_s4;
+    uint32_t depth;
+    uint32_t cap;  // candidate capacity (power of two >= k)
     uint64_t* out_ids;
     float* out_scores;
     uint32_t* out_counts;
     uint32_t* out_status;
 };
+
+__device__ __forceinline__ u64 probe_atleast_b(float s) { return (make_key(s, 0u) & 0xFFFFFFFF00000000ull) - 1ull; }
 
 __global__ void __launch_bounds__(kSelThreads) bselect_kernel(const SelectLaunch p) {
     extern __shared__ __align__(16) unsigned char s_dyn[];
@@ -335,24 +345,56 @@ __global__ void __launch_bounds__(kSelThreads) bselect_kernel(const SelectLaunch
         }
         T = s_prefix;
     }
-    // the top keys, then a bitonic sort (descending) of P2 slots
-    uint32_t P2 = 1;
-    while (P2 < k) P2 <<= 1;
-    for (uint32_t i = tid; i < P2; i += kSelThreads) top[i] = 0ull;
+    // Exact finishing. Every fast score is within E of the slot's exact score, so the exact top k
+    // lies among the keys whose fast score is >= F_k - 2E (F_k: the k-th fast score), provided no
+    // CTA list dropped such a key: a full list is safe when its last fast score + 4E < F_k. Those
+    // candidates are rescored in the reference's f32 order and sorted by exact key.
+    __shared__ __align__(16) float s_xt[kTabBw3 + kPrefix];
+    __shared__ float2 s_rho[256];
+    __shared__ float s_E;
+    const DevPlan* P = p.plans + q;
+    for (int i = tid; i < kPrefix * 16; i += kSelThreads) s_xt[i] = P->fp_prefix[i];
+    for (int i = tid; i < kRabitq; i += kSelThreads) s_xt[kTabMidW + i] = P->mid_w[i];
+    for (int i = tid; i < kFold; i += kSelThreads) s_xt[kTabTailW + i] = P->tail_w[i];
+    for (int i = tid; i < kPrefix; i += kSelThreads) s_xt[kTabBw3 + i] = P->qp.bit_weights[i][3];
+    fill_rho_tab(s_rho, tid, kSelThreads);
+    if (tid == 0) s_E = fast_error_bound(*P, __ldg(reinterpret_cast<const float4*>(p.metamax)), p.w_s4, p.depth);
+    const uint32_t cap = p.cap;
+    for (uint32_t i = tid; i < cap; i += kSelThreads) top[i] = 0ull;
     __syncthreads();
+    const float E = s_E;
+    const bool all = s_valid <= k;
+    const float fk = all ? 0.0f : key_score(T);
+    const u64 lo = all ? 0ull : probe_atleast_b(__fsub_rd(fk, 2.0f * E));
     for (uint32_t i = tid; i < n; i += kSelThreads) {
         const u64 x = keys[i];
-        if (x != 0ull && x >= T) {
+        if (x != 0ull && x > lo) {
             const unsigned at = atomicAdd(&s_cnt, 1u);
-            if (at < P2) top[at] = x;
+            if (at < cap) top[at] = x;
+            else atomicOr(&s_flag, 1u);  // more candidates than room: rerun on the single-query kernel
         }
-        // a full CTA list whose last key is inside the top k may have dropped a top-k key
-        if ((i & 31u) == 31u && x != 0ull && x >= T) atomicOr(&s_flag, 1u);
+        // a full CTA list may have dropped a slot that belongs to the exact top k
+        if ((i & 31u) == 31u && x != 0ull && (all || __fadd_ru(key_score(x), 4.0f * E) >= fk)) atomicOr(&s_flag, 1u);
     }
     __syncthreads();
-    for (uint32_t kk = 2; kk <= P2; kk <<= 1) {
+    {
+        Scalars S;
+        fill_scalars(P, p.w_s4, p.depth, 1, S);
+        const uint32_t nc = min(s_cnt, cap);
+        for (uint32_t i = tid; i < nc; i += kSelThreads) {
+            const uint32_t ord = key_ordinal(top[i]);
+            Slot4 sl;
+            load_slot(p.pages, ord >> 6, (int)(ord & 63u), sl);
+            float sc = 0.0f;
+            slot_score<MRL_MODE_EXACT>(sl.c0, sl.c1, sl.c2, sl.c3, reinterpret_cast<const int*>(s_xt), s_rho, S, sc,
+                                       nullptr);
+            top[i] = make_key(sc, ord);
+        }
+    }
+    __syncthreads();
+    for (uint32_t kk = 2; kk <= cap; kk <<= 1) {
         for (uint32_t j = kk >> 1; j > 0; j >>= 1) {
-            for (uint32_t i = tid; i < P2; i += kSelThreads) {
+            for (uint32_t i = tid; i < cap; i += kSelThreads) {
                 const uint32_t ixj = i ^ j;
                 if (ixj > i) {
                     const u64 a = top[i], b = top[ixj];
@@ -363,7 +405,7 @@ __global__ void __launch_bounds__(kSelThreads) bselect_kernel(const SelectLaunch
             __syncthreads();
         }
     }
-    const uint32_t m = min(s_cnt, k);
+    const uint32_t m = min(s_valid, k);
     for (uint32_t i = tid; i < m; i += kSelThreads) {
         const u64 key = top[i];
         const uint32_t ord = key_ordinal(key);
@@ -753,7 +795,7 @@ size_t batch_scratch_bytes(uint32_t ctas, uint32_t n_q) {
 }
 
 int launch_scan_batch(const uint4* pages, const uint2* block_ts, uint32_t n_blocks, uint32_t block_id_base,
-                      const DevPlan* plans, uint32_t n_q, uint32_t k, float w_s4, uint32_t depth, uint32_t use_time,
+                      const float* metamax, const DevPlan* plans, uint32_t n_q, uint32_t k, float w_s4, uint32_t depth, uint32_t use_time,
                       uint32_t has_lo, uint32_t lo, uint32_t has_hi, uint32_t hi, uint32_t ctas, uint32_t engine,
                       void* scratch, uint64_t* out_ids, float* out_scores, uint32_t* out_counts, uint32_t* out_status,
                       cudaStream_t stream) {
@@ -801,8 +843,9 @@ int launch_scan_batch(const uint4* pages, const uint2* block_ts, uint32_t n_bloc
         bscan_kernel<<<ctas, kBThreads, smem, stream>>>(b);
     }
     if (cudaGetLastError() != cudaSuccess) return -1;
+    // candidate room: k plus the near-ties of the k-th score, as a power of two
     uint32_t P2 = 1;
-    while (P2 < k) P2 <<= 1;
+    while (P2 < k + 64) P2 <<= 1;
     const size_t ssmem = (size_t)ctas * 32 * sizeof(u64) + kSelBins * sizeof(unsigned) + (size_t)P2 * sizeof(u64);
     if (ssmem > 227 * 1024) return -1;
     if (cudaFuncSetAttribute(bselect_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem) != cudaSuccess)
@@ -814,6 +857,12 @@ int launch_scan_batch(const uint4* pages, const uint2* block_ts, uint32_t n_bloc
     s.n_q = n_q;
     s.k = k;
     s.block_id_base = block_id_base;
+    s.pages = pages;
+    s.plans = plans;
+    s.metamax = metamax;
+    s.w_s4 = w_s4;
+    s.depth = depth;
+    s.cap = P2;
     s.out_ids = out_ids;
     s.out_scores = out_scores;
     s.out_counts = out_counts;

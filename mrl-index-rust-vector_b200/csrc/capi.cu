@@ -12,15 +12,17 @@
 
 // Scan scratch for mrl_scan_device_static, placed in the module's own global memory so that entry
 // point allocates nothing. Layout (bytes): control words [0, 256), per-CTA key lists
-// [256, 256 + 256*32*8), one owner byte per page after that. Sized for grids of at most
-// MRL_STATIC_MAX_CTAS CTAs and segments of at most MRL_STATIC_MAX_BLOCKS pages: 1,114,368 bytes
-// per device in all.
+// [256, 256 + 256*32*8), their exact-mode keys (the next 256*32*8), one owner byte per page after
+// that. Sized for grids of at most MRL_STATIC_MAX_CTAS CTAs and segments of at most
+// MRL_STATIC_MAX_BLOCKS pages: 1,179,904 bytes per device in all.
 namespace {
 constexpr size_t kStaticCtlOff = 0;
 constexpr size_t kStaticKeysOff = 256;
-constexpr size_t kStaticOwnerOff = kStaticKeysOff + (size_t)MRL_STATIC_MAX_CTAS * 32 * sizeof(unsigned long long);
+constexpr size_t kStaticListBytes = (size_t)MRL_STATIC_MAX_CTAS * 32 * sizeof(unsigned long long);
+constexpr size_t kStaticXKeysOff = kStaticKeysOff + kStaticListBytes;
+constexpr size_t kStaticOwnerOff = kStaticXKeysOff + kStaticListBytes;
 constexpr size_t kStaticBytes = kStaticOwnerOff + (size_t)MRL_STATIC_MAX_BLOCKS;
-static_assert(kStaticBytes == 1114368, "static scratch size is documented in the header");
+static_assert(kStaticBytes == 1179904, "static scratch size is documented in the header");
 static_assert(mrl::kCtlWords * sizeof(unsigned) <= kStaticKeysOff - kStaticCtlOff, "control words overflow");
 static_assert(MRL_STATIC_MAX_CTAS <= 256, "owner bytes hold CTA indices < 256");
 }  // namespace
@@ -33,7 +35,7 @@ struct mrl_ctx {
     cudaStream_t stream = nullptr;
     std::string err;
     // scan scratch: per-CTA lists, control words, per-page owner (grow-only)
-    unsigned long long* cta_keys = nullptr;  // sms * 32
+    unsigned long long* cta_keys = nullptr;  // 2 * sms * 32: scan keys, then their exact keys
     unsigned int* ctl = nullptr;             // mrl::kCtlWords
     uint8_t* owner = nullptr;
     size_t owner_bytes = 0;
@@ -79,6 +81,9 @@ struct mrl_seg {
     uint64_t n_blocks = 0;
     uint64_t cap_blocks = 0;
     uint32_t block_id_base = 0;
+    // device: maxima of the slots' score factors (mrl::launch_metamax), kept current by every call
+    // that adds pages; fast-mode scans derive their fast/exact score bound from them
+    float* metamax = nullptr;
 };
 
 struct mrl_plans {
@@ -190,7 +195,20 @@ uint32_t auto_list_len(uint32_t k, uint32_t ctas) {
     return l;
 }
 
-int check_cfg(mrl_ctx* ctx, const mrl_scan_cfg* cfg) {
+// The reference prunes with Cauchy-Schwarz bounds scaled by cs_tolerance (alpha) against the
+// shortlist's running threshold (src/scan.rs:508-514, 572-584, 587-607, 766-767). Where every bound
+// is >= the full score, a pruned vector could not have entered the shortlist anyway, so the
+// reference's result is the top-k by full score whatever order the blocks are scanned in. That is
+// what this library computes. It holds when
+//   * L0Only: alpha >= 0 (the bound adds alpha * |q_after_prefix| * |x_rest| to the pushed score);
+//   * L1Rabitq and deeper: alpha >= sqrt(2/pi), since |s1| <= sqrt(2/pi) |q_mid| (src/rotate.rs:46-49);
+//   * Full64b with a folded tail: also alpha >= 1 (the S4 budget bound is alpha * |s4|max) and
+//     |stratum4_weight| * sqrt(2/pi) * sqrt(B) <= alpha, B = min((dims - 192) / 64, 9) folded
+//     blocks, since |s4| <= sqrt(2/pi) sqrt(B) |q_tail| (src/rotate.rs:73-93, 120-126).
+// Outside that region the reference's result depends on the order the blocks are scanned in (its
+// serial scan and its Rayon shards already disagree), which no parallel scan can reproduce, so the
+// configuration is refused. `dims` = 0: the call does not select a shortlist (no check).
+int check_cfg(mrl_ctx* ctx, const mrl_scan_cfg* cfg, uint32_t dims) {
     if (!cfg) return fail(ctx, MRL_ERR_INVALID, "cfg is NULL");
     if (cfg->shortlist_cand < 1 || cfg->shortlist_cand > 4096)
         return fail(ctx, MRL_ERR_INVALID, "shortlist_cand must be in [1, 4096]");
@@ -198,6 +216,20 @@ int check_cfg(mrl_ctx* ctx, const mrl_scan_cfg* cfg) {
     if (cfg->mode > MRL_MODE_EXACT) return fail(ctx, MRL_ERR_INVALID, "mode must be MRL_MODE_FAST or MRL_MODE_EXACT");
     if (!std::isfinite(cfg->stratum4_weight) || !std::isfinite(cfg->cs_tolerance))
         return fail(ctx, MRL_ERR_INVALID, "stratum4_weight and cs_tolerance must be finite");
+    if (dims == 0) return MRL_OK;
+    const double alpha = cfg->cs_tolerance, sqrt_2_pi = std::sqrt(2.0 / 3.14159265358979323846);
+    const uint32_t B = dims > 192u ? std::min<uint32_t>((dims - 192u) / 64u, 9u) : 0u;
+    const bool tail = cfg->strata_depth == MRL_DEPTH_FULL && dims > 192u;
+    std::string why;
+    if (alpha < 0.0) why = "cs_tolerance < 0";
+    else if (cfg->strata_depth >= MRL_DEPTH_L1 && alpha < sqrt_2_pi) why = "cs_tolerance < sqrt(2/pi)";
+    else if (tail && alpha < 1.0) why = "cs_tolerance < 1 with the folded-tail stage (S4 budget bound)";
+    else if (tail && std::fabs((double)cfg->stratum4_weight) * sqrt_2_pi * std::sqrt((double)B) > alpha)
+        why = "stratum4_weight * sqrt(2/pi) * sqrt(" + std::to_string(B) + " folded blocks) > cs_tolerance";
+    if (!why.empty())
+        return fail(ctx, MRL_ERR_INVALID,
+                    why + ": the reference's pruning bounds are then lossy and its result depends on the block "
+                          "scan order; only order-independent configurations are supported");
     return MRL_OK;
 }
 
@@ -220,8 +252,10 @@ mrl::ScanLaunch make_launch(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
     p.has_hi = hi ? 1u : 0u;
     p.hi = hi ? *hi : 0u;
     p.cta_keys = ctx->cta_keys;
+    p.cta_xkeys = ctx->cta_keys + 32 * (size_t)ctx->sms;
     p.ctl = ctx->ctl;
     p.owner = ctx->owner;
+    p.metamax = seg->metamax;
     return p;
 }
 
@@ -250,6 +284,32 @@ int upload_means(mrl_ctx* ctx, const mrl_codec_desc* codec, float** out) {
         ctx->means_valid = true;
     }
     *out = ctx->d_means;
+    return MRL_OK;
+}
+
+// A new empty segment with its meta maxima zeroed (synchronous), or an error.
+int seg_new(mrl_ctx* ctx, uint32_t block_id_base, mrl_seg** out) {
+    *out = nullptr;
+    mrl_seg* s = new mrl_seg();
+    s->block_id_base = block_id_base;
+    if (cudaMalloc(&s->metamax, 4 * sizeof(float)) != cudaSuccess) {
+        delete s;
+        return fail(ctx, MRL_ERR_NOMEM, "cudaMalloc segment maxima");
+    }
+    const cudaError_t e = cudaMemset(s->metamax, 0, 4 * sizeof(float));
+    if (e != cudaSuccess) {
+        cudaFree(s->metamax);
+        delete s;
+        return cuda_fail(ctx, e, "cudaMemset segment maxima");
+    }
+    *out = s;
+    return MRL_OK;
+}
+
+// Fold pages [b0, b0 + nb) of s into its meta maxima (on the context stream).
+int seg_note_pages(mrl_ctx* ctx, mrl_seg* s, uint64_t b0, uint64_t nb) {
+    if (mrl::launch_metamax(s->pages + b0 * 256, nb, s->metamax, ctx->stream))
+        return cuda_fail(ctx, cudaGetLastError(), "segment maxima launch");
     return MRL_OK;
 }
 
@@ -297,7 +357,7 @@ int mrl_ctx_create(int device, mrl_ctx** out) {
         return MRL_ERR_CUDA;
     }
     ctx->stream = ctx->own_stream;
-    if (cudaMalloc(&ctx->cta_keys, sizeof(unsigned long long) * 32 * (size_t)ctx->sms) != cudaSuccess ||
+    if (cudaMalloc(&ctx->cta_keys, sizeof(unsigned long long) * 2 * 32 * (size_t)ctx->sms) != cudaSuccess ||
         cudaMalloc(&ctx->ctl, sizeof(unsigned int) * mrl::kCtlWords) != cudaSuccess ||
         cudaMalloc(&ctx->d_means, 192 * sizeof(float)) != cudaSuccess ||
         cudaMemset(ctx->ctl, 0, sizeof(unsigned int) * mrl::kCtlWords) != cudaSuccess ||
@@ -344,9 +404,9 @@ int mrl_segment_upload(mrl_ctx* ctx, const uint8_t* blocks, uint64_t n_blocks, u
     if (n_blocks >= (1ull << 26)) return fail(ctx, MRL_ERR_INVALID, "segment larger than 2^26 pages");
     if ((uint64_t)block_id_base + n_blocks > (1ull << 32)) return fail(ctx, MRL_ERR_INVALID, "block ids overflow u32");
     if (int rc = set_device(ctx)) return rc;
-    mrl_seg* s = new mrl_seg();
-    s->block_id_base = block_id_base;
-    if (int rc = seg_reserve(ctx, s, n_blocks ? n_blocks : 1)) { delete s; return rc; }
+    mrl_seg* s = nullptr;
+    if (int rc = seg_new(ctx, block_id_base, &s)) return rc;
+    if (int rc = seg_reserve(ctx, s, n_blocks ? n_blocks : 1)) { mrl_segment_free(ctx, s); return rc; }
     const uint64_t chunk = 16384;  // pages per staging copy (64 MiB)
     if (n_blocks) {
         if (int rc = ensure_tmp(ctx, std::min<uint64_t>(n_blocks, chunk) * mrl::kBlockBytes)) { mrl_segment_free(ctx, s); return rc; }
@@ -360,6 +420,7 @@ int mrl_segment_upload(mrl_ctx* ctx, const uint8_t* blocks, uint64_t n_blocks, u
                 return cuda_fail(ctx, cudaGetLastError(), "transcode launch");
             }
         }
+        if (int rc = seg_note_pages(ctx, s, 0, n_blocks)) { mrl_segment_free(ctx, s); return rc; }
     }
     const cudaError_t e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) { mrl_segment_free(ctx, s); return cuda_fail(ctx, e, "segment upload"); }
@@ -385,9 +446,9 @@ int mrl_segment_load(mrl_ctx* ctx, const char* path, uint32_t block_id_base, mrl
     if (n_blocks >= (1ull << 26)) { std::fclose(f); return fail(ctx, MRL_ERR_INVALID, "segment larger than 2^26 pages"); }
     if ((uint64_t)block_id_base + n_blocks > (1ull << 32)) { std::fclose(f); return fail(ctx, MRL_ERR_INVALID, "block ids overflow u32"); }
     if (int rc = set_device(ctx)) { std::fclose(f); return rc; }
-    mrl_seg* s = new mrl_seg();
-    s->block_id_base = block_id_base;
-    if (int rc = seg_reserve(ctx, s, n_blocks ? n_blocks : 1)) { std::fclose(f); delete s; return rc; }
+    mrl_seg* s = nullptr;
+    if (int rc = seg_new(ctx, block_id_base, &s)) { std::fclose(f); return rc; }
+    if (int rc = seg_reserve(ctx, s, n_blocks ? n_blocks : 1)) { std::fclose(f); mrl_segment_free(ctx, s); return rc; }
     // Two pinned host buffers and two device staging buffers: the file read of chunk c+1 overlaps
     // the copy and transcode of chunk c.
     const uint64_t chunk = 16384;  // pages (64 MiB)
@@ -414,6 +475,7 @@ int mrl_segment_load(mrl_ctx* ctx, const char* path, uint32_t block_id_base, mrl
         if (cudaEventRecord(done[i], ctx->stream) != cudaSuccess) { rc = fail(ctx, MRL_ERR_CUDA, "event record"); break; }
     }
     std::fclose(f);
+    if (rc == MRL_OK) rc = seg_note_pages(ctx, s, 0, n_blocks);
     const cudaError_t se = cudaStreamSynchronize(ctx->stream);
     if (rc == MRL_OK && se != cudaSuccess) rc = cuda_fail(ctx, se, "segment load");
     for (int i = 0; i < 2; ++i) {
@@ -435,6 +497,7 @@ int mrl_segment_append(mrl_ctx* ctx, mrl_seg* seg, const uint8_t* block4096) {
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->tmp, block4096, mrl::kBlockBytes, cudaMemcpyHostToDevice, ctx->stream));
     if (mrl::launch_transcode((const uint8_t*)ctx->tmp, 1, seg->pages + seg->n_blocks * 256, seg->ts + seg->n_blocks, ctx->stream))
         return cuda_fail(ctx, cudaGetLastError(), "transcode launch");
+    if (int rc = seg_note_pages(ctx, seg, seg->n_blocks, 1)) return rc;
     MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     seg->n_blocks += 1;
     return MRL_OK;
@@ -448,6 +511,7 @@ int mrl_segment_append_device(mrl_ctx* ctx, mrl_seg* seg, const uint8_t* d_block
     if (int rc = seg_reserve(ctx, seg, seg->n_blocks + n_blocks)) return rc;
     if (mrl::launch_transcode(d_blocks, n_blocks, seg->pages + seg->n_blocks * 256, seg->ts + seg->n_blocks, ctx->stream))
         return cuda_fail(ctx, cudaGetLastError(), "transcode launch");
+    if (int rc = seg_note_pages(ctx, seg, seg->n_blocks, n_blocks)) return rc;
     seg->n_blocks += n_blocks;
     return MRL_OK;
 }
@@ -457,6 +521,7 @@ int mrl_segment_free(mrl_ctx* ctx, mrl_seg* seg) {
     if (ctx) cudaSetDevice(ctx->device);
     cudaFree(seg->pages);
     cudaFree(seg->ts);
+    cudaFree(seg->metamax);
     delete seg;
     return MRL_OK;
 }
@@ -589,7 +654,7 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
                     const mrl_scan_cfg* cfg, const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* d_out_ids,
                     float* d_out_scores, uint32_t* d_out_counts, uint32_t* d_out_status) {
     if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
-    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (int rc = check_cfg(ctx, cfg, plans->dims)) return rc;
     if ((uint64_t)q0 + n_q > plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan range out of bounds");
     if (n_q && (!d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "output is NULL");
     if (int rc = set_device(ctx)) return rc;
@@ -615,7 +680,7 @@ int mrl_scan_batch_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pla
                           const mrl_scan_cfg* cfg, const uint32_t* time_lo, const uint32_t* time_hi,
                           uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_counts, uint32_t* d_out_status) {
     if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
-    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (int rc = check_cfg(ctx, cfg, plans->dims)) return rc;
     if ((uint64_t)q0 + n_q > plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan range out of bounds");
     if (n_q && (!d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "output is NULL");
     if (n_q == 0) return MRL_OK;
@@ -626,7 +691,8 @@ int mrl_scan_batch_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pla
     const uint32_t ctas = (uint32_t)ctx->sms;
     if (int rc = ensure_buf(ctx, &ctx->bbuf, &ctx->bbuf_bytes, mrl::batch_scratch_bytes(ctas, n_q))) return rc;
     const bool use_time = cfg->temporal_filter_enable && (time_lo || time_hi);
-    if (mrl::launch_scan_batch(seg->pages, seg->ts, (uint32_t)seg->n_blocks, seg->block_id_base, plans->d + q0, n_q,
+    if (mrl::launch_scan_batch(seg->pages, seg->ts, (uint32_t)seg->n_blocks, seg->block_id_base, seg->metamax,
+                               plans->d + q0, n_q,
                                cfg->shortlist_cand, cfg->stratum4_weight, cfg->strata_depth, use_time ? 1u : 0u,
                                time_lo ? 1u : 0u, time_lo ? *time_lo : 0u, time_hi ? 1u : 0u, time_hi ? *time_hi : 0u,
                                ctas, ctx->batch_engine, ctx->bbuf, d_out_ids, d_out_scores, d_out_counts, d_out_status,
@@ -649,7 +715,7 @@ int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pl
                            uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_counts,
                            uint32_t* d_out_status) {
     if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
-    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (int rc = check_cfg(ctx, cfg, plans->dims)) return rc;
     if ((uint64_t)q0 + n_q > plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan range out of bounds");
     if (n_q && (!d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "output is NULL");
     if (seg->n_blocks > MRL_STATIC_MAX_BLOCKS)
@@ -669,6 +735,7 @@ int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pl
     for (uint32_t i = 0; i < n_q; ++i) {
         mrl::ScanLaunch p = make_launch(ctx, seg, plans, q0 + i, cfg, time_lo, time_hi);
         p.cta_keys = reinterpret_cast<unsigned long long*>(base + kStaticKeysOff);
+        p.cta_xkeys = reinterpret_cast<unsigned long long*>(base + kStaticXKeysOff);
         p.ctl = reinterpret_cast<unsigned int*>(base + kStaticCtlOff);
         p.owner = base + kStaticOwnerOff;
         p.out_ids = d_out_ids + (size_t)i * k;
@@ -690,7 +757,7 @@ int mrl_query_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const float* d_queri
                           const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
                           uint32_t* d_out_counts, uint32_t* d_out_status) {
     if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
-    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (int rc = check_cfg(ctx, cfg, dims)) return rc;
     if (int rc = check_codec(ctx, codec)) return rc;
     if (n_q > plans->n_q || dims != plans->dims) return fail(ctx, MRL_ERR_INVALID, "plan storage too small or dims mismatch");
     if (n_q && (!d_queries || !d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
@@ -733,7 +800,7 @@ int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint3
                    const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                    const uint32_t* time_hi, uint64_t* out_ids, float* out_scores, uint32_t* out_counts) {
     if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
-    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (int rc = check_cfg(ctx, cfg, dims)) return rc;
     if (n_q == 0) return MRL_OK;
     if (!queries || !out_ids || !out_scores || !out_counts) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
     if (int rc = set_device(ctx)) return rc;
@@ -851,7 +918,7 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
                             const uint32_t* time_lo, const uint32_t* time_hi, mrl_exchange* ex, uint64_t* d_out_ids,
                             float* d_out_scores, uint32_t* d_out_count, uint32_t* d_out_status) {
     if (!ctx || !seg || !plans || !ex) return MRL_ERR_INVALID;
-    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (int rc = check_cfg(ctx, cfg, dims)) return rc;
     if (int rc = check_codec(ctx, codec)) return rc;
     if (!ex->opened) return fail(ctx, MRL_ERR_INVALID, "exchange not opened");
     if (ex->device != ctx->device) return fail(ctx, MRL_ERR_INVALID, "exchange belongs to another device");
@@ -1025,7 +1092,7 @@ int mrl_engine_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* d_query, uint
                     const uint32_t* time_hi, const mrl_ring* ring, uint64_t* d_out_ids, float* d_out_scores,
                     uint32_t* d_out_count, uint32_t* d_out_status) {
     if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
-    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (int rc = check_cfg(ctx, cfg, dims)) return rc;
     if (ring && ring->dims != dims) return fail(ctx, MRL_ERR_INVALID, "ring dims differ from the query's");
     if (!ring || ring->len == 0)  // nothing pending: the scan's list is the shortlist
         return mrl_query_scan_device(ctx, seg, d_query, 1, dims, codec, plans, cfg, time_lo, time_hi, d_out_ids,
@@ -1085,7 +1152,7 @@ int mrl_merge_topk_batch(mrl_ctx* ctx, const void* d_lists, uint32_t n_lists, ui
 int mrl_scan(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
              const uint32_t* time_hi, uint64_t* out_ids, float* out_scores, uint32_t* out_counts) {
     if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
-    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (int rc = check_cfg(ctx, cfg, plans->dims)) return rc;
     const uint32_t n_q = plans->n_q, k = cfg->shortlist_cand;
     if (n_q == 0) return MRL_OK;
     if (!out_ids || !out_scores || !out_counts) return fail(ctx, MRL_ERR_INVALID, "output is NULL");
@@ -1129,7 +1196,7 @@ int mrl_debug_vector_scores(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
                             const uint32_t* time_lo, const uint32_t* time_hi, float* out_scores, uint8_t* out_active,
                             int32_t* out_partials) {
     if (!ctx || !seg || !plans || !out_scores || !out_active) return MRL_ERR_INVALID;
-    if (int rc = check_cfg(ctx, cfg)) return rc;
+    if (int rc = check_cfg(ctx, cfg, 0)) return rc;
     if (q >= plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan index out of range");
     if (int rc = set_device(ctx)) return rc;
     const size_t n = (size_t)seg->n_blocks * 64;
@@ -1144,6 +1211,28 @@ int mrl_debug_vector_scores(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_active, d_act, n, cudaMemcpyDeviceToHost, ctx->stream));
     if (out_partials)
         MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_partials, d_parts, 3 * n * sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return MRL_OK;
+}
+
+int mrl_debug_score_bound(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q,
+                          const mrl_scan_cfg* cfg, float* out_bound) {
+    if (!ctx || !seg || !plans || !out_bound) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg, 0)) return rc;
+    if (q >= plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan index out of range");
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = ensure_out(ctx, 64)) return rc;
+    const mrl::ScanLaunch p = make_launch(ctx, seg, plans, q, cfg, nullptr, nullptr);
+    if (mrl::launch_score_bound(p, (float*)ctx->tmp_out, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "bound launch");
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_bound, ctx->tmp_out, sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return MRL_OK;
+}
+
+int mrl_debug_control_words(mrl_ctx* ctx, uint32_t* out) {
+    if (!ctx || !out) return MRL_ERR_INVALID;
+    if (int rc = set_device(ctx)) return rc;
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out, ctx->ctl, sizeof(unsigned) * mrl::kCtlWords, cudaMemcpyDeviceToHost, ctx->stream));
     MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     return MRL_OK;
 }
@@ -1163,9 +1252,8 @@ int mrl_encode_device(mrl_ctx* ctx, const float* d_rows, uint64_t n, uint32_t di
     if (int rc = upload_means(ctx, codec, &d_means)) return rc;
     mrl_seg* s = nullptr;
     if (seg_out) {
-        s = new mrl_seg();
-        s->block_id_base = block_id_base;
-        if (int rc = seg_reserve(ctx, s, nb ? nb : 1)) { delete s; return rc; }
+        if (int rc = seg_new(ctx, block_id_base, &s)) return rc;
+        if (int rc = seg_reserve(ctx, s, nb ? nb : 1)) { mrl_segment_free(ctx, s); return rc; }
     }
     if (mrl::launch_encode(d_rows, n, dims, nullptr, nullptr, src, codec->prefix_codec, d_means, codec->eden_seed,
                            codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr, codec->mid_seed, d_pages,
@@ -1173,6 +1261,8 @@ int mrl_encode_device(mrl_ctx* ctx, const float* d_rows, uint64_t n, uint32_t di
         mrl_segment_free(ctx, s);
         return cuda_fail(ctx, cudaGetLastError(), "encode launch");
     }
+    if (s)
+        if (int rc = seg_note_pages(ctx, s, 0, nb)) { mrl_segment_free(ctx, s); return rc; }
     const cudaError_t e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) { mrl_segment_free(ctx, s); return cuda_fail(ctx, e, "encode"); }
     if (s) { s->n_blocks = nb; *seg_out = s; }

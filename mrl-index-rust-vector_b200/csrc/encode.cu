@@ -11,6 +11,8 @@
 // * eden fit: EdenFit::fit_band (src/eden.rs:130-161), one thread per coordinate summing the
 //   rows in order.
 // * synthetic docs / queries: the integer recipe documented in mrl_cuda.h.
+#include <algorithm>
+
 #include "mrl_internal.cuh"
 
 namespace mrl {
@@ -355,7 +357,47 @@ __global__ void synth_queries_kernel(uint64_t doc_seed, uint64_t n_docs, uint64_
     for (uint32_t d = 0; d < dims; ++d) q[d] = f_div(q[d], nrm);
 }
 
+// Maxima of the per-slot score factors (|scale|, |offset|, mid_n, max(high_n, 1e-6)) over a run of
+// scan-layout pages, merged into m[0..3] with atomic max on the float bit patterns (valid for
+// nonnegative floats; NaN is mapped to +inf first so it cannot hide behind a smaller value).
+// Tombstoned slots are included: a superset only loosens the bound the scans derive from it.
+__device__ __forceinline__ unsigned max_word(float v) {
+    return v == v ? __float_as_uint(v) : 0x7F800000u;
+}
+
+__global__ void __launch_bounds__(256) metamax_kernel(const uint4* __restrict__ pages, uint64_t n_slots,
+                                                      float* __restrict__ m) {
+    unsigned a = 0u, b = 0u, c = 0u, d = 0u;
+    for (uint64_t i = blockIdx.x * 256ull + threadIdx.x; i < n_slots; i += (uint64_t)gridDim.x * 256ull) {
+        const uint4 w = __ldg(pages + (i >> 6) * 256 + 192 + (i & 63));  // chunk 3: meta words
+        const SlotMeta sm = decode_slot_meta(w.z, w.w);
+        a = max(a, max_word(fabsf(sm.scale)));
+        b = max(b, max_word(fabsf(sm.offset)));
+        c = max(c, max_word(sm.mid_n));
+        d = max(d, max_word(fmaxf(sm.high_n, 1e-6f)));
+    }
+    a = __reduce_max_sync(0xffffffffu, a);
+    b = __reduce_max_sync(0xffffffffu, b);
+    c = __reduce_max_sync(0xffffffffu, c);
+    d = __reduce_max_sync(0xffffffffu, d);
+    if ((threadIdx.x & 31) == 0) {
+        unsigned* mu = reinterpret_cast<unsigned*>(m);
+        atomicMax(mu + 0, a);
+        atomicMax(mu + 1, b);
+        atomicMax(mu + 2, c);
+        atomicMax(mu + 3, d);
+    }
+}
+
 }  // namespace
+
+int launch_metamax(const uint4* d_pages, uint64_t n_blocks, float* d_metamax, cudaStream_t stream) {
+    if (n_blocks == 0) return 0;
+    const uint64_t slots = n_blocks * 64;
+    const unsigned grid = (unsigned)std::min<uint64_t>((slots + 255) / 256, 148ull * 8);
+    metamax_kernel<<<grid, 256, 0, stream>>>(d_pages, slots, d_metamax);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
 
 int launch_transcode(const uint8_t* d_pax, uint64_t n_blocks, uint4* d_pages, uint2* d_ts, cudaStream_t stream) {
     if (n_blocks == 0) return 0;

@@ -54,7 +54,10 @@ struct DevPlan {
     float fp_prefix[kPrefix * 16];
     float mid_w[kRabitq];   // Rabitq: rabitq_weights2; EdenB1: (c1 - c0) * q
     float tail_w[kFold];    // tail_fold_weights2
-    float mid_base, tail_base, pad2, pad3;
+    float mid_base, tail_base;
+    // upper bounds of sum over dims of max |entry| per stage (prefix, mid band, folded tail,
+    // L0Only), rounded up: the magnitudes the fast/exact score difference bound scales with
+    float err_p, err_1, err_4, err_0, pad2, pad3;
 };
 static_assert(sizeof(mrl_query_plan) % 16 == 0, "plan alignment");
 static_assert(sizeof(DevPlan) % 16 == 0, "plan alignment");
@@ -151,6 +154,9 @@ int launch_plan_build(const float* d_queries, uint32_t n_q, uint32_t dims, uint3
                       cudaStream_t stream);
 int launch_transcode(const uint8_t* d_pax, uint64_t n_blocks, uint4* d_pages, uint2* d_ts,
                      cudaStream_t stream);
+// Merge into d_metamax[0..3] the maxima over pages [0, n_blocks) of the per-slot factors that scale
+// the stage sums in a score: |scale|, |offset|, mid_n, max(high_n, 1e-6) (NaN counts as +inf).
+int launch_metamax(const uint4* d_pages, uint64_t n_blocks, float* d_metamax, cudaStream_t stream);
 int launch_encode(const float* d_rows, uint64_t n, uint32_t dims, const uint32_t* d_ts,
                   const uint32_t* d_src, uint32_t src_const, uint32_t prefix_codec,
                   const float* d_eden_mean, uint64_t eden_seed, const float* d_mid_mean,
@@ -180,9 +186,12 @@ struct ScanLaunch {
     uint32_t use_time;  // temporal filter active for this call
     uint32_t has_lo, lo, has_hi, hi;
     // scratch (owned by the context; zero-initialised once, left zeroed by every launch)
-    unsigned long long* cta_keys;  // ctas * 32: each CTA's exact top-list_len keys
+    unsigned long long* cta_keys;  // ctas * 32: each CTA's exact top-list_len keys (scan order)
+    unsigned long long* cta_xkeys; // ctas * 32: fast mode, the same entries' exact-mode keys
     unsigned int* ctl;             // [0] page counter, [1] barrier count, [2] barrier generation,
-                                   // [5] barrier timeout, [6] CTAs done (exchange); others reserved
+                                   // [5] barrier timeout, [6] CTAs done (exchange), [7] CTAs exited;
+                                   // the last CTA to exit zeroes all but [2]
+    const float* metamax;          // the segment's 4 meta-factor maxima (launch_metamax)
     uint8_t* owner;                // n_blocks: CTA that scored each page
     uint64_t* out_ids;
     float* out_scores;
@@ -206,7 +215,7 @@ struct ScanLaunch {
     unsigned int* xch_flag[kMaxRanks];        // every rank's flag word of this parity
 };
 int scan_ctas(int device_sms);
-size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t xch_world);
+size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t xch_world, uint32_t mode);
 int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream);
 int launch_exact_dots(const float* d_query, const float* d_rows, uint64_t n_rows, uint32_t dims, const uint64_t* d_sel,
                       uint32_t n, float* d_scores, uint32_t* d_bad, cudaStream_t stream);
@@ -225,10 +234,13 @@ constexpr int kCtlWords = 8;
 // (batch_scratch_bytes), then one selection CTA per query
 size_t batch_scratch_bytes(uint32_t ctas, uint32_t n_q);
 int launch_scan_batch(const uint4* pages, const uint2* block_ts, uint32_t n_blocks, uint32_t block_id_base,
-                      const DevPlan* plans, uint32_t n_q, uint32_t k, float w_s4, uint32_t depth, uint32_t use_time,
+                      const float* metamax, const DevPlan* plans, uint32_t n_q, uint32_t k, float w_s4, uint32_t depth, uint32_t use_time,
                       uint32_t has_lo, uint32_t lo, uint32_t has_hi, uint32_t hi, uint32_t ctas, uint32_t engine,
                       void* scratch, uint64_t* out_ids, float* out_scores, uint32_t* out_counts, uint32_t* out_status,
                       cudaStream_t stream);
+// The fast/exact score difference bound the scan uses for plan p.plan over the segment whose maxima
+// are p.metamax (one float to d_out).
+int launch_score_bound(const ScanLaunch& p, float* d_out, cudaStream_t stream);
 int launch_debug_scores(const ScanLaunch& p, float* d_scores, uint8_t* d_active,
                         int32_t* d_partials, cudaStream_t stream);
 }  // namespace mrl

@@ -72,6 +72,14 @@ __device__ __forceinline__ double warp_max(double v) {
     for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+// A double sum of nonnegative terms rounded up to f32 with room for the double roundings: the
+// error-bound magnitudes stored in the plan (err_p, err_1, err_4, err_0).
+__device__ __forceinline__ float bound_up(double v) { return __double2float_ru(v * (1.0 + 0x1p-40)); }
 
 // Entry (g, m) of a fast-mode window table of one 1-bit stage (lut_s1 / lut_s4): the exact integer
 // sum over the window's dims i of fix(bit i of m ? val1 : val0). `fx` holds the fixed values per
@@ -215,18 +223,26 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
         double cbmax = 0.0;
 #pragma unroll
         for (int l = 0; l < 16; ++l) cbmax = fmax(cbmax, fabs((double)s_cb[l]));
-        double mx = 0.0, mx0 = 0.0;
+        double mx = 0.0, mx0 = 0.0, ea = 0.0, ea0 = 0.0;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const int d = lane + 32 * r;
             const float w = eden ? f_mul(s_rot[d], inv_sqrt_64) : 0.0f;
             sh.w[d] = w;
-            mx = fmax(mx, eden ? cbmax * fabs((double)w) : 15.0 * fabs((double)s_q[d]));
-            mx0 = fmax(mx0, fabs((double)f_mul(s_q[d], 8.0f)));
+            const double e = eden ? cbmax * fabs((double)w) : 15.0 * fabs((double)s_q[d]);
+            const double e0 = fabs((double)f_mul(s_q[d], 8.0f));
+            mx = fmax(mx, e);
+            mx0 = fmax(mx0, e0);
+            ea += e;
+            ea0 += e0;
         }
         const int sh_p = stage_shift(warp_max(mx), kPrefix);
         const int sh_0 = stage_shift(warp_max(mx0), kPrefix);  // L0Only (accum_plane, src/scan.rs:753-762)
+        ea = warp_sum(ea);
+        ea0 = warp_sum(ea0);
         if (lane == 0) {
+            P->err_p = bound_up(ea);
+            P->err_0 = bound_up(ea0);
             P->shift_prefix = sh_p;
             P->shift_l0 = sh_0;
             P->unscale_prefix = ldexp(1.0, -sh_p);
@@ -298,6 +314,7 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
         // fixed S1 values per dim for the window table
         const int sh_1 = stage_shift(warp_max(mx), kRabitq);
         const double pw_1 = ldexp(1.0, sh_1);
+        double ea = 0.0;
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int i = lane + 32 * r;
@@ -306,8 +323,11 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
             else v1 = (double)f_mul(s_rq[i], rabitq_scale);
             s_fx[2 * i] = fix(-v1, pw_1);
             s_fx[2 * i + 1] = fix(v1, pw_1);
+            ea += fabs(v1);
         }
+        ea = warp_sum(ea);
         if (lane == 0) {
+            P->err_1 = bound_up(ea);
             P->shift_s1 = sh_1;
             P->unscale_s1 = ldexp(1.0, -sh_1);
         }
@@ -355,14 +375,18 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
         // fixed S4 values per dim for the window table
         const int sh_4 = stage_shift(warp_max(mx), kFold);
         const double pw_4 = ldexp(1.0, sh_4);
+        double ea = 0.0;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const int d = lane + 32 * r;
             const double pos = has_tail ? (double)f_mul(s_tf[d], tail_scale) : 0.0;
             s_fx[2 * (kRabitq + d)] = fix(-pos, pw_4);
             s_fx[2 * (kRabitq + d) + 1] = fix(pos, pw_4);
+            ea += fabs(pos);
         }
+        ea = warp_sum(ea);
         if (lane == 0) {
+            P->err_4 = bound_up(ea);
             P->shift_s4 = sh_4;
             P->unscale_s4 = ldexp(1.0, -sh_4);
         }

@@ -46,101 +46,6 @@ namespace {
 constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kQueue = 64;
-constexpr int kTabInts = kPrefix * 16 + kS1Windows * 32 + kS4Windows * 32 + kPrefix * 16;  // 3296
-constexpr int kTabS1 = kPrefix * 16;
-constexpr int kTabS4 = kTabS1 + kS1Windows * 32;
-constexpr int kTabL0 = kTabS4 + kS4Windows * 32;
-// exact-mode layout inside the same table space (floats)
-constexpr int kTabMidW = kPrefix * 16;
-constexpr int kTabTailW = kTabMidW + kRabitq;
-constexpr int kTabBw3 = kTabTailW + kFold;
-
-// Full score of one slot; returns false for tombstoned slots.
-template <int MODE>
-__device__ __forceinline__ bool slot_score(const uint4& c0, const uint4& c1, const uint4& c2,
-                                           const uint4& c3, const int* tab, const float2* rho_tab,
-                                           const Scalars& S, float& score, Partials* parts) {
-    const SlotMeta m = slot_meta_tab(c3.z, c3.w, rho_tab);
-    if (m.tomb) return false;
-    if (MODE == MRL_MODE_FAST) {
-        const uint32_t s1w[4] = {c2.x, c2.y, c2.z, c2.w};
-        const uint32_t s4w[2] = {c3.x, c3.y};
-        if (S.depth == MRL_DEPTH_L0) {  // src/scan.rs:753-771
-            const int32_t P = prefix_fixed(c0, c1, tab + kTabL0, S.one);
-            const float cd = unfix(P, S.un_l0, S.unf_l0, S.f32_unscale);
-            score = __fadd_rn(__fmul_rn(cd, m.scale), __fmul_rn(m.offset, S.prefix_sum));
-            if (parts) {
-                parts->p = P;
-                parts->s1 = window_fixed<128>(s1w, tab + kTabS1, S.one);
-                parts->s4 = window_fixed<64>(s4w, tab + kTabS4, S.one);
-            }
-            return true;
-        }
-        const int32_t P = prefix_fixed(c0, c1, tab, S.one);
-        int32_t s1 = 0, s4 = 0;
-        if (S.depth >= MRL_DEPTH_L1 || parts) s1 = window_fixed<128>(s1w, tab + kTabS1, S.one);
-        if ((S.depth == MRL_DEPTH_FULL && S.has_tail) || parts) s4 = window_fixed<64>(s4w, tab + kTabS4, S.one);
-        if (parts) { parts->p = P; parts->s1 = s1; parts->s4 = s4; }
-        score = fast_score(m, P, s1, s4, S);
-        return true;
-    } else {
-        const float* ft = reinterpret_cast<const float*>(tab);
-        if (S.depth == MRL_DEPTH_L0) {
-            float acc = 0.0f;
-#pragma unroll
-            for (int d = 0; d < kPrefix; ++d)
-                if (level_of(c0, c1, d) & 8u) acc = __fadd_rn(acc, ft[kTabBw3 + d]);
-            score = __fadd_rn(__fmul_rn(acc, m.scale), __fmul_rn(m.offset, S.prefix_sum));
-            return true;
-        }
-        float acc = 0.0f;  // src/scan.rs:456-487, per-slot sequential order over d
-        {
-            const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-            for (int d = 0; d < kPrefix; ++d) {
-                const uint32_t sh = 4 * (d & 7);
-                const uint32_t idx4 = sh >= 2 ? ((w[d >> 3] >> (sh - 2)) & 0x3Cu) : ((w[d >> 3] << 2) & 0x3Cu);
-                acc = __fadd_rn(acc, *reinterpret_cast<const float*>(reinterpret_cast<const char*>(ft) + d * 64 + idx4));
-            }
-        }
-        float sc = S.eden ? __fadd_rn(S.eden_mean_ip, __fmul_rn(m.scale, acc))
-                          : __fadd_rn(__fmul_rn(acc, m.scale), __fmul_rn(m.offset, S.prefix_sum));
-        if (S.depth >= MRL_DEPTH_L1) {  // src/scan.rs:520-569
-            const uint32_t s1w[4] = {c2.x, c2.y, c2.z, c2.w};
-            float s = S.mid_base;
-            const float4* mw = reinterpret_cast<const float4*>(ft + kTabMidW);
-#pragma unroll
-            for (int g = 0; g < kRabitq / 4; ++g) {
-                const float4 w4 = mw[g];
-                const uint32_t bits = s1w[g >> 3] >> (4 * (g & 7));
-                if (bits & 1u) s = __fadd_rn(s, w4.x);
-                if (bits & 2u) s = __fadd_rn(s, w4.y);
-                if (bits & 4u) s = __fadd_rn(s, w4.z);
-                if (bits & 8u) s = __fadd_rn(s, w4.w);
-            }
-            if (S.mid_b1) sc = __fadd_rn(sc, __fadd_rn(S.mid_mean_ip, __fmul_rn(m.offset, s)));
-            else sc = __fadd_rn(sc, __fmul_rn(s, m.mid_n));
-        }
-        if (S.depth == MRL_DEPTH_FULL && S.has_tail) {  // src/scan.rs:610-634
-            const uint32_t s4w[2] = {c3.x, c3.y};
-            float t = S.tail_base;
-            const float4* tw = reinterpret_cast<const float4*>(ft + kTabTailW);
-#pragma unroll
-            for (int g = 0; g < kFold / 4; ++g) {
-                const float4 w4 = tw[g];
-                const uint32_t bits = s4w[g >> 3] >> (4 * (g & 7));
-                if (bits & 1u) t = __fadd_rn(t, w4.x);
-                if (bits & 2u) t = __fadd_rn(t, w4.y);
-                if (bits & 4u) t = __fadd_rn(t, w4.z);
-                if (bits & 8u) t = __fadd_rn(t, w4.w);
-            }
-            sc = __fadd_rn(sc, __fmul_rn(__fmul_rn(t, fmaxf(m.high_n, 1e-6f)), S.w_s4));
-        }
-        score = sc;
-        return true;
-    }
-}
-
 template <int MODE>
 __device__ __forceinline__ u64 slot_key(const Slot4& s, uint32_t ordinal, const int* tab, const float2* rho_tab,
                                         const Scalars& S) {
@@ -210,42 +115,48 @@ struct SelState {
 template <int MODE>
 struct Finisher {
     const ScanLaunch& p;
-    const int* tab;
+    const int* tab;         // the scan's tables (this mode's)
+    const int* xtab;        // exact-mode tables (== tab in MRL_MODE_EXACT)
     const float2* rho_tab;
     const Scalars& S;
-    const u64* cand;        // G * 32, the first list_len of each CTA are live
+    const u64* cand;        // G * 32 scan keys, the first list_len of each CTA are live
+    const u64* xcand;       // the same entries' exact keys (== cand in MRL_MODE_EXACT)
     const unsigned* flags;  // flagged CTA ids
     unsigned nflag;
     unsigned G;
     unsigned list_len;
 
-    // Visit every candidate of the (virtual) set: the CTA lists in shared memory plus, for flagged
-    // CTAs, a rescan of the pages they scored keeping keys below their list minimum.
-    // fn(valid, key, lane) is called warp-uniformly.
+    // Visit every candidate of the (virtual) set by its exact key: the CTA lists in shared memory
+    // plus, for flagged CTAs, a rescan of the pages they scored keeping the slots whose scan key is
+    // below their list minimum (the ones the list dropped). fn(valid, exact_key, lane) is called
+    // warp-uniformly.
     template <class Fn>
-    __device__ void visit(Fn fn) const {
+    __device__ __forceinline__ void visit(Fn fn) const {
         const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
         const unsigned nu = G * list_len;
         for (unsigned base = 0; base < nu; base += kThreads) {
             const unsigned i = base + tid;
-            const u64 x = i < nu ? cand[(i / list_len) * 32 + (i % list_len)] : 0ull;
-            fn(x != 0ull, x, lane);
+            const unsigned at = (i / list_len) * 32 + (i % list_len);
+            const u64 x = i < nu ? cand[at] : 0ull;
+            fn(x != 0ull, x != 0ull ? xcand[at] : 0ull, lane);
         }
         for (unsigned f = 0; f < nflag; ++f) {
             const unsigned c = flags[f];
             const u64 minc = cand[c * 32 + list_len - 1];
             for (uint32_t b = warp; b < p.n_blocks; b += kWarps) {
                 if (__ldcg(p.owner + b) != (uint8_t)c) continue;  // warp-uniform
-                u64 k0 = 0, k1 = 0;
+                u64 k0 = 0, k1 = 0, x0 = 0, x1 = 0;
                 if (block_live(p, b)) {
                     Slot4 s0, s1;
                     load_slot(p.pages, b, lane, s0);
                     load_slot(p.pages, b, lane + 32, s1);
                     k0 = slot_key<MODE>(s0, b * 64 + lane, tab, rho_tab, S);
                     k1 = slot_key<MODE>(s1, b * 64 + lane + 32, tab, rho_tab, S);
+                    x0 = MODE == MRL_MODE_FAST ? slot_key<MRL_MODE_EXACT>(s0, b * 64 + lane, xtab, rho_tab, S) : k0;
+                    x1 = MODE == MRL_MODE_FAST ? slot_key<MRL_MODE_EXACT>(s1, b * 64 + lane + 32, xtab, rho_tab, S) : k1;
                 }
-                fn(k0 != 0ull && k0 < minc, k0, lane);
-                fn(k1 != 0ull && k1 < minc, k1, lane);
+                fn(k0 != 0ull && k0 < minc, x0, lane);
+                fn(k1 != 0ull && k1 < minc, x1, lane);
             }
         }
     }
@@ -255,7 +166,7 @@ struct Finisher {
 // early exit once the current digit's bin holds exactly the keys still to be selected. Returns T
 // such that the keys >= T are exactly the top min(k, count) keys.
 template <int MODE>
-__device__ u64 select_threshold(const Finisher<MODE>& F, unsigned k, unsigned* hist, SelState* st) {
+__device__ __forceinline__ u64 select_threshold(const Finisher<MODE>& F, unsigned k, unsigned* hist, SelState* st) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) { st->prefix = 0; st->mask = 0; st->rem = k; st->done = 0; }
     if (tid == 0) hist[0] = 0;
@@ -320,15 +231,18 @@ __device__ u64 select_threshold(const Finisher<MODE>& F, unsigned k, unsigned* h
 // have dropped members. Reselect over the union of lists plus those CTAs' rescanned keys and write
 // the whole output.
 template <int MODE>
-__device__ void reselect(const ScanLaunch& p, const int* tab, const float2* rho_tab, const Scalars& S, u64* cand,
-                         u64* gath, unsigned* hist, const unsigned* flags, unsigned nflag, SelState* st,
-                         unsigned* s_misc) {
+__device__ __forceinline__ void reselect(const ScanLaunch& p, const int* tab, const int* xtab, const float2* rho_tab, const Scalars& S,
+                         u64* cand, u64* xcand, u64* gath, unsigned* hist, const unsigned* flags, unsigned nflag,
+                         SelState* st, unsigned* s_misc) {
     const int tid = threadIdx.x;
     const unsigned G = gridDim.x;
-    for (unsigned i = tid; i < G * 32; i += kThreads) cand[i] = __ldcg(p.cta_keys + i);
+    for (unsigned i = tid; i < G * 32; i += kThreads) {
+        cand[i] = __ldcg(p.cta_keys + i);
+        if (MODE == MRL_MODE_FAST) xcand[i] = __ldcg(p.cta_xkeys + i);
+    }
     if (tid == 0) s_misc[1] = 0;
     __syncthreads();
-    Finisher<MODE> F{p, tab, rho_tab, S, cand, flags, nflag, G, p.list_len};
+    Finisher<MODE> F{p, tab, xtab, rho_tab, S, cand, MODE == MRL_MODE_FAST ? xcand : cand, flags, nflag, G, p.list_len};
     const u64 tau = select_threshold<MODE>(F, p.k, hist, st);
     F.visit([&](bool valid, u64 x, int ln) {
         const bool in = valid && x >= tau;
@@ -414,6 +328,16 @@ __device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int m
     }
     fill_rho_tab(rho_tab, tid, kThreads);
     fill_scalars(P, p.w_s4, p.depth, (int32_t)(p.list_len != 0u), S);  // one: 1 for every launch, opaque to the compiler
+}
+
+// Fast mode's copy of the exact-mode tables (same layout as load_tables' exact branch), read only
+// by the exact rescoring of list entries.
+__device__ __forceinline__ void load_exact_tables(const DevPlan* __restrict__ P, float* ft) {
+    const int tid = threadIdx.x;
+    for (int i = tid; i < kPrefix * 16; i += kThreads) ft[i] = P->fp_prefix[i];
+    for (int i = tid; i < kRabitq; i += kThreads) ft[kTabMidW + i] = P->mid_w[i];
+    for (int i = tid; i < kFold; i += kThreads) ft[kTabTailW + i] = P->tail_w[i];
+    for (int i = tid; i < kPrefix; i += kThreads) ft[kTabBw3 + i] = P->qp.bit_weights[i][3];
 }
 
 // Page schedule: each warp's first two pages are static (pages gw and gw + W for global warp gw of
@@ -517,13 +441,25 @@ __host__ __device__ inline size_t fused_plan_bytes(uint32_t dims) {
     return align16(sizeof(DevPlan)) + align16((size_t)dims * sizeof(float)) + align16(sizeof(planb::PlanShared));
 }
 
+// Score-word probes for count_greater: the keys above probe_above(s) are those with a score > s, the
+// keys above probe_atleast(s) those with a score >= s.
+__device__ __forceinline__ u64 probe_above(float s) { return make_key(s, 0u) | 0xFFFFFFFFull; }
+__device__ __forceinline__ u64 probe_atleast(float s) { return (make_key(s, 0u) & 0xFFFFFFFF00000000ull) - 1ull; }
+
 template <int MODE, bool FUSED>
-__global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
+__device__ __forceinline__ void scan_body(const ScanLaunch& p) {
+    constexpr bool kFast = MODE == MRL_MODE_FAST;
     __shared__ __align__(16) int s_tab[kTabInts];
+    // fast mode: the exact-mode tables too, for the exact rescoring of the CTA's list
+    __shared__ __align__(16) float s_xtab[kFast ? kTabBw3 + kPrefix : 1];
     __shared__ float2 s_rho[256];
     __shared__ u64 s_cta_tau;
     __shared__ unsigned s_seed_min, s_seed_cnt;
     __shared__ unsigned s_part[kWarps * 32];
+    __shared__ unsigned s_part2[kFast ? kWarps * 32 : 1];
+    __shared__ unsigned s_band[32];
+    __shared__ unsigned s_nband;
+    __shared__ unsigned char s_bandkey[32];
     __shared__ u64 s_red64[kWarps];
     __shared__ unsigned s_red32[kWarps];
     __shared__ unsigned s_nflag;
@@ -534,9 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     extern __shared__ __align__(16) unsigned char s_dyn[];
     u64* s_queue = reinterpret_cast<u64*>(s_dyn);  // kWarps * kQueue
     u64* s_lists = s_queue + kWarps * kQueue;       // kWarps * 32
-    u64* s_cand = s_lists + kWarps * 32;            // G * 33
+    u64* s_cand = s_lists + kWarps * 32;            // G * 33: scan keys of every CTA list
     const unsigned G = gridDim.x;
-    u64* s_gath = s_cand + G * 33;                  // pow2 >= k
+    u64* s_xcand = s_cand + G * 33;                 // G * 33: their exact keys (fast mode)
+    u64* s_gath = s_xcand + (kFast ? G * 33 : 0);   // pow2 >= k
     unsigned P2 = 1;
     while (P2 < p.k) P2 <<= 1;
     unsigned* s_hist = reinterpret_cast<unsigned*>(s_gath + P2);  // kBins
@@ -545,6 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned L = p.list_len;
     unsigned* counter = p.ctl;
+    const int* xtab = kFast ? reinterpret_cast<const int*>(s_xtab) : s_tab;
 
     // fused plan build: its inputs first, so they are not queued behind the page loads
     DevPlan* ps = reinterpret_cast<DevPlan*>(s_dyn);
@@ -552,6 +490,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     planb::PlanShared* s_pb =
         reinterpret_cast<planb::PlanShared*>(s_dyn + align16(sizeof(DevPlan)) + align16((size_t)p.dims * sizeof(float)));
     if (FUSED) planb::plan_inputs(p.query, p.dims, p.eden_mean, p.mid_mean, s_qb, *s_pb);
+    float4 mm = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (kFast) mm = __ldg(reinterpret_cast<const float4*>(p.metamax));
 
     // first page in flight before the tables are read
     const uint32_t W = G * kWarps, gw = (uint32_t)warp * G + blockIdx.x, dyn0 = 2 * W;
@@ -560,16 +500,17 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     if (b < p.n_blocks) { load_slot(p.pages, b, lane, a0); load_slot(p.pages, b, lane + 32, a1); }
 
     Scalars S;
-    if (tid == 0) { s_cta_tau = 0ull; s_seed_min = 0xFFFFFFFFu; s_seed_cnt = 0u; s_nflag = 0u; }
+    if (tid == 0) { s_cta_tau = 0ull; s_seed_min = 0xFFFFFFFFu; s_seed_cnt = 0u; s_nflag = 0u; s_nband = 0u; }
     const DevPlan* plan = p.plan;
     if (FUSED) {
         // QueryPipeline::build_plan fused into the scan (src/pipeline.rs:63-74): every CTA builds the
         // plan in shared memory while its first pages are in flight; no CTA waits on another.
-        // CTA 0 stores the complete plan; the others build only what this mode scans with
+        // CTA 0 stores the complete plan; the others build only what this mode scans with (fast
+        // mode also needs the exact-mode prefix products for the rescoring of its list)
         const uint32_t need = blockIdx.x == 0 && p.plan_out
                                   ? planb::kNeedAll
-                                  : (MODE == MRL_MODE_FAST ? planb::kNeedFast | (p.depth == MRL_DEPTH_L0 ? planb::kNeedL0 : 0u)
-                                                           : planb::kNeedExact);
+                                  : (kFast ? planb::kNeedFast | planb::kNeedExact | (p.depth == MRL_DEPTH_L0 ? planb::kNeedL0 : 0u)
+                                           : planb::kNeedExact);
         planb::build_plan(p.dims, p.prefix_codec, p.mid_codec, p.eden_seed, p.mid_seed, ps, s_qb, *s_pb, need);
         __syncthreads();
         if (blockIdx.x == 0 && p.plan_out) {  // keep the plan for mrl_plan_read and later scans
@@ -580,6 +521,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
         plan = ps;
     }
     load_tables(plan, MODE, s_tab, s_rho, S, p);
+    if constexpr (kFast) load_exact_tables(plan, s_xtab);
+    // bound on |fast score - exact score| of every slot of this segment (0 in exact mode)
+    const float E = kFast ? fast_error_bound(*plan, mm, p.w_s4, p.depth) : 0.0f;
     __syncthreads();
 
     WarpSel ws{0ull, 0u, 0};
@@ -633,14 +577,24 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
         __syncthreads();
     }
     if (warp == 0) {
-        p.cta_keys[blockIdx.x * 32 + lane] = (uint32_t)lane < L ? s_lists[lane] : 0ull;
+        // publish the CTA's list; fast mode also rescores each entry in the reference's exact f32
+        // order (src/scan.rs:453-634) and publishes that key beside it
+        const u64 fk = (uint32_t)lane < L ? s_lists[lane] : 0ull;
+        u64 xk = fk;
+        if (kFast && fk != 0ull) {
+            const uint32_t ord = key_ordinal(fk);
+            Slot4 sl;
+            load_slot(p.pages, ord >> 6, (int)(ord & 63u), sl);
+            xk = slot_key<MRL_MODE_EXACT>(sl, ord, xtab, s_rho, S);
+        }
+        p.cta_keys[blockIdx.x * 32 + lane] = fk;
+        if (kFast) p.cta_xkeys[blockIdx.x * 32 + lane] = xk;
         __threadfence();
     }
     if (!grid_barrier(p.ctl, G, &s_ok)) {
         if (tid == 0 && p.out_status) *p.out_status = 2u;  // barrier timed out: no result
         return;
     }
-    if (blockIdx.x == 0 && tid == 0) atomicExch(counter, 0u);  // page counter ready for the next launch
 
     // Every CTA's list into shared memory, rows LP = L | 1 keys apart (an odd stride: threads that
     // each read a different list hit different banks).
@@ -649,24 +603,32 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
         // four loads in flight per thread before their stores (the lists come from L2)
         const unsigned nl = G * L, lsh = (unsigned)(__ffs((int)L) - 1);
         for (unsigned i0 = tid; i0 < nl; i0 += 4u * kThreads) {
-            u64 x[4];
+            u64 x[4], y[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const unsigned i = i0 + (unsigned)j * kThreads;
-                x[j] = i < nl ? __ldcg(p.cta_keys + (i >> lsh) * 32 + (i & (L - 1))) : 0ull;
+                const unsigned at = (i >> lsh) * 32 + (i & (L - 1));
+                x[j] = i < nl ? __ldcg(p.cta_keys + at) : 0ull;
+                y[j] = kFast && i < nl ? __ldcg(p.cta_xkeys + at) : 0ull;
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const unsigned i = i0 + (unsigned)j * kThreads;
-                if (i < nl) s_cand[(i >> lsh) * LP + (i & (L - 1))] = x[j];
+                if (i < nl) {
+                    s_cand[(i >> lsh) * LP + (i & (L - 1))] = x[j];
+                    if (kFast) s_xcand[(i >> lsh) * LP + (i & (L - 1))] = y[j];
+                }
             }
         }
     }
     __syncthreads();
 
-    // A CTA list may have dropped a top-k key only if it is full and its last key ranks below k.
-    // Ranks fall as keys grow, so ranking the largest last key of a full list (x_max) decides for
-    // all lists: rank(x_max) >= k clears every one. Each CTA computes this from the same lists, so
+    // A CTA list may have dropped a top-k member only if it is full and the slots it dropped could
+    // still rank below k. Exact mode: its last key ranks below k. Fast mode: a dropped slot's exact
+    // score is at most last + E and a top-k slot's exact score is at least F_k - E... so the list is
+    // safe when more than k keys score above F(last) + 4E (every top-k member's fast score is then
+    // within 2E of the k-th or above it). Ranks fall as keys grow, so testing the largest last key
+    // of a full list (x_max) decides for all lists. Each CTA computes this from the same lists, so
     // all reach the same decision without further communication.
     u64 last = 0ull;
     unsigned live = 0;
@@ -693,24 +655,42 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
         x_max = s_red64[w] > x_max ? s_red64[w] : x_max;
         total += s_red32[w];
     }
+    const u64 x_probe = kFast ? probe_above(__fadd_ru(key_score(x_max), 4.0f * E)) : x_max;
     // rank of x_max (threads c < G, list c) and of this CTA's own keys: lane l of warp w handles key
     // l % L against the lists of group g = w * (32 / L) + l / L (lists g, g + NG, ...), partial
-    // counts reduced through shared memory
-    unsigned rx = ((unsigned)tid < G && x_max != 0ull) ? count_greater(s_cand + tid * LP, L, x_max) : 0u;
+    // counts reduced through shared memory. Fast mode counts, per own key x, the keys scoring above
+    // F(x) + 2E (certainly above x in exact order) and those scoring at least F(x) - 2E (the rest
+    // are certainly below); the ones in between (x itself, and near-ties) are ordered by their
+    // exact keys.
+    unsigned rx = ((unsigned)tid < G && x_max != 0ull) ? count_greater(s_cand + tid * LP, L, x_probe) : 0u;
     const u64* mine = s_cand + blockIdx.x * LP;
+    const u64* xmine = s_xcand + blockIdx.x * LP;
     const unsigned per_warp = 32u / L, NG = kWarps * per_warp;
     const unsigned ki = (unsigned)lane % L, gi = (unsigned)lane / L;
     const u64 x = gi < per_warp ? mine[ki] : 0ull;
-    unsigned cnt = 0;
+    u64 xh = x, xl = x;
+    if (kFast && x != 0ull) {
+        const float f = key_score(x);
+        xh = probe_above(__fadd_ru(f, 2.0f * E));
+        xl = probe_atleast(__fsub_rd(f, 2.0f * E));
+    }
+    unsigned cnt = 0, cnt2 = 0;
     if (x != 0ull) {
 #pragma unroll 4
-        for (unsigned c = warp * per_warp + gi; c < G; c += NG) cnt += count_greater(s_cand + c * LP, L, x);
+        for (unsigned c = warp * per_warp + gi; c < G; c += NG) {
+            cnt += count_greater(s_cand + c * LP, L, xh);
+            if (kFast) cnt2 += count_greater(s_cand + c * LP, L, xl);
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) rx += __shfl_xor_sync(kFull, rx, o);
     // list_len is a power of two: fold the warp's key groups onto lanes 0 .. L-1
-    for (unsigned o = 16; o >= L; o >>= 1) cnt += __shfl_down_sync(kFull, cnt, o);
+    for (unsigned o = 16; o >= L; o >>= 1) {
+        cnt += __shfl_down_sync(kFull, cnt, o);
+        if (kFast) cnt2 += __shfl_down_sync(kFull, cnt2, o);
+    }
     s_part[warp * 32 + lane] = cnt;
+    if constexpr (kFast) s_part2[warp * 32 + lane] = cnt2;
     __syncthreads();  // every thread has read s_red32 above
     if (lane == 0) s_red32[warp] = rx;
     __syncthreads();
@@ -719,49 +699,72 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     for (int w = 0; w < kWarps; ++w) rank_xmax += s_red32[w];
     const bool clean = x_max == 0ull || rank_xmax >= p.k;
 
-    if (clean && p.xch_world) {
-        // this rank's top-k into its record in every rank's area (peer stores over NVLink)
-        const size_t kk = p.k;
-        if ((unsigned)tid < L) {
-            const u64 key = mine[tid];
-            unsigned r = 0;
+    if (clean) {
+        // Rank of each own key. Exact mode: the number of keys above it. Fast mode: the keys
+        // certainly above it, plus the near-ties whose exact key is larger (rare: resolved by
+        // every thread, one list each, below).
+        unsigned r = 0xFFFFFFFFu;
+        if ((unsigned)tid < L && mine[tid] != 0ull) {
+            r = 0;
 #pragma unroll
             for (int w = 0; w < kWarps; ++w) r += s_part[w * 32 + tid];
-            if (key != 0ull && r < p.k) {  // into this rank's own record (local memory)
-                const uint32_t ord = key_ordinal(key);
+            if constexpr (kFast) {
+                unsigned r2 = 0;
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) r2 += s_part2[w * 32 + tid];
+                s_band[tid] = 0u;
+                if (r2 - r > 1u && r < p.k) s_bandkey[atomicAdd(&s_nband, 1u)] = (unsigned char)tid;
+            }
+        }
+        if (kFast) {
+            __syncthreads();
+            for (unsigned j = 0; j < s_nband; ++j) {  // block-uniform
+                const unsigned t = s_bandkey[j];
+                const u64 fx = mine[t], ex = xmine[t];
+                const float f = key_score(fx);
+                const u64 hi = probe_above(__fadd_ru(f, 2.0f * E)), lo = probe_atleast(__fsub_rd(f, 2.0f * E));
+                if ((unsigned)tid < G) {
+                    const u64* lst = s_cand + tid * LP;
+                    const unsigned a = count_greater(lst, L, hi), e = count_greater(lst, L, lo);
+                    unsigned n = 0;
+                    for (unsigned i = a; i < e; ++i)
+                        n += (lst[i] != fx && s_xcand[tid * LP + i] > ex) ? 1u : 0u;
+                    if (n) atomicAdd(&s_band[t], n);
+                }
+            }
+            __syncthreads();
+            if ((unsigned)tid < L && r != 0xFFFFFFFFu) r += s_band[tid];
+        }
+        const u64 okey = kFast ? xmine[tid < 32 ? tid : 0] : mine[tid < 32 ? tid : 0];
+        if (p.xch_world) {
+            // this rank's top-k into its own record (local memory); peers pull it over NVLink after
+            // the release flag below
+            const size_t kk = p.k;
+            if ((unsigned)tid < L && r < p.k) {
+                const uint32_t ord = key_ordinal(okey);
                 unsigned char* rec = const_cast<unsigned char*>(p.xch_rec[p.xch_rank]);
                 reinterpret_cast<uint64_t*>(rec)[r] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
-                reinterpret_cast<float*>(rec + kk * 8)[r] = key_score(key);
+                reinterpret_cast<float*>(rec + kk * 8)[r] = key_score(okey);
             }
-        }
-        __syncthreads();
-        if (tid == 0) {
+            __syncthreads();
+            if (tid == 0) {
+                __threadfence();
+                s_last = atomicAdd(p.ctl + 6, 1u) == G - 1 ? 1u : 0u;
+            }
+            __syncthreads();
+            if (!s_last) return;
+            // the last CTA: every CTA's entries are in; add the count, then publish
             __threadfence();
-            s_last = atomicAdd(p.ctl + 6, 1u) == G - 1 ? 1u : 0u;
+            if (tid == 0)
+                *reinterpret_cast<uint32_t*>(const_cast<unsigned char*>(p.xch_rec[p.xch_rank]) + kk * 12) = min(total, p.k);
+            xch_publish_and_merge(p, s_dyn, &s_ok, 0u);
+            return;
         }
-        __syncthreads();
-        if (!s_last) return;
-        // the last CTA: every CTA's entries are in; add the count, then publish
-        __threadfence();
-        if (tid == 0) {
-            atomicExch(p.ctl + 6, 0u);  // ready for the next launch
-            *reinterpret_cast<uint32_t*>(const_cast<unsigned char*>(p.xch_rec[p.xch_rank]) + kk * 12) = min(total, p.k);
-        }
-        xch_publish_and_merge(p, s_dyn, &s_ok, 0u);
-        return;
-    }
-    if (clean) {
         // keys ranked below k are the top-k: each CTA writes its own in place
-        if ((unsigned)tid < L) {
-            const u64 key = mine[tid];
-            unsigned r = 0;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) r += s_part[w * 32 + tid];
-            if (key != 0ull && r < p.k) {
-                const uint32_t ord = key_ordinal(key);
-                p.out_ids[r] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
-                p.out_scores[r] = key_score(key);
-            }
+        if ((unsigned)tid < L && r < p.k) {
+            const uint32_t ord = key_ordinal(okey);
+            p.out_ids[r] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
+            p.out_scores[r] = key_score(okey);
         }
         if (blockIdx.x == 0 && tid == 0) {
             *p.out_count = min(total, p.k);
@@ -769,32 +772,55 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
         }
         return;
     }
-    // Rare path: CTA 0 alone finds the flagged lists (full, last key ranked below k), reselects over
-    // the lists plus those CTAs' rescanned pages, and writes the whole output.
+    // Rare path: CTA 0 alone finds the flagged lists (full, and dropped slots could rank below k),
+    // reselects by exact key over the lists plus those CTAs' rescanned pages, and writes the whole
+    // output.
     if (blockIdx.x != 0) return;
     for (unsigned c = warp; c < G; c += kWarps) {
         const u64 lc = s_cand[c * LP + L - 1];
         if (lc == 0ull) continue;  // warp-uniform: list not full
+        const u64 pr = kFast ? probe_above(__fadd_ru(key_score(lc), 4.0f * E)) : lc;
         unsigned r = 0;
-        for (unsigned j = lane; j < G; j += 32) r += count_greater(s_cand + j * LP, L, lc);
+        for (unsigned j = lane; j < G; j += 32) r += count_greater(s_cand + j * LP, L, pr);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(kFull, r, o);
         if (lane == 0 && r < p.k) s_flags[atomicAdd(&s_nflag, 1u)] = c;
     }
     __syncthreads();
     if (p.xch_world) {
-        // exchange: reselect into this rank's own record, copy it to the other ranks, signal, merge
+        // exchange: reselect into this rank's own record, signal, merge
         ScanLaunch own = p;
         unsigned char* mine_rec = const_cast<unsigned char*>(p.xch_rec[p.xch_rank]);
         own.out_ids = reinterpret_cast<uint64_t*>(mine_rec);
         own.out_scores = reinterpret_cast<float*>(mine_rec + (size_t)p.k * 8);
         own.out_count = reinterpret_cast<uint32_t*>(mine_rec + (size_t)p.k * 12);
-        reselect<MODE>(own, s_tab, s_rho, S, s_cand, s_gath, s_hist, s_flags, s_nflag, &s_sel, s_misc);
+        reselect<MODE>(own, s_tab, xtab, s_rho, S, s_cand, s_xcand, s_gath, s_hist, s_flags, s_nflag, &s_sel, s_misc);
         xch_publish_and_merge(p, s_dyn, &s_ok, 1u);
         return;
     }
-    reselect<MODE>(p, s_tab, s_rho, S, s_cand, s_gath, s_hist, s_flags, s_nflag, &s_sel, s_misc);
+    reselect<MODE>(p, s_tab, xtab, s_rho, S, s_cand, s_xcand, s_gath, s_hist, s_flags, s_nflag, &s_sel, s_misc);
     if (tid == 0 && p.out_status) *p.out_status = 1u;
+}
+
+template <int MODE, bool FUSED>
+__global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
+    scan_body<MODE, FUSED>(p);
+    // Exit ticket: the last CTA to leave zeroes the control words (page counter, barrier count,
+    // exchange count, timeout flag, the ticket), so the next launch on this scratch starts clean
+    // whichever path this one took, a bounded wait that ran out included. The barrier generation
+    // only ever advances and keeps its value.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(p.ctl + 7, 1u) == gridDim.x - 1) {
+            p.ctl[0] = 0u;
+            p.ctl[1] = 0u;
+            p.ctl[5] = 0u;
+            p.ctl[6] = 0u;
+            __threadfence();
+            atomicExch(p.ctl + 7, 0u);
+        }
+    }
 }
 
 template <int MODE>
@@ -824,7 +850,18 @@ __global__ void __launch_bounds__(kThreads) debug_scores_kernel(const ScanLaunch
     }
 }
 
+__global__ void score_bound_kernel(const DevPlan* __restrict__ plan, const float* __restrict__ metamax, float w_s4,
+                                   uint32_t depth, float* out) {
+    if (threadIdx.x == 0)
+        *out = fast_error_bound(*plan, *reinterpret_cast<const float4*>(metamax), w_s4, depth);
+}
+
 }  // namespace
+
+int launch_score_bound(const ScanLaunch& p, float* d_out, cudaStream_t stream) {
+    score_bound_kernel<<<1, 32, 0, stream>>>(p.plan, p.metamax, p.w_s4, p.depth, d_out);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
 
 int scan_ctas(int device_sms) { return device_sms; }
 
@@ -839,11 +876,11 @@ size_t xch_merge_bytes(uint32_t world, uint32_t k) {
     return (size_t)(xch_use_tree(world, k) ? world + (world + 1) / 2 : world) * MRL_MERGE_RECORD_BYTES(k);
 }
 
-size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t xch_world) {
+size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t xch_world, uint32_t mode) {
     size_t p2 = 1;
     while (p2 < k) p2 <<= 1;
-    size_t bytes = sizeof(u64) * (kWarps * kQueue + kWarps * 32 + (size_t)ctas * 33 + p2) +
-                   sizeof(unsigned) * (kBins + ctas);
+    const size_t lists = (size_t)ctas * 33 * (mode == MRL_MODE_FAST ? 2 : 1);  // scan keys (+ exact keys)
+    size_t bytes = sizeof(u64) * (kWarps * kQueue + kWarps * 32 + lists + p2) + sizeof(unsigned) * (kBins + ctas);
     if (fused_dims) bytes = std::max(bytes, fused_plan_bytes(fused_dims));
     if (xch_world) bytes = std::max(bytes, xch_merge_bytes(xch_world, k));  // records to merge
     return bytes;
@@ -852,7 +889,7 @@ size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t 
 // Cooperative launch: one CTA per SM, all co-resident (the grid barrier relies on it).
 int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream) {
     const bool fused = p.query != nullptr;
-    const size_t smem = scan_smem_bytes(ctas, p.k, fused ? p.dims : 0u, p.xch_world);
+    const size_t smem = scan_smem_bytes(ctas, p.k, fused ? p.dims : 0u, p.xch_world, p.mode);
     const void* fn = p.mode == MRL_MODE_FAST ? (fused ? (const void*)scan_kernel<MRL_MODE_FAST, true>
                                                       : (const void*)scan_kernel<MRL_MODE_FAST, false>)
                                              : (fused ? (const void*)scan_kernel<MRL_MODE_EXACT, true>

@@ -201,5 +201,140 @@ __device__ __forceinline__ void fill_rho_tab(float2* rho_tab, int tid, int nthr)
     }
 }
 
+// Shared-memory table layout of the single-query scan (ints in fast mode, floats in exact mode).
+constexpr int kTabInts = kPrefix * 16 + kS1Windows * 32 + kS4Windows * 32 + kPrefix * 16;  // 3296
+constexpr int kTabS1 = kPrefix * 16;
+constexpr int kTabS4 = kTabS1 + kS1Windows * 32;
+constexpr int kTabL0 = kTabS4 + kS4Windows * 32;
+// exact-mode layout inside the same table space (floats)
+constexpr int kTabMidW = kPrefix * 16;
+constexpr int kTabTailW = kTabMidW + kRabitq;
+constexpr int kTabBw3 = kTabTailW + kFold;
+
+// Full score of one slot; returns false for tombstoned slots.
+template <int MODE>
+__device__ __forceinline__ bool slot_score(const uint4& c0, const uint4& c1, const uint4& c2,
+                                           const uint4& c3, const int* tab, const float2* rho_tab,
+                                           const Scalars& S, float& score, Partials* parts) {
+    const SlotMeta m = slot_meta_tab(c3.z, c3.w, rho_tab);
+    if (m.tomb) return false;
+    if (MODE == MRL_MODE_FAST) {
+        const uint32_t s1w[4] = {c2.x, c2.y, c2.z, c2.w};
+        const uint32_t s4w[2] = {c3.x, c3.y};
+        if (S.depth == MRL_DEPTH_L0) {  // src/scan.rs:753-771
+            const int32_t P = prefix_fixed(c0, c1, tab + kTabL0, S.one);
+            const float cd = unfix(P, S.un_l0, S.unf_l0, S.f32_unscale);
+            score = __fadd_rn(__fmul_rn(cd, m.scale), __fmul_rn(m.offset, S.prefix_sum));
+            if (parts) {
+                parts->p = P;
+                parts->s1 = window_fixed<128>(s1w, tab + kTabS1, S.one);
+                parts->s4 = window_fixed<64>(s4w, tab + kTabS4, S.one);
+            }
+            return true;
+        }
+        const int32_t P = prefix_fixed(c0, c1, tab, S.one);
+        int32_t s1 = 0, s4 = 0;
+        if (S.depth >= MRL_DEPTH_L1 || parts) s1 = window_fixed<128>(s1w, tab + kTabS1, S.one);
+        if ((S.depth == MRL_DEPTH_FULL && S.has_tail) || parts) s4 = window_fixed<64>(s4w, tab + kTabS4, S.one);
+        if (parts) { parts->p = P; parts->s1 = s1; parts->s4 = s4; }
+        score = fast_score(m, P, s1, s4, S);
+        return true;
+    } else {
+        const float* ft = reinterpret_cast<const float*>(tab);
+        if (S.depth == MRL_DEPTH_L0) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int d = 0; d < kPrefix; ++d)
+                if (level_of(c0, c1, d) & 8u) acc = __fadd_rn(acc, ft[kTabBw3 + d]);
+            score = __fadd_rn(__fmul_rn(acc, m.scale), __fmul_rn(m.offset, S.prefix_sum));
+            return true;
+        }
+        float acc = 0.0f;  // src/scan.rs:456-487, per-slot sequential order over d
+        {
+            const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+            for (int d = 0; d < kPrefix; ++d) {
+                const uint32_t sh = 4 * (d & 7);
+                const uint32_t idx4 = sh >= 2 ? ((w[d >> 3] >> (sh - 2)) & 0x3Cu) : ((w[d >> 3] << 2) & 0x3Cu);
+                acc = __fadd_rn(acc, *reinterpret_cast<const float*>(reinterpret_cast<const char*>(ft) + d * 64 + idx4));
+            }
+        }
+        float sc = S.eden ? __fadd_rn(S.eden_mean_ip, __fmul_rn(m.scale, acc))
+                          : __fadd_rn(__fmul_rn(acc, m.scale), __fmul_rn(m.offset, S.prefix_sum));
+        if (S.depth >= MRL_DEPTH_L1) {  // src/scan.rs:520-569
+            const uint32_t s1w[4] = {c2.x, c2.y, c2.z, c2.w};
+            float s = S.mid_base;
+            const float4* mw = reinterpret_cast<const float4*>(ft + kTabMidW);
+#pragma unroll
+            for (int g = 0; g < kRabitq / 4; ++g) {
+                const float4 w4 = mw[g];
+                const uint32_t bits = s1w[g >> 3] >> (4 * (g & 7));
+                if (bits & 1u) s = __fadd_rn(s, w4.x);
+                if (bits & 2u) s = __fadd_rn(s, w4.y);
+                if (bits & 4u) s = __fadd_rn(s, w4.z);
+                if (bits & 8u) s = __fadd_rn(s, w4.w);
+            }
+            if (S.mid_b1) sc = __fadd_rn(sc, __fadd_rn(S.mid_mean_ip, __fmul_rn(m.offset, s)));
+            else sc = __fadd_rn(sc, __fmul_rn(s, m.mid_n));
+        }
+        if (S.depth == MRL_DEPTH_FULL && S.has_tail) {  // src/scan.rs:610-634
+            const uint32_t s4w[2] = {c3.x, c3.y};
+            float t = S.tail_base;
+            const float4* tw = reinterpret_cast<const float4*>(ft + kTabTailW);
+#pragma unroll
+            for (int g = 0; g < kFold / 4; ++g) {
+                const float4 w4 = tw[g];
+                const uint32_t bits = s4w[g >> 3] >> (4 * (g & 7));
+                if (bits & 1u) t = __fadd_rn(t, w4.x);
+                if (bits & 2u) t = __fadd_rn(t, w4.y);
+                if (bits & 4u) t = __fadd_rn(t, w4.z);
+                if (bits & 8u) t = __fadd_rn(t, w4.w);
+            }
+            sc = __fadd_rn(sc, __fmul_rn(__fmul_rn(t, fmaxf(m.high_n, 1e-6f)), S.w_s4));
+        }
+        score = sc;
+        return true;
+    }
+}
+
+// Upper bound on |fast-mode score - exact-mode score| for every slot whose meta factors lie within
+// mm = {max |scale|, max |offset|, max mid_n, max max(high_n, 1e-6)} (a segment's maxima). Both
+// modes approximate the same real-valued stage sums of the same f32 table values:
+//   * the exact mode's sequential f32 sum of n terms is within gamma_{n-1} * sum |terms| of the
+//     real sum (recursive summation; Higham, Accuracy and Stability of Numerical Algorithms,
+//     2nd ed., 4.2), plus one product rounding per term where the terms are products; the mid band
+//     and tail sums start from an f32 base that is itself a 128- or 64-term sum;
+//   * the fast mode's integer sum of n entries rint(v * 2^shift) is within n/2 units of 2^-shift of
+//     the real sum, plus the rounding of its conversion to f32;
+// and each mode's score formula (src/scan.rs:499-505, 546-547, 566, 631) rounds at most 8 times,
+// each time by at most u = 2^-24 of a value no larger than the sum of all term magnitudes. The
+// coefficients below round those counts up, and the total is doubled for slack. Not finite (+inf)
+// when the segment holds non-finite factors.
+__device__ __forceinline__ float fast_error_bound(const DevPlan& P, float4 mm, float w_s4, uint32_t depth) {
+    const double u = 0x1p-24;
+    const double sc = mm.x, of = mm.y, mid = mm.z, hp = mm.w, w = fabs((double)w_s4);
+    const bool eden = P.qp.prefix_codec == MRL_PREFIX_EDEN, b1 = P.qp.mid_codec == MRL_MID_EDEN_B1;
+    double dev, mag;
+    if (depth == MRL_DEPTH_L0) {  // code_dot * scale + offset * prefix_sum (src/scan.rs:753-771)
+        const double dp = 72.0 * u * P.err_0 + 40.0 * P.unscale_l0;
+        dev = sc * dp;
+        mag = sc * (P.err_0 + dp) + of * fabs((double)P.qp.prefix_sum);
+    } else {
+        const double dp = 72.0 * u * P.err_p + 40.0 * P.unscale_prefix;
+        dev = sc * dp;
+        mag = (eden ? fabs((double)P.qp.eden_mean_ip) : of * fabs((double)P.qp.prefix_sum)) + sc * (P.err_p + dp);
+        const double d1 = 530.0 * u * P.err_1 + 70.0 * P.unscale_s1, f1 = b1 ? of : mid;
+        dev += f1 * d1;
+        mag += f1 * (P.err_1 + d1) + (b1 ? fabs((double)P.qp.eden_mid_mean_ip) : 0.0);
+        if (depth == MRL_DEPTH_FULL && P.qp.has_tail_fold) {
+            const double d4 = 270.0 * u * P.err_4 + 40.0 * P.unscale_s4;
+            dev += hp * w * d4;
+            mag += hp * w * (P.err_4 + d4);
+        }
+    }
+    const double e = 2.0 * (dev + 16.0 * u * mag) + 1e-35;
+    return e < 3.0e38 ? __double2float_ru(e) : __int_as_float(0x7F800000);
+}
+
 }  // namespace
 }  // namespace mrl

@@ -30,6 +30,8 @@ from .api import (  # noqa: F401
     scan_blocks_batch,
     scored_hits_to_row_ids,
     vector_scores,
+    score_bound,
+    control_words,
 )
 from .index import (  # noqa: F401
     DeviceRing,

@@ -56,8 +56,8 @@ class StrataDepth(enum.IntEnum):
 
 
 class ScanMode(enum.IntEnum):
-    FAST = 0   # exact int32 stage sums, f32 scores within 1e-5 relative of the reference
-    EXACT = 1  # bit-identical f32 arithmetic of the reference
+    FAST = 0   # exact int32 stage sums choose the candidates; the final top-k is rescored in the exact mode
+    EXACT = 1  # bit-identical f32 arithmetic of the reference for every slot
 
 
 @dataclasses.dataclass
@@ -484,6 +484,23 @@ def vector_scores(segment: Segment, plan: QueryPlan, cfg, q: int = 0, time_lo=No
                                                    active.ctypes.data_as(C.c_void_p),
                                                    parts.ctypes.data_as(C.c_void_p)))
     return scores, active, parts.reshape(-1, 3)
+
+
+def score_bound(segment: Segment, plan: QueryPlan, cfg, q: int = 0) -> float:
+    """The bound E the fast mode's final ranking assumes: |fast score - exact score| <= E for every
+    slot of the segment under plan q (mrl_debug_score_bound)."""
+    c = _cfg_of(cfg).to_c()
+    out = C.c_float(0.0)
+    dev = segment.dev
+    check(dev.ptr, dev.lib.mrl_debug_score_bound(dev.ptr, segment.ptr, plan.ptr, q, C.byref(c), C.byref(out)))
+    return float(out.value)
+
+
+def control_words(dev: "Device") -> List[int]:
+    """The context's 8 scan control words (mrl_debug_control_words)."""
+    out = (C.c_uint32 * 8)()
+    check(dev.ptr, dev.lib.mrl_debug_control_words(dev.ptr, out))
+    return list(out)
 
 
 def encode_blocks(rows: np.ndarray, dims: int, eden: Optional[EdenFit] = None, eden_mid: Optional[EdenFit] = None,

@@ -2,7 +2,9 @@
 its engines (tcgen05 kind::i8 tensor cores, CUDA-core tables), against the single-query scan
 (mrl_scan_device): identical ids and bit-identical scores for every query that is not reported
 uncertified, across codecs, depths, tile remainders, k, tombstones and the temporal filter;
-uncertified queries are rerun by mrl_scan, so its results always match."""
+uncertified queries are rerun by mrl_scan, so its results always match. Both end in the exact-mode
+scores of the reference's f32 arithmetic (the integer sums only choose the candidates), checked
+against the oracle."""
 import ctypes as C
 
 import numpy as np
@@ -183,8 +185,9 @@ def test_batch_exact_mode_and_l0_fall_back(ora, dev):
     plans.free()
 
 
-def test_batch_against_oracle_fixed_scores(ora, dev, engine):
-    """The batched top-k equals the exact top-k of the oracle's fast-mode integer scores."""
+def test_batch_against_oracle_exact_topk(ora, dev, engine):
+    """The batched top-k equals the oracle's exact-mode top-k (the reference's f32 scores, bit for
+    bit) and the oracle's scan_blocks; the fast-mode integer scores only choose the candidates."""
     M = mb()
     docs, blocks, mean, _ = _corpus(ora, 64 * 120 + 5, seed=17)
     seg = M.Segment.upload(blocks, dev)
@@ -197,13 +200,15 @@ def test_batch_against_oracle_fixed_scores(ora, dev, engine):
     for q in range(n_q):
         op = ora.plan_build(qs[q], eden_mean=mean)
         ocfg = ora.scan_cfg(k=k)
-        fp = ora.fixed_plan_build(op, ocfg)
-        _, fsc, fact = ora.fixed_scores(blocks, op, fp, ocfg)
-        ti, ts = ora.topk_by_key(fsc, fact, k)
+        fs, act = ora.full_scores(blocks, op, ocfg)
+        ti, ts = ora.topk_by_key(fs, act, k)
+        rid, rsc = ora.scan_blocks(blocks, op, ocfg, threads=4)
         n = int(b[2][q])
         assert n == k and not b[3][q] & 8
         assert np.array_equal(b[0][q, :n], ti)
         assert np.array_equal(b[1][q, :n].view(np.uint32), ts.view(np.uint32))
+        assert np.array_equal(b[0][q, :n], rid.astype(np.uint64))
+        assert np.array_equal(b[1][q, :n].view(np.uint32), rsc.view(np.uint32))
     seg.free()
     plans.free()
 

@@ -3,7 +3,7 @@ independent numpy restatement, and the reference's property tests (ported).
 
 Reference tests ported (paths relative to the reference project root):
   src/eden.rs:374-424, src/rotate.rs:204-235, src/quantize.rs:375-427, src/scan.rs:925-1037,
-  src/geometry.rs:123-129, src/encoder.rs:284-323, src/pipeline.rs:333-373,
+  src/geometry.rs:123-129, src/encoder.rs:284-323, src/pipeline.rs:204-243,
   tests/test_challenger_architecture.rs:27-322, tests/test_operator_folding.rs:53-93.
 """
 import hashlib
@@ -345,6 +345,37 @@ def test_threaded_scan_equals_serial_and_exact_topk(ora):
             top = ora.topk_by_key(fs, act, 64)
             assert np.array_equal(par[0], ser[0]) and np.array_equal(par[0], top[0])
             assert np.array_equal(par[1].view(np.uint32), top[1].view(np.uint32))
+
+
+def test_scan_order_dependence_outside_exactness_region(ora):
+    """Why the device scans refuse cs_tolerance < 1 with the folded-tail stage: near-duplicate
+    vectors whose folded-tail bits all agree with the query (|s4| equal to the S4 budget) are pruned
+    by the budget bound alpha * budget < |s4| (src/scan.rs:587-607) depending on the shortlist's
+    running threshold, so the same vectors stored in the reverse block order give a different
+    top-k, and neither equals the top-k by full score. At cs_tolerance 1 every order gives that
+    top-k."""
+    rng = np.random.default_rng(5)
+    q = ora.synth_docs(21, 1, 768)[0]
+    n = 64 * 40
+    docs = np.repeat(q[None, :], n, axis=0).astype(np.float64)
+    docs[:, :192] += rng.standard_normal((n, 192)) * 0.02  # the tail keeps the query's direction
+    docs = (docs / np.linalg.norm(docs, axis=1, keepdims=True)).astype(np.float32)
+    mean = ora.eden_fit_prefix(docs)
+    blocks = ora.encode_corpus(docs, eden_mean=mean)
+    nb = n // 64
+    rev = blocks.reshape(nb, 4096)[::-1].reshape(-1).copy()
+    p = ora.plan_build(q, eden_mean=mean)
+
+    def unrev(ids):
+        return {((nb - 1 - (int(i) >> 16)) << 16) | (int(i) & 0xFFFF) for i in ids}
+
+    for alpha, differs in ((1.0, False), (0.9, True)):
+        cfg = ora.scan_cfg(k=64, cs_tolerance=alpha, numa_sharding=False)
+        fwd = set(map(int, ora.scan_blocks(blocks, p, cfg)[0]))
+        bwd = unrev(ora.scan_blocks(rev, p, cfg)[0])
+        fs, act = ora.full_scores(blocks, p, cfg)
+        top = set(map(int, ora.topk_by_key(fs, act, 64)[0]))
+        assert (fwd != bwd) == differs and (fwd != top) == differs and (bwd != top) == differs, alpha
 
 
 def test_temporal_filter_skips_blocks(ora):

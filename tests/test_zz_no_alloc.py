@@ -1,5 +1,7 @@
 """mrl_scan_device_static (scan scratch in the library's static device region, no allocation) against
-mrl_scan_device (scratch in the context) on the same inputs.
+mrl_scan_device (scratch in the context) and against the CPU oracle's scan on the same inputs, and
+the property the entry point exists for: once its first call on a device has looked the region up,
+its calls leave the device's free memory unchanged.
 
 The file name sorts last so the static region is exercised after every other GPU test has run;
 each test also stands alone. The two static calls of a test are issued back to back on the context
@@ -26,11 +28,12 @@ def case(ora, dev):
     n = 64 * 300 + 5  # ragged last page
     docs = ora.synth_docs(7, n, 768)
     mean = ora.eden_fit_prefix(docs)
-    seg = mb().Segment.upload(ora.encode_corpus(docs, eden_mean=mean), dev)
+    blocks = ora.encode_corpus(docs, eden_mean=mean)
+    seg = mb().Segment.upload(blocks, dev)
     qs, _ = ora.synth_queries(7, n, 3, 3, 768)
     plan = mb().QueryPlan.from_queries(qs, mb().PrefixCodec.EDEN_PROD, mb().MidCodec.RABITQ,
                                        eden=mb().EdenFit(64, 4, 1, mean), dev=dev)
-    yield dict(seg=seg, plan=plan, n_q=qs.shape[0])
+    yield dict(seg=seg, plan=plan, n_q=qs.shape[0], blocks=blocks, qs=qs, mean=mean)
     seg.free()
     plan.free()
 
@@ -144,3 +147,55 @@ def test_static_rejects_segment_over_limit(dev, case):
     got = _host(_run(dev, dev.lib.mrl_scan_device_static, case["seg"], case["plan"], case["n_q"],
                      mb().ScanConfig(shortlist_cand=8)))
     assert (got[2] == 8).all()
+
+
+@pytest.mark.parametrize("mode", ["FAST", "EXACT"])
+def test_static_matches_oracle_scan(ora, dev, case, mode):
+    """Two static calls in a row against the oracle's scan_blocks (the reference's algorithm) of
+    every query: ids identical and f32 scores bit-identical."""
+    k = 256
+    cfg = mb().ScanConfig(shortlist_cand=k, mode=getattr(mb().ScanMode, mode))
+    for got in _twice(dev, dev.lib.mrl_scan_device_static, case["seg"], case["plan"], case["n_q"], cfg):
+        for q in range(case["n_q"]):
+            op = ora.plan_build(case["qs"][q], eden_mean=case["mean"])
+            rid, rsc = ora.scan_blocks(case["blocks"], op, ora.scan_cfg(k=k), threads=4)
+            n = int(got[2][q])
+            assert n == len(rid)
+            np.testing.assert_array_equal(got[0][q, :n].view(np.uint64), rid.astype(np.uint64))
+            np.testing.assert_array_equal(got[1][q, :n].view(np.uint32), rsc.view(np.uint32))
+
+
+def test_static_calls_allocate_no_device_memory(ora, dev, case):
+    """A fresh context that has never scanned: after its first static call (which looks the region
+    up and may load the module), further static calls over segments of growing size, in both modes,
+    leave the device's free memory exactly unchanged. A call that allocated (a context scratch
+    buffer, or any cudaMalloc) would lower it by at least one allocation granule."""
+    import torch
+
+    M = mb()
+    fresh = M.Device(0)
+    try:
+        segs = [M.Segment.upload(case["blocks"][: p * 4096], fresh) for p in (1, 40, 301)]
+        plan = M.QueryPlan.from_queries(case["qs"], M.PrefixCodec.EDEN_PROD, M.MidCodec.RABITQ,
+                                        eden=M.EdenFit(64, 4, 1, case["mean"]), dev=fresh)
+        outs = [_outputs(case["n_q"], 256) for _ in range(7)]
+        cfgs = [M.ScanConfig(shortlist_cand=256, mode=m) for m in (M.ScanMode.FAST, M.ScanMode.EXACT)]
+        fn = fresh.lib.mrl_scan_device_static
+        _call(fresh, fn, segs[0], plan, case["n_q"], cfgs[0], outs[0])
+        torch.cuda.synchronize()
+        free0, _ = torch.cuda.mem_get_info()
+        i = 1
+        for sg in segs:
+            for c in cfgs:
+                _call(fresh, fn, sg, plan, case["n_q"], c, outs[min(i, 6)])
+                i += 1
+        torch.cuda.synchronize()
+        free1, _ = torch.cuda.mem_get_info()
+        assert free1 == free0, (free0, free1)
+        got = _host(outs[6])
+        assert (got[2] == 256).all() and ((got[3] & 2) == 0).all()
+        for sg in segs:
+            sg.free()
+        plan.free()
+    finally:
+        fresh.close()
