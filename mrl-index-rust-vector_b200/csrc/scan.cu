@@ -455,6 +455,7 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
     __shared__ float2 s_rho[256];
     __shared__ u64 s_cta_tau;
     __shared__ unsigned s_seed_min, s_seed_cnt;
+    __shared__ unsigned s_next;  // the CTA's next page of its range
     __shared__ unsigned s_part[kWarps * 32];
     __shared__ unsigned s_part2[kFast ? kWarps * 32 : 1];
     __shared__ unsigned s_band[32];
@@ -493,14 +494,34 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
     float4 mm = make_float4(0.f, 0.f, 0.f, 0.f);
     if (kFast) mm = __ldg(reinterpret_cast<const float4*>(p.metamax));
 
+    // Page schedule: the first 7/8 of the pages are split into one contiguous range per CTA, whose
+    // warps take pages from a shared-memory counter (the first two per warp static); the last 1/8
+    // is a pool handed out one page at a time from the global counter to CTAs that have finished
+    // their range, which evens out the finishing times. Global atomics are thus rare, and one
+    // page's grab is issued a page ahead so its latency overlaps the scoring.
+    const uint32_t n_pool = p.n_blocks / 8u, n_static = p.n_blocks - n_pool;
+    const uint32_t lo_c = (uint32_t)(((uint64_t)n_static * blockIdx.x) / G);
+    const uint32_t hi_c = (uint32_t)(((uint64_t)n_static * (blockIdx.x + 1)) / G);
+    auto grab = [&](uint32_t g) -> uint32_t {  // lane 0: a page from the range, else from the pool
+        if (g < hi_c) return g;
+        return n_static + atomicAdd(counter, 1u);
+    };
+    uint32_t b = 0, bn = 0;
+    if (lane == 0) {
+        b = grab(lo_c + (uint32_t)warp);
+        bn = grab(lo_c + (uint32_t)(kWarps + warp));
+    }
+    b = __shfl_sync(kFull, b, 0);
+    bn = __shfl_sync(kFull, bn, 0);
     // first page in flight before the tables are read
-    const uint32_t W = G * kWarps, gw = (uint32_t)warp * G + blockIdx.x, dyn0 = 2 * W;
-    uint32_t b = gw, bn = gw + W;
     Slot4 a0, a1;
     if (b < p.n_blocks) { load_slot(p.pages, b, lane, a0); load_slot(p.pages, b, lane + 32, a1); }
 
     Scalars S;
-    if (tid == 0) { s_cta_tau = 0ull; s_seed_min = 0xFFFFFFFFu; s_seed_cnt = 0u; s_nflag = 0u; s_nband = 0u; }
+    if (tid == 0) {
+        s_cta_tau = 0ull; s_seed_min = 0xFFFFFFFFu; s_seed_cnt = 0u; s_nflag = 0u; s_nband = 0u;
+        s_next = lo_c + 2u * kWarps;
+    }
     const DevPlan* plan = p.plan;
     if (FUSED) {
         // QueryPipeline::build_plan fused into the scan (src/pipeline.rs:63-74): every CTA builds the
@@ -534,7 +555,7 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
         if (bn < p.n_blocks) { load_slot(p.pages, bn, lane, n0); load_slot(p.pages, bn, lane + 32, n1); }
         const bool more = bn < p.n_blocks;  // warp-uniform
         uint32_t grabbed = 0;
-        if (more && lane == 0) grabbed = atomicAdd(counter, 1u);
+        if (more && lane == 0) grabbed = grab(atomicAdd(&s_next, 1u));
         u64 k0 = 0ull, k1 = 0ull;
         if (block_live(p, b)) {
             k0 = slot_key<MODE>(a0, b * 64 + lane, s_tab, s_rho, S);
@@ -557,7 +578,7 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
             }
         }
         warp_offer(ws, q, lane, L, &s_cta_tau, k0, k1);
-        const uint32_t bnn = more ? __shfl_sync(kFull, grabbed, 0) + dyn0 : bn;
+        const uint32_t bnn = more ? __shfl_sync(kFull, grabbed, 0) : bn;
         b = bn;
         bn = bnn;
         a0 = n0;
