@@ -208,6 +208,27 @@ int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pl
                            uint32_t n_q, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                            const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
                            uint32_t* d_out_counts, uint32_t* d_out_status);
+/* `ScanStats` (src/scan.rs:269-302): blocks scanned, their active vectors, and the survivors of the
+ * prefix bound, of the mid-band + CS-tail bound, of the S4 budget bound, and the pushed ones. */
+typedef struct mrl_scan_stats {
+    uint64_t blocks;
+    uint64_t active_vecs;
+    uint64_t after_prefix;
+    uint64_t after_s1;
+    uint64_t after_s4_budget;
+    uint64_t pushed;
+} mrl_scan_stats;
+/* scan_blocks_stats (src/scan.rs:813-886) for plan q: the results of mrl_scan (host buffers:
+ * shortlist_cand ids and scores, the hit count) and, when `stats` is non-NULL, the prune counters
+ * of src/scan.rs:654-799. The reference evaluates each block's bounds against its shortlist
+ * threshold at block entry, which rises as its serial scan proceeds, so its counts depend on the
+ * block order. Here every block is evaluated against the final threshold (the k-th score when the
+ * scan returned k hits, else -inf): the counts the reference reports once its shortlist is warm,
+ * exact for that threshold (the reference's f32 stage and bound expressions, in its order).
+ * Counting costs one more pass over the segment. Synchronous. */
+int mrl_scan_blocks_stats(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q,
+                   const mrl_scan_cfg* cfg, const uint32_t* time_lo, const uint32_t* time_hi,
+                   uint64_t* out_ids, float* out_scores, uint32_t* out_count, mrl_scan_stats* stats);
 /* ---- fused plan + scan: QueryPipeline::build_plan + scan_segments_into (src/pipeline.rs:63-133) -- */
 /* Build the plans of n_q device queries (row-major n_q x dims f32) into `plans` [0, n_q) and scan
  * the segment with each, in one launch per query: every CTA builds the query's plan in shared

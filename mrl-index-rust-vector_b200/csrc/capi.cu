@@ -752,6 +752,40 @@ int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pl
     return MRL_OK;
 }
 
+int mrl_scan_blocks_stats(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q, const mrl_scan_cfg* cfg,
+                   const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* out_ids, float* out_scores,
+                   uint32_t* out_count, mrl_scan_stats* stats) {
+    if (!ctx || !seg || !plans || !out_ids || !out_scores || !out_count) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg, plans->dims)) return rc;
+    if (q >= plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan index out of range");
+    if (int rc = set_device(ctx)) return rc;
+    const uint32_t k = cfg->shortlist_cand;
+    const size_t ids_b = (size_t)k * sizeof(uint64_t), sc_off = (ids_b + 255) & ~(size_t)255;
+    const size_t cnt_off = (sc_off + (size_t)k * sizeof(float) + 255) & ~(size_t)255, tot_off = cnt_off + 256;
+    if (int rc = ensure_out(ctx, tot_off + sizeof(mrl_scan_stats))) return rc;
+    unsigned char* base = static_cast<unsigned char*>(ctx->tmp_out);
+    uint64_t* d_ids = reinterpret_cast<uint64_t*>(base);
+    float* d_sc = reinterpret_cast<float*>(base + sc_off);
+    uint32_t* d_cnt = reinterpret_cast<uint32_t*>(base + cnt_off);
+    unsigned long long* d_tot = reinterpret_cast<unsigned long long*>(base + tot_off);
+    if (int rc = mrl_scan_device(ctx, seg, plans, q, 1, cfg, time_lo, time_hi, d_ids, d_sc, d_cnt, nullptr)) return rc;
+    if (stats) {
+        if (seg->n_blocks) {
+            if (mrl::launch_scan_stats(make_launch(ctx, seg, plans, q, cfg, time_lo, time_hi), cfg->cs_tolerance, d_cnt,
+                                       d_sc, d_tot, ctx->stream))
+                return cuda_fail(ctx, cudaGetLastError(), "stats launch");
+            MRL_CUDA_TRY(ctx, cudaMemcpyAsync(stats, d_tot, sizeof(mrl_scan_stats), cudaMemcpyDeviceToHost, ctx->stream));
+        } else {
+            std::memset(stats, 0, sizeof(mrl_scan_stats));
+        }
+    }
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_count, d_cnt, sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_ids, d_ids, ids_b, cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out_scores, d_sc, (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return MRL_OK;
+}
+
 int mrl_query_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const float* d_queries, uint32_t n_q, uint32_t dims,
                           const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg,
                           const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,

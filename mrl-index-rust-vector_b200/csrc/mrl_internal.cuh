@@ -241,6 +241,11 @@ int launch_scan_batch(const uint4* pages, const uint2* block_ts, uint32_t n_bloc
 // The fast/exact score difference bound the scan uses for plan p.plan over the segment whose maxima
 // are p.metamax (one float to d_out).
 int launch_score_bound(const ScanLaunch& p, float* d_out, cudaStream_t stream);
+// ScanStats counters (6 u64: blocks, active vectors, survivors after prefix / S1 / S4 budget,
+// pushed) of plan p.plan over the segment, every block pruned against the final shortlist
+// threshold of a scan whose count and scores (device, shortlist k = p.k) are given.
+int launch_scan_stats(const ScanLaunch& p, float cs_tolerance, const uint32_t* d_count, const float* d_scores,
+                      unsigned long long* d_totals, cudaStream_t stream);
 int launch_debug_scores(const ScanLaunch& p, float* d_scores, uint8_t* d_active,
                         int32_t* d_partials, cudaStream_t stream);
 }  // namespace mrl

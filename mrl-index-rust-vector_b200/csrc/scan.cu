@@ -844,6 +844,108 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     }
 }
 
+// ---- ScanStats (src/scan.rs:269-302, 654-799) ----------------------------------------------------
+// The reference counts, per block scanned, its active vectors and the survivors of each stage,
+// every stage pruning against the shortlist threshold tau at block entry with its Cauchy-Schwarz
+// bounds scaled by cs_tolerance. Its serial scan raises tau block by block, so its counts depend on
+// the scan order. The device counts every block against one tau: the shortlist's final threshold
+// (src/scan.rs:396-399: the k-th score once the list is full, else the floor, -inf), which is the
+// threshold every block would see if the scan were fully warmed. The stage values and the bounds
+// are the reference's f32 expressions in its order (exact-mode tables), so the counts are exact.
+struct StatsTotals {
+    unsigned long long blocks, active_vecs, after_prefix, after_s1, after_s4_budget, pushed;
+};
+
+// Survivor bits of one slot after the prefix (bit 0), mid-band + CS-tail (bit 1) and S4 budget
+// (bit 2) stages; 0 when tombstoned. `act` receives whether the slot is active.
+__device__ __forceinline__ uint32_t stats_slot(const Slot4& sl, const float* ft, const float2* rho_tab,
+                                               const Scalars& S, const DevPlan& P, float alpha, float tau,
+                                               bool& act) {
+    const SlotMeta m = slot_meta_tab(sl.c3.z, sl.c3.w, rho_tab);
+    act = !m.tomb;
+    if (m.tomb) return 0u;
+    const uint32_t w[8] = {sl.c0.x, sl.c0.y, sl.c0.z, sl.c0.w, sl.c1.x, sl.c1.y, sl.c1.z, sl.c1.w};
+    if (S.depth == MRL_DEPTH_L0) {  // src/scan.rs:753-790
+        float acc = 0.0f;
+#pragma unroll
+        for (int d = 0; d < kPrefix; ++d)
+            if ((w[d >> 3] >> (4 * (d & 7))) & 8u) acc = __fadd_rn(acc, ft[kTabBw3 + d]);
+        const float ip = __fadd_rn(__fmul_rn(acc, m.scale), __fmul_rn(m.offset, S.prefix_sum));
+        const float x_rest = fmaxf(__half2float(__ushort_as_half((unsigned short)(sl.c3.w & 0xFFFFu))), 0.0f);
+        const float ub = __fadd_rn(ip, __fmul_rn(__fmul_rn(alpha, P.qp.q_after_prefix), x_rest));
+        return ub >= tau ? 7u : 0u;
+    }
+    float acc = 0.0f;  // src/scan.rs:456-505
+#pragma unroll
+    for (int d = 0; d < kPrefix; ++d) acc = __fadd_rn(acc, ft[d * 16 + ((w[d >> 3] >> (4 * (d & 7))) & 15u)]);
+    float sc = S.eden ? __fadd_rn(S.eden_mean_ip, __fmul_rn(m.scale, acc))
+                      : __fadd_rn(__fmul_rn(acc, m.scale), __fmul_rn(m.offset, S.prefix_sum));
+    const float ub0 = __fadd_rn(sc, __fmul_rn(alpha, __fadd_rn(__fmul_rn(P.qp.q_mid_norm, m.mid_n),
+                                                            __fmul_rn(P.qp.q_tail_norm, m.high_n))));  // :508-514
+    uint32_t bits = ub0 >= tau ? 1u : 0u;
+    if (!bits) return 0u;
+    if (S.depth >= MRL_DEPTH_L1) {  // src/scan.rs:520-584
+        const uint32_t b1[4] = {sl.c2.x, sl.c2.y, sl.c2.z, sl.c2.w};
+        float v = S.mid_base;
+#pragma unroll
+        for (int d = 0; d < kRabitq; ++d)
+            if ((b1[d >> 5] >> (d & 31)) & 1u) v = __fadd_rn(v, ft[kTabMidW + d]);
+        if (S.mid_b1) sc = __fadd_rn(sc, __fadd_rn(S.mid_mean_ip, __fmul_rn(m.offset, v)));
+        else sc = __fadd_rn(sc, __fmul_rn(v, m.mid_n));
+        const float ub1 = __fadd_rn(sc, __fmul_rn(__fmul_rn(alpha, P.qp.q_after_s1), m.high_n));
+        if (!(ub1 >= tau)) return bits;
+    }
+    bits |= 2u;
+    if (S.depth == MRL_DEPTH_FULL && P.qp.has_tail_fold && P.qp.s4_abs_budget > 0.0f) {  // :587-607
+        const float ub2 = __fadd_rn(sc, __fmul_rn(__fmul_rn(__fmul_rn(alpha, fmaxf(m.high_n, 1e-6f)), S.w_s4),
+                                                  P.qp.s4_abs_budget));
+        if (!(ub2 >= tau)) return bits;
+    }
+    return bits | 4u;
+}
+
+// One warp per page (two slots per lane); tau from the scan's own results: the k-th score when it
+// returned k hits, else -inf.
+__global__ void __launch_bounds__(kThreads) stats_kernel(const ScanLaunch p, float alpha, const uint32_t* count,
+                                                         const float* scores, StatsTotals* tot) {
+    __shared__ __align__(16) float s_ft[kTabBw3 + kPrefix];
+    __shared__ float2 s_rho[256];
+    __shared__ unsigned long long s_tot[6];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const DevPlan& P = *p.plan;
+    load_exact_tables(p.plan, s_ft);
+    fill_rho_tab(s_rho, tid, kThreads);
+    Scalars S;
+    fill_scalars(p.plan, p.w_s4, p.depth, 1, S);
+    if (tid < 6) s_tot[tid] = 0ull;
+    __syncthreads();
+    const uint32_t n = *count;
+    const float tau = n >= p.k && n > 0 ? scores[p.k - 1] : -INFINITY;
+    unsigned long long c[6] = {0, 0, 0, 0, 0, 0};
+    for (uint32_t b = blockIdx.x * kWarps + warp; b < p.n_blocks; b += gridDim.x * kWarps) {
+        if (!block_live(p, b)) continue;  // warp-uniform
+        Slot4 s0, s1;
+        load_slot(p.pages, b, lane, s0);
+        load_slot(p.pages, b, lane + 32, s1);
+        bool a0, a1;
+        const uint32_t m0 = stats_slot(s0, s_ft, s_rho, S, P, alpha, tau, a0);
+        const uint32_t m1 = stats_slot(s1, s_ft, s_rho, S, P, alpha, tau, a1);
+        const unsigned act = __popc(__ballot_sync(kFull, a0)) + __popc(__ballot_sync(kFull, a1));
+        if (act == 0u) continue;
+        c[0] += 1;
+        c[1] += act;
+        c[2] += __popc(__ballot_sync(kFull, m0 & 1u)) + __popc(__ballot_sync(kFull, m1 & 1u));
+        c[3] += __popc(__ballot_sync(kFull, m0 & 2u)) + __popc(__ballot_sync(kFull, m1 & 2u));
+        c[4] += __popc(__ballot_sync(kFull, m0 & 4u)) + __popc(__ballot_sync(kFull, m1 & 4u));
+    }
+    c[5] = c[4];  // the tail-fold stage adds to scores but prunes nothing: its survivors are pushed
+    if (lane == 0)
+        for (int i = 0; i < 6; ++i)
+            if (c[i]) atomicAdd(&s_tot[i], c[i]);
+    __syncthreads();
+    if (tid < 6 && s_tot[tid]) atomicAdd(reinterpret_cast<unsigned long long*>(tot) + tid, s_tot[tid]);
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) debug_scores_kernel(const ScanLaunch p, float* out,
                                                                 uint8_t* active, int32_t* parts) {
@@ -929,6 +1031,16 @@ int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream) {
     void* args[] = {&arg};
     if (cudaLaunchCooperativeKernel(fn, dim3(ctas), dim3(kThreads), args, smem, stream) != cudaSuccess) return -1;
     return 0;
+}
+
+int launch_scan_stats(const ScanLaunch& p, float cs_tolerance, const uint32_t* d_count, const float* d_scores,
+                      unsigned long long* d_totals, cudaStream_t stream) {
+    if (cudaMemsetAsync(d_totals, 0, sizeof(StatsTotals), stream) != cudaSuccess) return -1;
+    const uint32_t grid = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(((uint64_t)p.n_blocks + kWarps - 1) / kWarps,
+                                                                            148u * 4u));
+    stats_kernel<<<grid, kThreads, 0, stream>>>(p, cs_tolerance, d_count, d_scores,
+                                                reinterpret_cast<StatsTotals*>(d_totals));
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 int launch_debug_scores(const ScanLaunch& p, float* d_scores, uint8_t* d_active, int32_t* d_partials,

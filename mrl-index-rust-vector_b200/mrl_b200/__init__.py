@@ -28,6 +28,8 @@ from .api import (  # noqa: F401
     query_scan,
     scan_blocks,
     scan_blocks_batch,
+    scan_blocks_stats,
+    ScanStats,
     scored_hits_to_row_ids,
     vector_scores,
     score_bound,

@@ -117,6 +117,7 @@ SIGNATURES = {
                              _vp, _vp, _vp, _vp]),
     "mrl_scan_device_static": (_i, [_vp, _vp, _vp, _u32, _u32, C.POINTER(ScanCfgC), _vp, _vp, _vp, _vp, _vp, _vp]),
     "mrl_debug_vector_scores": (_i, [_vp, _vp, _vp, _u32, C.POINTER(ScanCfgC), _vp, _vp, _vp, _vp, _vp]),
+    "mrl_scan_blocks_stats": (_i, [_vp, _vp, _vp, _u32, C.POINTER(ScanCfgC), _vp, _vp, _vp, _vp, _vp, _vp]),
     "mrl_debug_score_bound": (_i, [_vp, _vp, _vp, _u32, C.POINTER(ScanCfgC), C.POINTER(C.c_float)]),
     "mrl_debug_control_words": (_i, [_vp, C.POINTER(_u32)]),
     "mrl_encode_blocks": (_i, [_vp, _vp, _u64, _u32, _vp, _vp, C.POINTER(CodecDesc), _vp]),

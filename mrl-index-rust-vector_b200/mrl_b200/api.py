@@ -469,6 +469,54 @@ def scan_blocks(segment: Segment, plan: QueryPlan, cfg, time_lo=None, time_hi=No
     return [ScoredHit(VectorId.from_u64(int(i)), float(s)) for i, s in zip(ids[0, :n], scores[0, :n])]
 
 
+class ScanStatsC(C.Structure):
+    _fields_ = [("blocks", C.c_uint64), ("active_vecs", C.c_uint64), ("after_prefix", C.c_uint64),
+                ("after_s1", C.c_uint64), ("after_s4_budget", C.c_uint64), ("pushed", C.c_uint64)]
+
+
+@dataclasses.dataclass
+class ScanStats:
+    """`ScanStats` (src/scan.rs:269-302), counted by mrl_scan_blocks_stats against the final shortlist
+    threshold (the counts of a fully warmed scan)."""
+
+    blocks: int = 0
+    active_vecs: int = 0
+    after_prefix: int = 0
+    after_s1: int = 0
+    after_s4_budget: int = 0
+    pushed: int = 0
+
+    def merge(self, other: "ScanStats") -> None:  # src/scan.rs:281-288
+        for f in dataclasses.fields(self):
+            setattr(self, f.name, getattr(self, f.name) + getattr(other, f.name))
+
+    def summary(self) -> str:  # ScanStats::print_summary, src/scan.rs:290-301
+        a = float(max(self.active_vecs, 1))
+        return (f"scan-stats: blocks={self.blocks} active={self.active_vecs}  "
+                f"keep_prefix={100.0 * self.after_prefix / a:.2f}%  keep_s1={100.0 * self.after_s1 / a:.2f}%  "
+                f"keep_s4bud={100.0 * self.after_s4_budget / a:.2f}%  pushed={100.0 * self.pushed / a:.2f}%")
+
+
+def scan_blocks_stats(segment: Segment, plan: QueryPlan, cfg, time_lo=None, time_hi=None, q: int = 0):
+    """`scan_blocks_stats` (src/scan.rs:813-886): the hits of plan q and its ScanStats
+    (mrl_scan_blocks_stats)."""
+    sc = _cfg_of(cfg)
+    c = sc.to_c()
+    k = int(sc.shortlist_cand)
+    ids = np.zeros(k, np.uint64)
+    scores = np.zeros(k, np.float32)
+    count = C.c_uint32(0)
+    st = ScanStatsC()
+    lo, hi = _time_ptrs(time_lo, time_hi)
+    dev = segment.dev
+    check(dev.ptr, dev.lib.mrl_scan_blocks_stats(dev.ptr, segment.ptr, plan.ptr, q, C.byref(c), lo, hi,
+                                          ids.ctypes.data_as(C.c_void_p), scores.ctypes.data_as(C.c_void_p),
+                                          C.byref(count), C.byref(st)))
+    n = int(count.value)
+    hits = [ScoredHit(VectorId.from_u64(int(i)), float(s)) for i, s in zip(ids[:n], scores[:n])]
+    return hits, ScanStats(*(int(getattr(st, f[0])) for f in ScanStatsC._fields_))
+
+
 def vector_scores(segment: Segment, plan: QueryPlan, cfg, q: int = 0, time_lo=None, time_hi=None):
     """Per-slot scores (and fast-mode int32 stage sums) of plan q for every slot of the segment."""
     sc = _cfg_of(cfg)

@@ -376,6 +376,64 @@ def test_control_words_left_zero(ora, dev, corpus768):
     seg.free()
 
 
+def _oracle_stage_counts(ora, blocks, op, ocfg, tau, depth, time_lo=None):
+    """ScanStats from the oracle's per-block stage functions (src/scan.rs:453-634) at one tau."""
+    exp = [0] * 6
+    for b in range(blocks.size // 4096):
+        blk = blocks[b * 4096:(b + 1) * 4096]
+        if time_lo is not None and struct.unpack_from("<I", blk, 4)[0] < time_lo:
+            continue  # temporal skip (src/scan.rs:719-730)
+        act = 64 - bin(struct.unpack_from("<Q", blk, 16)[0]).count("1")
+        if act == 0:
+            continue
+        masks, _ = ora.block_stages(blk, op, ocfg, tau)
+        m = [bin(int(x)).count("1") for x in masks]
+        exp[0] += 1
+        exp[1] += act
+        exp[2] += m[0]
+        exp[3] += m[1]
+        exp[4] += m[2] if depth == 2 else m[1]
+        exp[5] += m[2] if depth == 2 else m[1]
+    return exp
+
+
+@pytest.mark.parametrize("k", [16, 256])
+@pytest.mark.parametrize("depth,alpha", [(2, 1.0), (2, 1.2), (1, 0.9)])
+def test_scan_stats_match_oracle_stages(ora, dev, corpus768, depth, alpha, k):
+    """mrl_scan_blocks_stats (scan_blocks_stats): the hits equal the oracle's scan and the ScanStats
+    counters equal the sums of the oracle's per-block stage masks (the reference's stage functions
+    and Cauchy-Schwarz bounds) evaluated at the final shortlist threshold, with and without the
+    temporal filter."""
+    M = mb()
+    blocks = corpus768["eden"]
+    mean = corpus768["mean"]
+    seg = M.Segment.upload(blocks, dev)
+    for qi, q in enumerate(corpus768["qs"][:2]):
+        gp = M.QueryPlan.from_query_eden(q, 768, fit(mean), dev=dev)
+        op = ora.plan_build(q, eden_mean=mean)
+        lo = None if qi == 0 else 64 * 9
+        cfg = M.ScanConfig(shortlist_cand=k, strata_depth=M.StrataDepth(depth), cs_tolerance=alpha)
+        hits, st = M.scan_blocks_stats(seg, gp, cfg, time_lo=lo)
+        ocfg = ora.scan_cfg(k=k, strata_depth=depth, cs_tolerance=alpha, temporal_filter_enable=True)
+        rid, rsc = ora.scan_blocks(blocks, op, ocfg, time_lo=lo, threads=4)
+        assert [h.id.as_u64() for h in hits] == [int(i) for i in rid]
+        tau = float(rsc[-1]) if len(rsc) == k else float("-inf")
+        exp = _oracle_stage_counts(ora, blocks, op, ocfg, tau, depth, time_lo=lo)
+        got = [st.blocks, st.active_vecs, st.after_prefix, st.after_s1, st.after_s4_budget, st.pushed]
+        assert got == exp, (got, exp)
+        assert st.pushed >= len(hits)  # every hit survived every bound
+        gp.free()
+    # L0Only: one bound, every counter equal; an empty segment counts nothing
+    gp = M.QueryPlan.from_query_eden(corpus768["qs"][0], 768, fit(mean), dev=dev)
+    _, st0 = M.scan_blocks_stats(seg, gp, M.ScanConfig(shortlist_cand=k, strata_depth=M.StrataDepth.L0_ONLY))
+    assert st0.after_prefix == st0.after_s1 == st0.after_s4_budget == st0.pushed <= st0.active_vecs
+    empty = M.Segment.upload(np.zeros(0, np.uint8), dev)
+    hits_e, st_e = M.scan_blocks_stats(empty, gp, M.ScanConfig(shortlist_cand=k))
+    assert hits_e == [] and st_e == M.ScanStats()
+    gp.free()
+    seg.free()
+
+
 def test_edge_cases(ora, dev):
     M = mb()
     docs = ora.synth_docs(4, 64 * 3, 384)
