@@ -92,8 +92,9 @@ struct mrl_plans {
     uint32_t dims = 0;
 };
 
-// NVLink exchange: this rank's area on this GPU (its record for both buffer parities, then one
-// flag word per parity) and the mapped areas of the other ranks of the node.
+// NVLink exchange: this rank's area on this GPU (for both buffer parities, one receive record per
+// sending rank, then one flag word per parity and sender) and the mapped areas of the other ranks
+// of the node, into which this rank pushes its record and raises its flags.
 struct mrl_exchange {
     int device = 0;
     uint32_t world = 0, rank = 0, k = 0;
@@ -102,7 +103,8 @@ struct mrl_exchange {
     unsigned char* area[mrl::kMaxRanks] = {};    // every rank's area (area[rank] == local)
     uint32_t epoch = 0;
     bool opened = false;
-    size_t bytes() const { return 2 * rb + 16; }
+    size_t flags_off() const { return 2 * (size_t)world * rb; }
+    size_t bytes() const { return flags_off() + ((2 * (size_t)world * sizeof(unsigned) + 15) & ~(size_t)15); }
 };
 
 namespace {
@@ -985,9 +987,11 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
     p.xch_rank = ex->rank;
     p.xch_epoch = epoch;
     for (uint32_t w = 0; w < ex->world; ++w) {
-        p.xch_rec[w] = ex->area[w] + parity * ex->rb;
-        p.xch_flag[w] = reinterpret_cast<unsigned*>(ex->area[w] + 2 * ex->rb) + parity;
+        p.xch_rec[w] = ex->area[w] + (parity * ex->world + ex->rank) * ex->rb;
+        p.xch_flag[w] = reinterpret_cast<unsigned*>(ex->area[w] + ex->flags_off()) + parity * ex->world + ex->rank;
     }
+    p.xch_recv = ex->local + parity * ex->world * ex->rb;
+    p.xch_flag_in = reinterpret_cast<const unsigned*>(ex->local + ex->flags_off()) + parity * ex->world;
     if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     return MRL_OK;
 }

@@ -205,14 +205,18 @@ struct ScanLaunch {
     const float* mid_mean;
     uint64_t eden_seed, mid_seed;
     DevPlan* plan_out;
-    // NVLink exchange (xch_world > 0): each rank's top-k record of this query stays in its own
-    // exchange area (buffer parity xch_epoch & 1); the last CTA completes this rank's record,
-    // raises its flag (release, system scope), waits (bounded) for every other rank's flag of
-    // this epoch, reads their records over NVLink and merges all into out_* (the global top-k)
+    // NVLink exchange (xch_world > 0), by pushes: every rank's area holds, per buffer parity
+    // (xch_epoch & 1), one receive record and one flag word per sending rank. This rank's CTAs store
+    // their entries of its top-k into its record slot in every rank's area (peer stores over NVLink
+    // for the others); the last CTA adds the count, raises this rank's flag in every other area
+    // (release, system scope), waits (bounded) for the other ranks' flags in its own area, and
+    // merges the records there, all in local memory, into out_* (the global top-k)
     uint32_t xch_world, xch_rank, xch_epoch;
     uint32_t xch_tree;  // set by launch_scan: merge as a pairwise tree (room for its buffers)
-    const unsigned char* xch_rec[kMaxRanks];  // every rank's record of this parity
-    unsigned int* xch_flag[kMaxRanks];        // every rank's flag word of this parity
+    unsigned char* xch_rec[kMaxRanks];   // this rank's record slot in rank w's area (this parity)
+    unsigned int* xch_flag[kMaxRanks];   // this rank's flag word in rank w's area (this parity)
+    const unsigned char* xch_recv;       // this parity's receive records in this rank's area, by sender
+    const unsigned int* xch_flag_in;     // this parity's flag words in this rank's area, by sender
 };
 int scan_ctas(int device_sms);
 size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t xch_world, uint32_t mode);

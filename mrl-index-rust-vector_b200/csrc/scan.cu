@@ -371,28 +371,42 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 }
 
 // Last step of the NVLink exchange, by the one CTA after this rank's record is complete in its own
-// area: raise this rank's flag (the release makes the record visible to the other GPUs), wait
-// (bounded, ~2-3 s) for every other rank's flag of this epoch, copy all records into shared memory
-// (`smem`, at least xch_world records; the others' over NVLink) and merge them into the
+// slot of its own area: push the record into this rank's slot of every other rank's area (peer
+// stores over NVLink), raise this rank's flag there (release, system scope), wait (bounded, ~2-3 s)
+// for every other rank's flag of this epoch in this rank's own area, copy all records of this area
+// into shared memory (`smem`, at least xch_world records; local loads only) and merge them into the
 // outputs. Status bit 2 reports a timeout.
 __device__ void xch_publish_and_merge(const ScanLaunch& p, unsigned char* smem, int* s_ok, unsigned status) {
     const int tid = threadIdx.x;
     const size_t rb = MRL_MERGE_RECORD_BYTES(p.k), words = rb / 16;
+    const unsigned nw = (unsigned)words;
+    __syncthreads();
+    {
+        // this rank's record (local) into its slot in every other rank's area: posted stores, all
+        // threads, so the copies to all peers are in flight at once
+        const uint4* src = reinterpret_cast<const uint4*>(p.xch_rec[p.xch_rank]);
+        const unsigned total = (p.xch_world - 1u) * nw;
+        for (unsigned i = tid; i < total; i += kThreads) {
+            unsigned w = i / nw;
+            w += w >= p.xch_rank ? 1u : 0u;
+            reinterpret_cast<uint4*>(p.xch_rec[w])[i % nw] = __ldcg(src + i % nw);
+        }
+    }
     __syncthreads();
     if (tid < 32) {
-        // warp 0: lane 0 publishes this rank's flag; lane r polls rank r's flag, so the waits for
-        // all ranks overlap (one NVLink round trip when every record is already there)
-        if (tid == 0) {
-            __threadfence();
-            st_release_sys(p.xch_flag[p.xch_rank], p.xch_epoch);
+        // warp 0: lane w raises this rank's flag in rank w's area; lane s polls rank s's flag in
+        // this area, so all waits overlap and every poll is a local load
+        const bool peer = (unsigned)tid < p.xch_world && (unsigned)tid != p.xch_rank;
+        if (peer) {
+            __threadfence_system();
+            st_release_sys(p.xch_flag[tid], p.xch_epoch);
         }
-        const bool mine = (unsigned)tid < p.xch_world && (unsigned)tid != p.xch_rank;
-        bool arrived = !mine;
+        bool arrived = !peer;
         unsigned it = 0;
         while (!__all_sync(kFull, arrived)) {
-            if (!arrived) arrived = ld_acquire_sys(p.xch_flag[tid]) == p.xch_epoch;
-            if (++it > (1u << 21)) break;  // ~2-3 s of remote polls
-            if (it > 64) __nanosleep(256);
+            if (!arrived) arrived = ld_acquire_sys(p.xch_flag_in + tid) == p.xch_epoch;
+            if (++it > (1u << 22)) break;  // ~2-3 s
+            if (it > 256) __nanosleep(128);
         }
         const bool ok = __all_sync(kFull, arrived);
         if (tid == 0) *s_ok = ok ? 1 : 0;
@@ -403,20 +417,21 @@ __device__ void xch_publish_and_merge(const ScanLaunch& p, unsigned char* smem, 
         return;
     }
     {
-        // every rank's record into shared memory; each thread has up to four (mostly remote) loads
-        // in flight before storing, instead of one NVLink round trip per rank in turn
-        const unsigned nw = (unsigned)words, total = p.xch_world * nw;
+        // every rank's record (this area's receive slots) into shared memory, four loads in flight per
+        // thread before their stores
+        const unsigned total = p.xch_world * nw;
+        const uint4* src = reinterpret_cast<const uint4*>(p.xch_recv);
         for (unsigned i0 = tid; i0 < total; i0 += 4u * kThreads) {
             uint4 x[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const unsigned i = i0 + (unsigned)j * kThreads;
-                if (i < total) x[j] = __ldcg(reinterpret_cast<const uint4*>(p.xch_rec[i / nw]) + (i % nw));
+                if (i < total) x[j] = __ldcg(src + i);
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const unsigned i = i0 + (unsigned)j * kThreads;
-                if (i < total) reinterpret_cast<uint4*>(smem + (i / nw) * rb)[i % nw] = x[j];
+                if (i < total) reinterpret_cast<uint4*>(smem)[i] = x[j];
             }
         }
     }
@@ -758,8 +773,8 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
         }
         const u64 okey = kFast ? xmine[tid < 32 ? tid : 0] : mine[tid < 32 ? tid : 0];
         if (p.xch_world) {
-            // this rank's top-k into its own record (local memory); peers pull it over NVLink after
-            // the release flag below
+            // this rank's top-k into its own record slot (local memory); the last CTA pushes the
+            // completed record to the other ranks
             const size_t kk = p.k;
             if ((unsigned)tid < L && r < p.k) {
                 const uint32_t ord = key_ordinal(okey);
