@@ -188,9 +188,9 @@ struct ScanLaunch {
     // scratch (owned by the context; zero-initialised once, left zeroed by every launch)
     unsigned long long* cta_keys;  // ctas * 32: each CTA's exact top-list_len keys (scan order)
     unsigned long long* cta_xkeys; // ctas * 32: fast mode, the same entries' exact-mode keys
-    unsigned int* ctl;             // [0] page counter, [1] barrier count, [2] barrier generation,
+    unsigned int* ctl;             // [0] page counter, [1] barrier arrivals, [2..4] unused,
                                    // [5] barrier timeout, [6] CTAs done (exchange), [7] CTAs exited;
-                                   // the last CTA to exit zeroes all but [2]
+                                   // the last CTA to exit zeroes [0], [1], [5], [6], [7]
     const float* metamax;          // the segment's 4 meta-factor maxima (launch_metamax)
     uint8_t* owner;                // n_blocks: CTA that scored each page
     uint64_t* out_ids;

@@ -4,33 +4,37 @@
 // live slot of a segment for one plan and leaves the top-k (by score, ties to the lower slot
 // ordinal) in the output buffers.
 //
-// Work split: a persistent cooperative grid of one 512-thread CTA per SM. Warps take pages from a
-// global counter (one atomic per warp and page, fetched one page ahead) and score two slots per
-// lane, reading each slot's 64 bytes of the vector-major page layout with four coalesced 16-byte
-// loads per slot, prefetching the next page while scoring the current one.
+// Work split: a persistent cooperative grid of one 512-thread CTA per SM. The first 7/8 of the
+// pages are split into one contiguous range per CTA, whose warps take pages from a shared-memory
+// counter; the last 1/8 is handed out one page at a time from a global counter to CTAs that have
+// finished their range. Each warp scores two slots per lane, reading each slot's 64 bytes of the
+// vector-major page layout with four coalesced 16-byte loads, and loads the next page while it
+// scores the current one.
 //
 // Scoring (one thread per slot):
 //   * MRL_MODE_FAST — every stage inner product is an exact int32 sum of table entries held in
 //     shared memory: 64 per-dimension 16-entry prefix tables indexed by the slot's 4-bit level, and
 //     5-bit-window tables over the 128 mid-band and 64 folded-tail bits. Tables have <= 32 entries,
-//     so a warp-uniform table index never causes a shared-memory bank conflict. The integer sums
-//     are converted to f32 once and combined with the reference's f32 formulas.
+//     so a warp-uniform table index never causes a shared-memory bank conflict. Each fast score is
+//     within a proven bound E of the slot's exact score; the fast scores only choose candidates,
+//     which are rescored in the reference's f32 order before the final ranking, so the results
+//     are the exact mode's.
 //   * MRL_MODE_EXACT — the reference's f32 loops in the reference order (sequential adds of
 //     rounded products), giving bit-identical scores.
 // Both compute the full score of every live slot (no stage pruning). Under the reference's
 // exactness condition (cs_tolerance >= 1 and w_s4*sqrt(2/pi)*sqrt(B) <= cs_tolerance, true for
 // the defaults) every stage bound of src/scan.rs:453-607 is >= the full score, so the reference's
 // final shortlist is exactly the top-k by full score; computing all scores reproduces it without
-// the order-dependent threshold.
+// the order-dependent threshold. Configurations outside that condition are refused by the host.
 //
 // Selection: each warp keeps a sorted top-32 of its keys in registers (one key per lane) and
 // filters new keys against max(its own list_len-th key, a CTA-wide bound in shared memory);
 // survivors go through a per-warp shared-memory queue and are merged 32 at a time with warp
-// bitonic networks. Each CTA tree-merges its warps' lists and publishes its exact top-`list_len`
-// to global scratch; after a bounded grid barrier every CTA ranks its own list keys against all
-// CTA lists (binary search) and writes the keys ranked below k straight to the output. The union
-// of per-CTA lists contains the global top-k unless some CTA's full list ends inside it; such
-// CTAs raise a flag, and the last CTA (atomic ticket) rescans their pages (owner[]) and redoes
+// bitonic networks. Each CTA tree-merges its warps' lists and publishes its top-`list_len` (fast
+// mode: with each entry's exact key) to global scratch; after a bounded grid barrier every CTA
+// ranks its own list keys against all CTA lists (binary search) and writes the keys ranked below
+// k straight to the output. The union of per-CTA lists contains the global top-k unless some
+// CTA's full list ends inside it; then CTA 0 alone rescans those CTAs' pages (owner[]) and redoes
 // the selection by radix select + bitonic sort, so the result is exact for every input (status
 // bit 0 reports it).
 #include <algorithm>
@@ -280,26 +284,24 @@ __device__ __forceinline__ void reselect(const ScanLaunch& p, const int* tab, co
     if (tid == 0) *p.out_count = ng;
 }
 
-// Grid-wide barrier (the launch is cooperative, so all CTAs are co-resident). Sense reversal
-// through a generation word; the wait is bounded and reports a timeout instead of hanging.
+// Grid-wide barrier, once per launch (the launch is cooperative, so all CTAs are co-resident).
+// Control word 1 counts arrivals; it starts every launch at 0 because the last CTA to exit zeroes
+// it. The arrival is an acquire-release add, so the last CTA to arrive, and every CTA that reads
+// the full count with an acquire load, sees what the others published before they arrived. The
+// wait is bounded and reports a timeout instead of hanging.
 __device__ bool grid_barrier(unsigned* ctl, unsigned G, volatile int* s_ok) {
     __syncthreads();
     if (threadIdx.x == 0) {
         unsigned* count = ctl + 1;
-        unsigned* gen = ctl + 2;
-        const unsigned my_gen = atomicAdd(gen, 0u);
-        __threadfence();
+        unsigned before;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(count) : "memory");
         int ok = 1;
-        if (atomicAdd(count, 1u) == G - 1) {
-            atomicExch(count, 0u);
-            __threadfence();
-            atomicAdd(gen, 1u);
-        } else {
+        if (before + 1u < G) {
             unsigned it = 0;
             while (true) {
-                unsigned g;
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(gen) : "memory");
-                if (g != my_gen) break;
+                unsigned c;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(c) : "l"(count) : "memory");
+                if (c >= G) break;
                 if (++it > (1u << 22)) { ok = 0; atomicExch(ctl + 5, 1u); break; }  // ~0.3 s
                 if (it > 256) __nanosleep(64);
             }
@@ -339,13 +341,6 @@ __device__ __forceinline__ void load_exact_tables(const DevPlan* __restrict__ P,
     for (int i = tid; i < kFold; i += kThreads) ft[kTabTailW + i] = P->tail_w[i];
     for (int i = tid; i < kPrefix; i += kThreads) ft[kTabBw3 + i] = P->qp.bit_weights[i][3];
 }
-
-// Page schedule: each warp's first two pages are static (pages gw and gw + W for global warp gw of
-// W), so the launch starts without contending on one atomic; later pages are handed out
-// dynamically from 2W on (one atomic per warp and page, issued by lane 0 at the top of an
-// iteration and read by the warp only after the current page is scored, so its latency overlaps
-// the scoring), so every warp finishes at about the same time. owner[] records which CTA scored
-// each page for the rare rescan.
 
 // Number of keys greater than x in lst[0..n), 1 <= n <= 32, sorted descending (keys unique, empty
 // slots 0 at the end): a branch-free binary lift of six fixed steps (clamped loads, selects), so
@@ -843,18 +838,20 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     scan_body<MODE, FUSED>(p);
     // Exit ticket: the last CTA to leave zeroes the control words (page counter, barrier count,
     // exchange count, timeout flag, the ticket), so the next launch on this scratch starts clean
-    // whichever path this one took, a bounded wait that ran out included. The barrier generation
-    // only ever advances and keeps its value.
+    // whichever path this one took, a bounded wait that ran out included. The ticket is an
+    // acquire-release add: every CTA's uses of the words come before its ticket, and the last
+    // ticket's holder sees them all before it stores the zeros, which the next launch sees at the
+    // kernel boundary.
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        if (atomicAdd(p.ctl + 7, 1u) == gridDim.x - 1) {
+        unsigned before;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(p.ctl + 7) : "memory");
+        if (before == gridDim.x - 1) {
             p.ctl[0] = 0u;
             p.ctl[1] = 0u;
             p.ctl[5] = 0u;
             p.ctl[6] = 0u;
-            __threadfence();
-            atomicExch(p.ctl + 7, 0u);
+            p.ctl[7] = 0u;
         }
     }
 }
