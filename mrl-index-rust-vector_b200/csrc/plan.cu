@@ -5,7 +5,7 @@
 namespace mrl {
 namespace {
 
-constexpr int kPlanKernelThreads = 512;  // four warps build the plan's branches, all fill its tables
+constexpr int kPlanKernelThreads = 512;  // six warps build the plan's branches, all fill its tables
 
 __global__ void __launch_bounds__(kPlanKernelThreads)
 plan_kernel(const float* __restrict__ queries, uint32_t dims, uint32_t prefix_codec,
@@ -13,8 +13,9 @@ plan_kernel(const float* __restrict__ queries, uint32_t dims, uint32_t prefix_co
             const float* __restrict__ mid_mean, uint64_t mid_seed, DevPlan* __restrict__ plans) {
     extern __shared__ float s_q[];  // dims floats
     __shared__ planb::PlanShared sh;
-    planb::plan_inputs(queries + (size_t)blockIdx.x * dims, dims, eden_mean, mid_mean, s_q, sh);
-    planb::build_plan(dims, prefix_codec, mid_codec, eden_seed, mid_seed, plans + blockIdx.x, s_q, sh, planb::kNeedAll);
+    planb::plan_inputs(queries + (size_t)blockIdx.x * dims, dims, eden_mean, mid_mean, eden_seed, mid_seed, s_q, sh);
+    planb::build_plan(dims, prefix_codec, mid_codec, plans + blockIdx.x, s_q, sh, planb::kNeedAll,
+                      planb::plan_dest(plans + blockIdx.x));
 }
 
 }  // namespace

@@ -1,14 +1,16 @@
 // plan_build.cuh — the query-side plan build (QueryPlan::from_query_codec, src/scan.rs:105-266) as
-// a device function run by a whole CTA (at least 128 threads), shared by the standalone plan kernel
+// a device function run by a whole CTA (at least 192 threads), shared by the standalone plan kernel
 // (plan.cu) and the scan kernel's fused plan prologue (scan.cu).
 //
-// Four warps build independent parts of the plan (prefix, mid band, folded tail, long reductions),
-// then every thread of the CTA fills the tables. FWHTs run on warp shuffles (each
-// butterfly output depends only on its two inputs, so the values equal the sequential loop's),
-// sequential reductions run on one lane in the reference's order, and every f32 operation is an
-// explicit round-to-nearest intrinsic (the library is compiled with -fmad=false) so the plan is
-// bit-identical to the reference arithmetic. The build also makes the two scoring-table sets the
-// scan uses:
+// The Rademacher signs are computed while the query loads are in flight; six warps then build
+// independent parts of the plan (prefix, mid band, folded tail, long reductions, the raw-query
+// sums), and every thread of the CTA fills the tables. FWHTs run on warp shuffles (each butterfly
+// output depends only on its two inputs, so the values equal the sequential loop's); each
+// sequential reduction runs on one lane in the reference's order over addends the warp formed in
+// parallel; every f32 operation is an explicit round-to-nearest intrinsic (the library is compiled
+// with -fmad=false), so the plan is bit-identical to the reference arithmetic. The build also makes
+// the two scoring-table sets the scan uses, written either into the plan or straight into a scan's
+// shared-memory tables:
 //   * fast mode: per-stage int32 tables whose exact integer sums replace the f32 loops; entries
 //     are rint(v * 2^shift) of exact double products, with shift chosen so that every stage sum
 //     stays below 2^30 in magnitude;
@@ -20,19 +22,28 @@
 namespace mrl {
 namespace planb {
 
-constexpr int kPlanThreads = 128;
-
 __device__ __forceinline__ float f_add(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ float f_sub(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ float f_mul(float a, float b) { return __fmul_rn(a, b); }
+
+// Correctly rounded f32 values of the reference's constant expressions: 1/sqrt(64), 1/sqrt(128),
+// 2/pi (pi rounded to f32 first), sqrt(2/pi)/sqrt(128) (src/rotate.rs:46-49) and sqrt(2/pi)/8
+// (src/rotate.rs:124-126), each operation rounded to nearest as the reference's f32 arithmetic
+// does. IEEE division and square root are correctly rounded, so these equal what __fdiv_rn and
+// __fsqrt_rn compute from the same operands.
+constexpr float kInvSqrt64 = 0x1p-3f;
+constexpr float kInvSqrt128 = 0x1.6a09e6p-4f;
+constexpr float kRabitqScale = 0x1.20dd74p-4f;
+constexpr float kTailScale = 0x1.988452p-4f;
 
 // One fwht_inplace (src/rotate.rs:13-33) over n = 32*R values held by one warp, element
 // lane + 32*r in v[r]. Stage h pairs elements j and j+h (bit h of j clear) into (x+y, x-y): for
 // h < 32 the partner sits in lane ^ h of the same register, for h >= 32 in register r ^ (h/32) of
 // the same lane. Each output is computed from the same two operands as the sequential loop, so
-// the values are identical.
+// the values are identical. The final scale is 1/sqrt(n) rounded to f32.
 template <int R>
 __device__ __forceinline__ void fwht_warp(float (&v)[R], int lane) {
+    static_assert(R == 2 || R == 4, "64 or 128 values");
 #pragma unroll
     for (int h = 1; h < 32; h <<= 1) {
 #pragma unroll
@@ -52,7 +63,7 @@ __device__ __forceinline__ void fwht_warp(float (&v)[R], int lane) {
             }
         }
     }
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)(32 * R)));
+    const float scale = R == 2 ? kInvSqrt64 : kInvSqrt128;
 #pragma unroll
     for (int r = 0; r < R; ++r) v[r] = f_mul(v[r], scale);
 }
@@ -63,19 +74,34 @@ __device__ __forceinline__ int stage_shift(double maxabs, int count) {
     frexp(maxabs * (double)count, &k);
     return 30 - k;
 }
+// 2^e as a double (exact for the shifts a plan uses; ldexp outside the normal range)
+__device__ __forceinline__ double pow2(int e) {
+    return e >= -1022 && e <= 1023 ? __longlong_as_double((long long)(1023 + e) << 52) : ldexp(1.0, e);
+}
 // rint(v * 2^shift): `pow2` = 2^shift exactly, so the product is exact and the conversion rounds
 // to nearest-even once.
 __device__ __forceinline__ int32_t fix(double v, double pow2) { return __double2int_rn(__dmul_rn(v, pow2)); }
 
-__device__ __forceinline__ double warp_max(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
+// Largest |x| over the warp, as a double, as fmax over the lanes would give it (NaN lanes ignored;
+// 0 if every lane is NaN or zero): nonnegative floats order like their bit patterns. fmaxf also
+// ignores a NaN operand, so per-lane maxima taken with it keep that rule.
+__device__ __forceinline__ double warp_max_abs(float x) {
+    const float a = fabsf(x);
+    const unsigned b = a == a ? __float_as_uint(a) : 0u;
+    return (double)__uint_as_float(__reduce_max_sync(0xffffffffu, b));
 }
 __device__ __forceinline__ double warp_sum(double v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
+}
+// One reference-order sequential f32 sum per lane: acc = ((0 + row[0]) + row[1]) + ... A lane
+// that subtracts holds the negated terms (x - y and x + (-y) round identically).
+__device__ __forceinline__ float lane_chain(const float* row, int len) {
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int d = 0; d < len; ++d) acc = f_add(acc, row[d]);
+    return acc;
 }
 // A double sum of nonnegative terms rounded up to f32 with room for the double roundings: the
 // error-bound magnitudes stored in the plan (err_p, err_1, err_4, err_0).
@@ -89,7 +115,9 @@ __device__ __forceinline__ int32_t window_entry(const int32_t* fx, int g, int m)
     const int w = min(5, DIMS - 5 * g);
     if (m >= (1 << w)) return 0;
     int32_t sum = 0;
-    for (int i = 0; i < w; ++i) sum += fx[2 * (5 * g + i) + ((m >> i) & 1)];
+#pragma unroll
+    for (int i = 0; i < 5; ++i)
+        if (i < w) sum += fx[2 * (5 * g + i) + ((m >> i) & 1)];
     return sum;
 }
 
@@ -97,14 +125,36 @@ __device__ __forceinline__ int32_t window_entry(const int32_t* fx, int g, int m)
 // over 4 dims instead of 5, so the batched scan's stage sums are the same integers.
 __device__ __forceinline__ int32_t window4_entry(const int32_t* fx, int g, int m) {
     int32_t sum = 0;
+#pragma unroll
     for (int i = 0; i < 4; ++i) sum += fx[2 * (4 * g + i) + ((m >> i) & 1)];
     return sum;
 }
 
 // What a plan build writes: kNeedAll = every field of DevPlan (the stored plan); a scan that only
 // needs its own mode's tables asks for kNeedFast (+ kNeedL0 at depth L0Only) or kNeedExact. The
-// scalars, shifts, bit weights, mid_w and tail_w are always written.
+// scalars and shifts are always written to the plan; the tables go where PlanDest points.
 constexpr uint32_t kNeedFast = 1u, kNeedExact = 2u, kNeedL0 = 4u, kNeedBatch = 8u, kNeedAll = 0xFu;
+
+// Where the build writes its scoring tables: the plan's own arrays (plan_dest), or a scan's
+// shared-memory tables directly. bw3 (bit_weights[d][3], contiguous) is null for the plan, whose
+// bit_weights hold all four columns.
+struct PlanDest {
+    int32_t* lut_prefix;
+    int32_t* lut_s1;
+    int32_t* lut_s4;
+    int32_t* lut_l0;
+    float* fp_prefix;
+    float* mid_w;
+    float* tail_w;
+    float* bw3;
+};
+__device__ __forceinline__ PlanDest plan_dest(DevPlan* P) {
+    return PlanDest{P->lut_prefix, P->lut_s1, P->lut_s4, P->lut_l0, P->fp_prefix, P->mid_w, P->tail_w, nullptr};
+}
+
+constexpr int kSigns = kPrefix + kRabitq + kFoldBlocks * kPrefix;  // 768
+// rows of PlanShared::terms: the addends of the reference-order sequential sums
+enum { kRowL1, kRowSum, kRowIp, kRowMs, kRowMip, kRowBase, kRowB1, kRowTb, kRowBud, kRows };
 
 // Shared scratch of one plan build (besides the dims-float query copy).
 struct PlanShared {
@@ -113,49 +163,67 @@ struct PlanShared {
     float rq[kRabitq];
     float mq[kRabitq];
     float tf[kFold];
-    int32_t fx[2 * (kRabitq + kFold)];  // fixed 1-bit stage values, see build_window_table
+    int32_t fx[2 * (kRabitq + kFold)];  // fixed 1-bit stage values, see window_entry
     float scal[16];
     float cb[16];
     float w[kPrefix];  // EDEN prefix weight per dim: rot[d] / sqrt(64)
     double pw[2];      // 2^shift of the prefix and L0 tables
+    // Rademacher signs: EDEN prefix rotation (64), EdenB1 mid-band rotation (128), tail fold
+    // blocks (9 x 64)
+    float sg[kSigns];
+    float terms[kRows][kRabitq];
 };
 
-// The build's inputs into shared memory: the query, the codec centres, the b=4 codebook. Every
-// thread of the CTA calls it; build_plan synchronises before reading them.
+// Sign t of PlanShared::sg: rademacher_diag (src/eden.rs:75-88) of the prefix and mid band, and
+// tail_rademacher (src/rotate.rs:53-67) of fold block b, dim d.
+__device__ __forceinline__ float plan_sign(int t, uint64_t eden_seed, uint64_t mid_seed) {
+    if (t < kPrefix) return sign_hash(eden_seed, (uint64_t)t);
+    if (t < kPrefix + kRabitq) return sign_hash(mid_seed, (uint64_t)(t - kPrefix));
+    const int f = t - kPrefix - kRabitq;
+    return sign_hash((uint64_t)(f / kPrefix), (uint64_t)(f % kPrefix));
+}
+
+// The build's inputs into shared memory: the query, the codec centres, the b=4 codebook, and the
+// Rademacher signs (computed while the loads are in flight). Every thread of the CTA calls it;
+// build_plan synchronises before reading them.
 __device__ __forceinline__ void plan_inputs(const float* __restrict__ q, uint32_t dims, const float* __restrict__ eden_mean,
-                                            const float* __restrict__ mid_mean, float* s_q, PlanShared& sh) {
+                                            const float* __restrict__ mid_mean, uint64_t eden_seed, uint64_t mid_seed,
+                                            float* s_q, PlanShared& sh) {
     const int tid = threadIdx.x, nthr = blockDim.x;
-    // the loads are issued before the stores that consume them, so their latencies overlap
+    // the loads are issued before the work and stores that consume them, so their latencies overlap
     float m = 0.0f, c = 0.0f;
     if (tid < kPrefix + kRabitq) {  // either centre array may be NULL
         const float* src = tid < kPrefix ? eden_mean : mid_mean;
         m = src ? __ldg(src + (tid < kPrefix ? tid : tid - kPrefix)) : 0.0f;
     }
     if (tid < 16) c = g_lloyd_b4[tid];
-    for (uint32_t i0 = tid; i0 < dims; i0 += 2u * nthr) {
-        const uint32_t i1 = i0 + nthr;
-        const float v0 = __ldg(q + i0);
-        const float v1 = i1 < dims ? __ldg(q + i1) : 0.0f;
-        s_q[i0] = v0;
-        if (i1 < dims) s_q[i1] = v1;
-    }
+    const uint32_t i0 = tid, i1 = tid + nthr;
+    const float v0 = i0 < dims ? __ldg(q + i0) : 0.0f;
+    const float v1 = i1 < dims ? __ldg(q + i1) : 0.0f;
+    for (int t = tid; t < kSigns; t += nthr) sh.sg[t] = plan_sign(t, eden_seed, mid_seed);
+    if (i0 < dims) s_q[i0] = v0;
+    if (i1 < dims) s_q[i1] = v1;
+    for (uint32_t i = tid + 2u * nthr; i < dims; i += nthr) s_q[i] = __ldg(q + i);
     if (tid < kPrefix + kRabitq) sh.mean[tid] = m;
     if (tid < 16) sh.cb[tid] = c;
 }
 
-// Phase A, threads 0..127 in four warp roles (the plan branches are independent until the final
-// scalars):
-//   warp 0: prefix — EDEN query rotation, prefix scalars, prefix weights and the prefix/L0 shifts;
-//   warp 1: mid band — RaBitQ and EdenB1 rotations, their scalars, mid_w, the S1 shift and fixed
-//           values;
-//   warp 2: folded tail — fold, rotation, tail scalars, tail_w, the S4 shift and fixed values;
-//   warp 3: q_tail_sq (the longest sequential sum) and, for a full plan, rabitq_lut.
-// Phase B, every thread of the CTA: the 1024-entry tables `need` asks for and the window tables.
-// Every thread of the CTA (at least 128) must call it, after plan_inputs; P may be global or shared
+// Phase A, threads 0..191 in six warp roles (independent until phase B):
+//   warp 0: prefix — EDEN query rotation, bit weights, prefix weights and the prefix shift;
+//   warp 1: mid band — RaBitQ and EdenB1 rotations, mid_w, the S1 shift and fixed values, then the
+//           rabitq_base and EdenB1 base sums;
+//   warp 2: folded tail — fold, rotation, tail_w, the S4 shift and fixed values, then the
+//           tail_fold_base and s4_abs_budget sums;
+//   warp 3: q_tail_sq (the longest sequential sum) and rabitq_lut, for a full plan only;
+//   warp 4: the prefix sums of the raw query (prefix_l1, prefix_sum, eden_mean_ip) and the L0 shift;
+//   warp 5: the mid-band sums of the raw query (q_mid_sq, eden_mid_mean_ip).
+// Each sequential sum keeps the reference's order: the warp first forms its addends in parallel,
+// then one lane per sum adds them in sequence (lane_chain).
+// Phase B, every thread of the CTA: the tables `need` asks for, written through `dst`.
+// Every thread of the CTA (at least 192) must call it, after plan_inputs; P may be global or shared
 // memory, s_q holds the dims floats plan_inputs loaded.
-__device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec, uint32_t mid_codec,
-                                           uint64_t eden_seed, uint64_t mid_seed, DevPlan* P, float* s_q,
-                                           PlanShared& sh, uint32_t need) {
+__device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec, uint32_t mid_codec, DevPlan* P,
+                                           float* s_q, PlanShared& sh, uint32_t need, const PlanDest& dst) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nthr = blockDim.x;
     const bool full = need == kNeedAll;
@@ -174,12 +242,6 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
 
     __syncthreads();  // plan_inputs done
 
-    const float inv_sqrt_64 = __fdiv_rn(1.0f, __fsqrt_rn(64.0f));
-    const float inv_sqrt_128 = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
-    const float two_over_pi = __fdiv_rn(2.0f, 3.14159265358979323846f);
-    const float rabitq_scale = __fdiv_rn(__fsqrt_rn(two_over_pi), __fsqrt_rn(128.0f));  // src/rotate.rs:46-49
-    const float tail_scale = __fdiv_rn(__fsqrt_rn(two_over_pi), __fsqrt_rn(64.0f));     // src/rotate.rs:124-126
-
     if (warp == 0) {
         // ---- prefix copy + bit weights (src/scan.rs:126-140), EDEN rotate_query (src/eden.rs:275-281)
         float v[2];
@@ -187,12 +249,15 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
         for (int r = 0; r < 2; ++r) {
             const int d = lane + 32 * r;
             const float qd = s_q[d];
-            if (full) qp->prefix[d] = qd;
-            qp->bit_weights[d][0] = f_mul(qd, 1.0f);
-            qp->bit_weights[d][1] = f_mul(qd, 2.0f);
-            qp->bit_weights[d][2] = f_mul(qd, 4.0f);
-            qp->bit_weights[d][3] = f_mul(qd, 8.0f);
-            v[r] = f_mul(qd, sign_hash(eden_seed, (uint64_t)d));
+            if (full) {
+                qp->prefix[d] = qd;
+                qp->bit_weights[d][0] = f_mul(qd, 1.0f);
+                qp->bit_weights[d][1] = f_mul(qd, 2.0f);
+                qp->bit_weights[d][2] = f_mul(qd, 4.0f);
+                qp->bit_weights[d][3] = f_mul(qd, 8.0f);
+            }
+            if (dst.bw3) dst.bw3[d] = f_mul(qd, 8.0f);
+            v[r] = f_mul(qd, sh.sg[d]);
         }
         fwht_warp<2>(v, lane);
 #pragma unroll
@@ -201,54 +266,28 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
             if (full) qp->eden_q_rot[lane + 32 * r] = eden ? v[r] : 0.0f;
         }
         if (full && lane < 16) qp->eden_codebook[lane] = eden ? s_cb[lane] : 0.0f;
-        __syncwarp();
-        // prefix_l1, prefix_sum, eden_mean_ip: sequential in the reference's order (src/scan.rs:126-151)
-        if (lane == 0) {
-            float l1 = 0.0f, sum = 0.0f, ip = 0.0f;
-#pragma unroll 8
-            for (int d = 0; d < kPrefix; ++d) {
-                const float qd = s_q[d];
-                l1 = f_add(l1, fabsf(qd));
-                sum = f_add(sum, qd);
-                ip = f_add(ip, f_mul(qd, s_mean[d]));
-            }
-            if (!eden) ip = 0.0f;
-            s_scal[0] = l1;
-            s_scal[1] = sum;
-            s_scal[4] = ip;
-        }
-        // Prefix weights and shifts. An entry is (double)cb[l] * w_d (EDEN) or (double)l * q_d
+        // Prefix weights and shift. An entry is (double)cb[l] * w_d (EDEN) or (double)l * q_d
         // (MinMax), both exact products, so the largest |entry| of dim d is max|cb| * |w_d| or
-        // 15 * |q_d|.
-        double cbmax = 0.0;
-#pragma unroll
-        for (int l = 0; l < 16; ++l) cbmax = fmax(cbmax, fabs((double)s_cb[l]));
-        double mx = 0.0, mx0 = 0.0, ea = 0.0, ea0 = 0.0;
+        // 15 * |q_d|, and the largest over the dims is max|cb| * max|w| or 15 * max|q|.
+        const double cbmax = warp_max_abs(lane < 16 ? s_cb[lane] : 0.0f);
+        double ea = 0.0;
+        float wq[2];
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const int d = lane + 32 * r;
-            const float w = eden ? f_mul(s_rot[d], inv_sqrt_64) : 0.0f;
+            const float w = eden ? f_mul(v[r], kInvSqrt64) : 0.0f;
             sh.w[d] = w;
-            const double e = eden ? cbmax * fabs((double)w) : 15.0 * fabs((double)s_q[d]);
-            const double e0 = fabs((double)f_mul(s_q[d], 8.0f));
-            mx = fmax(mx, e);
-            mx0 = fmax(mx0, e0);
-            ea += e;
-            ea0 += e0;
+            wq[r] = eden ? w : s_q[d];
+            ea += eden ? cbmax * fabs((double)w) : 15.0 * fabs((double)s_q[d]);
         }
-        const int sh_p = stage_shift(warp_max(mx), kPrefix);
-        const int sh_0 = stage_shift(warp_max(mx0), kPrefix);  // L0Only (accum_plane, src/scan.rs:753-762)
+        const double mxa = warp_max_abs(fmaxf(fabsf(wq[0]), fabsf(wq[1])));
+        const int sh_p = stage_shift(eden ? cbmax * mxa : 15.0 * mxa, kPrefix);
         ea = warp_sum(ea);
-        ea0 = warp_sum(ea0);
         if (lane == 0) {
             P->err_p = bound_up(ea);
-            P->err_0 = bound_up(ea0);
             P->shift_prefix = sh_p;
-            P->shift_l0 = sh_0;
-            P->unscale_prefix = ldexp(1.0, -sh_p);
-            P->unscale_l0 = ldexp(1.0, -sh_0);
-            sh.pw[0] = ldexp(1.0, sh_p);
-            sh.pw[1] = ldexp(1.0, sh_0);
+            P->unscale_prefix = pow2(-sh_p);
+            sh.pw[0] = pow2(sh_p);
         }
     } else if (warp == 1) {
         // ---- mid band: rotate_mid_band (src/rotate.rs:36-42) and the EdenB1 rotation (src/scan.rs:159-174)
@@ -257,79 +296,57 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
         for (int r = 0; r < 4; ++r) {
             const int i = lane + 32 * r;
             rq[r] = s_q[kPrefix + i];
-            mq[r] = f_mul(s_q[kPrefix + i], sign_hash(mid_seed, (uint64_t)i));
+            mq[r] = f_mul(s_q[kPrefix + i], sh.sg[kPrefix + i]);
         }
         fwht_warp<4>(rq, lane);
         if (mid_b1) fwht_warp<4>(mq, lane);
-        double mx = 0.0;
+        float v1f[4];
+        double ea = 0.0;
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int i = lane + 32 * r;
             s_rq[i] = rq[r];
             s_mq[i] = mq[r];
-            const float pos = f_mul(rq[r], rabitq_scale);
+            const float pos = f_mul(rq[r], kRabitqScale);
             if (full) {
                 qp->rabitq_q[i] = rq[r];
                 qp->eden_mid_q_rot[i] = mid_b1 ? mq[r] : 0.0f;
                 qp->rabitq_weights2[i] = f_mul(2.0f, pos);
             }
-            double v1;
-            if (mid_b1) {
-                const float qd = f_mul(mq[r], inv_sqrt_128);
-                P->mid_w[i] = f_mul(f_sub(kLloydB1Hi, -kLloydB1Hi), qd);
-                v1 = (double)kLloydB1Hi * (double)qd;
-            } else {
-                P->mid_w[i] = f_mul(2.0f, pos);
-                v1 = (double)pos;
-            }
-            mx = fmax(mx, fabs(v1));
+            const float qd = f_mul(mq[r], kInvSqrt128);
+            dst.mid_w[i] = mid_b1 ? f_mul(f_sub(kLloydB1Hi, -kLloydB1Hi), qd) : f_mul(2.0f, pos);
+            // the addends of rabitq_base (src/scan.rs:180-186, subtracted) and of the EdenB1 base
+            // (src/scan.rs:523-532)
+            sh.terms[kRowBase][i] = -pos;
+            sh.terms[kRowB1][i] = f_mul(-kLloydB1Hi, qd);
+            // fixed S1 value of bit 1 (bit 0: its negation): kLloydB1Hi * qd (exact double
+            // product) for EdenB1, pos for RaBitQ
+            v1f[r] = mid_b1 ? qd : pos;
+            const double v1 = mid_b1 ? (double)kLloydB1Hi * (double)qd : (double)pos;
+            ea += fabs(v1);
         }
-        __syncwarp();
-        // q_mid_sq, rabitq_base, eden_mid_mean_ip, EdenB1 base: sequential in reference order
-        // (src/scan.rs:209-213, 180-186, 167-169, 523-532)
-        if (lane == 0) {
-            float ms = 0.0f, base = 0.0f, mip = 0.0f, b1 = 0.0f;
-            if (mid_b1) {
-#pragma unroll 8
-                for (int d = 0; d < kRabitq; ++d) {
-                    const float qd = s_q[kPrefix + d];
-                    ms = f_add(ms, f_mul(qd, qd));
-                    base = f_sub(base, f_mul(s_rq[d], rabitq_scale));
-                    mip = f_add(mip, f_mul(qd, s_mean[kPrefix + d]));
-                    b1 = f_add(b1, f_mul(-kLloydB1Hi, f_mul(s_mq[d], inv_sqrt_128)));
-                }
-            } else {
-#pragma unroll 8
-                for (int d = 0; d < kRabitq; ++d) {
-                    const float qd = s_q[kPrefix + d];
-                    ms = f_add(ms, f_mul(qd, qd));
-                    base = f_sub(base, f_mul(s_rq[d], rabitq_scale));
-                }
-            }
-            s_scal[3] = ms;
-            s_scal[5] = mip;
-            s_scal[6] = base;
-            s_scal[9] = b1;
-        }
-        // fixed S1 values per dim for the window table
-        const int sh_1 = stage_shift(warp_max(mx), kRabitq);
-        const double pw_1 = ldexp(1.0, sh_1);
-        double ea = 0.0;
+        const double mv = warp_max_abs(fmaxf(fmaxf(fabsf(v1f[0]), fabsf(v1f[1])), fmaxf(fabsf(v1f[2]), fabsf(v1f[3]))));
+        const int sh_1 = stage_shift(mid_b1 ? (double)kLloydB1Hi * mv : mv, kRabitq);
+        const double pw_1 = pow2(sh_1);
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int i = lane + 32 * r;
-            double v1;
-            if (mid_b1) v1 = (double)kLloydB1Hi * (double)f_mul(s_mq[i], inv_sqrt_128);
-            else v1 = (double)f_mul(s_rq[i], rabitq_scale);
+            const double v1 = mid_b1 ? (double)kLloydB1Hi * (double)v1f[r] : (double)v1f[r];
             s_fx[2 * i] = fix(-v1, pw_1);
             s_fx[2 * i + 1] = fix(v1, pw_1);
-            ea += fabs(v1);
         }
         ea = warp_sum(ea);
         if (lane == 0) {
             P->err_1 = bound_up(ea);
             P->shift_s1 = sh_1;
-            P->unscale_s1 = ldexp(1.0, -sh_1);
+            P->unscale_s1 = pow2(-sh_1);
+        }
+        __syncwarp();
+        // rabitq_base and the EdenB1 base: sequential in reference order (lanes 0 and 1)
+        if (lane < 2) {
+            const float acc = lane_chain(sh.terms[kRowBase + lane], kRabitq);
+            if (lane == 0) s_scal[6] = acc;
+            else s_scal[9] = mid_b1 ? acc : 0.0f;
         }
     } else if (warp == 2) {
         // ---- folded tail: fold_tail (src/rotate.rs:73-93) then FWHT64 (rotate_tail_fold)
@@ -340,55 +357,46 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
             for (int r = 0; r < 2; ++r) {
                 const int d = lane + 32 * r;
                 for (int b = 0; b < nb; ++b)
-                    u[r] = f_add(u[r], f_mul(sign_hash((uint64_t)b, (uint64_t)d), s_q[kTailStart + b * kPrefix + d]));
+                    u[r] = f_add(u[r], f_mul(sh.sg[kPrefix + kRabitq + b * kPrefix + d], s_q[kTailStart + b * kPrefix + d]));
             }
         }
         fwht_warp<2>(u, lane);
-        double mx = 0.0;
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int d = lane + 32 * r;
-            s_tf[d] = u[r];
-            const float pos = has_tail ? f_mul(u[r], tail_scale) : 0.0f;
-            if (full) {
-                qp->tail_fold_q[d] = has_tail ? u[r] : 0.0f;
-                qp->tail_fold_weights2[d] = has_tail ? f_mul(2.0f, pos) : 0.0f;
-            }
-            P->tail_w[d] = has_tail ? f_mul(2.0f, pos) : 0.0f;
-            mx = fmax(mx, fabs((double)pos));
-        }
-        __syncwarp();
-        // tail_fold_base / s4_abs_budget (src/scan.rs:222-233): sequential in reference order
-        if (lane == 0) {
-            float tb = 0.0f, bud = 0.0f;
-            if (has_tail) {
-#pragma unroll 8
-                for (int d = 0; d < kFold; ++d) {
-                    const float pos = f_mul(s_tf[d], tail_scale);
-                    tb = f_sub(tb, pos);
-                    bud = f_add(bud, fabsf(pos));
-                }
-            }
-            s_scal[7] = tb;
-            s_scal[8] = bud;
-        }
-        // fixed S4 values per dim for the window table
-        const int sh_4 = stage_shift(warp_max(mx), kFold);
-        const double pw_4 = ldexp(1.0, sh_4);
+        float pf[2];
         double ea = 0.0;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const int d = lane + 32 * r;
-            const double pos = has_tail ? (double)f_mul(s_tf[d], tail_scale) : 0.0;
-            s_fx[2 * (kRabitq + d)] = fix(-pos, pw_4);
-            s_fx[2 * (kRabitq + d) + 1] = fix(pos, pw_4);
-            ea += fabs(pos);
+            s_tf[d] = u[r];
+            const float pos = has_tail ? f_mul(u[r], kTailScale) : 0.0f;
+            if (full) {
+                qp->tail_fold_q[d] = has_tail ? u[r] : 0.0f;
+                qp->tail_fold_weights2[d] = has_tail ? f_mul(2.0f, pos) : 0.0f;
+            }
+            dst.tail_w[d] = has_tail ? f_mul(2.0f, pos) : 0.0f;
+            // the addends of tail_fold_base (subtracted) and s4_abs_budget (src/scan.rs:222-233)
+            sh.terms[kRowTb][d] = -pos;
+            sh.terms[kRowBud][d] = fabsf(pos);
+            pf[r] = pos;
+            ea += fabs((double)pos);
+        }
+        const int sh_4 = stage_shift(warp_max_abs(fmaxf(fabsf(pf[0]), fabsf(pf[1]))), kFold);
+        const double pw_4 = pow2(sh_4);
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int d = lane + 32 * r;
+            s_fx[2 * (kRabitq + d)] = fix(-(double)pf[r], pw_4);
+            s_fx[2 * (kRabitq + d) + 1] = fix((double)pf[r], pw_4);
         }
         ea = warp_sum(ea);
         if (lane == 0) {
             P->err_4 = bound_up(ea);
             P->shift_s4 = sh_4;
-            P->unscale_s4 = ldexp(1.0, -sh_4);
+            P->unscale_s4 = pow2(-sh_4);
+        }
+        __syncwarp();
+        if (lane < 2) {
+            const float acc = has_tail ? lane_chain(sh.terms[kRowTb + lane], kFold) : 0.0f;
+            s_scal[7 + lane] = acc;
         }
     } else if (warp == 3) {
         // q_tail_sq (src/scan.rs:203-207): the longest sequential sum; only the stored plan's
@@ -412,7 +420,7 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 const int gl = (lane >> 2);  // group within this register's 32 dims
-                const float base_v = f_mul(rq[r], rabitq_scale);
+                const float base_v = f_mul(rq[r], kRabitqScale);
                 float p[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) p[j] = __shfl_sync(0xffffffffu, base_v, (gl << 2) + j);
@@ -427,27 +435,68 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
                 }
             }
         }
+    } else if (warp == 4) {
+        // prefix_l1, prefix_sum, eden_mean_ip (src/scan.rs:126-151) in reference order, lanes 0-2
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int d = lane + 32 * r;
+            const float qd = s_q[d];
+            sh.terms[kRowL1][d] = fabsf(qd);
+            sh.terms[kRowSum][d] = qd;
+            sh.terms[kRowIp][d] = f_mul(qd, s_mean[d]);
+        }
+        // L0Only shift (accum_plane, src/scan.rs:753-762): entries bit 3 of the level times
+        // f32(q_d * 8)
+        float e0[2];
+        double ea0 = 0.0;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            e0[r] = f_mul(s_q[lane + 32 * r], 8.0f);
+            ea0 += fabs((double)e0[r]);
+        }
+        const int sh_0 = stage_shift(warp_max_abs(fmaxf(fabsf(e0[0]), fabsf(e0[1]))), kPrefix);
+        ea0 = warp_sum(ea0);
+        if (lane == 0) {
+            P->err_0 = bound_up(ea0);
+            P->shift_l0 = sh_0;
+            P->unscale_l0 = pow2(-sh_0);
+            sh.pw[1] = pow2(sh_0);
+        }
+        __syncwarp();
+        if (lane < 3) {
+            const float acc = lane_chain(sh.terms[kRowL1 + lane], kPrefix);
+            if (lane == 0) s_scal[0] = acc;
+            else if (lane == 1) s_scal[1] = acc;
+            else s_scal[4] = eden ? acc : 0.0f;
+        }
+    } else if (warp == 5) {
+        // q_mid_sq (src/scan.rs:209-213) and eden_mid_mean_ip (src/scan.rs:167-169), lanes 0-1
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int i = lane + 32 * r;
+            const float qd = s_q[kPrefix + i];
+            sh.terms[kRowMs][i] = f_mul(qd, qd);
+            sh.terms[kRowMip][i] = f_mul(qd, s_mean[kPrefix + i]);
+        }
+        __syncwarp();
+        if (lane < 2) {
+            const float acc = lane_chain(sh.terms[kRowMs + lane], kRabitq);
+            if (lane == 0) s_scal[3] = acc;
+            else s_scal[5] = mid_b1 ? acc : 0.0f;
+        }
     }
     __syncthreads();
 
-    // ---- phase B: tables, four consecutive levels of one dim per item (entry e = 16 d + l)
+    // ---- phase B: tables, one entry per item (prefix entry e = 16 d + l)
     if (need & kNeedFast) {
         const double pw_p = sh.pw[0];
-        for (int t = tid; t < kPrefix * 4; t += nthr) {
-            const int d = t >> 2, l0 = (t & 3) * 4;
-            const float w = sh.w[d];
-            int4 o;
-            int* oi = &o.x;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int l = l0 + j;
-                oi[j] = fix(eden ? (double)s_cb[l] * (double)w : (double)l * (double)s_q[d], pw_p);
-            }
-            reinterpret_cast<int4*>(P->lut_prefix)[t] = o;
+        for (int t = tid; t < kPrefix * 16; t += nthr) {
+            const int d = t >> 4, l = t & 15;
+            dst.lut_prefix[t] = fix(eden ? (double)s_cb[l] * (double)sh.w[d] : (double)l * (double)s_q[d], pw_p);
         }
-        for (int t = tid; t < kS1Windows * 32; t += nthr) P->lut_s1[t] = window_entry<kRabitq>(s_fx, t >> 5, t & 31);
+        for (int t = tid; t < kS1Windows * 32; t += nthr) dst.lut_s1[t] = window_entry<kRabitq>(s_fx, t >> 5, t & 31);
         for (int t = tid; t < kS4Windows * 32; t += nthr)
-            P->lut_s4[t] = window_entry<kFold>(s_fx + 2 * kRabitq, t >> 5, t & 31);
+            dst.lut_s4[t] = window_entry<kFold>(s_fx + 2 * kRabitq, t >> 5, t & 31);
     }
     if (need & kNeedBatch) {
         for (int t = tid; t < (kRabitq / 4) * 16; t += nthr) P->lut4_s1[t] = window4_entry(s_fx, t >> 4, t & 15);
@@ -456,29 +505,15 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
     }
     if (need & kNeedL0) {  // bit 3 of the level times bit_weights[d][3] (accum_plane, src/scan.rs:753-762)
         const double pw_0 = sh.pw[1];
-        for (int t = tid; t < kPrefix * 4; t += nthr) {
-            const int d = t >> 2, l0 = (t & 3) * 4;
-            const int32_t f = fix((double)f_mul(s_q[d], 8.0f), pw_0);
-            int4 o;
-            o.x = ((l0 + 0) & 8) ? f : 0;
-            o.y = ((l0 + 1) & 8) ? f : 0;
-            o.z = ((l0 + 2) & 8) ? f : 0;
-            o.w = ((l0 + 3) & 8) ? f : 0;
-            reinterpret_cast<int4*>(P->lut_l0)[t] = o;
+        for (int t = tid; t < kPrefix * 16; t += nthr) {
+            const int d = t >> 4, l = t & 15;
+            dst.lut_l0[t] = (l & 8) ? fix((double)f_mul(s_q[d], 8.0f), pw_0) : 0;
         }
     }
     if (need & kNeedExact) {  // f32 products of the reference's prefix loop (src/scan.rs:456-487)
-        for (int t = tid; t < kPrefix * 4; t += nthr) {
-            const int d = t >> 2, l0 = (t & 3) * 4;
-            const float w = sh.w[d];
-            float4 o;
-            float* of = &o.x;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int l = l0 + j;
-                of[j] = eden ? f_mul(s_cb[l], w) : f_mul((float)l, s_q[d]);
-            }
-            reinterpret_cast<float4*>(P->fp_prefix)[t] = o;
+        for (int t = tid; t < kPrefix * 16; t += nthr) {
+            const int d = t >> 4, l = t & 15;
+            dst.fp_prefix[t] = eden ? f_mul(s_cb[l], sh.w[d]) : f_mul((float)l, s_q[d]);
         }
     }
     if (tid == 0) {
@@ -486,22 +521,24 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
         qp->prefix_codec = prefix_codec;
         qp->mid_codec = mid_codec;
         qp->has_tail_fold = has_tail ? 1u : 0u;
-        qp->rabitq_scale = rabitq_scale;
+        qp->rabitq_scale = kRabitqScale;
         qp->rabitq_base = s_scal[6];
         qp->tail_fold_base = s_scal[7];
-        qp->q_tail_norm = __fsqrt_rn(s_scal[2]);
-        qp->q_mid_norm = __fsqrt_rn(s_scal[3]);
-        qp->q_after_prefix = __fsqrt_rn(f_add(s_scal[3], s_scal[2]));
-        qp->q_after_s1 = qp->q_tail_norm;
         qp->s4_abs_budget = s_scal[8];
         qp->prefix_l1 = s_scal[0];
         qp->prefix_sum = s_scal[1];
         qp->eden_mean_ip = s_scal[4];
-        qp->eden_inv_sqrt_d = inv_sqrt_64;
+        qp->eden_inv_sqrt_d = kInvSqrt64;
         qp->eden_mid_mean_ip = s_scal[5];
-        qp->eden_mid_inv_sqrt_d = inv_sqrt_128;
+        qp->eden_mid_inv_sqrt_d = kInvSqrt128;
         qp->eden_mid_codebook[0] = mid_b1 ? -kLloydB1Hi : 0.0f;
         qp->eden_mid_codebook[1] = mid_b1 ? kLloydB1Hi : 0.0f;
+        if (full) {
+            qp->q_tail_norm = __fsqrt_rn(s_scal[2]);
+            qp->q_mid_norm = __fsqrt_rn(s_scal[3]);
+            qp->q_after_prefix = __fsqrt_rn(f_add(s_scal[3], s_scal[2]));
+            qp->q_after_s1 = qp->q_tail_norm;
+        }
         P->mid_base = mid_b1 ? s_scal[9] : s_scal[6];
         P->tail_base = s_scal[7];
         P->pad2 = 0.0f;

@@ -312,8 +312,8 @@ __device__ bool grid_barrier(unsigned* ctl, unsigned G, volatile int* s_ok) {
     return *s_ok != 0;
 }
 
-__device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int mode, int* tab, float2* rho_tab,
-                                            Scalars& S, const ScanLaunch& p) {
+// The scan's shared-memory tables from a plan (ints in fast mode, floats in exact mode).
+__device__ __forceinline__ void copy_tables(const DevPlan* __restrict__ P, int mode, int* tab, const ScanLaunch& p) {
     const int tid = threadIdx.x;
     if (mode == MRL_MODE_FAST) {
         for (int i = tid; i < kPrefix * 16; i += kThreads) tab[i] = P->lut_prefix[i];
@@ -328,7 +328,12 @@ __device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int m
         for (int i = tid; i < kFold; i += kThreads) ft[kTabTailW + i] = P->tail_w[i];
         for (int i = tid; i < kPrefix; i += kThreads) ft[kTabBw3 + i] = P->qp.bit_weights[i][3];
     }
-    fill_rho_tab(rho_tab, tid, kThreads);
+}
+
+__device__ __forceinline__ void load_tables(const DevPlan* __restrict__ P, int mode, int* tab, float2* rho_tab,
+                                            Scalars& S, const ScanLaunch& p) {
+    copy_tables(P, mode, tab, p);
+    fill_rho_tab(rho_tab, threadIdx.x, kThreads);
     fill_scalars(P, p.w_s4, p.depth, (int32_t)(p.list_len != 0u), S);  // one: 1 for every launch, opaque to the compiler
 }
 
@@ -500,7 +505,7 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
     float* s_qb = reinterpret_cast<float*>(s_dyn + align16(sizeof(DevPlan)));
     planb::PlanShared* s_pb =
         reinterpret_cast<planb::PlanShared*>(s_dyn + align16(sizeof(DevPlan)) + align16((size_t)p.dims * sizeof(float)));
-    if (FUSED) planb::plan_inputs(p.query, p.dims, p.eden_mean, p.mid_mean, s_qb, *s_pb);
+    if (FUSED) planb::plan_inputs(p.query, p.dims, p.eden_mean, p.mid_mean, p.eden_seed, p.mid_seed, s_qb, *s_pb);
     float4 mm = make_float4(0.f, 0.f, 0.f, 0.f);
     if (kFast) mm = __ldg(reinterpret_cast<const float4*>(p.metamax));
 
@@ -533,26 +538,38 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
         s_next = lo_c + 2u * kWarps;
     }
     const DevPlan* plan = p.plan;
+    bool built = false;  // the tables are in shared memory already
     if (FUSED) {
         // QueryPipeline::build_plan fused into the scan (src/pipeline.rs:63-74): every CTA builds the
         // plan in shared memory while its first pages are in flight; no CTA waits on another.
         // CTA 0 stores the complete plan; the others build only what this mode scans with (fast
-        // mode also needs the exact-mode prefix products for the rescoring of its list)
-        const uint32_t need = blockIdx.x == 0 && p.plan_out
-                                  ? planb::kNeedAll
-                                  : (kFast ? planb::kNeedFast | planb::kNeedExact | (p.depth == MRL_DEPTH_L0 ? planb::kNeedL0 : 0u)
-                                           : planb::kNeedExact);
-        planb::build_plan(p.dims, p.prefix_codec, p.mid_codec, p.eden_seed, p.mid_seed, ps, s_qb, *s_pb, need);
+        // mode also needs the exact-mode prefix products for the rescoring of its list), writing
+        // the tables straight into the scan's shared-memory tables
+        const bool full = blockIdx.x == 0 && p.plan_out;
+        const uint32_t need = full ? planb::kNeedAll
+                                   : (kFast ? planb::kNeedFast | planb::kNeedExact | (p.depth == MRL_DEPTH_L0 ? planb::kNeedL0 : 0u)
+                                            : planb::kNeedExact);
+        float* xt = kFast ? s_xtab : reinterpret_cast<float*>(s_tab);
+        const planb::PlanDest dst =
+            full ? planb::plan_dest(ps)
+                 : planb::PlanDest{s_tab, s_tab + kTabS1, s_tab + kTabS4, s_tab + kTabL0, xt, xt + kTabMidW, xt + kTabTailW,
+                                   xt + kTabBw3};
+        planb::build_plan(p.dims, p.prefix_codec, p.mid_codec, ps, s_qb, *s_pb, need, dst);
         __syncthreads();
-        if (blockIdx.x == 0 && p.plan_out) {  // keep the plan for mrl_plan_read and later scans
+        if (full) {  // keep the plan for mrl_plan_read and later scans
             const uint4* src = reinterpret_cast<const uint4*>(ps);
-            uint4* dst = reinterpret_cast<uint4*>(p.plan_out);
-            for (unsigned i = tid; i < sizeof(DevPlan) / 16; i += kThreads) dst[i] = src[i];
+            uint4* out = reinterpret_cast<uint4*>(p.plan_out);
+            for (unsigned i = tid; i < sizeof(DevPlan) / 16; i += kThreads) out[i] = src[i];
         }
         plan = ps;
+        built = !full;
     }
-    load_tables(plan, MODE, s_tab, s_rho, S, p);
-    if constexpr (kFast) load_exact_tables(plan, s_xtab);
+    if (!built) {
+        copy_tables(plan, MODE, s_tab, p);
+        if constexpr (kFast) load_exact_tables(plan, s_xtab);
+    }
+    fill_rho_tab(s_rho, tid, kThreads);
+    fill_scalars(plan, p.w_s4, p.depth, (int32_t)(p.list_len != 0u), S);  // one: 1 for every launch, opaque to the compiler
     // bound on |fast score - exact score| of every slot of this segment (0 in exact mode)
     const float E = kFast ? fast_error_bound(*plan, mm, p.w_s4, p.depth) : 0.0f;
     __syncthreads();
