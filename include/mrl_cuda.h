@@ -361,9 +361,9 @@ int mrl_debug_vector_scores(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
  * and max(high_n, 1e-6), which every call that adds pages keeps current. Synchronous. */
 int mrl_debug_score_bound(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q,
                           const mrl_scan_cfg* cfg, float* out_bound);
-/* The context's 8 scan control words (page counter, grid barrier arrivals, three unused words,
- * timeout flag, exchange count, exit count). Every scan launch leaves all of them at zero,
- * whichever path it took. Synchronous. */
+/* The context's scan control words into out[16]: 8 per launch parity (page counter, publish
+ * ticket, six unused words). Consecutive scan launches alternate the two parities; every launch
+ * leaves its parity's words at zero, whichever path it took. Synchronous. */
 int mrl_debug_control_words(mrl_ctx* ctx, uint32_t* out);
 
 /* ---- encode: encode_block_with_fits (src/quantize.rs:36-96) ----------------------------- */

@@ -34,11 +34,15 @@ struct mrl_ctx {
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
     std::string err;
-    // scan scratch: per-CTA lists, control words, per-page owner (grow-only)
-    unsigned long long* cta_keys = nullptr;  // 2 * sms * 32: scan keys, then their exact keys
-    unsigned int* ctl = nullptr;             // mrl::kCtlWords
+    // scan scratch, one set per launch parity (scan_seq & 1): consecutive scan launches on the
+    // stream may overlap (programmatic dependent launch), and a launch starts only once the one two
+    // back has completed. Per parity: per-CTA lists, control words, per-page owner (grow-only;
+    // each parity owns half of `owner`).
+    unsigned long long* cta_keys = nullptr;  // per parity 2 * sms * 32: scan keys, then their exact keys
+    unsigned int* ctl = nullptr;             // per parity mrl::kCtlWords
     uint8_t* owner = nullptr;
     size_t owner_bytes = 0;
+    uint32_t scan_seq = 0;
     uint32_t list_len_override = 0;
     // grow-only scratch for host-facing calls: inputs (queries, rows, means) and outputs
     void* tmp = nullptr;
@@ -253,12 +257,22 @@ mrl::ScanLaunch make_launch(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
     p.lo = lo ? *lo : 0u;
     p.has_hi = hi ? 1u : 0u;
     p.hi = hi ? *hi : 0u;
-    p.cta_keys = ctx->cta_keys;
-    p.cta_xkeys = ctx->cta_keys + 32 * (size_t)ctx->sms;
-    p.ctl = ctx->ctl;
-    p.owner = ctx->owner;
     p.metamax = seg->metamax;
     return p;
+}
+
+// Grows the per-page owner scratch to two parities of n_blocks bytes each.
+int ensure_owner(mrl_ctx* ctx, uint64_t n_blocks) {
+    return ensure_buf(ctx, (void**)&ctx->owner, &ctx->owner_bytes, 2 * (n_blocks ? n_blocks : 1));
+}
+
+// The context scratch of the next scan launch: the parities alternate launch by launch.
+void take_scratch(mrl_ctx* ctx, mrl::ScanLaunch& p) {
+    const size_t par = ctx->scan_seq++ & 1u;
+    p.cta_keys = ctx->cta_keys + par * 2 * 32 * (size_t)ctx->sms;
+    p.cta_xkeys = p.cta_keys + 32 * (size_t)ctx->sms;
+    p.ctl = ctx->ctl + par * mrl::kCtlWords;
+    p.owner = ctx->owner + par * (ctx->owner_bytes / 2);
 }
 
 int check_codec(mrl_ctx* ctx, const mrl_codec_desc* codec) {
@@ -359,10 +373,10 @@ int mrl_ctx_create(int device, mrl_ctx** out) {
         return MRL_ERR_CUDA;
     }
     ctx->stream = ctx->own_stream;
-    if (cudaMalloc(&ctx->cta_keys, sizeof(unsigned long long) * 2 * 32 * (size_t)ctx->sms) != cudaSuccess ||
-        cudaMalloc(&ctx->ctl, sizeof(unsigned int) * mrl::kCtlWords) != cudaSuccess ||
+    if (cudaMalloc(&ctx->cta_keys, sizeof(unsigned long long) * 2 * 2 * 32 * (size_t)ctx->sms) != cudaSuccess ||
+        cudaMalloc(&ctx->ctl, sizeof(unsigned int) * 2 * mrl::kCtlWords) != cudaSuccess ||
         cudaMalloc(&ctx->d_means, 192 * sizeof(float)) != cudaSuccess ||
-        cudaMemset(ctx->ctl, 0, sizeof(unsigned int) * mrl::kCtlWords) != cudaSuccess ||
+        cudaMemset(ctx->ctl, 0, sizeof(unsigned int) * 2 * mrl::kCtlWords) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) {
         mrl_ctx_destroy(ctx);
         return MRL_ERR_NOMEM;
@@ -660,7 +674,7 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
     if ((uint64_t)q0 + n_q > plans->n_q) return fail(ctx, MRL_ERR_INVALID, "plan range out of bounds");
     if (n_q && (!d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "output is NULL");
     if (int rc = set_device(ctx)) return rc;
-    if (int rc = ensure_buf(ctx, (void**)&ctx->owner, &ctx->owner_bytes, seg->n_blocks ? seg->n_blocks : 1)) return rc;
+    if (int rc = ensure_owner(ctx, seg->n_blocks)) return rc;
     const uint32_t k = cfg->shortlist_cand;
     for (uint32_t i = 0; i < n_q; ++i) {
         mrl::ScanLaunch p = make_launch(ctx, seg, plans, q0 + i, cfg, time_lo, time_hi);
@@ -673,7 +687,8 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
             if (p.out_status) MRL_CUDA_TRY(ctx, cudaMemsetAsync(p.out_status, 0, sizeof(uint32_t), ctx->stream));
             continue;
         }
-        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+        take_scratch(ctx, p);
+        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     }
     return MRL_OK;
 }
@@ -749,7 +764,8 @@ int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pl
             if (p.out_status) MRL_CUDA_TRY(ctx, cudaMemsetAsync(p.out_status, 0, sizeof(uint32_t), ctx->stream));
             continue;
         }
-        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+        // an ordinary launch (no programmatic dependent launch): every call shares the one region
+        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, false)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     }
     return MRL_OK;
 }
@@ -799,7 +815,7 @@ int mrl_query_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const float* d_queri
     if (n_q && (!d_queries || !d_out_ids || !d_out_scores || !d_out_counts)) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
     if (n_q == 0) return MRL_OK;
     if (int rc = set_device(ctx)) return rc;
-    if (int rc = ensure_buf(ctx, (void**)&ctx->owner, &ctx->owner_bytes, seg->n_blocks ? seg->n_blocks : 1)) return rc;
+    if (int rc = ensure_owner(ctx, seg->n_blocks)) return rc;
     float* d_means = nullptr;
     if (int rc = upload_means(ctx, codec, &d_means)) return rc;
     const float* d_mid = codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr;
@@ -827,7 +843,8 @@ int mrl_query_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const float* d_queri
         p.mid_mean = d_mid;
         p.mid_seed = codec->mid_seed;
         p.plan_out = plans->d + i;
-        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+        take_scratch(ctx, p);
+        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     }
     return MRL_OK;
 }
@@ -964,7 +981,7 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
     if (plans->n_q < 1 || dims != plans->dims) return fail(ctx, MRL_ERR_INVALID, "plan storage too small or dims mismatch");
     if (!d_query || !d_out_ids || !d_out_scores || !d_out_count) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
     if (int rc = set_device(ctx)) return rc;
-    if (int rc = ensure_buf(ctx, (void**)&ctx->owner, &ctx->owner_bytes, seg->n_blocks ? seg->n_blocks : 1)) return rc;
+    if (int rc = ensure_owner(ctx, seg->n_blocks)) return rc;
     float* d_means = nullptr;
     if (int rc = upload_means(ctx, codec, &d_means)) return rc;
     mrl::ScanLaunch p = make_launch(ctx, seg, plans, 0, cfg, time_lo, time_hi);
@@ -992,7 +1009,8 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
     }
     p.xch_recv = ex->local + parity * ex->world * ex->rb;
     p.xch_flag_in = reinterpret_cast<const unsigned*>(ex->local + ex->flags_off()) + parity * ex->world;
-    if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+    take_scratch(ctx, p);
+    if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     return MRL_OK;
 }
 
@@ -1270,7 +1288,7 @@ int mrl_debug_score_bound(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pla
 int mrl_debug_control_words(mrl_ctx* ctx, uint32_t* out) {
     if (!ctx || !out) return MRL_ERR_INVALID;
     if (int rc = set_device(ctx)) return rc;
-    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out, ctx->ctl, sizeof(unsigned) * mrl::kCtlWords, cudaMemcpyDeviceToHost, ctx->stream));
+    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out, ctx->ctl, sizeof(unsigned) * 2 * mrl::kCtlWords, cudaMemcpyDeviceToHost, ctx->stream));
     MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     return MRL_OK;
 }

@@ -143,6 +143,16 @@ __device__ __forceinline__ SlotMeta decode_slot_meta(uint32_t w2, uint32_t w3) {
     return m;
 }
 
+// rho_ratio = flags / 255 and sqrt(max(1 - r^2, 0)) (src/block.rs:74-84) for every flags byte,
+// filled by threads tid = 0 .. nthr-1.
+__device__ __forceinline__ void fill_rho_tab(float2* rho_tab, int tid, int nthr) {
+    for (int i = tid; i < 256; i += nthr) {
+        const float rho = __fdiv_rn((float)i, 255.0f);
+        const float r = fminf(fmaxf(rho, 0.0f), 1.0f);
+        rho_tab[i] = make_float2(rho, __fsqrt_rn(fmaxf(__fsub_rn(1.0f, __fmul_rn(r, r)), 0.0f)));
+    }
+}
+
 }  // namespace mrl
 
 // Host-side launchers implemented in the .cu files, used by the C ABI layer.
@@ -185,12 +195,12 @@ struct ScanLaunch {
     uint32_t mode;
     uint32_t use_time;  // temporal filter active for this call
     uint32_t has_lo, lo, has_hi, hi;
-    // scratch (owned by the context; zero-initialised once, left zeroed by every launch)
+    // scratch (owned by the context, one set per launch parity: consecutive launches on a stream
+    // may overlap; zero-initialised once, left zeroed by every launch)
     unsigned long long* cta_keys;  // ctas * 32: each CTA's exact top-list_len keys (scan order)
     unsigned long long* cta_xkeys; // ctas * 32: fast mode, the same entries' exact-mode keys
-    unsigned int* ctl;             // [0] page counter, [1] barrier arrivals, [2..4] unused,
-                                   // [5] barrier timeout, [6] CTAs done (exchange), [7] CTAs exited;
-                                   // the last CTA to exit zeroes [0], [1], [5], [6], [7]
+    unsigned int* ctl;             // [0] page counter, [1] publish ticket, [2..7] unused; the CTA
+                                   // holding the last ticket zeroes [0] and [1]
     const float* metamax;          // the segment's 4 meta-factor maxima (launch_metamax)
     uint8_t* owner;                // n_blocks: CTA that scored each page
     uint64_t* out_ids;
@@ -220,7 +230,7 @@ struct ScanLaunch {
 };
 int scan_ctas(int device_sms);
 size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t xch_world, uint32_t mode);
-int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream);
+int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream, bool pdl);
 int launch_exact_dots(const float* d_query, const float* d_rows, uint64_t n_rows, uint32_t dims, const uint64_t* d_sel,
                       uint32_t n, float* d_scores, uint32_t* d_bad, cudaStream_t stream);
 int launch_ring_search_batch(const float* d_queries, uint32_t n_q, uint32_t dims, const float* d_rows, uint32_t n,

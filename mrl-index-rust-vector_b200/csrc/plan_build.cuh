@@ -1,8 +1,8 @@
 // plan_build.cuh — the query-side plan build (QueryPlan::from_query_codec, src/scan.rs:105-266) as
-// a device function run by a whole CTA (at least 192 threads), shared by the standalone plan kernel
+// a device function run by a whole CTA (at least 256 threads), shared by the standalone plan kernel
 // (plan.cu) and the scan kernel's fused plan prologue (scan.cu).
 //
-// The Rademacher signs are computed while the query loads are in flight; six warps then build
+// The Rademacher signs are computed while the query loads are in flight; eight warps then build
 // independent parts of the plan (prefix, mid band, folded tail, long reductions, the raw-query
 // sums), and every thread of the CTA fills the tables. FWHTs run on warp shuffles (each butterfly
 // output depends only on its two inputs, so the values equal the sequential loop's); each
@@ -12,8 +12,9 @@
 // the two scoring-table sets the scan uses, written either into the plan or straight into a scan's
 // shared-memory tables:
 //   * fast mode: per-stage int32 tables whose exact integer sums replace the f32 loops; entries
-//     are rint(v * 2^shift) of exact double products, with shift chosen so that every stage sum
-//     stays below 2^30 in magnitude;
+//     are rint(v * 2^shift) of exact products v of two f32 values (computed in integer
+//     arithmetic, fix_prod), with shift chosen so that every stage sum stays below 2^30 in
+//     magnitude;
 //   * exact mode: the f32 products / addends of the reference loops.
 #pragma once
 
@@ -78,9 +79,32 @@ __device__ __forceinline__ int stage_shift(double maxabs, int count) {
 __device__ __forceinline__ double pow2(int e) {
     return e >= -1022 && e <= 1023 ? __longlong_as_double((long long)(1023 + e) << 52) : ldexp(1.0, e);
 }
-// rint(v * 2^shift): `pow2` = 2^shift exactly, so the product is exact and the conversion rounds
-// to nearest-even once.
-__device__ __forceinline__ int32_t fix(double v, double pow2) { return __double2int_rn(__dmul_rn(v, pow2)); }
+// rint(a * b * 2^sh), nearest-even, for finite f32 a and b: the exact product of the two 24-bit
+// significands (at most 48 bits), scaled by a power of two and rounded once, all in integer
+// arithmetic. It equals __double2int_rn((double)a * (double)b * 2^sh) (the double product is exact)
+// whenever the result fits in int32, which the stage shifts guarantee; double-precision
+// arithmetic is slow on this part and sits on every scan's critical path here.
+__device__ __forceinline__ int32_t fix_prod(float a, float b, int sh) {
+    const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+    const uint32_t xa = (ua >> 23) & 0xFFu, xb = (ub >> 23) & 0xFFu;
+    const uint64_t ma = (ua & 0x7FFFFFu) | (xa ? 0x800000u : 0u);
+    const uint64_t mb = (ub & 0x7FFFFFu) | (xb ? 0x800000u : 0u);
+    const uint64_t prod = ma * mb;
+    const int e = (int)(xa ? xa : 1u) + (int)(xb ? xb : 1u) - 300 + sh;  // |a * b * 2^sh| = prod * 2^e
+    uint64_t q;
+    if (e >= 0) {
+        q = e < 31 ? prod << e : 0ull;  // e >= 31 only for prod == 0 when the result fits
+    } else if (e <= -64) {
+        q = 0ull;  // prod < 2^48 < 2^(-e-1): below one half
+    } else {
+        const int n = -e;
+        q = prod >> n;
+        const uint64_t rem = prod - (q << n), half = 1ull << (n - 1);
+        q += (rem > half || (rem == half && (q & 1ull))) ? 1ull : 0ull;
+    }
+    const int32_t v = (int32_t)q;
+    return ((ua ^ ub) & 0x80000000u) ? -v : v;
+}
 
 // Largest |x| over the warp, as a double, as fmax over the lanes would give it (NaN lanes ignored;
 // 0 if every lane is NaN or zero): nonnegative floats order like their bit patterns. fmaxf also
@@ -160,14 +184,11 @@ enum { kRowL1, kRowSum, kRowIp, kRowMs, kRowMip, kRowBase, kRowB1, kRowTb, kRowB
 struct PlanShared {
     float mean[kPrefix + kRabitq];
     float rot[kPrefix];
-    float rq[kRabitq];
-    float mq[kRabitq];
-    float tf[kFold];
     int32_t fx[2 * (kRabitq + kFold)];  // fixed 1-bit stage values, see window_entry
     float scal[16];
     float cb[16];
     float w[kPrefix];  // EDEN prefix weight per dim: rot[d] / sqrt(64)
-    double pw[2];      // 2^shift of the prefix and L0 tables
+    int32_t psh[2];    // shift of the prefix and L0 tables
     // Rademacher signs: EDEN prefix rotation (64), EdenB1 mid-band rotation (128), tail fold
     // blocks (9 x 64)
     float sg[kSigns];
@@ -208,31 +229,63 @@ __device__ __forceinline__ void plan_inputs(const float* __restrict__ q, uint32_
     if (tid < 16) sh.cb[tid] = c;
 }
 
-// Phase A, threads 0..191 in six warp roles (independent until phase B):
+// The mid band's two rotations (src/rotate.rs:36-42 and, for EdenB1, src/scan.rs:159-174) by one
+// warp: rq = FWHT128 of the raw mid band, mq = FWHT128 of its Rademacher-signed copy (EdenB1 only).
+__device__ __forceinline__ void mid_rotations(const float* s_q, const PlanShared& sh, bool mid_b1, int lane,
+                                              float (&rq)[4], float (&mq)[4]) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int i = lane + 32 * r;
+        rq[r] = s_q[kPrefix + i];
+        mq[r] = f_mul(s_q[kPrefix + i], sh.sg[kPrefix + i]);
+    }
+    fwht_warp<4>(rq, lane);
+    if (mid_b1) fwht_warp<4>(mq, lane);
+}
+
+// fold_tail (src/rotate.rs:73-93) then FWHT64 (rotate_tail_fold) by one warp.
+__device__ __forceinline__ void tail_rotation(const float* s_q, const PlanShared& sh, uint32_t dims, bool has_tail,
+                                              int lane, float (&u)[2]) {
+    u[0] = 0.0f;
+    u[1] = 0.0f;
+    if (has_tail) {
+        const int nb = min((int)((dims - kTailStart) / kPrefix), kFoldBlocks);
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int d = lane + 32 * r;
+            for (int b = 0; b < nb; ++b)
+                u[r] = f_add(u[r], f_mul(sh.sg[kPrefix + kRabitq + b * kPrefix + d], s_q[kTailStart + b * kPrefix + d]));
+        }
+    }
+    fwht_warp<2>(u, lane);
+}
+
+// Phase A, threads 0..255 in eight warp roles (independent until phase B). The longest
+// sequential sums (128 terms) set its length, so each runs on a warp of its own, and the warps
+// that need a rotation's values for other work recompute the rotation instead of waiting for it:
 //   warp 0: prefix — EDEN query rotation, bit weights, prefix weights and the prefix shift;
-//   warp 1: mid band — RaBitQ and EdenB1 rotations, mid_w, the S1 shift and fixed values, then the
-//           rabitq_base and EdenB1 base sums;
-//   warp 2: folded tail — fold, rotation, tail_w, the S4 shift and fixed values, then the
-//           tail_fold_base and s4_abs_budget sums;
+//   warp 1: mid band — the rabitq_base and EdenB1 base sums;
+//   warp 6: mid band — mid_w, the S1 shift and fixed values, the stored plan's mid-band fields;
+//   warp 2: folded tail — the tail_fold_base and s4_abs_budget sums;
+//   warp 7: folded tail — tail_w, the S4 shift and fixed values, the stored plan's tail fields;
 //   warp 3: q_tail_sq (the longest sequential sum) and rabitq_lut, for a full plan only;
 //   warp 4: the prefix sums of the raw query (prefix_l1, prefix_sum, eden_mean_ip) and the L0 shift;
-//   warp 5: the mid-band sums of the raw query (q_mid_sq, eden_mid_mean_ip).
+//   warp 5: the mid-band sums of the raw query (q_mid_sq, eden_mid_mean_ip);
+//   warps 8 and up, when `rho_tab` is given: the scan's rho table (fill_rho_tab).
 // Each sequential sum keeps the reference's order: the warp first forms its addends in parallel,
 // then one lane per sum adds them in sequence (lane_chain).
 // Phase B, every thread of the CTA: the tables `need` asks for, written through `dst`.
-// Every thread of the CTA (at least 192) must call it, after plan_inputs; P may be global or shared
-// memory, s_q holds the dims floats plan_inputs loaded.
+// Every thread of the CTA (at least 256, and more than 256 to fill `rho_tab`) must call it, after
+// plan_inputs; P may be global or shared memory, s_q holds the dims floats plan_inputs loaded.
 __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec, uint32_t mid_codec, DevPlan* P,
-                                           float* s_q, PlanShared& sh, uint32_t need, const PlanDest& dst) {
+                                           float* s_q, PlanShared& sh, uint32_t need, const PlanDest& dst,
+                                           float2* rho_tab = nullptr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nthr = blockDim.x;
     const bool full = need == kNeedAll;
     mrl_query_plan* qp = &P->qp;
     float* s_mean = sh.mean;
     float* s_rot = sh.rot;
-    float* s_rq = sh.rq;
-    float* s_mq = sh.mq;
-    float* s_tf = sh.tf;
     int32_t* s_fx = sh.fx;
     float* s_scal = sh.scal;
     float* s_cb = sh.cb;
@@ -287,26 +340,34 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
             P->err_p = bound_up(ea);
             P->shift_prefix = sh_p;
             P->unscale_prefix = pow2(-sh_p);
-            sh.pw[0] = pow2(sh_p);
+            sh.psh[0] = sh_p;
         }
     } else if (warp == 1) {
-        // ---- mid band: rotate_mid_band (src/rotate.rs:36-42) and the EdenB1 rotation (src/scan.rs:159-174)
+        // ---- mid band: the addends of rabitq_base (src/scan.rs:180-186, subtracted) and of the
+        // EdenB1 base (src/scan.rs:523-532), then the two sums in reference order (lanes 0 and 1)
         float rq[4], mq[4];
+        mid_rotations(s_q, sh, mid_b1, lane, rq, mq);
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int i = lane + 32 * r;
-            rq[r] = s_q[kPrefix + i];
-            mq[r] = f_mul(s_q[kPrefix + i], sh.sg[kPrefix + i]);
+            sh.terms[kRowBase][i] = -f_mul(rq[r], kRabitqScale);
+            sh.terms[kRowB1][i] = f_mul(-kLloydB1Hi, f_mul(mq[r], kInvSqrt128));
         }
-        fwht_warp<4>(rq, lane);
-        if (mid_b1) fwht_warp<4>(mq, lane);
+        __syncwarp();
+        if (lane < 2) {
+            const float acc = lane_chain(sh.terms[kRowBase + lane], kRabitq);
+            if (lane == 0) s_scal[6] = acc;
+            else s_scal[9] = mid_b1 ? acc : 0.0f;
+        }
+    } else if (warp == 6) {
+        // ---- mid band: mid_w, the S1 shift and fixed values, the stored plan's fields
+        float rq[4], mq[4];
+        mid_rotations(s_q, sh, mid_b1, lane, rq, mq);
         float v1f[4];
         double ea = 0.0;
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int i = lane + 32 * r;
-            s_rq[i] = rq[r];
-            s_mq[i] = mq[r];
             const float pos = f_mul(rq[r], kRabitqScale);
             if (full) {
                 qp->rabitq_q[i] = rq[r];
@@ -315,10 +376,6 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
             }
             const float qd = f_mul(mq[r], kInvSqrt128);
             dst.mid_w[i] = mid_b1 ? f_mul(f_sub(kLloydB1Hi, -kLloydB1Hi), qd) : f_mul(2.0f, pos);
-            // the addends of rabitq_base (src/scan.rs:180-186, subtracted) and of the EdenB1 base
-            // (src/scan.rs:523-532)
-            sh.terms[kRowBase][i] = -pos;
-            sh.terms[kRowB1][i] = f_mul(-kLloydB1Hi, qd);
             // fixed S1 value of bit 1 (bit 0: its negation): kLloydB1Hi * qd (exact double
             // product) for EdenB1, pos for RaBitQ
             v1f[r] = mid_b1 ? qd : pos;
@@ -327,13 +384,12 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
         }
         const double mv = warp_max_abs(fmaxf(fmaxf(fabsf(v1f[0]), fabsf(v1f[1])), fmaxf(fabsf(v1f[2]), fabsf(v1f[3]))));
         const int sh_1 = stage_shift(mid_b1 ? (double)kLloydB1Hi * mv : mv, kRabitq);
-        const double pw_1 = pow2(sh_1);
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int i = lane + 32 * r;
-            const double v1 = mid_b1 ? (double)kLloydB1Hi * (double)v1f[r] : (double)v1f[r];
-            s_fx[2 * i] = fix(-v1, pw_1);
-            s_fx[2 * i + 1] = fix(v1, pw_1);
+            const int32_t f = fix_prod(mid_b1 ? kLloydB1Hi : v1f[r], mid_b1 ? v1f[r] : 1.0f, sh_1);
+            s_fx[2 * i] = -f;
+            s_fx[2 * i + 1] = f;
         }
         ea = warp_sum(ea);
         if (lane == 0) {
@@ -341,62 +397,54 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
             P->shift_s1 = sh_1;
             P->unscale_s1 = pow2(-sh_1);
         }
-        __syncwarp();
-        // rabitq_base and the EdenB1 base: sequential in reference order (lanes 0 and 1)
-        if (lane < 2) {
-            const float acc = lane_chain(sh.terms[kRowBase + lane], kRabitq);
-            if (lane == 0) s_scal[6] = acc;
-            else s_scal[9] = mid_b1 ? acc : 0.0f;
-        }
     } else if (warp == 2) {
-        // ---- folded tail: fold_tail (src/rotate.rs:73-93) then FWHT64 (rotate_tail_fold)
-        float u[2] = {0.0f, 0.0f};
-        if (has_tail) {
-            const int nb = min((int)((dims - kTailStart) / kPrefix), kFoldBlocks);
+        // ---- folded tail: the addends of tail_fold_base (subtracted) and s4_abs_budget
+        // (src/scan.rs:222-233), then the two sums in reference order (lanes 0 and 1)
+        float u[2];
+        tail_rotation(s_q, sh, dims, has_tail, lane, u);
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int d = lane + 32 * r;
-                for (int b = 0; b < nb; ++b)
-                    u[r] = f_add(u[r], f_mul(sh.sg[kPrefix + kRabitq + b * kPrefix + d], s_q[kTailStart + b * kPrefix + d]));
-            }
+        for (int r = 0; r < 2; ++r) {
+            const int d = lane + 32 * r;
+            const float pos = has_tail ? f_mul(u[r], kTailScale) : 0.0f;
+            sh.terms[kRowTb][d] = -pos;
+            sh.terms[kRowBud][d] = fabsf(pos);
         }
-        fwht_warp<2>(u, lane);
+        __syncwarp();
+        if (lane < 2) {
+            const float acc = has_tail ? lane_chain(sh.terms[kRowTb + lane], kFold) : 0.0f;
+            s_scal[7 + lane] = acc;
+        }
+    } else if (warp == 7) {
+        // ---- folded tail: tail_w, the S4 shift and fixed values, the stored plan's fields
+        float u[2];
+        tail_rotation(s_q, sh, dims, has_tail, lane, u);
         float pf[2];
         double ea = 0.0;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const int d = lane + 32 * r;
-            s_tf[d] = u[r];
             const float pos = has_tail ? f_mul(u[r], kTailScale) : 0.0f;
             if (full) {
                 qp->tail_fold_q[d] = has_tail ? u[r] : 0.0f;
                 qp->tail_fold_weights2[d] = has_tail ? f_mul(2.0f, pos) : 0.0f;
             }
             dst.tail_w[d] = has_tail ? f_mul(2.0f, pos) : 0.0f;
-            // the addends of tail_fold_base (subtracted) and s4_abs_budget (src/scan.rs:222-233)
-            sh.terms[kRowTb][d] = -pos;
-            sh.terms[kRowBud][d] = fabsf(pos);
             pf[r] = pos;
             ea += fabs((double)pos);
         }
         const int sh_4 = stage_shift(warp_max_abs(fmaxf(fabsf(pf[0]), fabsf(pf[1]))), kFold);
-        const double pw_4 = pow2(sh_4);
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const int d = lane + 32 * r;
-            s_fx[2 * (kRabitq + d)] = fix(-(double)pf[r], pw_4);
-            s_fx[2 * (kRabitq + d) + 1] = fix((double)pf[r], pw_4);
+            const int32_t f = fix_prod(pf[r], 1.0f, sh_4);
+            s_fx[2 * (kRabitq + d)] = -f;
+            s_fx[2 * (kRabitq + d) + 1] = f;
         }
         ea = warp_sum(ea);
         if (lane == 0) {
             P->err_4 = bound_up(ea);
             P->shift_s4 = sh_4;
             P->unscale_s4 = pow2(-sh_4);
-        }
-        __syncwarp();
-        if (lane < 2) {
-            const float acc = has_tail ? lane_chain(sh.terms[kRowTb + lane], kFold) : 0.0f;
-            s_scal[7 + lane] = acc;
         }
     } else if (warp == 3) {
         // q_tail_sq (src/scan.rs:203-207): the longest sequential sum; only the stored plan's
@@ -445,6 +493,13 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
             sh.terms[kRowSum][d] = qd;
             sh.terms[kRowIp][d] = f_mul(qd, s_mean[d]);
         }
+        __syncwarp();
+        if (lane < 3) {
+            const float acc = lane_chain(sh.terms[kRowL1 + lane], kPrefix);
+            if (lane == 0) s_scal[0] = acc;
+            else if (lane == 1) s_scal[1] = acc;
+            else s_scal[4] = eden ? acc : 0.0f;
+        }
         // L0Only shift (accum_plane, src/scan.rs:753-762): entries bit 3 of the level times
         // f32(q_d * 8)
         float e0[2];
@@ -460,14 +515,7 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
             P->err_0 = bound_up(ea0);
             P->shift_l0 = sh_0;
             P->unscale_l0 = pow2(-sh_0);
-            sh.pw[1] = pow2(sh_0);
-        }
-        __syncwarp();
-        if (lane < 3) {
-            const float acc = lane_chain(sh.terms[kRowL1 + lane], kPrefix);
-            if (lane == 0) s_scal[0] = acc;
-            else if (lane == 1) s_scal[1] = acc;
-            else s_scal[4] = eden ? acc : 0.0f;
+            sh.psh[1] = sh_0;
         }
     } else if (warp == 5) {
         // q_mid_sq (src/scan.rs:209-213) and eden_mid_mean_ip (src/scan.rs:167-169), lanes 0-1
@@ -484,15 +532,17 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
             if (lane == 0) s_scal[3] = acc;
             else s_scal[5] = mid_b1 ? acc : 0.0f;
         }
+    } else if (rho_tab) {
+        fill_rho_tab(rho_tab, tid - 256, nthr - 256);
     }
     __syncthreads();
 
     // ---- phase B: tables, one entry per item (prefix entry e = 16 d + l)
     if (need & kNeedFast) {
-        const double pw_p = sh.pw[0];
+        const int sp = sh.psh[0];
         for (int t = tid; t < kPrefix * 16; t += nthr) {
             const int d = t >> 4, l = t & 15;
-            dst.lut_prefix[t] = fix(eden ? (double)s_cb[l] * (double)sh.w[d] : (double)l * (double)s_q[d], pw_p);
+            dst.lut_prefix[t] = eden ? fix_prod(s_cb[l], sh.w[d], sp) : fix_prod((float)l, s_q[d], sp);
         }
         for (int t = tid; t < kS1Windows * 32; t += nthr) dst.lut_s1[t] = window_entry<kRabitq>(s_fx, t >> 5, t & 31);
         for (int t = tid; t < kS4Windows * 32; t += nthr)
@@ -504,10 +554,10 @@ __device__ __forceinline__ void build_plan(uint32_t dims, uint32_t prefix_codec,
             P->lut4_s4[t] = window4_entry(s_fx + 2 * kRabitq, t >> 4, t & 15);
     }
     if (need & kNeedL0) {  // bit 3 of the level times bit_weights[d][3] (accum_plane, src/scan.rs:753-762)
-        const double pw_0 = sh.pw[1];
+        const int s0 = sh.psh[1];
         for (int t = tid; t < kPrefix * 16; t += nthr) {
             const int d = t >> 4, l = t & 15;
-            dst.lut_l0[t] = (l & 8) ? fix((double)f_mul(s_q[d], 8.0f), pw_0) : 0;
+            dst.lut_l0[t] = (l & 8) ? fix_prod(f_mul(s_q[d], 8.0f), 1.0f, s0) : 0;
         }
     }
     if (need & kNeedExact) {  // f32 products of the reference's prefix loop (src/scan.rs:456-487)

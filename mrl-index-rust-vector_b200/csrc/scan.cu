@@ -284,34 +284,6 @@ __device__ __forceinline__ void reselect(const ScanLaunch& p, const int* tab, co
     if (tid == 0) *p.out_count = ng;
 }
 
-// Grid-wide barrier, once per launch (the launch is cooperative, so all CTAs are co-resident).
-// Control word 1 counts arrivals; it starts every launch at 0 because the last CTA to exit zeroes
-// it. The arrival is an acquire-release add, so the last CTA to arrive, and every CTA that reads
-// the full count with an acquire load, sees what the others published before they arrived. The
-// wait is bounded and reports a timeout instead of hanging.
-__device__ bool grid_barrier(unsigned* ctl, unsigned G, volatile int* s_ok) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        unsigned* count = ctl + 1;
-        unsigned before;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(count) : "memory");
-        int ok = 1;
-        if (before + 1u < G) {
-            unsigned it = 0;
-            while (true) {
-                unsigned c;
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(c) : "l"(count) : "memory");
-                if (c >= G) break;
-                if (++it > (1u << 22)) { ok = 0; atomicExch(ctl + 5, 1u); break; }  // ~0.3 s
-                if (it > 256) __nanosleep(64);
-            }
-        }
-        *s_ok = ok;
-    }
-    __syncthreads();
-    return *s_ok != 0;
-}
-
 // The scan's shared-memory tables from a plan (ints in fast mode, floats in exact mode).
 __device__ __forceinline__ void copy_tables(const DevPlan* __restrict__ P, int mode, int* tab, const ScanLaunch& p) {
     const int tid = threadIdx.x;
@@ -456,10 +428,186 @@ __host__ __device__ inline size_t fused_plan_bytes(uint32_t dims) {
     return align16(sizeof(DevPlan)) + align16((size_t)dims * sizeof(float)) + align16(sizeof(planb::PlanShared));
 }
 
-// Score-word probes for count_greater: the keys above probe_above(s) are those with a score > s, the
-// keys above probe_atleast(s) those with a score >= s.
+// Score-word probe for count_greater: the keys above probe_above(s) are those with a score > s.
 __device__ __forceinline__ u64 probe_above(float s) { return make_key(s, 0u) | 0xFFFFFFFFull; }
-__device__ __forceinline__ u64 probe_atleast(float s) { return (make_key(s, 0u) & 0xFFFFFFFF00000000ull) - 1ull; }
+
+// Order-preserving word of a score (the high word of its selection key): scores at least s are
+// the keys whose high word is at least score_word(s).
+__device__ __forceinline__ unsigned score_word(float s) { return (unsigned)(make_key(s, 0u) >> 32); }
+
+// Bin of a score word among kBins equal bins over [lo, lo + kBins / scale): monotone in w.
+__device__ __forceinline__ unsigned bin_of(unsigned w, unsigned lo, float scale) {
+    return min((unsigned)kBins - 1u, (unsigned)__fmul_rz(__uint2float_rz(w - lo), scale));
+}
+
+// The last CTA's finish. It loads every CTA's list into shared memory (rows LP keys apart) and
+// checks that their union holds the top k: a full list may have dropped a top-k member only if
+// the slots it dropped could still rank below k. Exact mode: its last key ranks below k. Fast mode:
+// a dropped slot's exact score is at most last + E and a top-k slot's exact score is at least
+// F_k - E, so the lists are safe when at least k keys score above F(x_max) + 4E, x_max being the
+// largest last key of a full list (ranks fall as keys grow, so it decides for all lists). Then the
+// keys whose fast score is at least F_k - 2E (F_k: the k-th largest fast score of the union) hold
+// the top k by exact key: the CTA locates F_k's bin in a histogram of the keys' score words,
+// gathers the exact keys of the keys whose score raised by 2E reaches that bin, sorts them in chunks
+// of 32 (one warp per chunk) and ranks each by binary searches over the chunks; the first k go to
+// the outputs in rank order. Exact mode (E = 0, exact keys = scan keys) takes the same path.
+// Returns false, having written no output, when the union may miss a top-k member or more than
+// `cap` keys pass the gather; the lists stay in cand / xcand for the caller's reselection.
+template <bool kFast>
+__device__ __forceinline__ bool finish_last(const ScanLaunch& p, uint64_t* out_ids, float* out_scores,
+                                            uint32_t* out_count, u64* cand, u64* xcand, unsigned LP, unsigned G,
+                                            float E, unsigned* hist, u64* gath, unsigned cap, unsigned* s_misc) {
+    __shared__ unsigned s_lo[kWarps], s_hi[kWarps], s_n[kWarps], s_a[kWarps];
+    __shared__ u64 s_xm[kWarps];
+    __shared__ unsigned s_b;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned L = p.list_len, k = p.k, n = G * L, lsh = (unsigned)(__ffs((int)L) - 1);
+    unsigned lo = 0xFFFFFFFFu, hi = 0u, cnt = 0u;
+    u64 xm = 0ull;
+    for (unsigned i0 = tid; i0 < n; i0 += 4u * kThreads) {
+        u64 x[4], y[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {  // four loads in flight per thread (the lists come from L2)
+            const unsigned i = i0 + (unsigned)j * kThreads;
+            const unsigned at = (i >> lsh) * 32 + (i & (L - 1));
+            x[j] = i < n ? __ldcg(p.cta_keys + at) : 0ull;
+            y[j] = kFast && i < n ? __ldcg(p.cta_xkeys + at) : 0ull;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const unsigned i = i0 + (unsigned)j * kThreads;
+            if (i < n) {
+                const unsigned at = (i >> lsh) * LP + (i & (L - 1));
+                cand[at] = x[j];
+                if (kFast) xcand[at] = y[j];
+                if (x[j]) {
+                    const unsigned w = (unsigned)(x[j] >> 32);
+                    lo = min(lo, w);
+                    hi = max(hi, w);
+                    ++cnt;
+                    if ((i & (L - 1)) == L - 1) xm = x[j] > xm ? x[j] : xm;
+                }
+            }
+        }
+    }
+    lo = __reduce_min_sync(kFull, lo);
+    hi = __reduce_max_sync(kFull, hi);
+    cnt = __reduce_add_sync(kFull, cnt);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const u64 y = shfl_xor_u64(xm, o);
+        xm = y > xm ? y : xm;
+    }
+    if (lane == 0) {
+        s_lo[warp] = lo;
+        s_hi[warp] = hi;
+        s_n[warp] = cnt;
+        s_xm[warp] = xm;
+    }
+    for (unsigned i = tid; i < (unsigned)kBins; i += kThreads) hist[i] = 0u;
+    if (tid == 0) s_misc[1] = 0u;
+    __syncthreads();
+    unsigned total = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+        total += s_n[w];
+        lo = min(lo, s_lo[w]);
+        hi = max(hi, s_hi[w]);
+        xm = s_xm[w] > xm ? s_xm[w] : xm;
+    }
+    if (total == 0u) {  // nothing live
+        if (tid == 0) *out_count = 0u;
+        return true;
+    }
+    // the clean test and the histogram of score words, in one pass
+    const u64 probe = kFast ? probe_above(__fadd_ru(key_score(xm), 4.0f * E)) : xm;
+    const float scale = __fdiv_rz((float)kBins, __fadd_ru(__uint2float_ru(hi - lo), 1.0f));
+    unsigned above = 0;
+    for (unsigned base = 0; base < n; base += kThreads) {  // warp-uniform trip count
+        const unsigned i = base + tid;
+        const u64 x = i < n ? cand[(i >> lsh) * LP + (i & (L - 1))] : 0ull;
+        above += x > probe ? 1u : 0u;
+        hist_add(hist, x != 0ull && total > k, x ? bin_of((unsigned)(x >> 32), lo, scale) : 0u, lane);
+    }
+    above = __reduce_add_sync(kFull, above);
+    if (lane == 0) s_a[warp] = above;
+    __syncthreads();
+    above = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) above += s_a[w];
+    if (xm != 0ull && above < k) return false;  // block-uniform
+    unsigned bstar = 0;
+    if (total > k) {
+        // bin of the k-th largest key: descending scan, thread t owns bins kBins-1-4t .. kBins-4-4t
+        unsigned c[4], lsum = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            c[j] = hist[kBins - 1 - 4 * tid - j];
+            lsum += c[j];
+        }
+        unsigned incl = lsum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned y = __shfl_up_sync(kFull, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane == 31) s_n[warp] = incl;  // every thread read s_n before the last barrier
+        __syncthreads();
+        unsigned cum = incl - lsum;
+        for (int w = 0; w < warp; ++w) cum += s_n[w];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (cum < k && k <= cum + c[j]) s_b = (unsigned)(kBins - 1 - 4 * tid - j);
+            cum += c[j];
+        }
+        __syncthreads();
+        bstar = s_b;
+    }
+    for (unsigned base = 0; base < n; base += kThreads) {  // warp-uniform trip count
+        const unsigned i = base + tid;
+        const unsigned at = (i >> lsh) * LP + (i & (L - 1));
+        const u64 x = i < n ? cand[at] : 0ull;
+        bool in = x != 0ull;
+        if (in && total > k) {
+            const unsigned w2 = kFast ? score_word(__fadd_ru(key_score(x), 2.0f * E)) : (unsigned)(x >> 32);
+            in = bin_of(w2, lo, scale) >= bstar;
+        }
+        const unsigned m = __ballot_sync(kFull, in);
+        unsigned b0 = 0;
+        if (lane == 0 && m) b0 = atomicAdd(&s_misc[1], (unsigned)__popc(m));
+        b0 = __shfl_sync(kFull, b0, 0);
+        const unsigned pos = b0 + (unsigned)__popc(m & ((1u << lane) - 1u));
+        if (in && pos < cap) gath[pos] = kFast ? xcand[at] : x;
+    }
+    __syncthreads();
+    const unsigned mc = s_misc[1];
+    if (mc > cap) return false;  // block-uniform
+    const unsigned nch = (mc + 31u) / 32u;
+    for (unsigned i = mc + tid; i < nch * 32u; i += kThreads) gath[i] = 0ull;
+    __syncthreads();
+    for (unsigned ch = warp; ch < nch; ch += kWarps) gath[ch * 32 + lane] = warp_sort32(gath[ch * 32 + lane], lane);
+    __syncthreads();
+    for (unsigned i = tid; i < nch * 32u; i += kThreads) {
+        const u64 x = gath[i];
+        if (!x) continue;
+        unsigned r0 = 0, r1 = 0, r2 = 0, r3 = 0, ch = 0;
+        for (; ch + 4u <= nch; ch += 4u) {  // four independent searches in flight
+            r0 += count_greater(gath + ch * 32, 32u, x);
+            r1 += count_greater(gath + ch * 32 + 32, 32u, x);
+            r2 += count_greater(gath + ch * 32 + 64, 32u, x);
+            r3 += count_greater(gath + ch * 32 + 96, 32u, x);
+        }
+        for (; ch < nch; ++ch) r0 += count_greater(gath + ch * 32, 32u, x);
+        const unsigned r = r0 + r1 + r2 + r3;
+        if (r < k) {
+            const uint32_t ord = key_ordinal(x);
+            out_ids[r] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
+            out_scores[r] = key_score(x);
+        }
+    }
+    if (tid == 0) *out_count = min(total, k);
+    return true;
+}
 
 template <int MODE, bool FUSED>
 __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
@@ -471,31 +619,29 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
     __shared__ u64 s_cta_tau;
     __shared__ unsigned s_seed_min, s_seed_cnt;
     __shared__ unsigned s_next;  // the CTA's next page of its range
-    __shared__ unsigned s_part[kWarps * 32];
-    __shared__ unsigned s_part2[kFast ? kWarps * 32 : 1];
-    __shared__ unsigned s_band[32];
-    __shared__ unsigned s_nband;
-    __shared__ unsigned char s_bandkey[32];
-    __shared__ u64 s_red64[kWarps];
-    __shared__ unsigned s_red32[kWarps];
     __shared__ unsigned s_nflag;
     __shared__ unsigned s_last;
     __shared__ int s_ok;
     __shared__ SelState s_sel;
     __shared__ unsigned s_misc[4];
+    __shared__ float s_E;
     extern __shared__ __align__(16) unsigned char s_dyn[];
     u64* s_queue = reinterpret_cast<u64*>(s_dyn);  // kWarps * kQueue
     u64* s_lists = s_queue + kWarps * kQueue;       // kWarps * 32
     u64* s_cand = s_lists + kWarps * 32;            // G * 33: scan keys of every CTA list
     const unsigned G = gridDim.x;
     u64* s_xcand = s_cand + G * 33;                 // G * 33: their exact keys (fast mode)
-    u64* s_gath = s_xcand + (kFast ? G * 33 : 0);   // pow2 >= k
+    u64* s_gath = s_xcand + (kFast ? G * 33 : 0);   // 2 * pow2 >= k
     unsigned P2 = 1;
     while (P2 < p.k) P2 <<= 1;
-    unsigned* s_hist = reinterpret_cast<unsigned*>(s_gath + P2);  // kBins
+    const unsigned gath_cap = 2u * P2;
+    unsigned* s_hist = reinterpret_cast<unsigned*>(s_gath + gath_cap);  // kBins
     unsigned* s_flags = s_hist + kBins;                          // G
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // The plan of an unfused launch may come from the launch before (a fused scan's stored plan),
+    // which may still be finishing under programmatic dependent launch: wait for it first.
+    if (!FUSED) asm volatile("griddepcontrol.wait;" ::: "memory");
     const unsigned L = p.list_len;
     unsigned* counter = p.ctl;
     const int* xtab = kFast ? reinterpret_cast<const int*>(s_xtab) : s_tab;
@@ -534,7 +680,7 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
 
     Scalars S;
     if (tid == 0) {
-        s_cta_tau = 0ull; s_seed_min = 0xFFFFFFFFu; s_seed_cnt = 0u; s_nflag = 0u; s_nband = 0u;
+        s_cta_tau = 0ull; s_seed_min = 0xFFFFFFFFu; s_seed_cnt = 0u; s_nflag = 0u;
         s_next = lo_c + 2u * kWarps;
     }
     const DevPlan* plan = p.plan;
@@ -554,7 +700,7 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
             full ? planb::plan_dest(ps)
                  : planb::PlanDest{s_tab, s_tab + kTabS1, s_tab + kTabS4, s_tab + kTabL0, xt, xt + kTabMidW, xt + kTabTailW,
                                    xt + kTabBw3};
-        planb::build_plan(p.dims, p.prefix_codec, p.mid_codec, ps, s_qb, *s_pb, need, dst);
+        planb::build_plan(p.dims, p.prefix_codec, p.mid_codec, ps, s_qb, *s_pb, need, dst, s_rho);
         __syncthreads();
         if (full) {  // keep the plan for mrl_plan_read and later scans
             const uint4* src = reinterpret_cast<const uint4*>(ps);
@@ -568,11 +714,13 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
         copy_tables(plan, MODE, s_tab, p);
         if constexpr (kFast) load_exact_tables(plan, s_xtab);
     }
-    fill_rho_tab(s_rho, tid, kThreads);
+    if (!FUSED) fill_rho_tab(s_rho, tid, kThreads);  // the fused build fills it with otherwise idle warps
     fill_scalars(plan, p.w_s4, p.depth, (int32_t)(p.list_len != 0u), S);  // one: 1 for every launch, opaque to the compiler
-    // bound on |fast score - exact score| of every slot of this segment (0 in exact mode)
-    const float E = kFast ? fast_error_bound(*plan, mm, p.w_s4, p.depth) : 0.0f;
+    // bound on |fast score - exact score| of every slot of this segment (0 in exact mode), by one
+    // thread (double-precision arithmetic)
+    if (kFast && tid == 0) s_E = fast_error_bound(*plan, mm, p.w_s4, p.depth);
     __syncthreads();
+    const float E = kFast ? s_E : 0.0f;
 
     WarpSel ws{0ull, 0u, 0};
     u64* q = s_queue + warp * kQueue;
@@ -639,191 +787,52 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
         if (kFast) p.cta_xkeys[blockIdx.x * 32 + lane] = xk;
         __threadfence();
     }
-    if (!grid_barrier(p.ctl, G, &s_ok)) {
-        if (tid == 0 && p.out_status) *p.out_status = 2u;  // barrier timed out: no result
-        return;
+    // Publish ticket (control word 1): the last CTA to publish its list finishes the query alone.
+    // The ticket is an acquire-release add, so its holder sees every list published before it; the
+    // other CTAs leave, and their SMs take the next launch's CTAs.
+    __syncthreads();
+    if (tid == 0) {
+        unsigned before;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(p.ctl + 1) : "memory");
+        s_last = before == G - 1u ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    // Programmatic dependent launch: wait until the previous launch on the stream has completed (its
+    // last CTA may still be finishing its query into the same outputs; two launches back used this
+    // launch's scratch), then let the next launch start on the SMs the other CTAs have left. With
+    // that order a launch starts only once the one two back has completed, which is what makes
+    // the context's two scratch parities enough.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (tid == 0) {  // every CTA is done with the page counter and the ticket
+        p.ctl[0] = 0u;
+        p.ctl[1] = 0u;
     }
 
-    // Every CTA's list into shared memory, rows LP = L | 1 keys apart (an odd stride: threads that
-    // each read a different list hit different banks).
     const unsigned LP = L | 1u;
-    {
-        // four loads in flight per thread before their stores (the lists come from L2)
-        const unsigned nl = G * L, lsh = (unsigned)(__ffs((int)L) - 1);
-        for (unsigned i0 = tid; i0 < nl; i0 += 4u * kThreads) {
-            u64 x[4], y[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const unsigned i = i0 + (unsigned)j * kThreads;
-                const unsigned at = (i >> lsh) * 32 + (i & (L - 1));
-                x[j] = i < nl ? __ldcg(p.cta_keys + at) : 0ull;
-                y[j] = kFast && i < nl ? __ldcg(p.cta_xkeys + at) : 0ull;
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const unsigned i = i0 + (unsigned)j * kThreads;
-                if (i < nl) {
-                    s_cand[(i >> lsh) * LP + (i & (L - 1))] = x[j];
-                    if (kFast) s_xcand[(i >> lsh) * LP + (i & (L - 1))] = y[j];
-                }
-            }
-        }
+    // outputs: the caller's, or this rank's record of the NVLink exchange
+    uint64_t* o_ids = p.out_ids;
+    float* o_scores = p.out_scores;
+    uint32_t* o_count = p.out_count;
+    if (p.xch_world) {
+        unsigned char* rec = const_cast<unsigned char*>(p.xch_rec[p.xch_rank]);
+        o_ids = reinterpret_cast<uint64_t*>(rec);
+        o_scores = reinterpret_cast<float*>(rec + (size_t)p.k * 8);
+        o_count = reinterpret_cast<uint32_t*>(rec + (size_t)p.k * 12);
     }
-    __syncthreads();
-
-    // A CTA list may have dropped a top-k member only if it is full and the slots it dropped could
-    // still rank below k. Exact mode: its last key ranks below k. Fast mode: a dropped slot's exact
-    // score is at most last + E and a top-k slot's exact score is at least F_k - E... so the list is
-    // safe when more than k keys score above F(last) + 4E (every top-k member's fast score is then
-    // within 2E of the k-th or above it). Ranks fall as keys grow, so testing the largest last key
-    // of a full list (x_max) decides for all lists. Each CTA computes this from the same lists, so
-    // all reach the same decision without further communication.
-    u64 last = 0ull;
-    unsigned live = 0;
-    if ((unsigned)tid < G) {
-        last = s_cand[tid * LP + L - 1];
-        live = count_greater(s_cand + tid * LP, L, 0ull);
-    }
-    {
-        u64 m = last;
-        unsigned t = live;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const u64 y = shfl_xor_u64(m, o);
-            m = y > m ? y : m;
-            t += __shfl_xor_sync(kFull, t, o);
-        }
-        if (lane == 0) { s_red64[warp] = m; s_red32[warp] = t; }
-    }
-    __syncthreads();
-    u64 x_max = 0ull;
-    unsigned total = 0;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-        x_max = s_red64[w] > x_max ? s_red64[w] : x_max;
-        total += s_red32[w];
-    }
-    const u64 x_probe = kFast ? probe_above(__fadd_ru(key_score(x_max), 4.0f * E)) : x_max;
-    // rank of x_max (threads c < G, list c) and of this CTA's own keys: lane l of warp w handles key
-    // l % L against the lists of group g = w * (32 / L) + l / L (lists g, g + NG, ...), partial
-    // counts reduced through shared memory. Fast mode counts, per own key x, the keys scoring above
-    // F(x) + 2E (certainly above x in exact order) and those scoring at least F(x) - 2E (the rest
-    // are certainly below); the ones in between (x itself, and near-ties) are ordered by their
-    // exact keys.
-    unsigned rx = ((unsigned)tid < G && x_max != 0ull) ? count_greater(s_cand + tid * LP, L, x_probe) : 0u;
-    const u64* mine = s_cand + blockIdx.x * LP;
-    const u64* xmine = s_xcand + blockIdx.x * LP;
-    const unsigned per_warp = 32u / L, NG = kWarps * per_warp;
-    const unsigned ki = (unsigned)lane % L, gi = (unsigned)lane / L;
-    const u64 x = gi < per_warp ? mine[ki] : 0ull;
-    u64 xh = x, xl = x;
-    if (kFast && x != 0ull) {
-        const float f = key_score(x);
-        xh = probe_above(__fadd_ru(f, 2.0f * E));
-        xl = probe_atleast(__fsub_rd(f, 2.0f * E));
-    }
-    unsigned cnt = 0, cnt2 = 0;
-    if (x != 0ull) {
-#pragma unroll 4
-        for (unsigned c = warp * per_warp + gi; c < G; c += NG) {
-            cnt += count_greater(s_cand + c * LP, L, xh);
-            if (kFast) cnt2 += count_greater(s_cand + c * LP, L, xl);
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) rx += __shfl_xor_sync(kFull, rx, o);
-    // list_len is a power of two: fold the warp's key groups onto lanes 0 .. L-1
-    for (unsigned o = 16; o >= L; o >>= 1) {
-        cnt += __shfl_down_sync(kFull, cnt, o);
-        if (kFast) cnt2 += __shfl_down_sync(kFull, cnt2, o);
-    }
-    s_part[warp * 32 + lane] = cnt;
-    if constexpr (kFast) s_part2[warp * 32 + lane] = cnt2;
-    __syncthreads();  // every thread has read s_red32 above
-    if (lane == 0) s_red32[warp] = rx;
-    __syncthreads();
-    unsigned rank_xmax = 0;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) rank_xmax += s_red32[w];
-    const bool clean = x_max == 0ull || rank_xmax >= p.k;
-
-    if (clean) {
-        // Rank of each own key. Exact mode: the number of keys above it. Fast mode: the keys
-        // certainly above it, plus the near-ties whose exact key is larger (rare: resolved by
-        // every thread, one list each, below).
-        unsigned r = 0xFFFFFFFFu;
-        if ((unsigned)tid < L && mine[tid] != 0ull) {
-            r = 0;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) r += s_part[w * 32 + tid];
-            if constexpr (kFast) {
-                unsigned r2 = 0;
-#pragma unroll
-                for (int w = 0; w < kWarps; ++w) r2 += s_part2[w * 32 + tid];
-                s_band[tid] = 0u;
-                if (r2 - r > 1u && r < p.k) s_bandkey[atomicAdd(&s_nband, 1u)] = (unsigned char)tid;
-            }
-        }
-        if (kFast) {
-            __syncthreads();
-            for (unsigned j = 0; j < s_nband; ++j) {  // block-uniform
-                const unsigned t = s_bandkey[j];
-                const u64 fx = mine[t], ex = xmine[t];
-                const float f = key_score(fx);
-                const u64 hi = probe_above(__fadd_ru(f, 2.0f * E)), lo = probe_atleast(__fsub_rd(f, 2.0f * E));
-                if ((unsigned)tid < G) {
-                    const u64* lst = s_cand + tid * LP;
-                    const unsigned a = count_greater(lst, L, hi), e = count_greater(lst, L, lo);
-                    unsigned n = 0;
-                    for (unsigned i = a; i < e; ++i)
-                        n += (lst[i] != fx && s_xcand[tid * LP + i] > ex) ? 1u : 0u;
-                    if (n) atomicAdd(&s_band[t], n);
-                }
-            }
-            __syncthreads();
-            if ((unsigned)tid < L && r != 0xFFFFFFFFu) r += s_band[tid];
-        }
-        const u64 okey = kFast ? xmine[tid < 32 ? tid : 0] : mine[tid < 32 ? tid : 0];
+    if (finish_last<kFast>(p, o_ids, o_scores, o_count, s_cand, kFast ? s_xcand : s_cand, LP, G, E, s_hist, s_gath,
+                           gath_cap, s_misc)) {
         if (p.xch_world) {
-            // this rank's top-k into its own record slot (local memory); the last CTA pushes the
-            // completed record to the other ranks
-            const size_t kk = p.k;
-            if ((unsigned)tid < L && r < p.k) {
-                const uint32_t ord = key_ordinal(okey);
-                unsigned char* rec = const_cast<unsigned char*>(p.xch_rec[p.xch_rank]);
-                reinterpret_cast<uint64_t*>(rec)[r] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
-                reinterpret_cast<float*>(rec + kk * 8)[r] = key_score(okey);
-            }
-            __syncthreads();
-            if (tid == 0) {
-                __threadfence();
-                s_last = atomicAdd(p.ctl + 6, 1u) == G - 1 ? 1u : 0u;
-            }
-            __syncthreads();
-            if (!s_last) return;
-            // the last CTA: every CTA's entries are in; add the count, then publish
-            __threadfence();
-            if (tid == 0)
-                *reinterpret_cast<uint32_t*>(const_cast<unsigned char*>(p.xch_rec[p.xch_rank]) + kk * 12) = min(total, p.k);
+            __threadfence();  // the record (stored by every thread) before its copies to the peers
             xch_publish_and_merge(p, s_dyn, &s_ok, 0u);
-            return;
-        }
-        // keys ranked below k are the top-k: each CTA writes its own in place
-        if ((unsigned)tid < L && r < p.k) {
-            const uint32_t ord = key_ordinal(okey);
-            p.out_ids[r] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
-            p.out_scores[r] = key_score(okey);
-        }
-        if (blockIdx.x == 0 && tid == 0) {
-            *p.out_count = min(total, p.k);
-            if (p.out_status) *p.out_status = 0u;
+        } else if (tid == 0 && p.out_status) {
+            *p.out_status = 0u;
         }
         return;
     }
-    // Rare path: CTA 0 alone finds the flagged lists (full, and dropped slots could rank below k),
-    // reselects by exact key over the lists plus those CTAs' rescanned pages, and writes the whole
-    // output.
-    if (blockIdx.x != 0) return;
+    // Rare path: find the flagged lists (full, and dropped slots could rank below k), reselect by
+    // exact key over the lists plus those CTAs' rescanned pages, and write the whole output.
     for (unsigned c = warp; c < G; c += kWarps) {
         const u64 lc = s_cand[c * LP + L - 1];
         if (lc == 0ull) continue;  // warp-uniform: list not full
@@ -835,42 +844,22 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
         if (lane == 0 && r < p.k) s_flags[atomicAdd(&s_nflag, 1u)] = c;
     }
     __syncthreads();
+    ScanLaunch own = p;
+    own.out_ids = o_ids;
+    own.out_scores = o_scores;
+    own.out_count = o_count;
+    reselect<MODE>(own, s_tab, xtab, s_rho, S, s_cand, s_xcand, s_gath, s_hist, s_flags, s_nflag, &s_sel, s_misc);
     if (p.xch_world) {
-        // exchange: reselect into this rank's own record, signal, merge
-        ScanLaunch own = p;
-        unsigned char* mine_rec = const_cast<unsigned char*>(p.xch_rec[p.xch_rank]);
-        own.out_ids = reinterpret_cast<uint64_t*>(mine_rec);
-        own.out_scores = reinterpret_cast<float*>(mine_rec + (size_t)p.k * 8);
-        own.out_count = reinterpret_cast<uint32_t*>(mine_rec + (size_t)p.k * 12);
-        reselect<MODE>(own, s_tab, xtab, s_rho, S, s_cand, s_xcand, s_gath, s_hist, s_flags, s_nflag, &s_sel, s_misc);
+        __threadfence();
         xch_publish_and_merge(p, s_dyn, &s_ok, 1u);
         return;
     }
-    reselect<MODE>(p, s_tab, xtab, s_rho, S, s_cand, s_xcand, s_gath, s_hist, s_flags, s_nflag, &s_sel, s_misc);
     if (tid == 0 && p.out_status) *p.out_status = 1u;
 }
 
 template <int MODE, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
     scan_body<MODE, FUSED>(p);
-    // Exit ticket: the last CTA to leave zeroes the control words (page counter, barrier count,
-    // exchange count, timeout flag, the ticket), so the next launch on this scratch starts clean
-    // whichever path this one took, a bounded wait that ran out included. The ticket is an
-    // acquire-release add: every CTA's uses of the words come before its ticket, and the last
-    // ticket's holder sees them all before it stores the zeros, which the next launch sees at the
-    // kernel boundary.
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        unsigned before;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(p.ctl + 7) : "memory");
-        if (before == gridDim.x - 1) {
-            p.ctl[0] = 0u;
-            p.ctl[1] = 0u;
-            p.ctl[5] = 0u;
-            p.ctl[6] = 0u;
-            p.ctl[7] = 0u;
-        }
-    }
 }
 
 // ---- ScanStats (src/scan.rs:269-302, 654-799) ----------------------------------------------------
@@ -1032,14 +1021,15 @@ size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t 
     size_t p2 = 1;
     while (p2 < k) p2 <<= 1;
     const size_t lists = (size_t)ctas * 33 * (mode == MRL_MODE_FAST ? 2 : 1);  // scan keys (+ exact keys)
-    size_t bytes = sizeof(u64) * (kWarps * kQueue + kWarps * 32 + lists + p2) + sizeof(unsigned) * (kBins + ctas);
+    size_t bytes = sizeof(u64) * (kWarps * kQueue + kWarps * 32 + lists + 2 * p2) + sizeof(unsigned) * (kBins + ctas);
     if (fused_dims) bytes = std::max(bytes, fused_plan_bytes(fused_dims));
     if (xch_world) bytes = std::max(bytes, xch_merge_bytes(xch_world, k));  // records to merge
     return bytes;
 }
 
-// Cooperative launch: one CTA per SM, all co-resident (the grid barrier relies on it).
-int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream) {
+// One CTA per SM. With `pdl` the launch may begin while the previous kernel on the stream finishes
+// (programmatic dependent launch; the kernel waits for it before touching what they share).
+int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream, bool pdl) {
     const bool fused = p.query != nullptr;
     const size_t smem = scan_smem_bytes(ctas, p.k, fused ? p.dims : 0u, p.xch_world, p.mode);
     const void* fn = p.mode == MRL_MODE_FAST ? (fused ? (const void*)scan_kernel<MRL_MODE_FAST, true>
@@ -1057,8 +1047,18 @@ int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream) {
     }
     ScanLaunch arg = p;
     arg.xch_tree = p.xch_world && xch_use_tree(p.xch_world, p.k) ? 1u : 0u;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     void* args[] = {&arg};
-    if (cudaLaunchCooperativeKernel(fn, dim3(ctas), dim3(kThreads), args, smem, stream) != cudaSuccess) return -1;
+    if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess) return -1;
     return 0;
 }
 

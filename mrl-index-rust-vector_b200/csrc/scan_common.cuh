@@ -192,14 +192,6 @@ __device__ __forceinline__ void fill_scalars(const DevPlan* __restrict__ P, floa
     S.one = one;
 }
 
-// rho_ratio = flags / 255 and sqrt(max(1 - r^2, 0)) (src/block.rs:74-84) for every flags byte.
-__device__ __forceinline__ void fill_rho_tab(float2* rho_tab, int tid, int nthr) {
-    for (int i = tid; i < 256; i += nthr) {
-        const float rho = __fdiv_rn((float)i, 255.0f);
-        const float r = fminf(fmaxf(rho, 0.0f), 1.0f);
-        rho_tab[i] = make_float2(rho, __fsqrt_rn(fmaxf(__fsub_rn(1.0f, __fmul_rn(r, r)), 0.0f)));
-    }
-}
 
 // Shared-memory table layout of the single-query scan (ints in fast mode, floats in exact mode).
 constexpr int kTabInts = kPrefix * 16 + kS1Windows * 32 + kS4Windows * 32 + kPrefix * 16;  // 3296

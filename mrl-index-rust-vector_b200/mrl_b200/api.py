@@ -545,8 +545,8 @@ def score_bound(segment: Segment, plan: QueryPlan, cfg, q: int = 0) -> float:
 
 
 def control_words(dev: "Device") -> List[int]:
-    """The context's 8 scan control words (mrl_debug_control_words)."""
-    out = (C.c_uint32 * 8)()
+    """The context's scan control words, 8 per launch parity (mrl_debug_control_words)."""
+    out = (C.c_uint32 * 16)()
     check(dev.ptr, dev.lib.mrl_debug_control_words(dev.ptr, out))
     return list(out)
 

@@ -352,9 +352,9 @@ def test_order_dependent_configs_refused(ora, dev, corpus768):
 
 
 def test_control_words_left_zero(ora, dev, corpus768):
-    """Every launch's last CTA to exit zeroes the scan control words, on the clean path, the
-    re-selection path and the fused path alike, so a launch never inherits a page counter or
-    barrier count from the one before."""
+    """Every launch's last CTA (the holder of the last publish ticket) zeroes its parity's control
+    words, on the clean path, the re-selection path and the fused path alike, so a launch never
+    inherits a page counter or ticket count from the one two before."""
     M = mb()
     seg = M.Segment.upload(corpus768["eden"], dev)
     qs = corpus768["qs"]
@@ -365,11 +365,11 @@ def test_control_words_left_zero(ora, dev, corpus768):
             for mode in (M.ScanMode.EXACT, M.ScanMode.FAST):
                 M.scan_blocks_batch(seg, gp, M.ScanConfig(shortlist_cand=256, mode=mode))
                 w = M.control_words(dev)
-                assert list(w) == [0] * 8, (ll, mode, w)
+                assert list(w) == [0] * 16, (ll, mode, w)
         M.query_scan(seg, qs, M.ScanConfig(shortlist_cand=64), prefix_codec=M.PrefixCodec.EDEN_PROD,
                      eden=fit(corpus768["mean"]))
         w = M.control_words(dev)
-        assert list(w) == [0] * 8, w
+        assert list(w) == [0] * 16, w
     finally:
         dev.set_list_len(0)
     gp.free()
