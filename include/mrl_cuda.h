@@ -192,7 +192,7 @@ int mrl_scan_batch_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pla
  * Same arguments, results and errors as mrl_scan_device, but the scan scratch comes from a static
  * per-device region inside the library instead of the context, so a successful call allocates no
  * device or host memory: for callers that must not allocate while answering a query. Limits, set
- * by that region's fixed size (1,179,904 bytes): seg must hold at most MRL_STATIC_MAX_BLOCKS pages
+ * by that region's fixed size (1,180,928 bytes): seg must hold at most MRL_STATIC_MAX_BLOCKS pages
  * and the device at most MRL_STATIC_MAX_CTAS SMs, else MRL_ERR_INVALID with a message naming the
  * limit. The first call on a device looks the region up (and may load the module), so make it
  * before any stream capture begins. The looked-up address is kept for the life of the process and

@@ -11,22 +11,27 @@
 #include "mrl_internal.cuh"
 
 // Scan scratch for mrl_scan_device_static, placed in the module's own global memory so that entry
-// point allocates nothing. Layout (bytes): control words [0, 256), per-CTA key lists
-// [256, 256 + 256*32*8), their exact-mode keys (the next 256*32*8), one owner byte per page after
-// that. Sized for grids of at most MRL_STATIC_MAX_CTAS CTAs and segments of at most
-// MRL_STATIC_MAX_BLOCKS pages: 1,179,904 bytes per device in all.
+// point allocates nothing. Layout (bytes): control words and per-CTA ready flags [0, 1280), per-CTA
+// key lists [1280, 1280 + 256*32*8), their exact-mode keys (the next 256*32*8), one owner byte per
+// page after that. Sized for grids of at most MRL_STATIC_MAX_CTAS CTAs and segments of at most
+// MRL_STATIC_MAX_BLOCKS pages: 1,180,928 bytes per device in all.
 namespace {
 constexpr size_t kStaticCtlOff = 0;
-constexpr size_t kStaticKeysOff = 256;
+constexpr size_t kStaticKeysOff = 1280;
 constexpr size_t kStaticListBytes = (size_t)MRL_STATIC_MAX_CTAS * 32 * sizeof(unsigned long long);
 constexpr size_t kStaticXKeysOff = kStaticKeysOff + kStaticListBytes;
 constexpr size_t kStaticOwnerOff = kStaticXKeysOff + kStaticListBytes;
 constexpr size_t kStaticBytes = kStaticOwnerOff + (size_t)MRL_STATIC_MAX_BLOCKS;
-static_assert(kStaticBytes == 1179904, "static scratch size is documented in the header");
+static_assert(kStaticBytes == 1180928, "static scratch size is documented in the header");
 static_assert(mrl::kCtlWords * sizeof(unsigned) <= kStaticKeysOff - kStaticCtlOff, "control words overflow");
-static_assert(MRL_STATIC_MAX_CTAS <= 256, "owner bytes hold CTA indices < 256");
+static_assert(MRL_STATIC_MAX_CTAS <= 256 && MRL_STATIC_MAX_CTAS <= mrl::kMaxScanCtas, "owner bytes hold CTA indices < 256");
 }  // namespace
 static __device__ __align__(256) unsigned char g_static_scan_scratch[kStaticBytes];
+
+namespace {
+// Initial done words of the two scratch parities: launch 0 waits for -2, launch 1 for -1.
+const unsigned int kDoneInit[2] = {0xFFFFFFFEu, 0xFFFFFFFFu};
+}  // namespace
 
 struct mrl_ctx {
     int device = 0;
@@ -42,7 +47,8 @@ struct mrl_ctx {
     unsigned int* ctl = nullptr;             // per parity mrl::kCtlWords
     uint8_t* owner = nullptr;
     size_t owner_bytes = 0;
-    uint32_t scan_seq = 0;
+    uint32_t scan_seq = 0;      // launches so far; launch s uses parity s & 1
+    unsigned int* done = nullptr;  // per parity: sequence number of the last launch that released it
     uint32_t list_len_override = 0;
     // grow-only scratch for host-facing calls: inputs (queries, rows, means) and outputs
     void* tmp = nullptr;
@@ -266,14 +272,20 @@ int ensure_owner(mrl_ctx* ctx, uint64_t n_blocks) {
     return ensure_buf(ctx, (void**)&ctx->owner, &ctx->owner_bytes, 2 * (n_blocks ? n_blocks : 1));
 }
 
-// The context scratch of the next scan launch: the parities alternate launch by launch.
+// The context scratch of the next scan launch: the parities alternate launch by launch. Launch s
+// waits until launch s - 2 (the previous user of its parity) has released it; a parity's done word
+// starts at the sequence number a launch two before the first would have had. launched() advances
+// the sequence once the launch has been issued.
 void take_scratch(mrl_ctx* ctx, mrl::ScanLaunch& p) {
-    const size_t par = ctx->scan_seq++ & 1u;
+    const size_t par = ctx->scan_seq & 1u;
     p.cta_keys = ctx->cta_keys + par * 2 * 32 * (size_t)ctx->sms;
     p.cta_xkeys = p.cta_keys + 32 * (size_t)ctx->sms;
     p.ctl = ctx->ctl + par * mrl::kCtlWords;
     p.owner = ctx->owner + par * (ctx->owner_bytes / 2);
+    p.done = ctx->done + par;
+    p.seq = ctx->scan_seq;
 }
+void launched(mrl_ctx* ctx) { ++ctx->scan_seq; }
 
 int check_codec(mrl_ctx* ctx, const mrl_codec_desc* codec) {
     if (!codec) return fail(ctx, MRL_ERR_INVALID, "codec is NULL");
@@ -368,6 +380,10 @@ int mrl_ctx_create(int device, mrl_ctx** out) {
     mrl_ctx* ctx = new mrl_ctx();
     ctx->device = device;
     ctx->sms = prop.multiProcessorCount;
+    if (ctx->sms > mrl::kMaxScanCtas) {  // one scan CTA per SM, each with a ready flag
+        delete ctx;
+        return MRL_ERR_INVALID;
+    }
     if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
         delete ctx;
         return MRL_ERR_CUDA;
@@ -375,8 +391,10 @@ int mrl_ctx_create(int device, mrl_ctx** out) {
     ctx->stream = ctx->own_stream;
     if (cudaMalloc(&ctx->cta_keys, sizeof(unsigned long long) * 2 * 2 * 32 * (size_t)ctx->sms) != cudaSuccess ||
         cudaMalloc(&ctx->ctl, sizeof(unsigned int) * 2 * mrl::kCtlWords) != cudaSuccess ||
+        cudaMalloc(&ctx->done, sizeof(unsigned int) * 2) != cudaSuccess ||
         cudaMalloc(&ctx->d_means, 192 * sizeof(float)) != cudaSuccess ||
         cudaMemset(ctx->ctl, 0, sizeof(unsigned int) * 2 * mrl::kCtlWords) != cudaSuccess ||
+        cudaMemcpy(ctx->done, kDoneInit, sizeof(kDoneInit), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) {
         mrl_ctx_destroy(ctx);
         return MRL_ERR_NOMEM;
@@ -391,6 +409,7 @@ void mrl_ctx_destroy(mrl_ctx* ctx) {
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->cta_keys);
     cudaFree(ctx->ctl);
+    cudaFree(ctx->done);
     cudaFree(ctx->owner);
     cudaFree(ctx->tmp);
     cudaFree(ctx->tmp_out);
@@ -689,6 +708,7 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
         }
         take_scratch(ctx, p);
         if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+        launched(ctx);
     }
     return MRL_OK;
 }
@@ -845,6 +865,7 @@ int mrl_query_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const float* d_queri
         p.plan_out = plans->d + i;
         take_scratch(ctx, p);
         if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+        launched(ctx);
     }
     return MRL_OK;
 }
@@ -1011,6 +1032,7 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
     p.xch_flag_in = reinterpret_cast<const unsigned*>(ex->local + ex->flags_off()) + parity * ex->world;
     take_scratch(ctx, p);
     if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+    launched(ctx);
     return MRL_OK;
 }
 
@@ -1288,7 +1310,9 @@ int mrl_debug_score_bound(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pla
 int mrl_debug_control_words(mrl_ctx* ctx, uint32_t* out) {
     if (!ctx || !out) return MRL_ERR_INVALID;
     if (int rc = set_device(ctx)) return rc;
-    MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out, ctx->ctl, sizeof(unsigned) * 2 * mrl::kCtlWords, cudaMemcpyDeviceToHost, ctx->stream));
+    for (int par = 0; par < 2; ++par)  // the 8 control words of each parity
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out + 8 * par, ctx->ctl + par * mrl::kCtlWords, 8 * sizeof(unsigned),
+                                          cudaMemcpyDeviceToHost, ctx->stream));
     MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     return MRL_OK;
 }

@@ -199,8 +199,12 @@ struct ScanLaunch {
     // may overlap; zero-initialised once, left zeroed by every launch)
     unsigned long long* cta_keys;  // ctas * 32: each CTA's exact top-list_len keys (scan order)
     unsigned long long* cta_xkeys; // ctas * 32: fast mode, the same entries' exact-mode keys
-    unsigned int* ctl;             // [0] page counter, [1] publish ticket, [2..7] unused; the CTA
-                                   // holding the last ticket zeroes [0] and [1]
+    unsigned int* ctl;             // kCtlWords: [0] page counter, [1] publish ticket, [7] exit ticket,
+                                   // [kCtlReady + c] CTA c's list is published; the last CTA to
+                                   // exit zeroes them all
+    unsigned int* done;            // launch sequence number of the last launch to release this
+                                   // scratch (nullptr: scratch of one launch at a time, no check)
+    uint32_t seq;                  // this launch's sequence number on the context
     const float* metamax;          // the segment's 4 meta-factor maxima (launch_metamax)
     uint8_t* owner;                // n_blocks: CTA that scored each page
     uint64_t* out_ids;
@@ -243,7 +247,11 @@ int launch_pack_records(const uint64_t* d_ids, const float* d_scores, const uint
                         uint32_t k, void* d_records, cudaStream_t stream);
 int launch_merge_topk_batch(const void* d_lists, uint32_t n_lists, uint32_t n_q, uint32_t stride, uint32_t k,
                             uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_counts, cudaStream_t stream);
-constexpr int kCtlWords = 8;
+// Scan control words per launch: [0] page counter, [1] publish ticket, [7] exit ticket, then from
+// kCtlReady one ready flag per CTA (at most kMaxScanCtas CTAs).
+constexpr int kMaxScanCtas = 256;
+constexpr int kCtlReady = 8;
+constexpr int kCtlWords = kCtlReady + kMaxScanCtas;
 // batched fast-mode scan (bscan.cu): per-(query, CTA) top-32 lists in `scratch`
 // (batch_scratch_bytes), then one selection CTA per query
 size_t batch_scratch_bytes(uint32_t ctas, uint32_t n_q);

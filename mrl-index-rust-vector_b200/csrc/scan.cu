@@ -416,10 +416,6 @@ __device__ void xch_publish_and_merge(const ScanLaunch& p, unsigned char* smem, 
     if (tid == 0 && p.out_status) *p.out_status = status;
 }
 
-__device__ __forceinline__ u64 shfl_xor_u64(u64 v, int o) {
-    const unsigned lo = __shfl_xor_sync(kFull, (unsigned)v, o), hi = __shfl_xor_sync(kFull, (unsigned)(v >> 32), o);
-    return ((u64)hi << 32) | lo;
-}
 
 // Shared-memory layout of the fused plan build, aliasing the selection buffers (unused until the
 // scoring loop): the plan, the query copy, the build's scratch.
@@ -440,52 +436,71 @@ __device__ __forceinline__ unsigned bin_of(unsigned w, unsigned lo, float scale)
     return min((unsigned)kBins - 1u, (unsigned)__fmul_rz(__uint2float_rz(w - lo), scale));
 }
 
-// The last CTA's finish. It loads every CTA's list into shared memory (rows LP keys apart) and
-// checks that their union holds the top k: a full list may have dropped a top-k member only if
-// the slots it dropped could still rank below k. Exact mode: its last key ranks below k. Fast mode:
-// a dropped slot's exact score is at most last + E and a top-k slot's exact score is at least
-// F_k - E, so the lists are safe when at least k keys score above F(x_max) + 4E, x_max being the
-// largest last key of a full list (ranks fall as keys grow, so it decides for all lists). Then the
-// keys whose fast score is at least F_k - 2E (F_k: the k-th largest fast score of the union) hold
-// the top k by exact key: the CTA locates F_k's bin in a histogram of the keys' score words,
-// gathers the exact keys of the keys whose score raised by 2E reaches that bin, sorts them in chunks
-// of 32 (one warp per chunk) and ranks each by binary searches over the chunks; the first k go to
-// the outputs in rank order. Exact mode (E = 0, exact keys = scan keys) takes the same path.
-// Returns false, having written no output, when the union may miss a top-k member or more than
-// `cap` keys pass the gather; the lists stay in cand / xcand for the caller's reselection.
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Summary of the CTA lists gathered by the finisher.
+struct ListSums {
+    unsigned total;  // keys in the union
+    unsigned lo, hi; // lowest and highest score word
+    u64 xm;          // largest last key of a full list (0: no list is full)
+};
+
+// The finisher (the first CTA to publish) loads every CTA's list into shared memory (rows LP keys
+// apart) as each list's ready flag appears, so the loads overlap the other CTAs' scoring: thread c
+// waits for CTA c's flag and loads its list, all lists in parallel. Every wait is bounded (about
+// 1 s); returns false if a list never arrived.
 template <bool kFast>
-__device__ __forceinline__ bool finish_last(const ScanLaunch& p, uint64_t* out_ids, float* out_scores,
-                                            uint32_t* out_count, u64* cand, u64* xcand, unsigned LP, unsigned G,
-                                            float E, unsigned* hist, u64* gath, unsigned cap, unsigned* s_misc) {
-    __shared__ unsigned s_lo[kWarps], s_hi[kWarps], s_n[kWarps], s_a[kWarps];
+__device__ __forceinline__ bool finisher_load(const ScanLaunch& p, u64* cand, u64* xcand, unsigned LP, unsigned G,
+                                              ListSums& out) {
+    __shared__ unsigned s_lo[kWarps], s_hi[kWarps], s_n[kWarps], s_ok[kWarps];
     __shared__ u64 s_xm[kWarps];
-    __shared__ unsigned s_b;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const unsigned L = p.list_len, k = p.k, n = G * L, lsh = (unsigned)(__ffs((int)L) - 1);
+    const unsigned L = p.list_len;
     unsigned lo = 0xFFFFFFFFu, hi = 0u, cnt = 0u;
     u64 xm = 0ull;
-    for (unsigned i0 = tid; i0 < n; i0 += 4u * kThreads) {
-        u64 x[4], y[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {  // four loads in flight per thread (the lists come from L2)
-            const unsigned i = i0 + (unsigned)j * kThreads;
-            const unsigned at = (i >> lsh) * 32 + (i & (L - 1));
-            x[j] = i < n ? __ldcg(p.cta_keys + at) : 0ull;
-            y[j] = kFast && i < n ? __ldcg(p.cta_xkeys + at) : 0ull;
+    bool ok = true;
+    for (unsigned c = tid; c < G; c += kThreads) {
+        const unsigned* ready = p.ctl + kCtlReady + c;
+        unsigned it = 0;
+        while (ld_acquire_gpu(ready) == 0u) {
+            if (++it > (1u << 20)) { ok = false; break; }
+            if (it > 8) __nanosleep(64);
         }
+        if (!ok) break;
+        const uint4* src = reinterpret_cast<const uint4*>(p.cta_keys + c * 32);
+        const uint4* xsrc = reinterpret_cast<const uint4*>(p.cta_xkeys + c * 32);
+        const unsigned nv = (L + 1u) / 2u;  // 16-byte pairs of entries (the row holds 32 entries)
+        for (unsigned h = 0; h < nv; h += 4u) {  // four 16-byte loads (8 keys) of each array in flight
+            uint4 v[4], xv[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const unsigned i = i0 + (unsigned)j * kThreads;
-            if (i < n) {
-                const unsigned at = (i >> lsh) * LP + (i & (L - 1));
-                cand[at] = x[j];
-                if (kFast) xcand[at] = y[j];
-                if (x[j]) {
-                    const unsigned w = (unsigned)(x[j] >> 32);
-                    lo = min(lo, w);
-                    hi = max(hi, w);
-                    ++cnt;
-                    if ((i & (L - 1)) == L - 1) xm = x[j] > xm ? x[j] : xm;
+            for (int j = 0; j < 4; ++j) {
+                if (h + j < nv) {
+                    v[j] = __ldcg(src + h + j);
+                    if (kFast) xv[j] = __ldcg(xsrc + h + j);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const unsigned e = 2u * (h + j);  // entry index of the pair's first key
+                if (e < L) {
+                    const u64 x0 = ((u64)v[j].y << 32) | v[j].x, x1 = ((u64)v[j].w << 32) | v[j].z;
+                    cand[c * LP + e] = x0;
+                    if (kFast) xcand[c * LP + e] = ((u64)xv[j].y << 32) | xv[j].x;
+                    if (x0) { lo = min(lo, (unsigned)(x0 >> 32)); hi = max(hi, (unsigned)(x0 >> 32)); ++cnt; }
+                    if (e == L - 1u) xm = x0 > xm ? x0 : xm;  // the list's last key
+                    if (e + 1u < L) {
+                        cand[c * LP + e + 1] = x1;
+                        if (kFast) xcand[c * LP + e + 1] = ((u64)xv[j].w << 32) | xv[j].z;
+                        if (x1) { lo = min(lo, (unsigned)(x1 >> 32)); hi = max(hi, (unsigned)(x1 >> 32)); ++cnt; }
+                        if (e + 1u == L - 1u) xm = x1 > xm ? x1 : xm;
+                    }
                 }
             }
         }
@@ -493,9 +508,10 @@ __device__ __forceinline__ bool finish_last(const ScanLaunch& p, uint64_t* out_i
     lo = __reduce_min_sync(kFull, lo);
     hi = __reduce_max_sync(kFull, hi);
     cnt = __reduce_add_sync(kFull, cnt);
+    const bool wok = __all_sync(kFull, ok);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-        const u64 y = shfl_xor_u64(xm, o);
+        const u64 y = __shfl_xor_sync(kFull, xm, o);
         xm = y > xm ? y : xm;
     }
     if (lane == 0) {
@@ -503,31 +519,74 @@ __device__ __forceinline__ bool finish_last(const ScanLaunch& p, uint64_t* out_i
         s_hi[warp] = hi;
         s_n[warp] = cnt;
         s_xm[warp] = xm;
+        s_ok[warp] = wok ? 1u : 0u;
     }
-    for (unsigned i = tid; i < (unsigned)kBins; i += kThreads) hist[i] = 0u;
-    if (tid == 0) s_misc[1] = 0u;
     __syncthreads();
-    unsigned total = 0;
+    out.total = 0;
+    out.lo = 0xFFFFFFFFu;
+    out.hi = 0u;
+    out.xm = 0ull;
+    bool all = true;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
-        total += s_n[w];
-        lo = min(lo, s_lo[w]);
-        hi = max(hi, s_hi[w]);
-        xm = s_xm[w] > xm ? s_xm[w] : xm;
+        out.total += s_n[w];
+        out.lo = min(out.lo, s_lo[w]);
+        out.hi = max(out.hi, s_hi[w]);
+        out.xm = s_xm[w] > out.xm ? s_xm[w] : out.xm;
+        all = all && s_ok[w] != 0u;
     }
+    return all;
+}
+
+// The finisher's ranking, every list in shared memory. The lists' union holds the top k unless a
+// full list dropped a member: a list may have dropped one only if it is full and the slots it
+// dropped could still rank below k. Exact mode: its last key ranks below k. Fast mode: a dropped
+// slot's exact score is at most last + E and a top-k slot's exact score is at least F_k - E, so
+// the lists are safe when at least k keys score above F(x_max) + 4E, x_max being the largest last
+// key of a full list (ranks fall as keys grow, so it decides for all lists). In that (clean) case
+// the keys whose fast score is at least F_k - 2E (F_k: the k-th largest fast score of the union)
+// hold the top k by exact key, and they all score above x_max. The CTA locates F_k's bin in a
+// histogram of the score words above x_max, gathers the exact keys of the keys whose score raised
+// by 2E reaches that bin, and ranks each gathered key by counting the larger ones; the first k go to
+// the outputs in rank order. Exact mode (E = 0, exact keys = scan keys) takes the same path. Returns
+// false, having written no output, when the union may miss a top-k member or more than `cap` keys
+// pass the gather; the caller then reselects.
+template <bool kFast>
+__device__ __forceinline__ bool finish_rank(const ScanLaunch& p, uint64_t* out_ids, float* out_scores,
+                                            uint32_t* out_count, const u64* cand, const u64* xcand, unsigned LP,
+                                            unsigned G, float E, const ListSums& ls, unsigned* hist, u64* gath,
+                                            unsigned cap, unsigned* s_misc) {
+    __shared__ unsigned s_a[kWarps], s_n[kWarps];
+    __shared__ unsigned s_b;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned L = p.list_len, k = p.k, n = G * L, lsh = (unsigned)(__ffs((int)L) - 1);
+    const unsigned total = ls.total;
     if (total == 0u) {  // nothing live
         if (tid == 0) *out_count = 0u;
         return true;
     }
-    // the clean test and the histogram of score words, in one pass
+    const u64 xm = ls.xm;
     const u64 probe = kFast ? probe_above(__fadd_ru(key_score(xm), 4.0f * E)) : xm;
-    const float scale = __fdiv_rz((float)kBins, __fadd_ru(__uint2float_ru(hi - lo), 1.0f));
+    const unsigned base = xm ? (unsigned)(xm >> 32) : ls.lo;  // the histogram covers [base, hi]
+    const float scale = __fdiv_rz((float)kBins, __fadd_ru(__uint2float_ru(ls.hi - base), 1.0f));
+    for (unsigned i = tid; i < (unsigned)kBins; i += kThreads) hist[i] = 0u;
+    if (tid == 0) s_misc[1] = 0u;
+    __syncthreads();
+    // the clean test and the histogram, one pass (four keys in flight per thread)
     unsigned above = 0;
-    for (unsigned base = 0; base < n; base += kThreads) {  // warp-uniform trip count
-        const unsigned i = base + tid;
-        const u64 x = i < n ? cand[(i >> lsh) * LP + (i & (L - 1))] : 0ull;
-        above += x > probe ? 1u : 0u;
-        hist_add(hist, x != 0ull && total > k, x ? bin_of((unsigned)(x >> 32), lo, scale) : 0u, lane);
+    for (unsigned b0 = tid; b0 < n; b0 += 4u * kThreads) {
+        u64 x[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const unsigned i = b0 + (unsigned)j * kThreads;
+            x[j] = i < n ? cand[(i >> lsh) * LP + (i & (L - 1))] : 0ull;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const unsigned w = (unsigned)(x[j] >> 32);
+            above += x[j] > probe ? 1u : 0u;
+            if (x[j] != 0ull && w >= base && total > k) atomicAdd(&hist[bin_of(w, base, scale)], 1u);
+        }
     }
     above = __reduce_add_sync(kFull, above);
     if (lane == 0) s_a[warp] = above;
@@ -551,7 +610,7 @@ __device__ __forceinline__ bool finish_last(const ScanLaunch& p, uint64_t* out_i
             const unsigned y = __shfl_up_sync(kFull, incl, o);
             if (lane >= o) incl += y;
         }
-        if (lane == 31) s_n[warp] = incl;  // every thread read s_n before the last barrier
+        if (lane == 31) s_n[warp] = incl;
         __syncthreads();
         unsigned cum = incl - lsum;
         for (int w = 0; w < warp; ++w) cum += s_n[w];
@@ -563,54 +622,66 @@ __device__ __forceinline__ bool finish_last(const ScanLaunch& p, uint64_t* out_i
         __syncthreads();
         bstar = s_b;
     }
-    for (unsigned base = 0; base < n; base += kThreads) {  // warp-uniform trip count
-        const unsigned i = base + tid;
-        const unsigned at = (i >> lsh) * LP + (i & (L - 1));
-        const u64 x = i < n ? cand[at] : 0ull;
-        bool in = x != 0ull;
-        if (in && total > k) {
-            const unsigned w2 = kFast ? score_word(__fadd_ru(key_score(x), 2.0f * E)) : (unsigned)(x >> 32);
-            in = bin_of(w2, lo, scale) >= bstar;
+    for (unsigned b0 = tid; b0 < n; b0 += 4u * kThreads) {  // four keys in flight per thread
+        u64 x[4];
+        unsigned at[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const unsigned i = b0 + (unsigned)j * kThreads;
+            at[j] = (i >> lsh) * LP + (i & (L - 1));
+            x[j] = i < n ? cand[at[j]] : 0ull;
         }
-        const unsigned m = __ballot_sync(kFull, in);
-        unsigned b0 = 0;
-        if (lane == 0 && m) b0 = atomicAdd(&s_misc[1], (unsigned)__popc(m));
-        b0 = __shfl_sync(kFull, b0, 0);
-        const unsigned pos = b0 + (unsigned)__popc(m & ((1u << lane) - 1u));
-        if (in && pos < cap) gath[pos] = kFast ? xcand[at] : x;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            bool in = x[j] != 0ull;
+            if (in && total > k) {
+                const unsigned w2 = kFast ? score_word(__fadd_ru(key_score(x[j]), 2.0f * E)) : (unsigned)(x[j] >> 32);
+                in = w2 >= base && bin_of(w2, base, scale) >= bstar;
+            }
+            if (in) {
+                const unsigned pos = atomicAdd(&s_misc[1], 1u);
+                if (pos < cap) gath[pos] = kFast ? xcand[at[j]] : x[j];
+            }
+        }
     }
     __syncthreads();
     const unsigned mc = s_misc[1];
     if (mc > cap) return false;  // block-uniform
-    const unsigned nch = (mc + 31u) / 32u;
-    for (unsigned i = mc + tid; i < nch * 32u; i += kThreads) gath[i] = 0ull;
+    if (tid == 0) gath[mc] = 0ull;  // pad to an even count for the pair loads (gath holds cap + 2)
     __syncthreads();
-    for (unsigned ch = warp; ch < nch; ch += kWarps) gath[ch * 32 + lane] = warp_sort32(gath[ch * 32 + lane], lane);
-    __syncthreads();
-    for (unsigned i = tid; i < nch * 32u; i += kThreads) {
+    const ulonglong2* g2 = reinterpret_cast<const ulonglong2*>(gath);
+    const unsigned np = (mc + 1u) / 2u;
+    for (unsigned i = tid; i < mc; i += kThreads) {
         const u64 x = gath[i];
-        if (!x) continue;
-        unsigned r0 = 0, r1 = 0, r2 = 0, r3 = 0, ch = 0;
-        for (; ch + 4u <= nch; ch += 4u) {  // four independent searches in flight
-            r0 += count_greater(gath + ch * 32, 32u, x);
-            r1 += count_greater(gath + ch * 32 + 32, 32u, x);
-            r2 += count_greater(gath + ch * 32 + 64, 32u, x);
-            r3 += count_greater(gath + ch * 32 + 96, 32u, x);
+        unsigned r[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        unsigned j = 0;
+        for (; j + 4u <= np; j += 4u) {  // every thread reads the same entries: broadcasts
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const ulonglong2 y = g2[j + q];
+                r[2 * q] += y.x > x ? 1u : 0u;
+                r[2 * q + 1] += y.y > x ? 1u : 0u;
+            }
         }
-        for (; ch < nch; ++ch) r0 += count_greater(gath + ch * 32, 32u, x);
-        const unsigned r = r0 + r1 + r2 + r3;
-        if (r < k) {
+        for (; j < np; ++j) {
+            const ulonglong2 y = g2[j];
+            r[0] += y.x > x ? 1u : 0u;
+            r[1] += y.y > x ? 1u : 0u;
+        }
+        const unsigned rk = r[0] + r[1] + r[2] + r[3] + r[4] + r[5] + r[6] + r[7];
+        if (rk < k) {
             const uint32_t ord = key_ordinal(x);
-            out_ids[r] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
-            out_scores[r] = key_score(x);
+            out_ids[rk] = ((uint64_t)(p.block_id_base + (ord >> 6)) << 16) | (uint64_t)(ord & 63u);
+            out_scores[rk] = key_score(x);
         }
     }
     if (tid == 0) *out_count = min(total, k);
     return true;
 }
 
+// Returns false only when the launch left without touching its scratch (the scratch stayed busy).
 template <int MODE, bool FUSED>
-__device__ __forceinline__ void scan_body(const ScanLaunch& p) {
+__device__ __forceinline__ bool scan_body(const ScanLaunch& p) {
     constexpr bool kFast = MODE == MRL_MODE_FAST;
     __shared__ __align__(16) int s_tab[kTabInts];
     // fast mode: the exact-mode tables too, for the exact rescoring of the CTA's list
@@ -635,13 +706,18 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
     unsigned P2 = 1;
     while (P2 < p.k) P2 <<= 1;
     const unsigned gath_cap = 2u * P2;
-    unsigned* s_hist = reinterpret_cast<unsigned*>(s_gath + gath_cap);  // kBins
+    unsigned* s_hist = reinterpret_cast<unsigned*>(s_gath + gath_cap + 2);  // kBins
     unsigned* s_flags = s_hist + kBins;                          // G
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // The plan of an unfused launch may come from the launch before (a fused scan's stored plan),
     // which may still be finishing under programmatic dependent launch: wait for it first.
     if (!FUSED) asm volatile("griddepcontrol.wait;" ::: "memory");
+    // Programmatic dependent launch: the next launch on the stream may start now; its CTAs take the
+    // SMs this launch's CTAs leave as they publish. It touches its scratch (the other parity) only
+    // once the launch that used that scratch before has released it (p.done), and its outputs only
+    // after this launch has completed (griddepcontrol.wait in its finisher).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const unsigned L = p.list_len;
     unsigned* counter = p.ctl;
     const int* xtab = kFast ? reinterpret_cast<const int*>(s_xtab) : s_tab;
@@ -667,16 +743,14 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
         if (g < hi_c) return g;
         return n_static + atomicAdd(counter, 1u);
     };
-    uint32_t b = 0, bn = 0;
-    if (lane == 0) {
-        b = grab(lo_c + (uint32_t)warp);
-        bn = grab(lo_c + (uint32_t)(kWarps + warp));
-    }
-    b = __shfl_sync(kFull, b, 0);
-    bn = __shfl_sync(kFull, bn, 0);
+    // The warps' first two pages come from the CTA's own range when it has them (no scratch is
+    // touched before the scratch wait below), else from the pool after that wait.
+    const uint32_t none = 0xFFFFFFFFu;
+    uint32_t b = lo_c + (uint32_t)warp < hi_c ? lo_c + (uint32_t)warp : none;
+    uint32_t bn = lo_c + (uint32_t)(kWarps + warp) < hi_c ? lo_c + (uint32_t)(kWarps + warp) : none;
     // first page in flight before the tables are read
     Slot4 a0, a1;
-    if (b < p.n_blocks) { load_slot(p.pages, b, lane, a0); load_slot(p.pages, b, lane + 32, a1); }
+    if (b != none) { load_slot(p.pages, b, lane, a0); load_slot(p.pages, b, lane + 32, a1); }
 
     Scalars S;
     if (tid == 0) {
@@ -719,8 +793,34 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
     // bound on |fast score - exact score| of every slot of this segment (0 in exact mode), by one
     // thread (double-precision arithmetic)
     if (kFast && tid == 0) s_E = fast_error_bound(*plan, mm, p.w_s4, p.depth);
+    // This launch's scratch (page counter, lists, ready flags, owner) is free once the launch that
+    // used it before (two launches back) has released it; under full residency it always has by
+    // now. Bounded (about 1 s).
+    if (p.done && tid == 0) {
+        unsigned it = 0;
+        int ok = 1;
+        while (ld_acquire_gpu(p.done) != p.seq - 2u) {
+            if (++it > (1u << 20)) { ok = 0; break; }
+            if (it > 8) __nanosleep(128);
+        }
+        s_ok = ok;
+    }
     __syncthreads();
+    if (p.done && !s_ok) {
+        if (tid == 0 && p.out_status) *p.out_status = 8u;  // the scratch stayed busy: no result
+        return false;
+    }
     const float E = kFast ? s_E : 0.0f;
+    {
+        const bool b_static = b != none;  // warp-uniform
+        if (lane == 0) {  // pool pages for warps whose range had none left
+            if (b == none) b = n_static + atomicAdd(counter, 1u);
+            if (bn == none) bn = n_static + atomicAdd(counter, 1u);
+        }
+        b = __shfl_sync(kFull, b, 0);
+        bn = __shfl_sync(kFull, bn, 0);
+        if (!b_static && b < p.n_blocks) { load_slot(p.pages, b, lane, a0); load_slot(p.pages, b, lane + 32, a1); }
+    }
 
     WarpSel ws{0ull, 0u, 0};
     u64* q = s_queue + warp * kQueue;
@@ -786,31 +886,25 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
         p.cta_keys[blockIdx.x * 32 + lane] = fk;
         if (kFast) p.cta_xkeys[blockIdx.x * 32 + lane] = xk;
         __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_gpu(p.ctl + kCtlReady + blockIdx.x, 1u);  // this CTA's list is out
     }
-    // Publish ticket (control word 1): the last CTA to publish its list finishes the query alone.
-    // The ticket is an acquire-release add, so its holder sees every list published before it; the
-    // other CTAs leave, and their SMs take the next launch's CTAs.
+    // Publish ticket (control word 1): the first CTA to publish its list (ticket 0) finishes the
+    // query; the others leave, and their SMs take the next launch's CTAs.
     __syncthreads();
-    if (tid == 0) {
-        unsigned before;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(p.ctl + 1) : "memory");
-        s_last = before == G - 1u ? 1u : 0u;
-    }
+    if (tid == 0) s_last = atomicAdd(p.ctl + 1, 1u) == 0u ? 1u : 0u;
     __syncthreads();
-    if (!s_last) return;
-    // Programmatic dependent launch: wait until the previous launch on the stream has completed (its
-    // last CTA may still be finishing its query into the same outputs; two launches back used this
-    // launch's scratch), then let the next launch start on the SMs the other CTAs have left. With
-    // that order a launch starts only once the one two back has completed, which is what makes
-    // the context's two scratch parities enough.
+    if (!s_last) return true;
+    // Wait until the previous launch on the stream has completed: its finisher may still be writing
+    // its query's result into the same outputs.
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (tid == 0) {  // every CTA is done with the page counter and the ticket
-        p.ctl[0] = 0u;
-        p.ctl[1] = 0u;
+    const unsigned LP = L | 1u;
+    ListSums ls;
+    if (!finisher_load<kFast>(p, s_cand, s_xcand, LP, G, ls)) {
+        if (tid == 0 && p.out_status) *p.out_status = 2u;  // a CTA's list never arrived: no result
+        return true;
     }
 
-    const unsigned LP = L | 1u;
     // outputs: the caller's, or this rank's record of the NVLink exchange
     uint64_t* o_ids = p.out_ids;
     float* o_scores = p.out_scores;
@@ -821,7 +915,7 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
         o_scores = reinterpret_cast<float*>(rec + (size_t)p.k * 8);
         o_count = reinterpret_cast<uint32_t*>(rec + (size_t)p.k * 12);
     }
-    if (finish_last<kFast>(p, o_ids, o_scores, o_count, s_cand, kFast ? s_xcand : s_cand, LP, G, E, s_hist, s_gath,
+    if (finish_rank<kFast>(p, o_ids, o_scores, o_count, s_cand, kFast ? s_xcand : s_cand, LP, G, E, ls, s_hist, s_gath,
                            gath_cap, s_misc)) {
         if (p.xch_world) {
             __threadfence();  // the record (stored by every thread) before its copies to the peers
@@ -829,7 +923,7 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
         } else if (tid == 0 && p.out_status) {
             *p.out_status = 0u;
         }
-        return;
+        return true;
     }
     // Rare path: find the flagged lists (full, and dropped slots could rank below k), reselect by
     // exact key over the lists plus those CTAs' rescanned pages, and write the whole output.
@@ -852,14 +946,36 @@ __device__ __forceinline__ void scan_body(const ScanLaunch& p) {
     if (p.xch_world) {
         __threadfence();
         xch_publish_and_merge(p, s_dyn, &s_ok, 1u);
-        return;
+        return true;
     }
     if (tid == 0 && p.out_status) *p.out_status = 1u;
+    return true;
 }
 
 template <int MODE, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
-    scan_body<MODE, FUSED>(p);
+    if (!scan_body<MODE, FUSED>(p)) return;  // the scratch stayed busy: leave it untouched
+    // Exit ticket (control word 7): the last CTA to leave zeroes this launch's control words and
+    // ready flags, so the launch that next uses this scratch starts clean whichever path this one
+    // took, a wait that ran out included. The ticket is an acquire-release add: every CTA's uses of
+    // the words come before its ticket, and the last holder sees them all before it stores the zeros,
+    // which the next launch on this scratch sees at the kernel boundary.
+    __shared__ unsigned s_exit;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned before;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(p.ctl + 7) : "memory");
+        s_exit = before == gridDim.x - 1 ? 1u : 0u;
+    }
+    __syncthreads();
+    if (s_exit) {
+        for (unsigned i = threadIdx.x; i < (unsigned)kCtlWords; i += blockDim.x) p.ctl[i] = 0u;
+        __syncthreads();
+        if (threadIdx.x == 0 && p.done) {  // the scratch is free for the launch after next
+            __threadfence();
+            st_release_gpu(p.done, p.seq);
+        }
+    }
 }
 
 // ---- ScanStats (src/scan.rs:269-302, 654-799) ----------------------------------------------------
@@ -1021,7 +1137,7 @@ size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t 
     size_t p2 = 1;
     while (p2 < k) p2 <<= 1;
     const size_t lists = (size_t)ctas * 33 * (mode == MRL_MODE_FAST ? 2 : 1);  // scan keys (+ exact keys)
-    size_t bytes = sizeof(u64) * (kWarps * kQueue + kWarps * 32 + lists + 2 * p2) + sizeof(unsigned) * (kBins + ctas);
+    size_t bytes = sizeof(u64) * (kWarps * kQueue + kWarps * 32 + lists + 2 * p2 + 2) + sizeof(unsigned) * (kBins + ctas);
     if (fused_dims) bytes = std::max(bytes, fused_plan_bytes(fused_dims));
     if (xch_world) bytes = std::max(bytes, xch_merge_bytes(xch_world, k));  // records to merge
     return bytes;
