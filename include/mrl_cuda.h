@@ -239,14 +239,33 @@ int mrl_query_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const float* d_queri
                           const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                           const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
                           uint32_t* d_out_counts, uint32_t* d_out_status);
-/* The same from host queries to host results (synchronous). The query goes to the device from a
- * pinned staging buffer of the context, and the scan stores its results straight into that
- * buffer's device mapping, so the call makes one host-to-device copy and no device-to-host copy;
- * the results are then copied to the caller's buffers on the host. */
+/* The same from host queries to host results (synchronous). Each query (dims <= 1024) travels in
+ * its scan launch's parameters, and the scan stores its top-k straight into a pinned,
+ * device-mapped result slot of the context (mrl_query_submit / mrl_query_collect below), so the
+ * call issues no separate copy in either direction; up to MRL_MAX_INFLIGHT of its queries are in
+ * flight at once. Larger dims or an empty segment go through a pinned staging buffer instead (one
+ * host-to-device copy). Fails with MRL_ERR_INVALID while submitted queries are uncollected. */
 int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint32_t n_q, uint32_t dims,
                    const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg,
                    const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* out_ids,
                    float* out_scores, uint32_t* out_counts);
+/* ---- pipelined host queries (no counterpart in the reference, whose scan is a blocking call) --- */
+/* mrl_query_submit launches the fused plan + scan of one host query (dims <= 1024 floats, carried in
+ * the launch's parameters; non-finite values refused) and returns without waiting; the scan stores
+ * the query's top-k, count and status in the context's result slot `slot` (pinned, device-mapped
+ * host memory) and then that slot's completion word. mrl_query_collect waits for the slot's word
+ * (spinning on host memory; about 10 s at most), then copies the `count` hits into out_ids /
+ * out_scores (room for shortlist_cand each) and frees the slot. Queries on different slots may be in
+ * flight together: consecutive scan launches on the context's stream overlap, so a caller that keeps
+ * two or more submitted reaches the device's throughput from host memory. Results and errors are
+ * those of mrl_query_scan; a slot must be collected before it is submitted again, and a larger
+ * shortlist_cand than before needs every slot collected. The plan is not stored. */
+#define MRL_MAX_INFLIGHT 8
+int mrl_query_submit(mrl_ctx* ctx, const mrl_seg* seg, const float* query, uint32_t dims,
+                     const mrl_codec_desc* codec, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+                     const uint32_t* time_hi, uint32_t slot);
+int mrl_query_collect(mrl_ctx* ctx, uint32_t slot, uint64_t* out_ids, float* out_scores,
+                      uint32_t* out_count);
 /* ---- NVLink exchange: the sharded scan's merge inside the scan launch --------------------- */
 /* One exchange per rank (one process per GPU of a node, up to 8). Each rank's scan leaves its
  * top-k record (layout below) in its own exchange area and raises a flag there; the last CTA to

@@ -1,6 +1,8 @@
 // capi.cu — the C ABI of libmrl_b200 (include/mrl_cuda.h): contexts, device segments, plans,
 // scans and encodes. Host-side C++; every entry point catches its own failures and reports them
 // through a status code plus mrl_last_error, never by aborting.
+#include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -76,6 +78,15 @@ struct mrl_ctx {
     void* h_io = nullptr;
     void* h_io_dev = nullptr;
     size_t h_io_bytes = 0;
+    // pipelined host queries (mrl_query_submit / mrl_query_collect): MRL_MAX_INFLIGHT result slots
+    // in pinned, device-mapped memory, laid out for shortlists up to slot_k; the scan stores each
+    // query's top-k there and then the slot's completion word, on which the host waits
+    unsigned char* h_slots = nullptr;
+    unsigned char* d_slots = nullptr;
+    size_t slot_stride = 0;
+    uint32_t slot_k = 0;
+    uint32_t slot_seq[MRL_MAX_INFLIGHT] = {};
+    bool slot_busy[MRL_MAX_INFLIGHT] = {};
 };
 
 // RingBuffer's pending embeddings (src/ring.rs:49-119) mirrored in HBM: `len` rows of `dims` f32
@@ -252,7 +263,7 @@ mrl::ScanLaunch make_launch(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
     p.block_ts = seg->ts;
     p.n_blocks = (uint32_t)seg->n_blocks;
     p.block_id_base = seg->block_id_base;
-    p.plan = plans->d + q;
+    p.plan = plans ? plans->d + q : nullptr;
     p.k = cfg->shortlist_cand;
     p.list_len = ctx->list_len_override ? ctx->list_len_override : auto_list_len(p.k, (uint32_t)ctx->sms);
     p.w_s4 = cfg->stratum4_weight;
@@ -418,6 +429,7 @@ void mrl_ctx_destroy(mrl_ctx* ctx) {
     cudaFree(ctx->ebuf);
     cudaFree(ctx->bbuf);
     if (ctx->h_io) cudaFreeHost(ctx->h_io);
+    if (ctx->h_slots) cudaFreeHost(ctx->h_slots);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
 }
@@ -870,14 +882,12 @@ int mrl_query_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const float* d_queri
     return MRL_OK;
 }
 
-int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint32_t n_q, uint32_t dims,
-                   const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
-                   const uint32_t* time_hi, uint64_t* out_ids, float* out_scores, uint32_t* out_counts) {
-    if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
-    if (int rc = check_cfg(ctx, cfg, dims)) return rc;
-    if (n_q == 0) return MRL_OK;
-    if (!queries || !out_ids || !out_scores || !out_counts) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
-    if (int rc = set_device(ctx)) return rc;
+// mrl_query_scan for queries a launch cannot carry (dims > kInlineQueryMax) or an empty segment:
+// the queries go to the device from the context's pinned staging, and the results come back into it.
+static int query_scan_staged(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint32_t n_q, uint32_t dims,
+                             const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg,
+                             const uint32_t* time_lo, const uint32_t* time_hi, uint64_t* out_ids, float* out_scores,
+                             uint32_t* out_counts) {
     const size_t qbytes = (size_t)n_q * dims * sizeof(float);
     const size_t nk = (size_t)n_q * cfg->shortlist_cand;
     const size_t o_off = (qbytes + 255) & ~(size_t)255;
@@ -917,6 +927,169 @@ int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint3
     std::memcpy(out_scores, h_out + nk * sizeof(uint64_t), nk * sizeof(float));
     std::memcpy(out_counts, cs, n_q * sizeof(uint32_t));
     return MRL_OK;
+}
+
+namespace {
+
+// Result slot layout (bytes) for shortlists up to k: ids k*8 | scores k*4 | count | status |
+// completion word.
+size_t slot_stride_for(uint32_t k) { return ((size_t)k * 12 + 12 + 255) & ~(size_t)255; }
+
+int ensure_slots(mrl_ctx* ctx, uint32_t k) {
+    if (ctx->slot_k >= k && ctx->h_slots) return MRL_OK;
+    for (int s = 0; s < MRL_MAX_INFLIGHT; ++s)
+        if (ctx->slot_busy[s]) return fail(ctx, MRL_ERR_INVALID, "a larger shortlist_cand needs every query slot collected first");
+    if (ctx->h_slots) cudaFreeHost(ctx->h_slots);
+    ctx->h_slots = ctx->d_slots = nullptr;
+    ctx->slot_k = 0;
+    const size_t stride = slot_stride_for(k);
+    void* h = nullptr;
+    cudaError_t e = cudaHostAlloc(&h, stride * MRL_MAX_INFLIGHT, cudaHostAllocMapped | cudaHostAllocPortable);
+    if (e != cudaSuccess) return fail(ctx, MRL_ERR_NOMEM, std::string("cudaHostAlloc query slots: ") + cudaGetErrorString(e));
+    void* d = nullptr;
+    e = cudaHostGetDevicePointer(&d, h, 0);
+    if (e != cudaSuccess) {
+        cudaFreeHost(h);
+        return cuda_fail(ctx, e, "cudaHostGetDevicePointer query slots");
+    }
+    std::memset(h, 0, stride * MRL_MAX_INFLIGHT);
+    ctx->h_slots = static_cast<unsigned char*>(h);
+    ctx->d_slots = static_cast<unsigned char*>(d);
+    ctx->slot_stride = stride;
+    ctx->slot_k = k;
+    for (int s = 0; s < MRL_MAX_INFLIGHT; ++s) ctx->slot_seq[s] = 0;
+    return MRL_OK;
+}
+
+// Submits one host query into `slot`; plan_out (device, may be NULL) receives its plan.
+int query_submit(mrl_ctx* ctx, const mrl_seg* seg, const float* query, uint32_t dims, const mrl_codec_desc* codec,
+                 mrl::DevPlan* plan_out, const mrl_scan_cfg* cfg, const uint32_t* time_lo, const uint32_t* time_hi,
+                 uint32_t slot) {
+    if (!ctx || !seg || !query) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg, dims)) return rc;
+    if (int rc = check_codec(ctx, codec)) return rc;
+    if (slot >= MRL_MAX_INFLIGHT) return fail(ctx, MRL_ERR_INVALID, "slot >= MRL_MAX_INFLIGHT");
+    if (ctx->slot_busy[slot]) return fail(ctx, MRL_ERR_INVALID, "slot still holds a query that was not collected");
+    if (dims > mrl::kInlineQueryMax) return fail(ctx, MRL_ERR_INVALID, "dims > 1024: use mrl_query_scan_device");
+    for (uint32_t i = 0; i < dims; ++i)
+        if (!std::isfinite(query[i])) return fail(ctx, MRL_ERR_INVALID, "query contains a non-finite value");
+    if (int rc = set_device(ctx)) return rc;
+    if (int rc = ensure_slots(ctx, cfg->shortlist_cand)) return rc;
+    const size_t kk = ctx->slot_k;  // the slots' layout
+    unsigned char* h = ctx->h_slots + slot * ctx->slot_stride;
+    unsigned char* d = ctx->d_slots + slot * ctx->slot_stride;
+    const uint32_t expect = ++ctx->slot_seq[slot];
+    if (seg->n_blocks == 0) {  // nothing to scan
+        volatile uint32_t* cs = reinterpret_cast<volatile uint32_t*>(h + kk * 12);
+        cs[0] = 0u;
+        cs[1] = 0u;
+        cs[2] = expect;
+        ctx->slot_busy[slot] = true;
+        return MRL_OK;
+    }
+    if (int rc = ensure_owner(ctx, seg->n_blocks)) return rc;
+    float* d_means = nullptr;
+    if (int rc = upload_means(ctx, codec, &d_means)) return rc;
+    mrl::ScanLaunch p = make_launch(ctx, seg, nullptr, 0, cfg, time_lo, time_hi);
+    p.out_ids = reinterpret_cast<uint64_t*>(d);
+    p.out_scores = reinterpret_cast<float*>(d + kk * 8);
+    p.out_count = reinterpret_cast<uint32_t*>(d + kk * 12);
+    p.out_status = p.out_count + 1;
+    p.out_flag = p.out_count + 2;
+    p.out_flag_val = expect;
+    p.dims = dims;
+    p.prefix_codec = codec->prefix_codec;
+    p.mid_codec = codec->mid_codec;
+    p.eden_mean = d_means;
+    p.eden_seed = codec->eden_seed;
+    p.mid_mean = codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr;
+    p.mid_seed = codec->mid_seed;
+    p.plan_out = plan_out;
+    take_scratch(ctx, p);
+    if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, true, query)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+    launched(ctx);
+    ctx->slot_busy[slot] = true;
+    return MRL_OK;
+}
+
+// Waits (spinning on the slot's completion word, at most about 10 s) for the query in `slot`.
+int query_collect(mrl_ctx* ctx, uint32_t slot, uint64_t* out_ids, float* out_scores, uint32_t* out_count) {
+    if (!ctx) return MRL_ERR_INVALID;
+    if (slot >= MRL_MAX_INFLIGHT || !ctx->slot_busy[slot]) return fail(ctx, MRL_ERR_INVALID, "slot holds no query");
+    const size_t kk = ctx->slot_k;
+    const unsigned char* h = ctx->h_slots + slot * ctx->slot_stride;
+    const volatile uint32_t* cs = reinterpret_cast<const volatile uint32_t*>(h + kk * 12);
+    const uint32_t expect = ctx->slot_seq[slot];
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint64_t it = 1; cs[2] != expect; ++it) {
+        if ((it & 4095u) == 0u) {
+            const cudaError_t e = cudaStreamQuery(ctx->stream);
+            if (e != cudaSuccess && e != cudaErrorNotReady) {
+                ctx->slot_busy[slot] = false;
+                return cuda_fail(ctx, e, "scan (query slot)");
+            }
+            if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(10)) {
+                ctx->slot_busy[slot] = false;
+                return fail(ctx, MRL_ERR_CUDA, "query slot: no result within 10 s");
+            }
+        }
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);
+    ctx->slot_busy[slot] = false;
+    const uint32_t n = cs[0], st = cs[1];
+    if (st & 2u) return fail(ctx, MRL_ERR_CUDA, "scan: a CTA's list never arrived (waited about 1 s)");
+    if (st & 8u) return fail(ctx, MRL_ERR_CUDA, "scan: the context's scratch stayed busy (waited about 1 s)");
+    if (out_count) *out_count = n;
+    if (out_ids) std::memcpy(out_ids, h, (size_t)n * sizeof(uint64_t));
+    if (out_scores) std::memcpy(out_scores, h + kk * 8, (size_t)n * sizeof(float));
+    return MRL_OK;
+}
+
+}  // namespace
+
+int mrl_query_submit(mrl_ctx* ctx, const mrl_seg* seg, const float* query, uint32_t dims, const mrl_codec_desc* codec,
+                     const mrl_scan_cfg* cfg, const uint32_t* time_lo, const uint32_t* time_hi, uint32_t slot) {
+    return query_submit(ctx, seg, query, dims, codec, nullptr, cfg, time_lo, time_hi, slot);
+}
+
+int mrl_query_collect(mrl_ctx* ctx, uint32_t slot, uint64_t* out_ids, float* out_scores, uint32_t* out_count) {
+    return query_collect(ctx, slot, out_ids, out_scores, out_count);
+}
+
+int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint32_t n_q, uint32_t dims,
+                   const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+                   const uint32_t* time_hi, uint64_t* out_ids, float* out_scores, uint32_t* out_counts) {
+    if (!ctx || !seg || !plans) return MRL_ERR_INVALID;
+    if (int rc = check_cfg(ctx, cfg, dims)) return rc;
+    if (n_q == 0) return MRL_OK;
+    if (!queries || !out_ids || !out_scores || !out_counts) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
+    if (n_q > plans->n_q || dims != plans->dims) return fail(ctx, MRL_ERR_INVALID, "plan storage too small or dims mismatch");
+    for (int s = 0; s < MRL_MAX_INFLIGHT; ++s)
+        if (ctx->slot_busy[s]) return fail(ctx, MRL_ERR_INVALID, "mrl_query_scan while submitted queries are uncollected");
+    if (dims > mrl::kInlineQueryMax || seg->n_blocks == 0)
+        return query_scan_staged(ctx, seg, queries, n_q, dims, codec, plans, cfg, time_lo, time_hi, out_ids, out_scores,
+                                 out_counts);
+    // every query's scan is launched with the query in its parameters; up to MRL_MAX_INFLIGHT are
+    // in flight, and each result is collected from its slot in order
+    const size_t k = cfg->shortlist_cand;
+    int rc = MRL_OK;
+    uint32_t next = 0;  // next query to collect
+    for (uint32_t i = 0; i < n_q && rc == MRL_OK; ++i) {
+        const uint32_t slot = i % MRL_MAX_INFLIGHT;
+        if (i >= MRL_MAX_INFLIGHT) {
+            rc = query_collect(ctx, slot, out_ids + next * k, out_scores + next * k, out_counts + next);
+            ++next;
+            if (rc) break;
+        }
+        rc = query_submit(ctx, seg, queries + (size_t)i * dims, dims, codec, plans->d + i, cfg, time_lo, time_hi, slot);
+    }
+    for (; next < n_q; ++next) {  // drain (also after a failure, so no slot stays busy)
+        const uint32_t slot = next % MRL_MAX_INFLIGHT;
+        if (!ctx->slot_busy[slot]) continue;
+        const int r = query_collect(ctx, slot, out_ids + next * k, out_scores + next * k, out_counts + next);
+        if (rc == MRL_OK) rc = r;
+    }
+    return rc;
 }
 
 int mrl_exchange_create(mrl_ctx* ctx, uint32_t world, uint32_t rank, uint32_t k, void* ipc_handle,

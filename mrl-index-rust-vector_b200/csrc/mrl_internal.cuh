@@ -202,6 +202,10 @@ struct ScanLaunch {
     unsigned int* ctl;             // kCtlWords: [0] page counter, [1] publish ticket, [7] exit ticket,
                                    // [kCtlReady + c] CTA c's list is published; the last CTA to
                                    // exit zeroes them all
+    // completion word (nullptr: none): the finisher stores out_flag_val there, system scope, after
+    // every output (for a host that waits on pinned, device-mapped outputs)
+    unsigned int* out_flag;
+    uint32_t out_flag_val;
     unsigned int* done;            // launch sequence number of the last launch to release this
                                    // scratch (nullptr: scratch of one launch at a time, no check)
     uint32_t seq;                  // this launch's sequence number on the context
@@ -234,7 +238,9 @@ struct ScanLaunch {
 };
 int scan_ctas(int device_sms);
 size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t xch_world, uint32_t mode);
-int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream, bool pdl);
+// Longest query a launch can carry in its parameters (launch_scan's h_query).
+constexpr uint32_t kInlineQueryMax = 1024;
+int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream, bool pdl, const float* h_query = nullptr);
 int launch_exact_dots(const float* d_query, const float* d_rows, uint64_t n_rows, uint32_t dims, const uint64_t* d_sel,
                       uint32_t n, float* d_scores, uint32_t* d_bad, cudaStream_t stream);
 int launch_ring_search_batch(const float* d_queries, uint32_t n_q, uint32_t dims, const float* d_rows, uint32_t n,

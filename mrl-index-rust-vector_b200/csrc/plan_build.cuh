@@ -219,12 +219,12 @@ __device__ __forceinline__ void plan_inputs(const float* __restrict__ q, uint32_
     }
     if (tid < 16) c = g_lloyd_b4[tid];
     const uint32_t i0 = tid, i1 = tid + nthr;
-    const float v0 = i0 < dims ? __ldg(q + i0) : 0.0f;
-    const float v1 = i1 < dims ? __ldg(q + i1) : 0.0f;
+    const float v0 = i0 < dims ? q[i0] : 0.0f;  // plain loads: q may be global or kernel-parameter memory
+    const float v1 = i1 < dims ? q[i1] : 0.0f;
     for (int t = tid; t < kSigns; t += nthr) sh.sg[t] = plan_sign(t, eden_seed, mid_seed);
     if (i0 < dims) s_q[i0] = v0;
     if (i1 < dims) s_q[i1] = v1;
-    for (uint32_t i = tid + 2u * nthr; i < dims; i += nthr) s_q[i] = __ldg(q + i);
+    for (uint32_t i = tid + 2u * nthr; i < dims; i += nthr) s_q[i] = q[i];
     if (tid < kPrefix + kRabitq) sh.mean[tid] = m;
     if (tid < 16) sh.cb[tid] = c;
 }

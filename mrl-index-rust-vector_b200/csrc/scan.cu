@@ -39,6 +39,7 @@
 // bit 0 reports it).
 #include <algorithm>
 #include <atomic>
+#include <cstring>
 
 #include "exchange.cuh"
 #include "plan_build.cuh"
@@ -679,9 +680,19 @@ __device__ __forceinline__ bool finish_rank(const ScanLaunch& p, uint64_t* out_i
     return true;
 }
 
+// The finisher's last act when the caller waits on a completion word (p.out_flag, typically in
+// pinned host memory): every thread's output stores, then the word, at system scope.
+__device__ __forceinline__ void signal_done(const ScanLaunch& p) {
+    if (!p.out_flag) return;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.out_flag), "r"(p.out_flag_val) : "memory");
+}
+
 // Returns false only when the launch left without touching its scratch (the scratch stayed busy).
+// `query` (fused launches): the query's dims floats, in global or kernel-parameter memory.
 template <int MODE, bool FUSED>
-__device__ __forceinline__ bool scan_body(const ScanLaunch& p) {
+__device__ __forceinline__ bool scan_body(const ScanLaunch& p, const float* query) {
     constexpr bool kFast = MODE == MRL_MODE_FAST;
     __shared__ __align__(16) int s_tab[kTabInts];
     // fast mode: the exact-mode tables too, for the exact rescoring of the CTA's list
@@ -727,7 +738,7 @@ __device__ __forceinline__ bool scan_body(const ScanLaunch& p) {
     float* s_qb = reinterpret_cast<float*>(s_dyn + align16(sizeof(DevPlan)));
     planb::PlanShared* s_pb =
         reinterpret_cast<planb::PlanShared*>(s_dyn + align16(sizeof(DevPlan)) + align16((size_t)p.dims * sizeof(float)));
-    if (FUSED) planb::plan_inputs(p.query, p.dims, p.eden_mean, p.mid_mean, p.eden_seed, p.mid_seed, s_qb, *s_pb);
+    if (FUSED) planb::plan_inputs(query, p.dims, p.eden_mean, p.mid_mean, p.eden_seed, p.mid_seed, s_qb, *s_pb);
     float4 mm = make_float4(0.f, 0.f, 0.f, 0.f);
     if (kFast) mm = __ldg(reinterpret_cast<const float4*>(p.metamax));
 
@@ -902,6 +913,7 @@ __device__ __forceinline__ bool scan_body(const ScanLaunch& p) {
     ListSums ls;
     if (!finisher_load<kFast>(p, s_cand, s_xcand, LP, G, ls)) {
         if (tid == 0 && p.out_status) *p.out_status = 2u;  // a CTA's list never arrived: no result
+        signal_done(p);
         return true;
     }
 
@@ -920,8 +932,9 @@ __device__ __forceinline__ bool scan_body(const ScanLaunch& p) {
         if (p.xch_world) {
             __threadfence();  // the record (stored by every thread) before its copies to the peers
             xch_publish_and_merge(p, s_dyn, &s_ok, 0u);
-        } else if (tid == 0 && p.out_status) {
-            *p.out_status = 0u;
+        } else {
+            if (tid == 0 && p.out_status) *p.out_status = 0u;
+            signal_done(p);
         }
         return true;
     }
@@ -949,17 +962,35 @@ __device__ __forceinline__ bool scan_body(const ScanLaunch& p) {
         return true;
     }
     if (tid == 0 && p.out_status) *p.out_status = 1u;
+    signal_done(p);
     return true;
 }
 
+// Exit ticket (control word 7): the last CTA to leave zeroes this launch's control words and
+// ready flags, so the launch that next uses this scratch starts clean whichever path this one
+// took, a wait that ran out included. The ticket is an acquire-release add: every CTA's uses of
+// the words come before its ticket, and the last holder sees them all before it stores the zeros,
+// which the next launch on this scratch sees at the kernel boundary.
+__device__ __forceinline__ void scan_exit(const ScanLaunch& p);
+
 template <int MODE, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
-    if (!scan_body<MODE, FUSED>(p)) return;  // the scratch stayed busy: leave it untouched
-    // Exit ticket (control word 7): the last CTA to leave zeroes this launch's control words and
-    // ready flags, so the launch that next uses this scratch starts clean whichever path this one
-    // took, a wait that ran out included. The ticket is an acquire-release add: every CTA's uses of
-    // the words come before its ticket, and the last holder sees them all before it stores the zeros,
-    // which the next launch on this scratch sees at the kernel boundary.
+    if (!scan_body<MODE, FUSED>(p, p.query)) return;  // the scratch stayed busy: leave it untouched
+    scan_exit(p);
+}
+
+// The fused scan of one query passed in the launch's parameters (host queries: no copy precedes
+// the launch, so consecutive launches on a stream still overlap).
+struct QueryParam {
+    float q[kInlineQueryMax];
+};
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1) scan_kernel_q(const ScanLaunch p, const __grid_constant__ QueryParam qp) {
+    if (!scan_body<MODE, true>(p, qp.q)) return;
+    scan_exit(p);
+}
+
+__device__ __forceinline__ void scan_exit(const ScanLaunch& p) {
     __shared__ unsigned s_exit;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -1144,19 +1175,22 @@ size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t 
 }
 
 // One CTA per SM. With `pdl` the launch may begin while the previous kernel on the stream finishes
-// (programmatic dependent launch; the kernel waits for it before touching what they share).
-int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream, bool pdl) {
-    const bool fused = p.query != nullptr;
+// (programmatic dependent launch; the kernel waits for it before touching what they share). With
+// `h_query` (host memory, p.dims <= kInlineQueryMax floats) the fused scan takes the query in its
+// launch parameters.
+int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream, bool pdl, const float* h_query) {
+    const bool fused = p.query != nullptr || h_query != nullptr;
+    if (h_query && p.dims > kInlineQueryMax) return -1;
     const size_t smem = scan_smem_bytes(ctas, p.k, fused ? p.dims : 0u, p.xch_world, p.mode);
-    const void* fn = p.mode == MRL_MODE_FAST ? (fused ? (const void*)scan_kernel<MRL_MODE_FAST, true>
-                                                      : (const void*)scan_kernel<MRL_MODE_FAST, false>)
-                                             : (fused ? (const void*)scan_kernel<MRL_MODE_EXACT, true>
-                                                      : (const void*)scan_kernel<MRL_MODE_EXACT, false>);
+    const bool fast = p.mode == MRL_MODE_FAST;
+    const void* fn = h_query ? (fast ? (const void*)scan_kernel_q<MRL_MODE_FAST> : (const void*)scan_kernel_q<MRL_MODE_EXACT>)
+                   : fast ? (fused ? (const void*)scan_kernel<MRL_MODE_FAST, true> : (const void*)scan_kernel<MRL_MODE_FAST, false>)
+                          : (fused ? (const void*)scan_kernel<MRL_MODE_EXACT, true> : (const void*)scan_kernel<MRL_MODE_EXACT, false>);
     // the attribute is per function and device: set it only when a launch needs more than before
-    static std::atomic<size_t> set_bytes[64][4];
+    static std::atomic<size_t> set_bytes[64][6];
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess) return -1;
-    std::atomic<size_t>& cur = set_bytes[device & 63][(p.mode == MRL_MODE_FAST ? 0 : 2) + (fused ? 1 : 0)];
+    std::atomic<size_t>& cur = set_bytes[device & 63][h_query ? 4 + (fast ? 0 : 1) : (fast ? 0 : 2) + (fused ? 1 : 0)];
     if (smem > cur.load(std::memory_order_relaxed)) {
         if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -1;
         cur.store(smem, std::memory_order_relaxed);
@@ -1173,6 +1207,12 @@ int launch_scan(const ScanLaunch& p, uint32_t ctas, cudaStream_t stream, bool pd
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (h_query) {
+        QueryParam qp;
+        std::memcpy(qp.q, h_query, sizeof(float) * p.dims);
+        void* args[] = {&arg, &qp};
+        return cudaLaunchKernelExC(&cfg, fn, args) == cudaSuccess ? 0 : -1;
+    }
     void* args[] = {&arg};
     if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess) return -1;
     return 0;

@@ -26,6 +26,8 @@ from .api import (  # noqa: F401
     encode_blocks,
     row_id_to_vector_id,
     query_scan,
+    QueryStream,
+    MAX_INFLIGHT,
     scan_blocks,
     scan_blocks_batch,
     scan_blocks_stats,

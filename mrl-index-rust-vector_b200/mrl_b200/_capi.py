@@ -93,6 +93,8 @@ SIGNATURES = {
                                    _vp, _vp, _vp, _vp]),
     "mrl_query_scan": (_i, [_vp, _vp, _vp, _u32, _u32, C.POINTER(CodecDesc), _vp, C.POINTER(ScanCfgC), _vp, _vp, _vp,
                             _vp, _vp]),
+    "mrl_query_submit": (_i, [_vp, _vp, _vp, _u32, C.POINTER(CodecDesc), C.POINTER(ScanCfgC), _vp, _vp, _u32]),
+    "mrl_query_collect": (_i, [_vp, _u32, _vp, _vp, _vp]),
     "mrl_exchange_create": (_i, [_vp, _u32, _u32, _u32, _vp, C.POINTER(_vp)]),
     "mrl_exchange_open": (_i, [_vp, _vp, _vp]),
     "mrl_exchange_destroy": (_i, [_vp, _vp]),

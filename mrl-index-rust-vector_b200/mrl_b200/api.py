@@ -460,6 +460,49 @@ def query_scan(segment: Segment, queries, cfg, prefix_codec=PrefixCodec.MIN_MAX4
     return ids, scores, counts, plan
 
 
+MAX_INFLIGHT = 8  # MRL_MAX_INFLIGHT
+
+
+class QueryStream:
+    """Pipelined host queries over one segment (mrl_query_submit / mrl_query_collect): submit()
+    launches the fused plan + scan of one query into a result slot and returns at once; collect()
+    waits for that slot's top-k. Keeping two or more queries submitted lets consecutive scans
+    overlap on the device. The reference's scan is a blocking call; this has no counterpart there."""
+
+    def __init__(self, segment: Segment, cfg, prefix_codec=PrefixCodec.MIN_MAX4, mid_codec=MidCodec.RABITQ,
+                 eden: Optional[EdenFit] = None, eden_mid: Optional[EdenFit] = None, time_lo=None, time_hi=None):
+        self.segment = segment
+        self.dev = segment.dev
+        sc = _cfg_of(cfg)
+        self.c = sc.to_c()
+        self.k = int(sc.shortlist_cand)
+        self.desc, self._keep = _codec_desc(prefix_codec, mid_codec, eden, eden_mid)
+        self._tl = (np.array([time_lo], np.uint32) if time_lo is not None else None,
+                    np.array([time_hi], np.uint32) if time_hi is not None else None)
+        self._ids = np.zeros(self.k, np.uint64)
+        self._sc = np.zeros(self.k, np.float32)
+        self._n = np.zeros(1, np.uint32)
+
+    def _time(self):
+        lo, hi = self._tl
+        return (lo.ctypes.data_as(C.c_void_p) if lo is not None else None,
+                hi.ctypes.data_as(C.c_void_p) if hi is not None else None)
+
+    def submit(self, query, slot: int) -> None:
+        q = np.ascontiguousarray(query, np.float32).reshape(-1)
+        lo, hi = self._time()
+        check(self.dev.ptr, self.dev.lib.mrl_query_submit(self.dev.ptr, self.segment.ptr, q.ctypes.data_as(C.c_void_p),
+                                                          q.shape[0], C.byref(self.desc), C.byref(self.c), lo, hi, slot))
+
+    def collect(self, slot: int):
+        """(ids [count] u64, scores [count] f32) of the query in `slot`."""
+        check(self.dev.ptr, self.dev.lib.mrl_query_collect(self.dev.ptr, slot, self._ids.ctypes.data_as(C.c_void_p),
+                                                           self._sc.ctypes.data_as(C.c_void_p),
+                                                           self._n.ctypes.data_as(C.c_void_p)))
+        n = int(self._n[0])
+        return self._ids[:n].copy(), self._sc[:n].copy()
+
+
 def scan_blocks(segment: Segment, plan: QueryPlan, cfg, time_lo=None, time_hi=None) -> List[ScoredHit]:
     """`scan_blocks` (src/scan.rs:802-810): top `shortlist_cand` hits, score descending."""
     if plan.n_q != 1:

@@ -635,3 +635,59 @@ def test_query_scan_host_staging_regrows(ora, dev, corpus768):
         M.query_scan(seg, bad, M.ScanConfig(shortlist_cand=16), **kw)
     ref.free()
     seg.free()
+
+
+@pytest.mark.parametrize("mode", ["fast", "exact"])
+def test_query_stream_pipelined_matches_device_scan(ora, dev, corpus768, mode):
+    """mrl_query_submit / mrl_query_collect with three queries in flight and the slots reused: each
+    result equals the plan + scan of the same query on the device path, bit for bit, and the first
+    query equals the oracle's scan_blocks. Shortlists that shrink after a larger one keep working."""
+    M = mb()
+    seg = M.Segment.upload(corpus768["eden"], dev)
+    mean = corpus768["mean"]
+    qs = np.concatenate([corpus768["qs"]] * 3)[:11]
+    kw = dict(prefix_codec=M.PrefixCodec.EDEN_PROD, mid_codec=M.MidCodec.RABITQ, eden=fit(mean))
+    m = M.ScanMode.EXACT if mode == "exact" else M.ScanMode.FAST
+    big = M.QueryStream(seg, M.ScanConfig(shortlist_cand=256, mode=m), **kw)
+    big.submit(qs[0], 0)
+    big.collect(0)  # the slots now hold room for 256 hits
+    for k in (96, 16):
+        cfg = M.ScanConfig(shortlist_cand=k, mode=m)
+        ref_plans = M.QueryPlan.from_queries(qs, dev=dev, **kw)
+        r_ids, r_sc, r_cnt = M.scan_blocks_batch(seg, ref_plans, cfg)
+        st = M.QueryStream(seg, cfg, **kw)
+        depth, slots = 3, 4
+        got = {}
+        for i in range(len(qs)):
+            if i >= depth:
+                got[i - depth] = st.collect((i - depth) % slots)
+            st.submit(qs[i], i % slots)
+        for j in range(len(qs) - depth, len(qs)):
+            got[j] = st.collect(j % slots)
+        for qi in range(len(qs)):
+            ids, sc = got[qi]
+            n = int(r_cnt[qi])
+            assert len(ids) == n
+            assert np.array_equal(ids, r_ids[qi, :n])
+            assert np.array_equal(sc.view(np.uint32), r_sc[qi, :n].view(np.uint32))
+        op = ora.plan_build(qs[0], eden_mean=mean)
+        rid, rsc = ora.scan_blocks(corpus768["eden"], op, ora.scan_cfg(k=k))
+        assert [int(x) for x in got[0][0]] == [int(x) for x in rid]
+        assert np.array_equal(got[0][1].view(np.uint32), rsc.view(np.uint32))
+        ref_plans.free()
+    # misuse: a free slot, a busy slot, a non-finite query, dims beyond the launch's capacity
+    with pytest.raises(M.MrlError):
+        st.collect(0)
+    st.submit(qs[0], 5)
+    with pytest.raises(M.MrlError):
+        st.submit(qs[1], 5)
+    st.collect(5)
+    bad = qs[0].copy()
+    bad[3] = np.nan
+    with pytest.raises(M.MrlError):
+        st.submit(bad, 6)
+    with pytest.raises(M.MrlError):
+        st.submit(np.zeros(1040, np.float32), 6)
+    with pytest.raises(M.MrlError):
+        st.submit(qs[0], M.MAX_INFLIGHT)
+    seg.free()
