@@ -164,8 +164,9 @@ int mrl_scan(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, const mrl
              float* out_scores, uint32_t* out_counts);
 /* Same scan for plans [q0, q0+n_q) writing device buffers, asynchronously on the context
  * stream (no host synchronisation). out_status[q] (device, may be NULL) receives the selection
- * status word: bit 0 = the exact re-selection path ran, bit 1 = a bounded wait ran out (no
- * result). */
+ * status word: bit 0 = the exact re-selection path ran, bit 1 = a CTA's list did not reach the
+ * finishing CTA within about 1 s (no result), bit 3 = the context's scratch stayed busy for about
+ * 1 s (the launch two before on the stream never released it; no result). */
 int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q0,
                     uint32_t n_q, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
                     const uint32_t* time_hi, uint64_t* d_out_ids, float* d_out_scores,
@@ -201,7 +202,8 @@ int mrl_scan_batch_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pla
  * region is shared by every context on a device: calls in
  * flight at the same time on one device (other streams, contexts or threads) race on it, while
  * calls ordered on one stream do not. Each call zeroes the region's control words on the context
- * stream before its first launch. out_status bit 1 = grid barrier timed out (no result). */
+ * stream before its first launch. out_status bit 1 = a CTA's list did not reach the finishing CTA
+ * within about 1 s (no result). */
 #define MRL_STATIC_MAX_BLOCKS 1048576u
 #define MRL_STATIC_MAX_CTAS 256u
 int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q0,
@@ -286,8 +288,9 @@ int mrl_exchange_open(mrl_ctx* ctx, mrl_exchange* ex, const void* ipc_handles);
 int mrl_exchange_destroy(mrl_ctx* ctx, mrl_exchange* ex);
 /* Fused plan + scan of one device query (as mrl_query_scan_device with n_q = 1) whose outputs are
  * the GLOBAL top-k over all ranks' segments. cfg->shortlist_cand must equal the exchange's k.
- * out_status: bit 0 = re-selection ran, bit 1 = grid barrier timed out, bit 2 = a rank's record
- * did not arrive in time (no result). */
+ * out_status: bit 0 = re-selection ran, bit 1 = a CTA's list did not reach the finishing CTA in
+ * time, bit 2 = a rank's record did not arrive in time, bit 3 = the scratch stayed busy (bits 1-3:
+ * no result). */
 int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_query, uint32_t dims,
                             const mrl_codec_desc* codec, mrl_plans* plans, const mrl_scan_cfg* cfg,
                             const uint32_t* time_lo, const uint32_t* time_hi, mrl_exchange* ex,

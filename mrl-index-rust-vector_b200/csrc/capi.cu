@@ -755,8 +755,8 @@ int mrl_scan_batch_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pla
 // allocate while answering a query, such as a serving process that reserved its device memory at
 // start-up, where a cudaMalloc could stall other streams or fail under memory pressure mid-request.
 // Of the scratch, only the control words must be zero when a launch starts; every completed scan
-// leaves them zero, and each call also zeroes them (one 32-byte memset on the context stream) so a
-// call after a barrier timeout starts clean. Lists, flags and owner bytes are written before they
+// leaves them zero, and each call also zeroes them (one memset on the context stream) so a call
+// after a wait that ran out starts clean. Lists, flags and owner bytes are written before they
 // are read. The scratch is one per device per process, so two calls in flight on the same device
 // at once (different streams, contexts or threads) race on it; calls ordered on one stream do not.
 int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q0, uint32_t n_q,
@@ -922,7 +922,7 @@ static int query_scan_staged(mrl_ctx* ctx, const mrl_seg* seg, const float* quer
     MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     const uint32_t* cs = reinterpret_cast<const uint32_t*>(h_out + nk * (sizeof(uint64_t) + sizeof(float)));
     for (uint32_t q = 0; q < n_q; ++q)
-        if (cs[n_q + q] & 2u) return fail(ctx, MRL_ERR_CUDA, "scan grid barrier timed out (CTAs not co-resident)");
+        if (cs[n_q + q] & 10u) return fail(ctx, MRL_ERR_CUDA, "scan: a bounded wait ran out (status bits 1/3)");
     std::memcpy(out_ids, h_out, nk * sizeof(uint64_t));
     std::memcpy(out_scores, h_out + nk * sizeof(uint64_t), nk * sizeof(float));
     std::memcpy(out_counts, cs, n_q * sizeof(uint32_t));
@@ -1439,7 +1439,7 @@ int mrl_scan(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, const mrl
     MRL_CUDA_TRY(ctx, cudaMemcpyAsync(st.data(), d_st, n_q * sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx->stream));
     MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     for (uint32_t q = 0; q < n_q; ++q)
-        if (st[q] & 2u) return fail(ctx, MRL_ERR_CUDA, "scan grid barrier timed out (CTAs not co-resident)");
+        if (st[q] & 10u) return fail(ctx, MRL_ERR_CUDA, "scan: a bounded wait ran out (status bits 1/3)");
     return MRL_OK;
 }
 

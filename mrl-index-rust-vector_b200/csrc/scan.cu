@@ -4,12 +4,11 @@
 // live slot of a segment for one plan and leaves the top-k (by score, ties to the lower slot
 // ordinal) in the output buffers.
 //
-// Work split: a persistent cooperative grid of one 512-thread CTA per SM. The first 7/8 of the
-// pages are split into one contiguous range per CTA, whose warps take pages from a shared-memory
-// counter; the last 1/8 is handed out one page at a time from a global counter to CTAs that have
-// finished their range. Each warp scores two slots per lane, reading each slot's 64 bytes of the
-// vector-major page layout with four coalesced 16-byte loads, and loads the next page while it
-// scores the current one.
+// Work split: one 512-thread CTA per SM. The first 7/8 of the pages are split into one contiguous
+// range per CTA, whose warps take pages from a shared-memory counter; the last 1/8 is handed out one
+// page at a time from a global counter to CTAs that have finished their range. Each warp scores two
+// slots per lane, reading each slot's 64 bytes of the vector-major page layout with four coalesced
+// 16-byte loads, and loads the next page while it scores the current one.
 //
 // Scoring (one thread per slot):
 //   * MRL_MODE_FAST — every stage inner product is an exact int32 sum of table entries held in
@@ -30,13 +29,21 @@
 // Selection: each warp keeps a sorted top-32 of its keys in registers (one key per lane) and
 // filters new keys against max(its own list_len-th key, a CTA-wide bound in shared memory);
 // survivors go through a per-warp shared-memory queue and are merged 32 at a time with warp
-// bitonic networks. Each CTA tree-merges its warps' lists and publishes its top-`list_len` (fast
-// mode: with each entry's exact key) to global scratch; after a bounded grid barrier every CTA
-// ranks its own list keys against all CTA lists (binary search) and writes the keys ranked below
-// k straight to the output. The union of per-CTA lists contains the global top-k unless some
-// CTA's full list ends inside it; then CTA 0 alone rescans those CTAs' pages (owner[]) and redoes
-// the selection by radix select + bitonic sort, so the result is exact for every input (status
+// bitonic networks. Each CTA tree-merges its warps' lists, rescores them exactly (fast mode) and
+// publishes its top-`list_len` with a ready flag. The first CTA to publish is the finisher: it loads
+// every CTA's list as that list's flag appears (overlapping the other CTAs' scoring), checks that
+// the union of the lists holds the top-k, locates the k-th key in a histogram of score words,
+// gathers the keys within 2E of it and ranks them by exact key. The other CTAs exit at once. If a
+// CTA's full list may have dropped a top-k member, the finisher rescans that CTA's pages (owner[])
+// and reselects by radix select + bitonic sort, so the result is exact for every input (status
 // bit 0 reports it).
+//
+// Overlapping queries: every CTA lets the next launch on the stream start (programmatic dependent
+// launch) at its own start, so the next query's CTAs take each SM as soon as this query's CTA there
+// has published. The context's scratch comes in two parities used by alternate launches; a launch
+// touches its parity only once the launch two back has released it (a done word the last CTA to
+// exit stores after zeroing the control words), and its finisher writes the outputs only after the
+// previous launch has completed (griddepcontrol.wait).
 #include <algorithm>
 #include <atomic>
 #include <cstring>

@@ -431,8 +431,8 @@ class IndexDir:
         torch.cuda.synchronize(dq.device)  # the library runs on its own stream
         h = cs.cpu().numpy()
         del keep
-        if int(h[1]) & 2:
-            raise RuntimeError("scan grid barrier timed out (CTAs not co-resident)")
+        if int(h[1]) & 10:
+            raise RuntimeError("scan: a bounded wait ran out (status bits 1/3)")
         n = int(h[0])
         hi_ids = ids[:n].cpu().numpy().view(np.uint64)
         hi_sc = scores[:n].cpu().numpy()
