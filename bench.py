@@ -375,15 +375,25 @@ def run_ours(args):
         depth, maxi = max(1, min(args.e2e_depth, M.MAX_INFLIGHT)), M.MAX_INFLIGHT
         nseg = len(segs)
 
+        host_us = {"submit": 0.0, "collect": 0.0}
+
         def pipelined(nsteps):
-            s0 = time.perf_counter()
+            t_sub = t_col = 0.0
+            pc = time.perf_counter
+            s0 = pc()
             for i in range(nsteps + depth):
                 if i >= depth:
+                    a = pc()
                     check(ctx, fn_c(ctx, (i - depth) % maxi, out_i, out_s, out_c))
+                    t_col += pc() - a
                 if i < nsteps:
+                    a = pc()
                     check(ctx, fn_s(ctx, seg_ptrs[i % nseg], q_ptrs[i % n_q], dims, desc_ref, cfg_ref, None, None,
                                     i % maxi))
-            return time.perf_counter() - s0
+                    t_sub += pc() - a
+            el = pc() - s0
+            host_us["submit"], host_us["collect"] = 1e6 * t_sub / max(nsteps, 1), 1e6 * t_col / max(nsteps, 1)
+            return el
 
         if args.l2 == "flush":
             pipelined_s = None  # the L2 flush between steps would serialise them
@@ -410,6 +420,7 @@ def run_ours(args):
         if pipelined_s is not None:
             e2e = {"value": e2e_steps / pipelined_s, "unit": "QPS", "h2d_bytes_per_step": qbytes,
                    "d2h_bytes_per_step": k * 12 + 4, "steps": e2e_steps, "in_flight": depth,
+                   "host_us_per_step": {kk: round(v, 2) for kk, v in host_us.items()},
                    "path": f"mrl_query_submit + mrl_query_collect with {depth} queries in flight: each host query "
                            "travels in its scan launch's parameters (host to device), the scan stores its top-256, "
                            "count and status into a pinned device-mapped result slot (device to host) that the host "

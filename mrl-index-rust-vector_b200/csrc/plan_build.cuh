@@ -207,6 +207,7 @@ __device__ __forceinline__ float plan_sign(int t, uint64_t eden_seed, uint64_t m
 // The build's inputs into shared memory: the query, the codec centres, the b=4 codebook, and the
 // Rademacher signs (computed while the loads are in flight). Every thread of the CTA calls it;
 // build_plan synchronises before reading them.
+template <bool kParamQuery = false>
 __device__ __forceinline__ void plan_inputs(const float* __restrict__ q, uint32_t dims, const float* __restrict__ eden_mean,
                                             const float* __restrict__ mid_mean, uint64_t eden_seed, uint64_t mid_seed,
                                             float* s_q, PlanShared& sh) {
@@ -218,13 +219,37 @@ __device__ __forceinline__ void plan_inputs(const float* __restrict__ q, uint32_
         m = src ? __ldg(src + (tid < kPrefix ? tid : tid - kPrefix)) : 0.0f;
     }
     if (tid < 16) c = g_lloyd_b4[tid];
-    const uint32_t i0 = tid, i1 = tid + nthr;
-    const float v0 = i0 < dims ? q[i0] : 0.0f;  // plain loads: q may be global or kernel-parameter memory
-    const float v1 = i1 < dims ? q[i1] : 0.0f;
-    for (int t = tid; t < kSigns; t += nthr) sh.sg[t] = plan_sign(t, eden_seed, mid_seed);
-    if (i0 < dims) s_q[i0] = v0;
-    if (i1 < dims) s_q[i1] = v1;
-    for (uint32_t i = tid + 2u * nthr; i < dims; i += nthr) s_q[i] = q[i];
+    if (kParamQuery) {
+        // the query sits in the kernel's parameter bank (16-byte aligned), where lanes that read
+        // different addresses are served one address at a time: each warp reads whole 16-byte
+        // chunks at one address per instruction, and one lane stores them
+        const int lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
+        const uint32_t n4 = dims / 4u;
+        const float4* q4 = reinterpret_cast<const float4*>(q);
+        float4* s4 = reinterpret_cast<float4*>(s_q);
+        for (uint32_t j = warp; j < n4; j += 4u * nw) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (j + u * nw < n4) v[u] = q4[j + u * nw];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (lane == 0 && j + u * nw < n4) s4[j + u * nw] = v[u];
+        }
+        for (uint32_t i = 4u * n4 + warp; i < dims; i += nw) {
+            const float v = q[i];
+            if (lane == 0) s_q[i] = v;
+        }
+        for (int t = tid; t < kSigns; t += nthr) sh.sg[t] = plan_sign(t, eden_seed, mid_seed);
+    } else {
+        const uint32_t i0 = tid, i1 = tid + nthr;
+        const float v0 = i0 < dims ? q[i0] : 0.0f;  // plain loads: q may be global or kernel-parameter memory
+        const float v1 = i1 < dims ? q[i1] : 0.0f;
+        for (int t = tid; t < kSigns; t += nthr) sh.sg[t] = plan_sign(t, eden_seed, mid_seed);
+        if (i0 < dims) s_q[i0] = v0;
+        if (i1 < dims) s_q[i1] = v1;
+        for (uint32_t i = tid + 2u * nthr; i < dims; i += nthr) s_q[i] = q[i];
+    }
     if (tid < kPrefix + kRabitq) sh.mean[tid] = m;
     if (tid < 16) sh.cb[tid] = c;
 }

@@ -698,7 +698,7 @@ __device__ __forceinline__ void signal_done(const ScanLaunch& p) {
 
 // Returns false only when the launch left without touching its scratch (the scratch stayed busy).
 // `query` (fused launches): the query's dims floats, in global or kernel-parameter memory.
-template <int MODE, bool FUSED>
+template <int MODE, bool FUSED, bool QPARAM = false>
 __device__ __forceinline__ bool scan_body(const ScanLaunch& p, const float* query) {
     constexpr bool kFast = MODE == MRL_MODE_FAST;
     __shared__ __align__(16) int s_tab[kTabInts];
@@ -745,7 +745,7 @@ __device__ __forceinline__ bool scan_body(const ScanLaunch& p, const float* quer
     float* s_qb = reinterpret_cast<float*>(s_dyn + align16(sizeof(DevPlan)));
     planb::PlanShared* s_pb =
         reinterpret_cast<planb::PlanShared*>(s_dyn + align16(sizeof(DevPlan)) + align16((size_t)p.dims * sizeof(float)));
-    if (FUSED) planb::plan_inputs(query, p.dims, p.eden_mean, p.mid_mean, p.eden_seed, p.mid_seed, s_qb, *s_pb);
+    if (FUSED) planb::plan_inputs<QPARAM>(query, p.dims, p.eden_mean, p.mid_mean, p.eden_seed, p.mid_seed, s_qb, *s_pb);
     float4 mm = make_float4(0.f, 0.f, 0.f, 0.f);
     if (kFast) mm = __ldg(reinterpret_cast<const float4*>(p.metamax));
 
@@ -988,12 +988,12 @@ __global__ void __launch_bounds__(kThreads, 1) scan_kernel(const ScanLaunch p) {
 
 // The fused scan of one query passed in the launch's parameters (host queries: no copy precedes
 // the launch, so consecutive launches on a stream still overlap).
-struct QueryParam {
+struct __align__(16) QueryParam {
     float q[kInlineQueryMax];
 };
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) scan_kernel_q(const ScanLaunch p, const __grid_constant__ QueryParam qp) {
-    if (!scan_body<MODE, true>(p, qp.q)) return;
+    if (!scan_body<MODE, true, true>(p, qp.q)) return;
     scan_exit(p);
 }
 
