@@ -58,6 +58,10 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--e2e-depth", type=int, default=3, help="host queries in flight in the pipelined e2e")
+    ap.add_argument("--ctas-per-query", type=int, default=24,
+                    help="CTAs per single-query scan launch in the throughput loops (0: one per SM); fewer let "
+                         "consecutive queries run side by side (mrl_set_scan_ctas). The synchronous latency "
+                         "measurements use one CTA per SM")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--l2", choices=["rotate", "flush"], default="rotate",
                     help="keep the scanned pages out of L2 by rotating over segments whose total exceeds L2 "
@@ -192,6 +196,7 @@ def run_ours(args):
     dev = M.Device(local)
     torch_stream = torch.cuda.current_stream().cuda_stream
     dev.set_stream(torch_stream)  # library kernels and torch events share one stream
+    dev.set_scan_ctas(args.ctas_per_query)
     n, dims, k = args.docs, args.dims, args.k
     nb = (n + 63) // 64
     warm = max(args.warmup, 3)
@@ -400,7 +405,9 @@ def run_ours(args):
         else:
             pipelined(warm)
             pipelined_s = pipelined(e2e_steps)
-        # synchronous: one mrl_query_scan call per query (launch + wait), its latency
+        # synchronous: one mrl_query_scan call per query (launch + wait), its latency, with one CTA
+        # per SM (the lowest latency for one query at a time)
+        dev.set_scan_ctas(0)
         lat = []
         sync_steps = min(e2e_steps, 500)
         for i in range(sync_steps + warm):
@@ -415,8 +422,10 @@ def run_ours(args):
         sync = {"value": len(lat) / sum(lat), "unit": "QPS", "steps": len(lat),
                 "latency_us_p50": 1e6 * float(np.percentile(lat, 50)),
                 "latency_us_p99": 1e6 * float(np.percentile(lat, 99)),
+                "ctas_per_query": torch.cuda.get_device_properties(local).multi_processor_count,
                 "path": "mrl_query_scan per query: the query in the launch's parameters, the top-256 in pinned "
                         "device-mapped memory, the call waits for it"}
+        dev.set_scan_ctas(args.ctas_per_query)
         if pipelined_s is not None:
             e2e = {"value": e2e_steps / pipelined_s, "unit": "QPS", "h2d_bytes_per_step": qbytes,
                    "d2h_bytes_per_step": k * 12 + 4, "steps": e2e_steps, "in_flight": depth,
@@ -430,7 +439,9 @@ def run_ours(args):
             e2e = dict(sync, h2d_bytes_per_step=qbytes, d2h_bytes_per_step=k * 12 + 4)
         dev.set_stream(torch_stream)
     else:
-        # every rank: host query -> plan -> local scan -> NCCL all-gather + merge kernel -> host result
+        # every rank: host query -> plan -> local scan -> NCCL all-gather + merge kernel -> host result;
+        # synchronous per query, so with one CTA per SM (the lowest latency)
+        dev.set_scan_ctas(0)
         qh = torch.empty((n_q, dims), dtype=torch.float32, pin_memory=True)
         qh.copy_(qd.cpu())
         ids_h = torch.empty(k, dtype=torch.int64, pin_memory=True)
@@ -478,6 +489,8 @@ def run_ours(args):
                         "per rank: query copy from pinned host memory + mrl_query_scan_device (fused plan + scan) + "
                         "NCCL all-gather + mrl_merge_topk + copy of the merged top-k to pinned host memory")
                        + "; max over ranks"}
+        e2e["ctas_per_query"] = torch.cuda.get_device_properties(local).multi_processor_count
+        dev.set_scan_ctas(args.ctas_per_query)
 
     peak, peak_kind = measured_peaks()
     alg_bytes = nb * 4096
@@ -507,6 +520,7 @@ def run_ours(args):
                           "flushed before every step (read+write of a 512 MiB buffer, outside the per-step events)"),
                    "wall_s_bracketed": t1 - t0,
                    "step_kernels": "one fused launch per query (plan build in every CTA + scan + top-256)",
+                   "ctas_per_query": args.ctas_per_query or torch.cuda.get_device_properties(local).multi_processor_count,
                    "host_enqueue_us_per_step": host_enqueue_us, "device_us_per_step_same_pass": device_us,
                    "timing": ("one CUDA event pair around the K timed steps (nothing runs between steps)"
                               if args.l2 == "rotate" else "per-step CUDA events, flush excluded"),

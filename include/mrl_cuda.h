@@ -383,9 +383,9 @@ int mrl_debug_vector_scores(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
  * and max(high_n, 1e-6), which every call that adds pages keeps current. Synchronous. */
 int mrl_debug_score_bound(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q,
                           const mrl_scan_cfg* cfg, float* out_bound);
-/* The context's scan control words into out[16]: 8 per launch parity (page counter, publish
- * ticket, six unused words). Consecutive scan launches alternate the two parities; every launch
- * leaves its parity's words at zero, whichever path it took. Synchronous. */
+/* The context's scan control words into out[128]: 8 per scratch set (page counter, publish ticket,
+ * five unused words, exit ticket). Consecutive scan launches use the sixteen sets in turn; every
+ * launch leaves its set's words at zero, whichever path it took. Synchronous. */
 int mrl_debug_control_words(mrl_ctx* ctx, uint32_t* out);
 
 /* ---- encode: encode_block_with_fits (src/quantize.rs:36-96) ----------------------------- */
@@ -419,6 +419,13 @@ int mrl_scan_geometry(mrl_ctx* ctx, uint32_t k, uint32_t* ctas, uint32_t* list_l
 /* Override the per-CTA candidate list length: 0 = automatic, else a power of two <= 32. Smaller
  * values exercise the exact re-selection path in tests. */
 int mrl_set_list_len(mrl_ctx* ctx, uint32_t list_len);
+/* CTAs of each single-query scan launch (mrl_scan, mrl_query_scan*, mrl_query_submit, the
+ * exchange): 0 (the default) = one per SM, the lowest latency for one query at a time; fewer
+ * spread each CTA's fixed costs (its plan build and its list) over more pages, and consecutive
+ * queries then run side by side on the free SMs, which raises the throughput of a stream of
+ * queries at the cost of each query's latency. At most the device's SM count. No counterpart in the
+ * reference. */
+int mrl_set_scan_ctas(mrl_ctx* ctx, uint32_t ctas);
 
 #ifdef __cplusplus
 }

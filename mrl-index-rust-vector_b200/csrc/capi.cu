@@ -31,8 +31,12 @@ static_assert(MRL_STATIC_MAX_CTAS <= 256 && MRL_STATIC_MAX_CTAS <= mrl::kMaxScan
 static __device__ __align__(256) unsigned char g_static_scan_scratch[kStaticBytes];
 
 namespace {
-// Initial done words of the two scratch parities: launch 0 waits for -2, launch 1 for -1.
-const unsigned int kDoneInit[2] = {0xFFFFFFFEu, 0xFFFFFFFFu};
+// Scratch sets of the single-query scans (consecutive launches may be in flight together).
+constexpr uint32_t kScratchSets = 16;
+// Initial done words of the scratch sets: launch s < kScratchSets waits for s - kScratchSets.
+const unsigned int kDoneInit[kScratchSets] = {
+    0xFFFFFFF0u, 0xFFFFFFF1u, 0xFFFFFFF2u, 0xFFFFFFF3u, 0xFFFFFFF4u, 0xFFFFFFF5u, 0xFFFFFFF6u, 0xFFFFFFF7u,
+    0xFFFFFFF8u, 0xFFFFFFF9u, 0xFFFFFFFAu, 0xFFFFFFFBu, 0xFFFFFFFCu, 0xFFFFFFFDu, 0xFFFFFFFEu, 0xFFFFFFFFu};
 }  // namespace
 
 struct mrl_ctx {
@@ -41,16 +45,17 @@ struct mrl_ctx {
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
     std::string err;
-    // scan scratch, one set per launch parity (scan_seq & 1): consecutive scan launches on the
-    // stream may overlap (programmatic dependent launch), and a launch starts only once the one two
-    // back has completed. Per parity: per-CTA lists, control words, per-page owner (grow-only;
-    // each parity owns half of `owner`).
-    unsigned long long* cta_keys = nullptr;  // per parity 2 * sms * 32: scan keys, then their exact keys
-    unsigned int* ctl = nullptr;             // per parity mrl::kCtlWords
+    // scan scratch, kScratchSets sets used by consecutive scan launches in turn: launches on the
+    // stream may overlap (programmatic dependent launch), and a launch touches its set only once the
+    // launch that used it before has released it. Per set: per-CTA lists, control words, per-page
+    // owner (grow-only; each set owns an equal share of `owner`).
+    unsigned long long* cta_keys = nullptr;  // per set 2 * sms * 32: scan keys, then their exact keys
+    unsigned int* ctl = nullptr;             // per set mrl::kCtlWords
     uint8_t* owner = nullptr;
     size_t owner_bytes = 0;
-    uint32_t scan_seq = 0;      // launches so far; launch s uses parity s & 1
-    unsigned int* done = nullptr;  // per parity: sequence number of the last launch that released it
+    uint32_t scan_seq = 0;      // launches so far; launch s uses scratch set s % kScratchSets
+    uint32_t scan_ctas = 0;     // CTAs per single-query scan launch (0: one per SM)
+    unsigned int* done = nullptr;  // per set: sequence number of the last launch that released it
     uint32_t list_len_override = 0;
     // grow-only scratch for host-facing calls: inputs (queries, rows, means) and outputs
     void* tmp = nullptr;
@@ -256,6 +261,9 @@ int check_cfg(mrl_ctx* ctx, const mrl_scan_cfg* cfg, uint32_t dims) {
     return MRL_OK;
 }
 
+// CTAs of a single-query scan launch.
+uint32_t scan_grid(const mrl_ctx* ctx) { return ctx->scan_ctas ? ctx->scan_ctas : (uint32_t)ctx->sms; }
+
 mrl::ScanLaunch make_launch(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, uint32_t q,
                             const mrl_scan_cfg* cfg, const uint32_t* lo, const uint32_t* hi) {
     mrl::ScanLaunch p{};
@@ -265,7 +273,7 @@ mrl::ScanLaunch make_launch(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
     p.block_id_base = seg->block_id_base;
     p.plan = plans ? plans->d + q : nullptr;
     p.k = cfg->shortlist_cand;
-    p.list_len = ctx->list_len_override ? ctx->list_len_override : auto_list_len(p.k, (uint32_t)ctx->sms);
+    p.list_len = ctx->list_len_override ? ctx->list_len_override : auto_list_len(p.k, scan_grid(ctx));
     p.w_s4 = cfg->stratum4_weight;
     p.depth = cfg->strata_depth;
     p.mode = cfg->mode;
@@ -278,23 +286,24 @@ mrl::ScanLaunch make_launch(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* p
     return p;
 }
 
-// Grows the per-page owner scratch to two parities of n_blocks bytes each.
+// Grows the per-page owner scratch to kScratchSets sets of n_blocks bytes each.
 int ensure_owner(mrl_ctx* ctx, uint64_t n_blocks) {
-    return ensure_buf(ctx, (void**)&ctx->owner, &ctx->owner_bytes, 2 * (n_blocks ? n_blocks : 1));
+    return ensure_buf(ctx, (void**)&ctx->owner, &ctx->owner_bytes, kScratchSets * (n_blocks ? n_blocks : 1));
 }
 
-// The context scratch of the next scan launch: the parities alternate launch by launch. Launch s
-// waits until launch s - 2 (the previous user of its parity) has released it; a parity's done word
-// starts at the sequence number a launch two before the first would have had. launched() advances
-// the sequence once the launch has been issued.
+// The context scratch of the next scan launch: the sets are used in turn. Launch s waits until
+// launch s - kScratchSets (the previous user of its set) has released it; a set's done word starts
+// at the sequence number such a launch before the first would have had. launched() advances the
+// sequence once the launch has been issued.
 void take_scratch(mrl_ctx* ctx, mrl::ScanLaunch& p) {
-    const size_t par = ctx->scan_seq & 1u;
-    p.cta_keys = ctx->cta_keys + par * 2 * 32 * (size_t)ctx->sms;
+    const size_t set = ctx->scan_seq % kScratchSets;
+    p.cta_keys = ctx->cta_keys + set * 2 * 32 * (size_t)ctx->sms;
     p.cta_xkeys = p.cta_keys + 32 * (size_t)ctx->sms;
-    p.ctl = ctx->ctl + par * mrl::kCtlWords;
-    p.owner = ctx->owner + par * (ctx->owner_bytes / 2);
-    p.done = ctx->done + par;
+    p.ctl = ctx->ctl + set * mrl::kCtlWords;
+    p.owner = ctx->owner + set * (ctx->owner_bytes / kScratchSets);
+    p.done = ctx->done + set;
     p.seq = ctx->scan_seq;
+    p.done_prev = ctx->scan_seq - kScratchSets;
 }
 void launched(mrl_ctx* ctx) { ++ctx->scan_seq; }
 
@@ -400,11 +409,11 @@ int mrl_ctx_create(int device, mrl_ctx** out) {
         return MRL_ERR_CUDA;
     }
     ctx->stream = ctx->own_stream;
-    if (cudaMalloc(&ctx->cta_keys, sizeof(unsigned long long) * 2 * 2 * 32 * (size_t)ctx->sms) != cudaSuccess ||
-        cudaMalloc(&ctx->ctl, sizeof(unsigned int) * 2 * mrl::kCtlWords) != cudaSuccess ||
-        cudaMalloc(&ctx->done, sizeof(unsigned int) * 2) != cudaSuccess ||
+    if (cudaMalloc(&ctx->cta_keys, sizeof(unsigned long long) * kScratchSets * 2 * 32 * (size_t)ctx->sms) != cudaSuccess ||
+        cudaMalloc(&ctx->ctl, sizeof(unsigned int) * kScratchSets * mrl::kCtlWords) != cudaSuccess ||
+        cudaMalloc(&ctx->done, sizeof(unsigned int) * kScratchSets) != cudaSuccess ||
         cudaMalloc(&ctx->d_means, 192 * sizeof(float)) != cudaSuccess ||
-        cudaMemset(ctx->ctl, 0, sizeof(unsigned int) * 2 * mrl::kCtlWords) != cudaSuccess ||
+        cudaMemset(ctx->ctl, 0, sizeof(unsigned int) * kScratchSets * mrl::kCtlWords) != cudaSuccess ||
         cudaMemcpy(ctx->done, kDoneInit, sizeof(kDoneInit), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) {
         mrl_ctx_destroy(ctx);
@@ -719,7 +728,7 @@ int mrl_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* plans, ui
             continue;
         }
         take_scratch(ctx, p);
-        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+        if (mrl::launch_scan(p, scan_grid(ctx), ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
         launched(ctx);
     }
     return MRL_OK;
@@ -797,7 +806,7 @@ int mrl_scan_device_static(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pl
             continue;
         }
         // an ordinary launch (no programmatic dependent launch): every call shares the one region
-        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, false)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+        if (mrl::launch_scan(p, scan_grid(ctx), ctx->stream, false)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     }
     return MRL_OK;
 }
@@ -876,7 +885,7 @@ int mrl_query_scan_device(mrl_ctx* ctx, const mrl_seg* seg, const float* d_queri
         p.mid_seed = codec->mid_seed;
         p.plan_out = plans->d + i;
         take_scratch(ctx, p);
-        if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+        if (mrl::launch_scan(p, scan_grid(ctx), ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
         launched(ctx);
     }
     return MRL_OK;
@@ -1006,7 +1015,7 @@ int query_submit(mrl_ctx* ctx, const mrl_seg* seg, const float* query, uint32_t 
     p.mid_seed = codec->mid_seed;
     p.plan_out = plan_out;
     take_scratch(ctx, p);
-    if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, true, query)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+    if (mrl::launch_scan(p, scan_grid(ctx), ctx->stream, true, query)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     launched(ctx);
     ctx->slot_busy[slot] = true;
     return MRL_OK;
@@ -1204,7 +1213,7 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
     p.xch_recv = ex->local + parity * ex->world * ex->rb;
     p.xch_flag_in = reinterpret_cast<const unsigned*>(ex->local + ex->flags_off()) + parity * ex->world;
     take_scratch(ctx, p);
-    if (mrl::launch_scan(p, (uint32_t)ctx->sms, ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
+    if (mrl::launch_scan(p, scan_grid(ctx), ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     launched(ctx);
     return MRL_OK;
 }
@@ -1483,8 +1492,8 @@ int mrl_debug_score_bound(mrl_ctx* ctx, const mrl_seg* seg, const mrl_plans* pla
 int mrl_debug_control_words(mrl_ctx* ctx, uint32_t* out) {
     if (!ctx || !out) return MRL_ERR_INVALID;
     if (int rc = set_device(ctx)) return rc;
-    for (int par = 0; par < 2; ++par)  // the 8 control words of each parity
-        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out + 8 * par, ctx->ctl + par * mrl::kCtlWords, 8 * sizeof(unsigned),
+    for (uint32_t set = 0; set < kScratchSets; ++set)  // the 8 control words of each scratch set
+        MRL_CUDA_TRY(ctx, cudaMemcpyAsync(out + 8 * set, ctx->ctl + set * mrl::kCtlWords, 8 * sizeof(unsigned),
                                           cudaMemcpyDeviceToHost, ctx->stream));
     MRL_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
     return MRL_OK;
@@ -1590,8 +1599,16 @@ int mrl_synth_queries_device(mrl_ctx* ctx, uint64_t doc_seed, uint64_t n_docs, u
 
 int mrl_scan_geometry(mrl_ctx* ctx, uint32_t k, uint32_t* ctas, uint32_t* list_len) {
     if (!ctx) return MRL_ERR_INVALID;
-    if (ctas) *ctas = (uint32_t)ctx->sms;
-    if (list_len) *list_len = ctx->list_len_override ? ctx->list_len_override : auto_list_len(k, (uint32_t)ctx->sms);
+    if (ctas) *ctas = scan_grid(ctx);
+    if (list_len) *list_len = ctx->list_len_override ? ctx->list_len_override : auto_list_len(k, scan_grid(ctx));
+    return MRL_OK;
+}
+
+int mrl_set_scan_ctas(mrl_ctx* ctx, uint32_t ctas) {
+    if (!ctx) return MRL_ERR_INVALID;
+    if (ctas > (uint32_t)ctx->sms)
+        return fail(ctx, MRL_ERR_INVALID, "ctas must be 0 (one per SM) or at most the device's " + std::to_string(ctx->sms) + " SMs");
+    ctx->scan_ctas = ctas;
     return MRL_OK;
 }
 

@@ -209,6 +209,8 @@ struct ScanLaunch {
     unsigned int* done;            // launch sequence number of the last launch to release this
                                    // scratch (nullptr: scratch of one launch at a time, no check)
     uint32_t seq;                  // this launch's sequence number on the context
+    uint32_t done_prev;            // *done must hold this (the previous user's seq) before the
+                                   // launch touches the scratch
     const float* metamax;          // the segment's 4 meta-factor maxima (launch_metamax)
     uint8_t* owner;                // n_blocks: CTA that scored each page
     uint64_t* out_ids;

@@ -812,12 +812,12 @@ __device__ __forceinline__ bool scan_body(const ScanLaunch& p, const float* quer
     // thread (double-precision arithmetic)
     if (kFast && tid == 0) s_E = fast_error_bound(*plan, mm, p.w_s4, p.depth);
     // This launch's scratch (page counter, lists, ready flags, owner) is free once the launch that
-    // used it before (two launches back) has released it; under full residency it always has by
-    // now. Bounded (about 1 s).
+    // used it before has released it (*done == done_prev); normally it has long before. Bounded
+    // (about 1 s).
     if (p.done && tid == 0) {
         unsigned it = 0;
         int ok = 1;
-        while (ld_acquire_gpu(p.done) != p.seq - 2u) {
+        while (ld_acquire_gpu(p.done) != p.done_prev) {
             if (++it > (1u << 20)) { ok = 0; break; }
             if (it > 8) __nanosleep(128);
         }

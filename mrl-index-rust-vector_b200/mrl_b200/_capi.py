@@ -129,6 +129,7 @@ SIGNATURES = {
     "mrl_synth_queries_device": (_i, [_vp, _u64, _u64, _u64, _u64, _u32, C.c_float, _vp, _vp]),
     "mrl_scan_geometry": (_i, [_vp, _u32, C.POINTER(_u32), C.POINTER(_u32)]),
     "mrl_set_list_len": (_i, [_vp, _u32]),
+    "mrl_set_scan_ctas": (_i, [_vp, _u32]),
     "mrl_set_batch_engine": (_i, [_vp, _u32]),
 }
 

@@ -237,6 +237,10 @@ class Device:
     def set_list_len(self, n: int) -> None:
         check(self.ptr, self.lib.mrl_set_list_len(self.ptr, n))
 
+    def set_scan_ctas(self, n: int) -> None:
+        """CTAs per single-query scan launch (mrl_set_scan_ctas): 0 = one per SM."""
+        check(self.ptr, self.lib.mrl_set_scan_ctas(self.ptr, n))
+
 
 _default_device: Optional[Device] = None
 
@@ -588,8 +592,8 @@ def score_bound(segment: Segment, plan: QueryPlan, cfg, q: int = 0) -> float:
 
 
 def control_words(dev: "Device") -> List[int]:
-    """The context's scan control words, 8 per launch parity (mrl_debug_control_words)."""
-    out = (C.c_uint32 * 16)()
+    """The context's scan control words, 8 per scratch set (mrl_debug_control_words)."""
+    out = (C.c_uint32 * 128)()
     check(dev.ptr, dev.lib.mrl_debug_control_words(dev.ptr, out))
     return list(out)
 

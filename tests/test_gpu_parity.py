@@ -352,9 +352,9 @@ def test_order_dependent_configs_refused(ora, dev, corpus768):
 
 
 def test_control_words_left_zero(ora, dev, corpus768):
-    """Every launch's last CTA (the holder of the last publish ticket) zeroes its parity's control
-    words, on the clean path, the re-selection path and the fused path alike, so a launch never
-    inherits a page counter or ticket count from the one two before."""
+    """Every launch's last CTA to exit zeroes its scratch set's control words, on the clean path,
+    the re-selection path and the fused path alike, so a launch never inherits a page counter or
+    ticket count from the launch that used the set before."""
     M = mb()
     seg = M.Segment.upload(corpus768["eden"], dev)
     qs = corpus768["qs"]
@@ -365,11 +365,11 @@ def test_control_words_left_zero(ora, dev, corpus768):
             for mode in (M.ScanMode.EXACT, M.ScanMode.FAST):
                 M.scan_blocks_batch(seg, gp, M.ScanConfig(shortlist_cand=256, mode=mode))
                 w = M.control_words(dev)
-                assert list(w) == [0] * 16, (ll, mode, w)
+                assert list(w) == [0] * 128, (ll, mode, w)
         M.query_scan(seg, qs, M.ScanConfig(shortlist_cand=64), prefix_codec=M.PrefixCodec.EDEN_PROD,
                      eden=fit(corpus768["mean"]))
         w = M.control_words(dev)
-        assert list(w) == [0] * 16, w
+        assert list(w) == [0] * 128, w
     finally:
         dev.set_list_len(0)
     gp.free()
@@ -690,4 +690,48 @@ def test_query_stream_pipelined_matches_device_scan(ora, dev, corpus768, mode):
         st.submit(np.zeros(1040, np.float32), 6)
     with pytest.raises(M.MrlError):
         st.submit(qs[0], M.MAX_INFLIGHT)
+    seg.free()
+
+
+@pytest.mark.parametrize("ctas", [1, 16, 24, 74])
+def test_fewer_ctas_per_query_same_results(ora, dev, corpus768, ctas):
+    """mrl_set_scan_ctas: with fewer CTAs per launch (several queries then run side by side on the
+    device), the results of the fused device path and of pipelined host queries are bit-identical
+    to one CTA per SM, and every scratch set's control words end at zero."""
+    import torch
+
+    M = mb()
+    seg = M.Segment.upload(corpus768["eden"], dev)
+    mean = corpus768["mean"]
+    qs = np.concatenate([corpus768["qs"]] * 3)[:9]
+    kw = dict(prefix_codec=M.PrefixCodec.EDEN_PROD, mid_codec=M.MidCodec.RABITQ, eden=fit(mean))
+    cfg = M.ScanConfig(shortlist_cand=128)
+    r_ids, r_sc, r_cnt, r_plans = M.query_scan(seg, qs, cfg, **kw)
+    try:
+        dev.set_scan_ctas(ctas)
+        ids, sc, cnt, plans = M.query_scan(seg, qs, cfg, **kw)  # several launches in flight
+        assert np.array_equal(cnt, r_cnt)
+        for qi in range(len(qs)):
+            n = int(r_cnt[qi])
+            assert np.array_equal(ids[qi, :n], r_ids[qi, :n])
+            assert np.array_equal(sc[qi, :n].view(np.uint32), r_sc[qi, :n].view(np.uint32))
+        st = M.QueryStream(seg, cfg, **kw)
+        for i in range(len(qs)):
+            st.submit(qs[i], i % M.MAX_INFLIGHT)
+            if i >= 5:
+                j = i - 5
+                gi, gs = st.collect(j % M.MAX_INFLIGHT)
+                assert np.array_equal(gi, r_ids[j, : int(r_cnt[j])])
+        for j in range(len(qs) - 5, len(qs)):
+            gi, gs = st.collect(j % M.MAX_INFLIGHT)
+            assert np.array_equal(gs.view(np.uint32), r_sc[j, : int(r_cnt[j])].view(np.uint32))
+        torch.cuda.synchronize()
+        assert list(M.control_words(dev)) == [0] * 128
+        plans.free()
+    finally:
+        dev.set_scan_ctas(0)
+    op = ora.plan_build(qs[0], eden_mean=mean)
+    rid, rsc = ora.scan_blocks(corpus768["eden"], op, ora.scan_cfg(k=128))
+    assert [int(x) for x in r_ids[0, : int(r_cnt[0])]] == [int(x) for x in rid]
+    r_plans.free()
     seg.free()
