@@ -494,7 +494,8 @@ def run_ours(args):
 
     peak, peak_kind = measured_peaks()
     alg_bytes = nb * 4096
-    # the dominant kernel's mean duration: the timed per-step time when the step is that one launch
+    # the dominant kernel's mean time per launch: the timed per-step time when the step is that one launch
+    # (consecutive launches overlap, so this is the period at which they complete)
     scan_avg_s = (total_ms / args.steps if exch is None else float(scan_ms.mean())) / 1e3
     achieved = alg_bytes / scan_avg_s / 1e9
     line = {
