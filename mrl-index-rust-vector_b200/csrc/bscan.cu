@@ -518,6 +518,7 @@ struct TShared {
     BWarpState wst[kTG][kBWarps][4];
     u64 wlist[kTG][kBWarps][4][32];      // [tile][warp][query of its group][32]
     u64 queue[kTG][kBWarps][4][32];
+    uint32_t pub[kTG * kTQ][16];         // per query: 8th/16th/24th/32nd key words of each lane quarter
     uint64_t bar;
     uint32_t taddr;
 };
@@ -529,20 +530,65 @@ struct TensorLaunch {
     uint32_t* err;
 };
 
-__device__ __forceinline__ void bsel_offer1(u64* wl, u64* q, int lane, u64* cta_tau, BWarpState* st, u64 k0) {
+// The tensor engine's flush: bsel_flush, and the list also publishes the high words of its 8th,
+// 16th, 24th and 32nd keys in its query's row `pub` (4 lane quarters x 4 words; 0 = no such key).
+// A published word w_i of a list certifies 8 (i + 1) keys of that list with high word >= w_i, so
+// the CTA holds >= 32 keys with high word >= v whenever at least four of the row's 16 words are
+// >= v; the CTA bound rises to the largest such v (a key below it is not among the CTA's top 32).
+// Words of other lists are read as they are: a list's i-th key only rises, so an older word still
+// certifies its count.
+__device__ __forceinline__ void tsel_flush(u64* wl, u64* q, int lane, u64* cta_tau, BWarpState* st, uint32_t* pub,
+                                           int qw) {
+    __syncwarp();
+    const int qn = st->qn;
+    u64 list = wl[lane];
+    for (int base = 0; base < qn; base += 32) {
+        u64 x = (base + lane < qn) ? q[base + lane] : 0ull;
+        x = warp_sort32(x, lane);
+        list = warp_merge32(list, x, lane);
+    }
+    const u64 t = __shfl_sync(kFull, list, 31);
+    wl[lane] = list;
+    volatile uint32_t* vp = pub;
+    if ((lane & 7) == 7) vp[4 * qw + (lane >> 3)] = (uint32_t)(list >> 32);
+    __syncwarp();
+    uint32_t best = 0u;
+    if (lane < 16) {
+        const uint32_t v = vp[lane];
+        if (v) {
+            int c = 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const uint32_t w = vp[i];
+                c += (w != 0u && w >= v) ? 1 : 0;
+            }
+            if (c >= 4) best = v;
+        }
+    }
+    best = __reduce_max_sync(kFull, best);
+    if (lane == 0) {
+        st->qn = 0;
+        st->tau = (uint32_t)(t >> 32);
+        if (best) atomicMax(cta_tau, (u64)best << 32);
+    }
+    __syncwarp();
+}
+
+__device__ __forceinline__ void tsel_offer1(u64* wl, u64* q, int lane, u64* cta_tau, BWarpState* st, uint32_t* pub,
+                                            int qw, u64 k0) {
     const uint32_t tc_ = (uint32_t)(*reinterpret_cast<volatile u64*>(cta_tau) >> 32);
     const uint32_t tau = max(max(st->tau, tc_), 1u);
     const bool p0 = (uint32_t)(k0 >> 32) >= tau;
     const unsigned m0 = __ballot_sync(kFull, p0);
     if (m0 == 0u) return;
     const int nn = __popc(m0);
-    if (st->qn + nn > 32) bsel_flush(wl, q, lane, cta_tau, st);
+    if (st->qn + nn > 32) tsel_flush(wl, q, lane, cta_tau, st, pub, qw);
     const int qn = st->qn;
     if (p0) q[qn + __popc(m0 & ((1u << lane) - 1u))] = k0;
     __syncwarp();
     if (lane == 0) st->qn = qn + nn;
     __syncwarp();
-    if (qn + nn >= 32) bsel_flush(wl, q, lane, cta_tau, st);
+    if (qn + nn >= 32) tsel_flush(wl, q, lane, cta_tau, st, pub, qw);
 }
 
 // One-hot bytes of the four 4-bit levels in nibbles 0..3 of `w`, 4 columns each: level l sets
@@ -592,23 +638,31 @@ __device__ __forceinline__ void tile_mmas(uint32_t tbase, uint32_t b_smem, uint3
 }
 
 // Scores of this thread's slot for queries 4 g4 .. 4 g4 + 3 of query tile tt (stage sums as
-// digit columns dp, d1, d4), offered to the tile's selection.
+// digit columns dp, d1, d4), then offered to the tile's selection. The four scores are made
+// unrolled (the digit columns stay in registers); the offers run in a rolled loop, so the
+// selection code (the flush's sort and merge) exists once per call site: with one copy per query
+// the kernel's code overflowed the instruction cache (about 4% of a batch's time).
 __device__ __forceinline__ void tile_epilogue(TShared& sh, int tt, uint32_t nq, int g4, int warp, int lane,
                                              const SlotMeta& m, bool live, uint32_t gid, const uint32_t (&dp)[16],
                                              const uint32_t (&d1)[16], const uint32_t (&d4)[16]) {
+    u64 key[4];  // a query past the tile's last is scored on a stale constant row, never offered
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const int q = 4 * g4 + j;
-        if ((uint32_t)q < nq) {  // warp-uniform
-            const int qi = tt * kTQ + q;
-            const QConst c = sh.qc[qi];
-            const int32_t P = digits4(dp + 4 * j);
-            const int32_t A1 = c.c1 + digits4(d1 + 4 * j);
-            const int32_t A4 = c.c4 + digits4(d4 + 4 * j);
-            const float sc = (c.flags & 16u) ? qscore(m, P, A1, A4, c) : fast_score(m, P, A1, A4, sh.S[qi]);
-            const u64 key = (!live || m.tomb) ? 0ull : make_key(sc, gid);
-            bsel_offer1(sh.wlist[tt][warp][j], sh.queue[tt][warp][j], lane, &sh.tau[qi], &sh.wst[tt][warp][j], key);
-        }
+        const int qi = tt * kTQ + min(4 * g4 + j, kTQ - 1);
+        const QConst c = sh.qc[qi];
+        const int32_t P = digits4(dp + 4 * j);
+        const int32_t A1 = c.c1 + digits4(d1 + 4 * j);
+        const int32_t A4 = c.c4 + digits4(d4 + 4 * j);
+        const float sc = (c.flags & 16u) ? qscore(m, P, A1, A4, c) : fast_score(m, P, A1, A4, sh.S[qi]);
+        key[j] = (!live || m.tomb) ? 0ull : make_key(sc, gid);
+    }
+    const int nj = min(4, max(0, (int)nq - 4 * g4));  // warp-uniform: this group's queries in the tile
+#pragma unroll 1
+    for (int j = 0; j < nj; ++j) {
+        const int qi = tt * kTQ + 4 * g4 + j;
+        const u64 k0 = j == 0 ? key[0] : (j == 1 ? key[1] : (j == 2 ? key[2] : key[3]));
+        tsel_offer1(sh.wlist[tt][warp][j], sh.queue[tt][warp][j], lane, &sh.tau[qi], &sh.wst[tt][warp][j],
+                    sh.pub[qi], warp & 3, k0);
     }
 }
 
@@ -674,6 +728,7 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
         }
         if (tid < kTG * kBWarps * 4) (&sh.wst[0][0][0])[tid] = BWarpState{0u, 0};
         for (int i = tid; i < kTG * kBWarps * 4 * 32; i += kBThreads) (&sh.wlist[0][0][0][0])[i] = 0ull;
+        for (int i = tid; i < kTG * kTQ * 16; i += kBThreads) (&sh.pub[0][0])[i] = 0u;
         tc::fence_proxy_async_smem();  // generic-proxy writes of B -> tensor-core reads
         tc::fence_before();
         __syncthreads();
@@ -762,11 +817,13 @@ __global__ void __launch_bounds__(kBThreads, 1) tscan_kernel(const TensorLaunch 
             __syncthreads();  // tensor memory (A and D) free for the next slot tile
         }
         if (failed) break;
+#pragma unroll 1
         for (int tt = 0; tt < nt; ++tt)
+#pragma unroll 1
             for (int j = 0; j < 4; ++j)
                 if (sh.wst[tt][warp][j].qn)
-                    bsel_flush(sh.wlist[tt][warp][j], sh.queue[tt][warp][j], lane, &sh.tau[tt * kTQ + 4 * g4 + j],
-                               &sh.wst[tt][warp][j]);
+                    tsel_flush(sh.wlist[tt][warp][j], sh.queue[tt][warp][j], lane, &sh.tau[tt * kTQ + 4 * g4 + j],
+                               &sh.wst[tt][warp][j], sh.pub[tt * kTQ + 4 * g4 + j], qw);
         __syncthreads();
         for (int tt = 0; tt < nt; ++tt) {
             if ((uint32_t)warp < (tt == 0 ? nq0 : nq1)) {  // warp w merges query w: the 4 lane quarters' lists

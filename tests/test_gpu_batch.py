@@ -213,9 +213,13 @@ def test_batch_against_oracle_exact_topk(ora, dev, engine):
     plans.free()
 
 
-def test_batch_many_pages_per_sm(dev, engine):
-    """A segment of 4,000 pages (about 27 per SM): every warp scores several pages per tile, so the
-    candidate queues fill and flush repeatedly; results stay identical to the single-query scan."""
+@pytest.mark.parametrize("n_q", [16, 40])
+def test_batch_many_pages_per_sm(dev, engine, n_q):
+    """A segment of 4,000 pages (27 or 28 per SM, so some CTAs end on a half slot tile): every warp
+    scores several pages per tile, so the candidate queues fill and flush repeatedly; 40 queries
+    take a group of two query tiles (the second tile's MMAs overlapping the first's scores, the
+    next slot tile's overlapping the second's) and a group of one. Results stay identical to the
+    single-query scan."""
     import torch
 
     M = mb()
@@ -231,7 +235,6 @@ def test_batch_many_pages_per_sm(dev, engine):
     M._capi.check(dev.ptr, lib.mrl_encode_device(dev.ptr, C.c_void_p(x.data_ptr()), n, dims, 8, C.byref(desc), None,
                                                  0, C.byref(sp)))
     seg = M.Segment(sp, dev)
-    n_q = 16
     qd = torch.empty((n_q, dims), dtype=torch.float32, device="cuda")
     M._capi.check(dev.ptr, lib.mrl_synth_queries_device(dev.ptr, 77, n, 5, n_q, dims, C.c_float(0.1),
                                                         C.c_void_p(qd.data_ptr()), None))
