@@ -591,19 +591,22 @@ __device__ __forceinline__ void tsel_offer1(u64* wl, u64* q, int lane, u64* cta_
     if (qn + nn >= 32) tsel_flush(wl, q, lane, cta_tau, st, pub, qw);
 }
 
+// 1 << s, or 0 when s >= 32 (PTX shl.b32 clamps the shift amount to 32).
+__device__ __forceinline__ uint32_t shl_clamp(uint32_t a, uint32_t s) {
+    uint32_t d;
+    asm("shl.b32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(s));
+    return d;
+}
 // One-hot bytes of the four 4-bit levels in nibbles 0..3 of `w`, 4 columns each: level l sets
-// byte l & 3 of column l >> 2 (ALU only; a shared-memory pattern table costs bank conflicts
-// under the data-dependent indices).
+// byte l & 3 of column l >> 2, i.e. column c = 1 << (8 l - 32 c), zero when that shift is outside
+// 0..31 (a negative one wraps to a large unsigned shift). ALU only; a shared-memory pattern table
+// costs bank conflicts under the data-dependent indices.
 __device__ __forceinline__ void onehot4(uint32_t w, uint32_t (&r)[16]) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const uint32_t l = (w >> (4 * i)) & 15u;
-        const uint32_t bit = 1u << ((l & 3u) << 3);
-        const uint32_t c = l >> 2;
-        r[4 * i] = c == 0u ? bit : 0u;
-        r[4 * i + 1] = c == 1u ? bit : 0u;
-        r[4 * i + 2] = c == 2u ? bit : 0u;
-        r[4 * i + 3] = c == 3u ? bit : 0u;
+        const uint32_t s8 = i == 0 ? (w << 3) & 0x78u : (w >> (4 * i - 3)) & 0x78u;  // 8 x level i
+#pragma unroll
+        for (int c = 0; c < 4; ++c) r[4 * i + c] = shl_clamp(1u, s8 - 32u * (uint32_t)c);
     }
 }
 // 0/1 bytes of the 16 nibbles' bits of two words (64 bits) into 16 columns.
