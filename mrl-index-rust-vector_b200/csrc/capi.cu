@@ -127,6 +127,7 @@ struct mrl_exchange {
     size_t rb = 0;                               // bytes per record
     unsigned char* local = nullptr;              // this rank's area (cudaMalloc)
     unsigned char* area[mrl::kMaxRanks] = {};    // every rank's area (area[rank] == local)
+    unsigned char* stage = nullptr;              // kScratchSets staged records, one per scratch set
     uint32_t epoch = 0;
     bool opened = false;
     size_t flags_off() const { return 2 * (size_t)world * rb; }
@@ -1120,13 +1121,28 @@ int mrl_exchange_create(mrl_ctx* ctx, uint32_t world, uint32_t rank, uint32_t k,
         delete ex;
         return fail(ctx, MRL_ERR_NOMEM, "cudaMalloc exchange area");
     }
+    if (cudaMalloc(&ex->stage, kScratchSets * ex->rb) != cudaSuccess) {
+        cudaFree(ex->local);
+        delete ex;
+        return fail(ctx, MRL_ERR_NOMEM, "cudaMalloc exchange staging records");
+    }
     const cudaError_t e = cudaMemset(ex->local, 0, ex->bytes());
-    if (e != cudaSuccess) { cudaFree(ex->local); delete ex; return cuda_fail(ctx, e, "exchange area memset"); }
+    if (e != cudaSuccess) {
+        cudaFree(ex->stage);
+        cudaFree(ex->local);
+        delete ex;
+        return cuda_fail(ctx, e, "exchange area memset");
+    }
     ex->area[rank] = ex->local;
     if (world > 1) {
         cudaIpcMemHandle_t h;
         const cudaError_t he = cudaIpcGetMemHandle(&h, ex->local);
-        if (he != cudaSuccess) { cudaFree(ex->local); delete ex; return cuda_fail(ctx, he, "cudaIpcGetMemHandle"); }
+        if (he != cudaSuccess) {
+            cudaFree(ex->stage);
+            cudaFree(ex->local);
+            delete ex;
+            return cuda_fail(ctx, he, "cudaIpcGetMemHandle");
+        }
         std::memcpy(ipc_handle, &h, sizeof(h));
     } else {
         ex->opened = true;
@@ -1163,6 +1179,7 @@ int mrl_exchange_destroy(mrl_ctx* ctx, mrl_exchange* ex) {
     cudaDeviceSynchronize();
     for (uint32_t r = 0; r < ex->world; ++r)
         if (r != ex->rank && ex->area[r]) cudaIpcCloseMemHandle(ex->area[r]);
+    cudaFree(ex->stage);
     cudaFree(ex->local);
     delete ex;
     (void)ctx;
@@ -1212,6 +1229,9 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
     }
     p.xch_recv = ex->local + parity * ex->world * ex->rb;
     p.xch_flag_in = reinterpret_cast<const unsigned*>(ex->local + ex->flags_off()) + parity * ex->world;
+    // the staged record of this launch's scratch set: free once the set's previous user has
+    // completed, which the launch waits for before its scoring loop
+    p.xch_stage = ex->stage + (ctx->scan_seq % kScratchSets) * ex->rb;
     take_scratch(ctx, p);
     if (mrl::launch_scan(p, scan_grid(ctx), ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     launched(ctx);

@@ -226,17 +226,20 @@ struct ScanLaunch {
     uint64_t eden_seed, mid_seed;
     DevPlan* plan_out;
     // NVLink exchange (xch_world > 0), by pushes: every rank's area holds, per buffer parity
-    // (xch_epoch & 1), one receive record and one flag word per sending rank. This rank's CTAs store
-    // their entries of its top-k into its record slot in every rank's area (peer stores over NVLink
-    // for the others); the last CTA adds the count, raises this rank's flag in every other area
-    // (release, system scope), waits (bounded) for the other ranks' flags in its own area, and
-    // merges the records there, all in local memory, into out_* (the global top-k)
+    // (xch_epoch & 1), one receive record and one flag word per sending rank. The finisher ranks
+    // this rank's top-k into xch_stage (a record of this launch's scratch set, so it needs no
+    // ordering against the previous launch), then, once the previous launch has completed, copies
+    // it into its record slot in every rank's area (peer stores over NVLink for the others), raises
+    // this rank's flag in every other area (release, system scope), waits (bounded) for the other
+    // ranks' flags in its own area, and merges the records there, all in local memory, into out_*
+    // (the global top-k)
     uint32_t xch_world, xch_rank, xch_epoch;
     uint32_t xch_tree;  // set by launch_scan: merge as a pairwise tree (room for its buffers)
     unsigned char* xch_rec[kMaxRanks];   // this rank's record slot in rank w's area (this parity)
     unsigned int* xch_flag[kMaxRanks];   // this rank's flag word in rank w's area (this parity)
     const unsigned char* xch_recv;       // this parity's receive records in this rank's area, by sender
     const unsigned int* xch_flag_in;     // this parity's flag words in this rank's area, by sender
+    unsigned char* xch_stage;            // this rank's record of this launch, before its copies
 };
 int scan_ctas(int device_sms);
 size_t scan_smem_bytes(uint32_t ctas, uint32_t k, uint32_t fused_dims, uint32_t xch_world, uint32_t mode);

@@ -350,27 +350,28 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-// Last step of the NVLink exchange, by the one CTA after this rank's record is complete in its own
-// slot of its own area: push the record into this rank's slot of every other rank's area (peer
-// stores over NVLink), raise this rank's flag there (release, system scope), wait (bounded, ~2-3 s)
-// for every other rank's flag of this epoch in this rank's own area, copy all records of this area
-// into shared memory (`smem`, at least xch_world records; local loads only) and merge them into the
-// outputs. Status bit 2 reports a timeout.
+// Last step of the NVLink exchange, by the finisher once this rank's record is complete in
+// xch_stage: wait until the previous launch on the stream has completed (its finisher may still be
+// merging from this parity's area two launches back, or writing the same outputs), copy the record
+// into this rank's slot of every rank's area (peer stores over NVLink for the others), raise this
+// rank's flag in the other areas (release, system scope), wait (bounded, ~2-3 s) for every other
+// rank's flag of this epoch in this rank's own area, copy all records of this area into shared
+// memory (`smem`, at least xch_world records; local loads only) and merge them into the outputs.
+// Only this step is ordered after the previous launch; the load and ranking of this rank's lists
+// before it overlap the previous query's exchange. Status bit 2 reports a timeout.
 __device__ void xch_publish_and_merge(const ScanLaunch& p, unsigned char* smem, int* s_ok, unsigned status) {
     const int tid = threadIdx.x;
     const size_t rb = MRL_MERGE_RECORD_BYTES(p.k), words = rb / 16;
     const unsigned nw = (unsigned)words;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     __syncthreads();
     {
-        // this rank's record (local) into its slot in every other rank's area: posted stores, all
+        // this rank's record (staged) into its slot in every rank's area: posted stores, all
         // threads, so the copies to all peers are in flight at once
-        const uint4* src = reinterpret_cast<const uint4*>(p.xch_rec[p.xch_rank]);
-        const unsigned total = (p.xch_world - 1u) * nw;
-        for (unsigned i = tid; i < total; i += kThreads) {
-            unsigned w = i / nw;
-            w += w >= p.xch_rank ? 1u : 0u;
-            reinterpret_cast<uint4*>(p.xch_rec[w])[i % nw] = __ldcg(src + i % nw);
-        }
+        const uint4* src = reinterpret_cast<const uint4*>(p.xch_stage);
+        const unsigned total = p.xch_world * nw;
+        for (unsigned i = tid; i < total; i += kThreads)
+            reinterpret_cast<uint4*>(p.xch_rec[i / nw])[i % nw] = __ldcg(src + i % nw);
     }
     __syncthreads();
     if (tid < 32) {
@@ -914,22 +915,24 @@ __device__ __forceinline__ bool scan_body(const ScanLaunch& p, const float* quer
     __syncthreads();
     if (!s_last) return true;
     // Wait until the previous launch on the stream has completed: its finisher may still be writing
-    // its query's result into the same outputs.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // its query's result into the same outputs. With the exchange, this rank's ranking goes to its
+    // own staged record first and the wait comes before the exchange (xch_publish_and_merge).
+    if (!p.xch_world) asm volatile("griddepcontrol.wait;" ::: "memory");
     const unsigned LP = L | 1u;
     ListSums ls;
     if (!finisher_load<kFast>(p, s_cand, s_xcand, LP, G, ls)) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // (a no-op when it has returned before)
         if (tid == 0 && p.out_status) *p.out_status = 2u;  // a CTA's list never arrived: no result
         signal_done(p);
         return true;
     }
 
-    // outputs: the caller's, or this rank's record of the NVLink exchange
+    // outputs: the caller's, or this rank's staged record of the NVLink exchange
     uint64_t* o_ids = p.out_ids;
     float* o_scores = p.out_scores;
     uint32_t* o_count = p.out_count;
     if (p.xch_world) {
-        unsigned char* rec = const_cast<unsigned char*>(p.xch_rec[p.xch_rank]);
+        unsigned char* rec = p.xch_stage;
         o_ids = reinterpret_cast<uint64_t*>(rec);
         o_scores = reinterpret_cast<float*>(rec + (size_t)p.k * 8);
         o_count = reinterpret_cast<uint32_t*>(rec + (size_t)p.k * 12);
