@@ -57,7 +57,7 @@ def parse():
     ap.add_argument("--mode", choices=["fast", "exact"], default="fast")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--e2e-steps", type=int, default=2000)
-    ap.add_argument("--e2e-depth", type=int, default=3, help="host queries in flight in the pipelined e2e")
+    ap.add_argument("--e2e-depth", type=int, default=8, help="host queries in flight in the pipelined e2e")
     ap.add_argument("--ctas-per-query", type=int, default=24,
                     help="CTAs per single-query scan launch in the throughput loops (0: one per SM); fewer let "
                          "consecutive queries run side by side (mrl_set_scan_ctas). The synchronous latency "
@@ -439,11 +439,45 @@ def run_ours(args):
             e2e = dict(sync, h2d_bytes_per_step=qbytes, d2h_bytes_per_step=k * 12 + 4)
         dev.set_stream(torch_stream)
     else:
-        # every rank: host query -> plan -> local scan -> NCCL all-gather + merge kernel -> host result;
-        # synchronous per query, so with one CTA per SM (the lowest latency)
-        dev.set_scan_ctas(0)
         qh = torch.empty((n_q, dims), dtype=torch.float32, pin_memory=True)
         qh.copy_(qd.cpu())
+        piped = None
+        if peer is not None:
+            # pipelined over the NVLink exchange: every rank submits the same host queries with
+            # mrl_query_submit_exchange (the query in its launch's parameters, the merged global top-k
+            # stored by the launch into a pinned device-mapped result slot) and collects them
+            # `depth` behind; one wall-clock interval per rank, max over ranks
+            dev.set_stream(0)
+            depth, maxi = max(1, min(args.e2e_depth, M.MAX_INFLIGHT)), M.MAX_INFLIGHT
+            qn = [qh[j].numpy() for j in range(n_q)]
+            e2e_steps_p = min(args.e2e_steps, n_q)
+
+            def pipelined_x(nsteps):
+                for i in range(nsteps + depth):
+                    if i >= depth:
+                        peer.collect((i - depth) % maxi)
+                    if i < nsteps:
+                        peer.submit(segs[i % len(segs)], qn[i % n_q], desc, cfg, i % maxi)
+
+            pipelined_x(warm)
+            torch.cuda.synchronize()
+            dist.barrier()
+            s0 = time.perf_counter()
+            pipelined_x(e2e_steps_p)
+            tp = torch.tensor([time.perf_counter() - s0], dtype=torch.float64, device="cuda")
+            dev.set_stream(torch_stream)
+            dist.all_reduce(tp, op=dist.ReduceOp.MAX)
+            piped = {"value": world * e2e_steps_p / float(tp.item()), "unit": "QPS", "h2d_bytes_per_step": qbytes,
+                     "d2h_bytes_per_step": k * 12 + 4, "steps": e2e_steps_p, "in_flight": depth,
+                     "ctas_per_query": args.ctas_per_query,
+                     "path": f"per rank: mrl_query_submit_exchange + mrl_query_collect with {depth} queries in "
+                             "flight: each host query travels in its launch's parameters, the launch scans this "
+                             "rank's shard, exchanges records over NVLink and stores the merged global top-256 into "
+                             "a pinned device-mapped result slot that the host reads; one wall-clock interval per "
+                             "rank, max over ranks"}
+        # every rank: host query -> plan -> local scan -> exchange + merge -> host result;
+        # synchronous per query, so with one CTA per SM (the lowest latency)
+        dev.set_scan_ctas(0)
         ids_h = torch.empty(k, dtype=torch.int64, pin_memory=True)
         sc_h = torch.empty(k, dtype=torch.float32, pin_memory=True)
         cnt_h = torch.empty(1, dtype=torch.int32, pin_memory=True)
@@ -491,6 +525,8 @@ def run_ours(args):
                        + "; max over ranks"}
         e2e["ctas_per_query"] = torch.cuda.get_device_properties(local).multi_processor_count
         dev.set_scan_ctas(args.ctas_per_query)
+        if piped is not None:
+            e2e = dict(piped, sync=e2e)
 
     peak, peak_kind = measured_peaks()
     alg_bytes = nb * 4096

@@ -296,6 +296,14 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
                             const uint32_t* time_lo, const uint32_t* time_hi, mrl_exchange* ex,
                             uint64_t* d_out_ids, float* d_out_scores, uint32_t* d_out_count,
                             uint32_t* d_out_status);
+/* mrl_query_submit over the exchange: the host query's fused plan + scan + merge, whose result slot
+ * (collected with mrl_query_collect) receives the GLOBAL top-k over all ranks' segments. Every rank
+ * must submit the same sequence of queries; consecutive submits overlap on the device as with
+ * mrl_query_submit, and a rank ranks its own lists while the previous query's exchange runs.
+ * mrl_query_collect fails when a rank's record did not arrive in time (status bit 2). */
+int mrl_query_submit_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* query, uint32_t dims,
+                              const mrl_codec_desc* codec, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+                              const uint32_t* time_hi, mrl_exchange* ex, uint32_t slot);
 /* ---- exact inner products: dot (src/embed.rs:115-152), bit-identical ------------------------ */
 /* RingBuffer::search_exact (src/ring.rs:109-119): exact dots of the query against n_pending
  * unflushed vectors (device rows, n_pending x dims f32), top k written as one exchange record

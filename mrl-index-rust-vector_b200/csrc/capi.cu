@@ -971,13 +971,45 @@ int ensure_slots(mrl_ctx* ctx, uint32_t k) {
     return MRL_OK;
 }
 
-// Submits one host query into `slot`; plan_out (device, may be NULL) receives its plan.
+// The exchange's checks for a scan of cfg on ctx (mrl_query_scan_exchange, mrl_query_submit_exchange).
+int check_exchange(mrl_ctx* ctx, const mrl_exchange* ex, const mrl_scan_cfg* cfg) {
+    if (!ex->opened) return fail(ctx, MRL_ERR_INVALID, "exchange not opened");
+    if (ex->device != ctx->device) return fail(ctx, MRL_ERR_INVALID, "exchange belongs to another device");
+    if (cfg->shortlist_cand != ex->k) return fail(ctx, MRL_ERR_INVALID, "shortlist_cand differs from the exchange's k");
+    if ((size_t)ex->world * ex->rb > 200 * 1024)
+        return fail(ctx, MRL_ERR_INVALID, "k x world too large to merge in shared memory; use mrl_merge_topk");
+    return MRL_OK;
+}
+
+// The exchange fields of the next scan launch on ctx: the next epoch's buffer parity, this rank's
+// record and flag slots in every area, and the staged record of the launch's scratch set (free once
+// the set's previous user has completed, which the launch waits for before its scoring loop).
+// Call right before take_scratch.
+void set_exchange(mrl_ctx* ctx, mrl_exchange* ex, mrl::ScanLaunch& p) {
+    const uint32_t epoch = ++ex->epoch;
+    const size_t parity = epoch & 1u;
+    p.xch_world = ex->world;
+    p.xch_rank = ex->rank;
+    p.xch_epoch = epoch;
+    for (uint32_t w = 0; w < ex->world; ++w) {
+        p.xch_rec[w] = ex->area[w] + (parity * ex->world + ex->rank) * ex->rb;
+        p.xch_flag[w] = reinterpret_cast<unsigned*>(ex->area[w] + ex->flags_off()) + parity * ex->world + ex->rank;
+    }
+    p.xch_recv = ex->local + parity * ex->world * ex->rb;
+    p.xch_flag_in = reinterpret_cast<const unsigned*>(ex->local + ex->flags_off()) + parity * ex->world;
+    p.xch_stage = ex->stage + (ctx->scan_seq % kScratchSets) * ex->rb;
+}
+
+// Submits one host query into `slot`; plan_out (device, may be NULL) receives its plan. With `ex`
+// the slot receives the global top-k over every rank of the exchange.
 int query_submit(mrl_ctx* ctx, const mrl_seg* seg, const float* query, uint32_t dims, const mrl_codec_desc* codec,
                  mrl::DevPlan* plan_out, const mrl_scan_cfg* cfg, const uint32_t* time_lo, const uint32_t* time_hi,
-                 uint32_t slot) {
+                 uint32_t slot, mrl_exchange* ex = nullptr) {
     if (!ctx || !seg || !query) return MRL_ERR_INVALID;
     if (int rc = check_cfg(ctx, cfg, dims)) return rc;
     if (int rc = check_codec(ctx, codec)) return rc;
+    if (ex)
+        if (int rc = check_exchange(ctx, ex, cfg)) return rc;
     if (slot >= MRL_MAX_INFLIGHT) return fail(ctx, MRL_ERR_INVALID, "slot >= MRL_MAX_INFLIGHT");
     if (ctx->slot_busy[slot]) return fail(ctx, MRL_ERR_INVALID, "slot still holds a query that was not collected");
     if (dims > mrl::kInlineQueryMax) return fail(ctx, MRL_ERR_INVALID, "dims > 1024: use mrl_query_scan_device");
@@ -989,7 +1021,7 @@ int query_submit(mrl_ctx* ctx, const mrl_seg* seg, const float* query, uint32_t 
     unsigned char* h = ctx->h_slots + slot * ctx->slot_stride;
     unsigned char* d = ctx->d_slots + slot * ctx->slot_stride;
     const uint32_t expect = ++ctx->slot_seq[slot];
-    if (seg->n_blocks == 0) {  // nothing to scan
+    if (seg->n_blocks == 0 && !ex) {  // nothing to scan (an exchange rank still takes part)
         volatile uint32_t* cs = reinterpret_cast<volatile uint32_t*>(h + kk * 12);
         cs[0] = 0u;
         cs[1] = 0u;
@@ -1015,6 +1047,7 @@ int query_submit(mrl_ctx* ctx, const mrl_seg* seg, const float* query, uint32_t 
     p.mid_mean = codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr;
     p.mid_seed = codec->mid_seed;
     p.plan_out = plan_out;
+    if (ex) set_exchange(ctx, ex, p);
     take_scratch(ctx, p);
     if (mrl::launch_scan(p, scan_grid(ctx), ctx->stream, true, query)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     launched(ctx);
@@ -1048,6 +1081,7 @@ int query_collect(mrl_ctx* ctx, uint32_t slot, uint64_t* out_ids, float* out_sco
     ctx->slot_busy[slot] = false;
     const uint32_t n = cs[0], st = cs[1];
     if (st & 2u) return fail(ctx, MRL_ERR_CUDA, "scan: a CTA's list never arrived (waited about 1 s)");
+    if (st & 4u) return fail(ctx, MRL_ERR_CUDA, "exchange: a rank's record never arrived (waited about 2-3 s)");
     if (st & 8u) return fail(ctx, MRL_ERR_CUDA, "scan: the context's scratch stayed busy (waited about 1 s)");
     if (out_count) *out_count = n;
     if (out_ids) std::memcpy(out_ids, h, (size_t)n * sizeof(uint64_t));
@@ -1064,6 +1098,13 @@ int mrl_query_submit(mrl_ctx* ctx, const mrl_seg* seg, const float* query, uint3
 
 int mrl_query_collect(mrl_ctx* ctx, uint32_t slot, uint64_t* out_ids, float* out_scores, uint32_t* out_count) {
     return query_collect(ctx, slot, out_ids, out_scores, out_count);
+}
+
+int mrl_query_submit_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* query, uint32_t dims,
+                              const mrl_codec_desc* codec, const mrl_scan_cfg* cfg, const uint32_t* time_lo,
+                              const uint32_t* time_hi, mrl_exchange* ex, uint32_t slot) {
+    if (!ex) return MRL_ERR_INVALID;
+    return query_submit(ctx, seg, query, dims, codec, nullptr, cfg, time_lo, time_hi, slot, ex);
 }
 
 int mrl_query_scan(mrl_ctx* ctx, const mrl_seg* seg, const float* queries, uint32_t n_q, uint32_t dims,
@@ -1193,11 +1234,7 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
     if (!ctx || !seg || !plans || !ex) return MRL_ERR_INVALID;
     if (int rc = check_cfg(ctx, cfg, dims)) return rc;
     if (int rc = check_codec(ctx, codec)) return rc;
-    if (!ex->opened) return fail(ctx, MRL_ERR_INVALID, "exchange not opened");
-    if (ex->device != ctx->device) return fail(ctx, MRL_ERR_INVALID, "exchange belongs to another device");
-    if (cfg->shortlist_cand != ex->k) return fail(ctx, MRL_ERR_INVALID, "shortlist_cand differs from the exchange's k");
-    if ((size_t)ex->world * ex->rb > 200 * 1024)
-        return fail(ctx, MRL_ERR_INVALID, "k x world too large to merge in shared memory; use mrl_merge_topk");
+    if (int rc = check_exchange(ctx, ex, cfg)) return rc;
     if (plans->n_q < 1 || dims != plans->dims) return fail(ctx, MRL_ERR_INVALID, "plan storage too small or dims mismatch");
     if (!d_query || !d_out_ids || !d_out_scores || !d_out_count) return fail(ctx, MRL_ERR_INVALID, "buffer is NULL");
     if (int rc = set_device(ctx)) return rc;
@@ -1218,20 +1255,7 @@ int mrl_query_scan_exchange(mrl_ctx* ctx, const mrl_seg* seg, const float* d_que
     p.mid_mean = codec->mid_codec == MRL_MID_EDEN_B1 ? d_means + 64 : nullptr;
     p.mid_seed = codec->mid_seed;
     p.plan_out = plans->d;
-    const uint32_t epoch = ++ex->epoch;
-    const size_t parity = epoch & 1u;
-    p.xch_world = ex->world;
-    p.xch_rank = ex->rank;
-    p.xch_epoch = epoch;
-    for (uint32_t w = 0; w < ex->world; ++w) {
-        p.xch_rec[w] = ex->area[w] + (parity * ex->world + ex->rank) * ex->rb;
-        p.xch_flag[w] = reinterpret_cast<unsigned*>(ex->area[w] + ex->flags_off()) + parity * ex->world + ex->rank;
-    }
-    p.xch_recv = ex->local + parity * ex->world * ex->rb;
-    p.xch_flag_in = reinterpret_cast<const unsigned*>(ex->local + ex->flags_off()) + parity * ex->world;
-    // the staged record of this launch's scratch set: free once the set's previous user has
-    // completed, which the launch waits for before its scoring loop
-    p.xch_stage = ex->stage + (ctx->scan_seq % kScratchSets) * ex->rb;
+    set_exchange(ctx, ex, p);
     take_scratch(ctx, p);
     if (mrl::launch_scan(p, scan_grid(ctx), ctx->stream, true)) return cuda_fail(ctx, cudaGetLastError(), "scan launch");
     launched(ctx);

@@ -942,6 +942,7 @@ __device__ __forceinline__ bool scan_body(const ScanLaunch& p, const float* quer
         if (p.xch_world) {
             __threadfence();  // the record (stored by every thread) before its copies to the peers
             xch_publish_and_merge(p, s_dyn, &s_ok, 0u);
+            signal_done(p);
         } else {
             if (tid == 0 && p.out_status) *p.out_status = 0u;
             signal_done(p);
@@ -969,6 +970,7 @@ __device__ __forceinline__ bool scan_body(const ScanLaunch& p, const float* quer
     if (p.xch_world) {
         __threadfence();
         xch_publish_and_merge(p, s_dyn, &s_ok, 1u);
+        signal_done(p);
         return true;
     }
     if (tid == 0 && p.out_status) *p.out_status = 1u;

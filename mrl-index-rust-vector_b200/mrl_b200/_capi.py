@@ -98,6 +98,8 @@ SIGNATURES = {
     "mrl_exchange_create": (_i, [_vp, _u32, _u32, _u32, _vp, C.POINTER(_vp)]),
     "mrl_exchange_open": (_i, [_vp, _vp, _vp]),
     "mrl_exchange_destroy": (_i, [_vp, _vp]),
+    "mrl_query_submit_exchange": (_i, [_vp, _vp, _vp, _u32, C.POINTER(CodecDesc), C.POINTER(ScanCfgC), _vp, _vp, _vp,
+                                       _u32]),
     "mrl_query_scan_exchange": (_i, [_vp, _vp, _vp, _u32, C.POINTER(CodecDesc), _vp, C.POINTER(ScanCfgC), _vp, _vp,
                                      _vp, _vp, _vp, _vp, _vp]),
     "mrl_segment_load": (_i, [_vp, C.c_char_p, _u32, C.POINTER(_vp)]),

@@ -182,6 +182,26 @@ class PeerExchange:
             self.ptr, C.c_void_p(d_ids), C.c_void_p(d_scores), C.c_void_p(d_count),
             C.c_void_p(d_status) if d_status else None))
 
+    def submit(self, segment, query, desc, cfg_c, slot: int, time_lo=None, time_hi=None):
+        """Pipelined host query (mrl_query_submit_exchange): launches the fused plan + scan + merge
+        of the host query `query` into the context's result slot `slot` and returns at once; every
+        rank submits the same sequence. `collect(slot)` returns the global top-k."""
+        q = np.ascontiguousarray(query, np.float32).reshape(-1)
+        lo = None if time_lo is None else C.byref(C.c_uint32(int(time_lo)))
+        hi = None if time_hi is None else C.byref(C.c_uint32(int(time_hi)))
+        check(self.dev.ptr, self.dev.lib.mrl_query_submit_exchange(
+            self.dev.ptr, segment.ptr, q.ctypes.data_as(C.c_void_p), q.shape[0], C.byref(desc), C.byref(cfg_c), lo, hi,
+            self.ptr, slot))
+
+    def collect(self, slot: int):
+        """(ids [count] u64, scores [count] f32): the global top-k of the query in `slot`."""
+        ids = np.zeros(self.k, np.uint64)
+        sc = np.zeros(self.k, np.float32)
+        n = np.zeros(1, np.uint32)
+        check(self.dev.ptr, self.dev.lib.mrl_query_collect(self.dev.ptr, slot, ids.ctypes.data_as(C.c_void_p),
+                                                           sc.ctypes.data_as(C.c_void_p), n.ctypes.data_as(C.c_void_p)))
+        return ids[:int(n[0])], sc[:int(n[0])]
+
     def close(self):
         import torch.distributed as dist
 

@@ -89,6 +89,64 @@ def test_exchange_world1_matches_device_scan(ora, dev, mode, list_len):
     del keep
 
 
+@pytest.mark.parametrize("mode", ["FAST", "EXACT"])
+def test_exchange_world1_submit_pipelined(ora, dev, mode):
+    """mrl_query_submit_exchange with world 1: host queries submitted several at a time (slots,
+    scratch sets and buffer parities reused) end in the same top-k as mrl_query_scan_device."""
+    import torch
+
+    M = mb()
+    lib = dev.lib
+    blocks, mean, qs = _corpus(ora)
+    qs = np.concatenate([qs, qs[::-1] * 0.5])  # 8 queries
+    seg = M.Segment.upload(blocks, dev)
+    k = 256
+    cfg = M.ScanConfig(shortlist_cand=k, mode=getattr(M.ScanMode, mode)).to_c()
+    desc, keep = M.api._codec_desc(M.PrefixCodec.EDEN_PROD, M.MidCodec.RABITQ, M.EdenFit(64, 4, 1, mean), None)
+    plans = C.c_void_p()
+    M._capi.check(dev.ptr, lib.mrl_plans_alloc(dev.ptr, 1, 768, C.byref(plans)))
+    ex = C.c_void_p()
+    M._capi.check(dev.ptr, lib.mrl_exchange_create(dev.ptr, 1, 0, k, None, C.byref(ex)))
+    dq = torch.from_numpy(np.ascontiguousarray(qs, np.float32)).cuda()
+    try:
+        want = []
+        for qi in range(len(qs)):
+            a = _device_outputs(k)
+            M._capi.check(dev.ptr, lib.mrl_query_scan_device(dev.ptr, seg.ptr, C.c_void_p(dq.data_ptr() + qi * 768 * 4),
+                                                             1, 768, C.byref(desc), plans, C.byref(cfg), None, None,
+                                                             *[C.c_void_p(t.data_ptr()) for t in a]))
+            torch.cuda.synchronize()
+            n = int(a[2].item())
+            want.append((a[0][:n].cpu().numpy().view(np.uint64).copy(), a[1][:n].cpu().numpy().view(np.uint32).copy()))
+        ids = np.zeros(k, np.uint64)
+        sc = np.zeros(k, np.float32)
+        cnt = np.zeros(1, np.uint32)
+        order = list(range(len(qs))) * 3  # 24 queries over 8 slots, 8 in flight at a time
+        for i0 in range(0, len(order), 8):
+            batch = order[i0:i0 + 8]
+            for slot, qi in enumerate(batch):
+                q = np.ascontiguousarray(qs[qi], np.float32)
+                M._capi.check(dev.ptr, lib.mrl_query_submit_exchange(dev.ptr, seg.ptr, q.ctypes.data_as(C.c_void_p), 768,
+                                                                     C.byref(desc), C.byref(cfg), None, None, ex, slot))
+            for slot, qi in enumerate(batch):
+                M._capi.check(dev.ptr, lib.mrl_query_collect(dev.ptr, slot, ids.ctypes.data_as(C.c_void_p),
+                                                             sc.ctypes.data_as(C.c_void_p), cnt.ctypes.data_as(C.c_void_p)))
+                n = int(cnt[0])
+                assert n == len(want[qi][0]), (i0, slot)
+                assert np.array_equal(ids[:n], want[qi][0]), (i0, slot)
+                assert np.array_equal(sc[:n].view(np.uint32), want[qi][1]), (i0, slot)
+        # misuse: a different k than the exchange's is refused
+        bad = M.ScanConfig(shortlist_cand=16, mode=getattr(M.ScanMode, mode)).to_c()
+        q = np.ascontiguousarray(qs[0], np.float32)
+        assert lib.mrl_query_submit_exchange(dev.ptr, seg.ptr, q.ctypes.data_as(C.c_void_p), 768, C.byref(desc),
+                                             C.byref(bad), None, None, ex, 0) != 0
+    finally:
+        lib.mrl_exchange_destroy(dev.ptr, ex)
+        lib.mrl_plans_free(dev.ptr, plans)
+        seg.free()
+    del keep
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -124,6 +182,7 @@ def _rank_main(rank, world, port, k, mode, list_len):
         px = M.PeerExchange(dev, k)
         dq = torch.from_numpy(np.ascontiguousarray(qs, np.float32)).cuda()
         dev.set_list_len(list_len)
+        want = []
         for qi in range(len(qs)):
             a = _device_outputs(k)
             b = _device_outputs(k)
@@ -139,6 +198,16 @@ def _rank_main(rank, world, port, k, mode, list_len):
             assert int(b[3].item()) & 6 == 0, (rank, qi, int(b[3].item()))
             assert torch.equal(a[0][:n], b[0][:n]), (rank, qi)
             assert np.array_equal(a[1][:n].cpu().numpy().view(np.uint32), b[1][:n].cpu().numpy().view(np.uint32))
+            want.append((a[0][:n].cpu().numpy().view(np.uint64).copy(), a[1][:n].cpu().numpy().view(np.uint32).copy()))
+        # pipelined host queries over the exchange: every query submitted before the first collect
+        # (all in flight together), twice over so slots, scratch sets and parities are reused
+        for rnd in range(2):
+            for qi in range(len(qs)):
+                px.submit(seg, qs[qi], desc, cfg, qi)
+            for qi in range(len(qs)):
+                ids, sc = px.collect(qi)
+                assert np.array_equal(ids, want[qi][0]), (rank, rnd, qi)
+                assert np.array_equal(sc.view(np.uint32), want[qi][1]), (rank, rnd, qi)
         dev.set_list_len(0)
         px.close()
         del keep
