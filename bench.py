@@ -449,15 +449,24 @@ def run_ours(args):
             # `depth` behind; one wall-clock interval per rank, max over ranks
             dev.set_stream(0)
             depth, maxi = max(1, min(args.e2e_depth, M.MAX_INFLIGHT)), M.MAX_INFLIGHT
-            qn = [qh[j].numpy() for j in range(n_q)]
             e2e_steps_p = min(args.e2e_steps, n_q)
+            # the calls' fixed arguments built once, as a serving loop would hold them
+            fn_sx, fn_c, ctx, check = lib.mrl_query_submit_exchange, lib.mrl_query_collect, dev.ptr, M._capi.check
+            seg_ptrs = [sg.ptr for sg in segs]
+            q_ptrs = [C.c_void_p(qh.data_ptr() + j * qbytes) for j in range(n_q)]
+            desc_ref, cfg_ref = C.byref(desc), C.byref(cfg)
+            ids_x = torch.empty(k, dtype=torch.int64, pin_memory=True)
+            sc_x = torch.empty(k, dtype=torch.float32, pin_memory=True)
+            cnt_x = torch.empty(1, dtype=torch.int32, pin_memory=True)
+            out_x = (C.c_void_p(ids_x.data_ptr()), C.c_void_p(sc_x.data_ptr()), C.c_void_p(cnt_x.data_ptr()))
 
             def pipelined_x(nsteps):
                 for i in range(nsteps + depth):
                     if i >= depth:
-                        peer.collect((i - depth) % maxi)
+                        check(ctx, fn_c(ctx, (i - depth) % maxi, *out_x))
                     if i < nsteps:
-                        peer.submit(segs[i % len(segs)], qn[i % n_q], desc, cfg, i % maxi)
+                        check(ctx, fn_sx(ctx, seg_ptrs[i % len(segs)], q_ptrs[i % n_q], dims, desc_ref, cfg_ref, None,
+                                         None, peer.ptr, i % maxi))
 
             pipelined_x(warm)
             torch.cuda.synchronize()

@@ -195,12 +195,12 @@ class PeerExchange:
 
     def collect(self, slot: int):
         """(ids [count] u64, scores [count] f32): the global top-k of the query in `slot`."""
-        ids = np.zeros(self.k, np.uint64)
-        sc = np.zeros(self.k, np.float32)
-        n = np.zeros(1, np.uint32)
-        check(self.dev.ptr, self.dev.lib.mrl_query_collect(self.dev.ptr, slot, ids.ctypes.data_as(C.c_void_p),
-                                                           sc.ctypes.data_as(C.c_void_p), n.ctypes.data_as(C.c_void_p)))
-        return ids[:int(n[0])], sc[:int(n[0])]
+        if not hasattr(self, "_out"):  # result buffers kept across calls
+            self._out = (np.zeros(self.k, np.uint64), np.zeros(self.k, np.float32), np.zeros(1, np.uint32))
+            self._out_p = tuple(a.ctypes.data_as(C.c_void_p) for a in self._out)
+        ids, sc, n = self._out
+        check(self.dev.ptr, self.dev.lib.mrl_query_collect(self.dev.ptr, slot, *self._out_p))
+        return ids[:int(n[0])].copy(), sc[:int(n[0])].copy()
 
     def close(self):
         import torch.distributed as dist
