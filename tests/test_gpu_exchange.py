@@ -2,9 +2,11 @@
 records inside the scan launch.
 
 On one GPU an exchange of world 1 must reproduce mrl_query_scan_device exactly, across
-consecutive queries (both buffer parities) and through the rare re-selection path. With two or
-more GPUs, two ranks (one process per GPU, handles exchanged over gloo) scan one half of a corpus
-each, and every rank must end with the global top-k of a single-GPU scan of the whole corpus.
+consecutive queries (both buffer parities), through the rare re-selection path, and for host
+queries submitted several at a time (mrl_query_submit_exchange). With two or more GPUs, two ranks
+(one process per GPU, handles exchanged over gloo) scan one half of a corpus each, and every rank
+must end with the global top-k of a single-GPU scan of the whole corpus, for device queries and
+for host queries in flight.
 """
 import ctypes as C
 import os
